@@ -1,0 +1,484 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 kvcache path: LMCache-style multi-layer batch copy.
+
+Workload ("cfg2"): Llama-3-8B KV shape, bf16, 32 layers,
+8 kv heads x 128, block_size 16, 32768 blocks per layer held as an LMCache layer
+list of ``[2, NB, BS, NH, HS]`` tensors (64 GiB per GPU); 64 requests with
+lengths uniform in [256, 4096] whose block tables come from one random
+permutation.  One step = gather every layer into the contiguous buffer
+``[2, 32, T, 1024]`` (``lmcache_kv_paged_to_buffer``) and scatter it back
+(``lmcache_kv_buffer_to_paged``), all layers in one launch each.
+
+Metric: achieved HBM GB/s of algorithmic bytes (payload read + written, index
+arrays excluded) = 4 * (2 * L * T * 1024 * 2 B) per step / device time.
+
+Multi-GPU (torchrun, one process per GPU): each rank owns its own 32-layer
+layer shard (weak scaling, no collective on the data path); the timed region
+is bracketed by barriers + device syncs and the max over ranks is reported.
+
+``--impl reference`` times the reference algorithm's CPU restatement
+(``oracle/``) on the host cores instead (rank 0 only under torchrun).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "musa-aiter_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "KV gather/scatter/FP8-store HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("native", "reference"), default="native")
+    ap.add_argument("--layers", type=int, default=32, help="layers per rank (32 = configs[1])")
+    ap.add_argument("--blocks", type=int, default=32768)
+    ap.add_argument("--requests", type=int, default=64)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-requests", type=int, default=8, help="requests in the bounded CPU sample")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+BS, NH, HS = 16, 8, 128
+HIDDEN = NH * HS
+
+
+def request_lengths(n: int) -> list[int]:
+    g = torch.Generator().manual_seed(2)
+    return torch.randint(256, 4097, (n,), generator=g).tolist()
+
+
+def block_slots(lens: list[int], nb: int) -> torch.Tensor:
+    """Per-request block tables from one permutation of the block ids (seed 1)."""
+    g = torch.Generator().manual_seed(1)
+    perm = torch.randperm(nb, generator=g)
+    out, used = [], 0
+    for n in lens:
+        k = (n + BS - 1) // BS
+        bt = perm[used: used + k]
+        used += k
+        pos = torch.arange(n)
+        out.append(bt[pos // BS] * BS + pos % BS)
+    if used > nb:
+        raise ValueError("not enough blocks for the requests")
+    return torch.cat(out).to(torch.int64)
+
+
+def payload_bytes(layers: int, tokens: int) -> int:
+    return 2 * layers * tokens * HIDDEN * 2
+
+
+# ---------------------------------------------------------------------------
+# measurement helpers
+# ---------------------------------------------------------------------------
+
+
+def load_peak() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic(name: str) -> dict | None:
+    """Per-launch DRAM bytes from a committed ncu summary (``profiles/<name>``), if present."""
+    path = ROOT / "profiles" / name
+    if not path.exists():
+        return None
+    fields = {}
+    for line in path.read_text().splitlines():
+        if line.startswith("bench-traffic:"):
+            for kv in line.split(":", 1)[1].split():
+                k, v = kv.split("=")
+                fields[k] = float(v)
+    return fields or None
+
+
+class ClockSampler:
+    """NVML sampling of SM clock and clock-event reasons during the timed region."""
+
+    REASONS = {
+        0x1: "gpu_idle",
+        0x2: "applications_clocks_setting",
+        0x4: "sw_power_cap",
+        0x8: "hw_slowdown",
+        0x10: "sync_boost",
+        0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int):
+        self.samples: list[int] = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def start(self):
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self) -> dict:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+        names = sorted(n for bit, n in self.REASONS.items() if self.reasons & bit)
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": names,
+            "samples": len(self.samples),
+        }
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle restatement of the reference algorithm)
+# ---------------------------------------------------------------------------
+
+
+def cpu_sample(layers: int, nb_total: int, n_requests: int, caches_gpu=None):
+    """Compacted host copy of the first ``n_requests`` requests' blocks for every layer.
+
+    Returns (caches as numpy uint16 [2, nb_s, BS, NH, HS] per layer, remapped slots, tokens).
+    With ``caches_gpu`` the values are the GPU caches' own blocks; otherwise seeded random.
+    """
+    lens = request_lengths(64)[:n_requests]
+    slots = block_slots(lens, nb_total)
+    blocks = torch.unique(slots // BS)
+    remap = torch.full((nb_total,), -1, dtype=torch.int64)
+    remap[blocks] = torch.arange(blocks.numel())
+    new_slots = (remap[slots // BS] * BS + slots % BS).numpy()
+    caches = []
+    rng = np.random.default_rng(0)
+    for layer in range(layers):
+        if caches_gpu is not None:
+            c = caches_gpu[layer].index_select(1, blocks.to(caches_gpu[layer].device)).cpu()
+            caches.append(c.view(torch.int16).numpy().view(np.uint16))
+        else:
+            caches.append(rng.integers(0, 1 << 16, size=(2, blocks.numel(), BS, NH, HS), dtype=np.uint16))
+    return caches, new_slots, int(slots.numel())
+
+
+def cpu_step(caches, slots, mem, threads: int):
+    from oracle import kv_oracle as O
+
+    O.lmcache_list_paged_to_buffer(caches, mem, slots, threads=threads)
+    O.lmcache_list_buffer_to_paged(mem, caches, slots, 0, threads=threads)
+
+
+def time_cpu(caches, slots, tokens: int, steps: int, warmup: int, threads: int):
+    mem = np.empty((2, len(caches), tokens, HIDDEN), dtype=np.uint16)
+    for _ in range(warmup):
+        cpu_step(caches, slots, mem, threads)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_step(caches, slots, mem, threads)
+    dt = (time.perf_counter() - t0) / steps
+    return 4 * payload_bytes(len(caches), tokens) / dt / 1e9, dt
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+
+
+def config_block(args, tokens: int, world: int) -> dict:
+    return {
+        "workload": "cfg2 LMCache-style multi-layer batch copy (gather to [2,L,T,1024] + scatter back, all layers one launch each)",
+        "layers_per_rank": args.layers,
+        "total_layers": args.layers * world,
+        "num_blocks": args.blocks,
+        "block_size": BS,
+        "kv_heads": NH,
+        "head_size": HS,
+        "requests": args.requests,
+        "tokens": tokens,
+        "cache_layout": "LMCache layer list of [2, NB, BS, NH, HS]",
+        "parallelism": f"layer-sharded x{world} (weak: {args.layers} layers per rank)",
+        "l2": "inputs larger than L2 (buffer and caches are tens of GB), no flush needed",
+    }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    n_req = min(args.cpu_requests, args.requests)
+    caches, slots, tokens = cpu_sample(args.layers, args.blocks, n_req)
+    gbs, dt = time_cpu(caches, slots, tokens, max(1, args.steps), max(0, args.warmup), threads)
+    sample = f"first {n_req} of {args.requests} requests ({tokens} tokens) x {args.layers} layers, touched blocks compacted"
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": config_block(args, int(block_slots(request_lengths(args.requests), args.blocks).numel()), 1),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_native(args) -> None:
+    import torch.distributed as dist
+
+    import musa_aiter as ma
+    from musa_aiter import _native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    lens = request_lengths(args.requests)
+    slots_cpu = block_slots(lens, args.blocks)
+    tokens = int(slots_cpu.numel())
+    slots = slots_cpu.to(dev)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    caches = []
+    for _ in range(args.layers):
+        c = torch.empty((2, args.blocks, BS, NH, HS), dtype=torch.bfloat16, device=dev)
+        c.normal_(generator=g)
+        caches.append(c)
+    mem = torch.empty((2, args.layers, tokens, HIDDEN), dtype=torch.bfloat16, device=dev)
+    P = payload_bytes(args.layers, tokens)
+
+    def gather():
+        ma.lmcache_kv_paged_to_buffer(caches, mem, slots, BS, NH, HS)
+
+    def scatter():
+        ma.lmcache_kv_buffer_to_paged(mem, caches, slots, 0, BS, NH, HS)
+
+    for _ in range(args.warmup):
+        gather()
+        scatter()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+
+    sampler = ClockSampler(local)
+    stream = torch.cuda.current_stream(dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _native.launch_count()
+    sampler.start()
+    start.record(stream)
+    for k in range(args.steps):
+        ev[k][0].record(stream)
+        gather()
+        ev[k][1].record(stream)
+        scatter()
+        ev[k][2].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    launches = _native.launch_count() - launches0
+    barrier()
+    torch.cuda.synchronize(dev)
+
+    total_ms = start.elapsed_time(end)
+    gather_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    scatter_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+
+    step_ms = total_ms / args.steps
+    value = world * 4 * P / (step_ms * 1e-3) / 1e9
+    peak, peak_kind = load_peak()
+    achieved = 2 * P / (gather_ms * 1e-3) / 1e9
+    traffic = None
+    prof = load_traffic("rows_kernel_cfg2.md")
+    if prof and "dram_bytes_per_unit_row" in prof:
+        traffic = int(prof["dram_bytes_per_unit_row"] * 2 * args.layers * tokens)
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, dev, caches, mem, slots_cpu, P, gather, scatter, barrier, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        n_req = min(args.cpu_requests, args.requests)
+        c_caches, c_slots, c_tokens = cpu_sample(args.layers, args.blocks, n_req, caches)
+        gbs, _ = time_cpu(c_caches, c_slots, c_tokens, 1, 0, threads)
+        cpu = {
+            "value": round(gbs, 3),
+            "unit": "GB/s",
+            "cores": threads,
+            "kind": "port",
+            "sample": f"first {n_req} of {args.requests} requests ({c_tokens} tokens) x {args.layers} layers, touched blocks compacted; numpy restatement of the reference loops",
+        }
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(step_ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": config_block(args, tokens, world),
+            "frac_of_8tbs": round(value / world / 8000.0, 4),
+            "gather_gbs": round(2 * P / (gather_ms * 1e-3) / 1e9, 2),
+            "scatter_call_gbs": round(2 * P / (scatter_ms * 1e-3) / 1e9, 2),
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "rows_kernel<16> (gather launch)",
+                "achieved": round(achieved, 2),
+                "peak": peak,
+                "peak_source": f"{peak_kind} hbm_gbs",
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "traffic": traffic,
+                "algorithmic_bytes_per_launch": 2 * P,
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(args, dev, caches, mem, slots_cpu, P, gather, scatter, barrier, world):
+    """End to end through the public API with HOST buffers: each step copies the
+    slot mapping host->device, gathers every layer, copies the buffer to pinned
+    host memory (the LMCache store), copies it back and scatters it (retrieve)."""
+    import psutil
+
+    import musa_aiter as ma
+
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    avail = psutil.virtual_memory().available
+    if P * local_world * 1.3 > avail:
+        return {"value": None, "unit": "GB/s", "skipped": f"host RAM {avail >> 30} GiB too small for {local_world} x {P >> 30} GiB pinned buffers"}
+    host_mem = torch.empty(mem.shape, dtype=mem.dtype, pin_memory=True)
+    host_slots = slots_cpu.pin_memory()
+    dev_slots = torch.empty_like(slots_cpu, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    bs = BS
+
+    def step():
+        dev_slots.copy_(host_slots, non_blocking=True)
+        ma.lmcache_kv_paged_to_buffer(caches, mem, dev_slots, bs, NH, HS)
+        host_mem.copy_(mem, non_blocking=True)
+        mem.copy_(host_mem, non_blocking=True)
+        ma.lmcache_kv_buffer_to_paged(mem, caches, dev_slots, 0, bs, NH, HS)
+
+    steps = max(2, min(args.steps, 5))
+    step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / steps
+    barrier()
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del host_mem
+    return {
+        "value": round(world * 4 * P / (ms * 1e-3) / 1e9, 3),
+        "unit": "GB/s",
+        "h2d_bytes_per_step": int(P + slots_cpu.numel() * 8),
+        "d2h_bytes_per_step": int(P),
+        "steps": steps,
+        "ms_per_step": round(ms, 3),
+        "path": "pinned host slots -> device; lmcache_kv_paged_to_buffer; buffer D2H to pinned host; H2D back; lmcache_kv_buffer_to_paged",
+    }
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,268 @@
+/*
+ * mak_kvcache.h — C ABI of the B200 (sm_100a) KV-cache movement and FP8
+ * quantization library (libmak_kvcache.so).
+ *
+ * This is the drop-in native boundary for the `kvcache` operator family of
+ * musa-aiter.  Every entry point takes plain device pointers, sizes and a
+ * CUDA stream (`void*` holding a cudaStream_t; NULL = legacy default stream),
+ * enqueues its kernels on that stream without synchronising, and returns
+ * MAK_OK (0) or a negative MAK_E_* status.  `mak_last_error()` gives a
+ * thread-local message for the last failing call on the calling thread.
+ *
+ * The library allocates no device memory.  Entry points that need scratch
+ * memory (last-writer-wins resolution of duplicate destination slots) take a
+ * caller-owned workspace whose size is given by `mak_scatter_workspace_bytes`.
+ *
+ * Layout vocabulary (element strides unless stated otherwise):
+ *   - "tile" caches keep block_size innermost: [L][NB][NH][HD][BS]
+ *     (reference layout of musa_aiter/ops/kv_transfer.py:2987-3000);
+ *   - "row" caches keep a token's hidden vector contiguous: [..][NB][BS][W]
+ *     (LMCache, SGLang MP, MLA flat caches, DSV4 byte rows, HiCache pages).
+ *
+ * Each entry point names the reference launcher(s) it replaces.  Reference
+ * paths are relative to the musa-aiter v0.5.0 source tree.
+ */
+#ifndef MAK_KVCACHE_H
+#define MAK_KVCACHE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MAK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MAK_API __attribute__((visibility("default")))
+#else
+#define MAK_API
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define MAK_OK 0
+#define MAK_E_INVALID (-1)     /* bad shape, stride, pointer or argument */
+#define MAK_E_UNSUPPORTED (-2) /* valid request this build does not handle */
+#define MAK_E_WORKSPACE (-3)   /* workspace missing or too small */
+#define MAK_E_CUDA (-4)        /* a CUDA runtime call or launch failed */
+
+/* ---- element / index type codes ----------------------------------------- */
+#define MAK_DT_U8 0
+#define MAK_DT_F16 1
+#define MAK_DT_BF16 2
+#define MAK_DT_F32 3
+#define MAK_DT_I32 4
+#define MAK_DT_I64 5
+
+/* ---- FP8 formats and scale modes ---------------------------------------- */
+#define MAK_FP8_E4M3 1 /* 4 exponent bits, bias 7, finite max 480 (code 0x7F) */
+#define MAK_FP8_E5M2 2 /* 5 exponent bits, bias 15, finite max 114688 */
+
+#define MAK_SCALE_SCALAR 0         /* scale[0] */
+#define MAK_SCALE_PER_HEAD 1       /* scale[h], h < num_heads */
+#define MAK_SCALE_PER_LAYER_HEAD 2 /* scale[l * num_heads + h] */
+
+/* Maximum planes (cache tensors) one row-family call may name. */
+#define MAK_MAX_PLANES 4096
+
+/*
+ * Tile cache: element (l, b, h, d, o) of plane kv lives at
+ *   k_or_v + l*stride_layer + b*stride_block + h*stride_head + d*stride_dim + o
+ * (the block-offset stride is 1).  `v` may be NULL for single-plane calls.
+ */
+typedef struct mak_paged_desc {
+  void* k;
+  void* v;
+  int64_t num_layers;
+  int64_t num_blocks;
+  int64_t num_heads;
+  int64_t head_dim;
+  int64_t block_size;
+  int64_t stride_layer;
+  int64_t stride_block;
+  int64_t stride_head;
+  int64_t stride_dim;
+  int32_t dtype; /* MAK_DT_* of the stored elements (U8 for FP8 caches) */
+  int32_t reserved;
+} mak_paged_desc;
+
+/*
+ * Token-major linear buffer: element (l, t, h, d) of plane kv lives at
+ *   k_or_v + l*stride_layer + t*stride_token + h*stride_head + d
+ * (head_dim stride is 1).  Merged [T,2,NH,HD] buffers are two planes whose
+ * pointers differ by NH*HD elements and whose stride_token is 2*NH*HD.
+ */
+typedef struct mak_linear_desc {
+  void* k;
+  void* v;
+  int64_t num_tokens;
+  int64_t stride_layer;
+  int64_t stride_token;
+  int64_t stride_head;
+  int32_t dtype;
+  int32_t reserved;
+} mak_linear_desc;
+
+/*
+ * Row side: `num_planes` planes whose row r lives at
+ *   plane_ptrs[p] + (r / rows_per_block)*block_stride + (r % rows_per_block)*row_stride
+ * (strides in BYTES).  Rows r outside [0, num_rows) are skipped by the
+ * kernels (never read or written), so a bad index cannot fault the GPU;
+ * callers that must reject them validate first with `mak_slot_max`.
+ * `plane_ptrs` is a HOST array of device addresses; `row_bytes` (host array,
+ * may be NULL = all planes use `row_bytes0`) gives each plane's row width.
+ */
+typedef struct mak_rows_desc {
+  const uint64_t* plane_ptrs;
+  int64_t num_planes;
+  int64_t rows_per_block;
+  int64_t block_stride;
+  int64_t row_stride;
+  int64_t num_rows;
+} mak_rows_desc;
+
+/* ---- library probes ------------------------------------------------------ */
+
+/* ABI version (replaces the *_abi_version getters,
+ * csrc/kvcache/kv_transfer_float.mu:3021-3027, fp8_kv_cache.mu:1529,
+ * hicache_transfer.mu:53). */
+MAK_API int mak_abi_version(void);
+
+/* Thread-local message of the last failing call on this thread. */
+MAK_API const char* mak_last_error(void);
+
+/* Number of SMs of the current device (cached per device). */
+MAK_API int mak_device_sm_count(void);
+
+/* Host-side count of kernels this library has launched since load (all
+ * devices, all threads).  Used by benchmarks to report their launch count. */
+MAK_API uint64_t mak_launch_count(void);
+
+/* ---- plan builder --------------------------------------------------------- */
+
+/*
+ * Device reduction for slot validation: writes max(slots) (or -1 when every
+ * slot is negative) to *out_max (device int64).  One launch; no sync.
+ * Replaces the host-synchronising checks of musa_aiter/ops/kv_transfer.py:3020-3028.
+ */
+MAK_API int mak_slot_max(const void* slots, int32_t slot_dtype, int64_t n, int64_t* out_max, void* stream);
+
+/* Bytes of workspace the scatter entry points need for `n_items` slots. */
+MAK_API size_t mak_scatter_workspace_bytes(int64_t n_items);
+
+/*
+ * Last-writer-wins resolution: writes eff[i] = slots[i] when i is the last
+ * index holding that slot value, else -1 (negative slots stay -1).  Uses the
+ * workspace as an open-addressing hash table.  `eff` (int64, n entries) may
+ * live inside the workspace tail (see mak_scatter_workspace_bytes).
+ * Reference semantics: sequential token loop of musa_aiter/ops/kv_transfer.py:3092-3112.
+ */
+MAK_API int mak_resolve_last_writer(const void* slots, int32_t slot_dtype, int64_t n, int64_t* eff, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/*
+ * Dense slot mapping from block tables: for sequence b and position s < max_seq,
+ *   slots[b*max_seq + s] = s < seq_lens[b] ? block_tables[b*bt_stride + s/block_size]*block_size + s%block_size : -1.
+ * Replaces the per-sequence Python slot building of
+ * musa_aiter/ops/kv_transfer.py:1779-1791 and the block-table walk of
+ * csrc/kvcache/kv_transfer_float.mu:985-1164.
+ */
+MAK_API int mak_build_slot_mapping(const void* block_tables, int32_t bt_dtype, int64_t bt_stride, const void* seq_lens,
+                           int32_t len_dtype, int64_t batch, int64_t max_seq, int64_t block_size, int64_t* slots,
+                           void* stream);
+
+/* ---- tile family ([L][NB][NH][HD][BS] caches) --------------------------- */
+
+/*
+ * Gather cache slots into token rows, every layer of `cache` in one launch.
+ * fill_zero=1 writes zeros for negative slots ("zeros"), 0 leaves them
+ * untouched ("preserve").  Slots >= NB*BS are skipped.
+ * Replaces musa_aiter_kv_paged_to_linear_{float,half,bfloat16},
+ * ..._multi_layer_*, ..._paged_to_merged_linear[_multi_layer]_*
+ * (csrc/kvcache/kv_transfer_float.mu:16-86, 237-312, 387-671;
+ *  lmcache_kv_transfer_extended.mu:241-401).
+ */
+MAK_API int mak_kv_paged_to_linear(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
+                           int32_t slot_dtype, int32_t fill_zero, void* stream);
+
+/*
+ * Scatter token rows into cache slots (negative slots skipped, duplicate
+ * slots: the last token wins).  Needs mak_scatter_workspace_bytes(T) bytes.
+ * Replaces musa_aiter_kv_linear_to_paged_*, ..._multi_layer_*,
+ * ..._merged_linear_to_paged[_multi_layer]_*
+ * (csrc/kvcache/kv_transfer_float.mu:169-235, 314-385, 387-671).
+ */
+MAK_API int mak_kv_linear_to_paged(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                           int32_t slot_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * FP8 gather + dequantize: out = decode(cache byte) * scale, rounded to the
+ * output dtype (F16/BF16/F32); negative slots give zeros.
+ * Replaces musa_aiter_kv_paged_fp8_to_linear_{e4m3,e5m2}, the vec4/hd*_bs*
+ * variants and the multi-layer ones (csrc/kvcache/fp8_kv_cache.mu:183-272,
+ * 363-452, 454-740, 742-1460).
+ */
+MAK_API int mak_kv_paged_fp8_to_linear(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
+                               int32_t slot_dtype, const float* k_scale, const float* v_scale, int32_t scale_mode,
+                               int32_t fp8_format, void* stream);
+
+/*
+ * FP8 quantize + scatter: byte = encode(x / scale) with the musa-aiter
+ * reference encoder (round-half-even mantissa, flush below min-normal,
+ * saturate to the format's largest finite code, non-finite -> signed zero).
+ * Duplicate slots: the last token wins.
+ * Replaces musa_aiter_kv_linear_to_paged_fp8_{e4m3,e5m2} and the vec4 and
+ * multi-layer variants (csrc/kvcache/fp8_kv_cache.mu:146-272, 326-452,
+ * 454-740, 742-882).
+ */
+MAK_API int mak_kv_linear_to_paged_fp8(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                               int32_t slot_dtype, const float* k_scale, const float* v_scale, int32_t scale_mode,
+                               int32_t fp8_format, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- row family (token-major caches) ------------------------------------ */
+
+/*
+ * Gather: for every plane p and token t < linear->num_rows,
+ *   t < n_slots and slots[t] valid -> linear row t = paged row slots[t];
+ *   otherwise (negative slot, out-of-range slot, or t >= n_slots) the linear
+ *   row is zeroed when fill_zero=1 and left untouched when fill_zero=0.
+ * paged and linear must name the same number of planes.
+ * Replaces lmcache_paged_to_kv_buffer[_u16], ..._mla[_u16], ..._list_{u16,float},
+ * ..._two_x_nl_{u16,float}, ..._two_x_nl_coalesced_u16, lmcache_mla_paged_to_buffer_list_*,
+ * musa_aiter_kv_paged_to_mla_linear_* (csrc/kvcache/kv_transfer_float.mu:1592-1934,
+ * 2032-2441, 673-826; lmcache_kv_transfer_extended.mu:7-239, 403-478).
+ */
+MAK_API int mak_rows_gather(const mak_rows_desc* paged, const mak_rows_desc* linear, const int64_t* row_bytes,
+                    int64_t row_bytes0, const void* slots, int32_t slot_dtype, int64_t n_slots, int32_t fill_zero,
+                    void* stream);
+
+/*
+ * Scatter: for every plane p and t < n_slots with slots[t] >= 0,
+ *   paged row slots[t] = linear row (t + skip_prefix); duplicates: last t wins.
+ * Needs mak_scatter_workspace_bytes(n_slots) bytes of workspace.
+ * Replaces lmcache_kv_buffer_to_paged[_u16], ..._mla[_u16], ..._list_*,
+ * ..._two_x_nl_*, lmcache_mla_buffer_to_paged_list_*, musa_aiter_kv_mla_linear_to_paged_*.
+ */
+MAK_API int mak_rows_scatter(const mak_rows_desc* linear, const mak_rows_desc* paged, const int64_t* row_bytes,
+                     int64_t row_bytes0, const void* slots, int32_t slot_dtype, int64_t n_slots, int64_t skip_prefix,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Indexed row copy: dst row dst_idx[i] = src row src_idx[i] for i < n, on
+ * every plane pair.  A NULL index array means the identity (i).  Negative
+ * indices on either side skip the item; rows out of range are skipped.  Duplicate destinations: the last i wins (needs workspace).
+ * Replaces musa_aiter_kv_copy_paged_rows_{u8,layer_table_u8,contig_layers_u8}
+ * (csrc/kvcache/kv_transfer_float.mu:3047-3279), musa_aiter_kv_copy_paged_blocks_*
+ * and ..._fp8_vec8 (kv_transfer_float.mu:907-983, 1379; fp8_kv_cache.mu:1462-1527).
+ */
+MAK_API int mak_rows_copy(const mak_rows_desc* src, const mak_rows_desc* dst, const int64_t* row_bytes, int64_t row_bytes0,
+                  const void* src_idx, int32_t src_idx_dtype, const void* dst_idx, int32_t dst_idx_dtype, int64_t n,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAK_KVCACHE_H */

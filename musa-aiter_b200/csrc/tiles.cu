@@ -1,0 +1,511 @@
+// Tile engine: gather/scatter between "tile" caches that keep block_size
+// innermost ([L][NB][NH][HD][BS], the musa-aiter paged layout of
+// musa_aiter/ops/kv_transfer.py:2987-3000) and token-major rows ([L][T][NH][HD]).
+//
+// A CTA owns a chunk of kTT consecutive tokens of one (layer, kv) plane and
+// walks the heads a few at a time.  Tokens whose slots form an aligned run of
+// G = 16 / sizeof(cache element) consecutive offsets inside one block are
+// "packed": for each head_dim index d the CTA moves all G of them with one
+// 16-byte access of the cache row [d][o0 .. o0+G).  The [token][d] <-> [d][token]
+// transpose happens in shared memory; the token-major side always moves in
+// 16-byte vectors.  Unpacked tokens (random slots, partial blocks, skipped
+// slots) fall back to element accesses, so any slot mapping is handled.
+//
+// FP8 caches (raw uint8) fuse the musa-aiter reference codec into the
+// transpose: decode(byte) * scale on gather, encode(x / scale) on scatter
+// (musa_aiter/ops/kv_transfer.py:2161-2200).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace mak {
+
+constexpr int kTT = 32;  // tokens per chunk (multiple of every G: 4, 8, 16)
+
+struct TileLaunch {
+  uint64_t cache[2];
+  uint64_t lin[2];
+  const float* scale[2];
+  const void* slots;
+  int64_t c_sl, c_sb, c_sh, c_sd;  // cache strides (elements); block offset stride is 1
+  int64_t l_sl, l_st, l_sh;        // linear strides (elements); head_dim stride is 1
+  int64_t num_layers, num_heads, head_dim, block_size, num_slots, n_tokens, n_chunks;
+  int32_t slots64, n_kv, fill_zero, cache_vec, lin_vec, scale_mode, heads_per_step;
+};
+
+// ---- element conversions (round-to-nearest-even everywhere) ---------------
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+template <typename T>
+__device__ __forceinline__ T zero_of() {
+  T z;
+  memset(&z, 0, sizeof(T));
+  return z;
+}
+
+// ---- musa-aiter FP8 codec ---------------------------------------------------
+// Encoder semantics (musa_aiter/ops/kv_transfer.py:2161-2183): w = x / scale in
+// fp32; non-finite -> zero carrying the sign of (w < 0); |w| below the smallest
+// normal -> signed zero; |w| clamped to (2 - 2^-m) * 2^emax (480 for E4M3 with
+// exponent field 15 / mantissa 7, 114688 for E5M2 with exponent field 31); the
+// mantissa rounds half-to-even.  Inside the formats' standard finite range this
+// is exactly cvt.rn.satfinite; the extra top codes are handled explicitly.
+__device__ __forceinline__ uint32_t cvt_e4m3(float a) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(r) : "f"(a));
+  return r & 0xFFu;
+}
+__device__ __forceinline__ uint32_t cvt_e5m2(float a) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %1;" : "=h"(r) : "f"(a));
+  return r & 0xFFu;
+}
+
+template <int F>
+__device__ __forceinline__ uint8_t fp8_encode(float w) {
+  const uint32_t sign = (w < 0.f) ? 0x80u : 0u;
+  const float a = fabsf(w);
+  if (!(a <= 3.40282346638528859812e+38f)) return static_cast<uint8_t>(sign);  // inf / nan
+  if (F == MAK_FP8_E4M3) {
+    if (a < 0.015625f) return static_cast<uint8_t>(sign);  // below 2^-6
+    // 464 is the midpoint of 448 (mantissa 6) and 480 (mantissa 7): ties go to 448.
+    if (a > 464.f) return static_cast<uint8_t>(sign | 0x7Fu);
+    return static_cast<uint8_t>(sign | cvt_e4m3(a));
+  } else {
+    if (a < 6.103515625e-05f) return static_cast<uint8_t>(sign);  // below 2^-14
+    if (a >= 61440.f) {
+      // Exponent field 31: scale by 2^-16 (exact) into field 15, add 16 back.
+      const float y = fminf(a, 114688.f) * 1.52587890625e-05f;
+      return static_cast<uint8_t>(sign | (cvt_e5m2(y) + 0x40u));
+    }
+    return static_cast<uint8_t>(sign | cvt_e5m2(a));
+  }
+}
+
+// Decoder (musa_aiter/ops/kv_transfer.py:2186-2200): exponent field 0 -> 0,
+// otherwise (1 + m / 2^mb) * 2^(e - bias), all codes finite; built bit-exactly.
+template <int F>
+__device__ __forceinline__ float fp8_decode(uint32_t code) {
+  constexpr int mb = (F == MAK_FP8_E4M3) ? 3 : 2;
+  constexpr int bias = (F == MAK_FP8_E4M3) ? 7 : 15;
+  const uint32_t e = (code >> mb) & ((1u << (7 - mb)) - 1u);
+  const uint32_t m = code & ((1u << mb) - 1u);
+  uint32_t bits = e ? (((e - bias + 127u) << 23) | (m << (23 - mb))) : 0u;
+  bits |= (code & 0x80u) << 24;
+  return __uint_as_float(bits);
+}
+
+template <typename CT, typename LT, int CODEC>
+struct Codec {
+  // raw copy: CT and LT are same-width integer carriers
+  __device__ static __forceinline__ LT load(CT c, float) { return c; }
+  __device__ static __forceinline__ CT store(LT x, float) { return x; }
+};
+template <typename LT>
+struct Codec<uint8_t, LT, MAK_FP8_E4M3> {
+  __device__ static __forceinline__ LT load(uint8_t c, float sc) {
+    return from_f32<LT>(__fmul_rn(fp8_decode<MAK_FP8_E4M3>(c), sc));
+  }
+  __device__ static __forceinline__ uint8_t store(LT x, float sc) {
+    return fp8_encode<MAK_FP8_E4M3>(__fdiv_rn(to_f32<LT>(x), sc));
+  }
+};
+template <typename LT>
+struct Codec<uint8_t, LT, MAK_FP8_E5M2> {
+  __device__ static __forceinline__ LT load(uint8_t c, float sc) {
+    return from_f32<LT>(__fmul_rn(fp8_decode<MAK_FP8_E5M2>(c), sc));
+  }
+  __device__ static __forceinline__ uint8_t store(LT x, float sc) {
+    return fp8_encode<MAK_FP8_E5M2>(__fdiv_rn(to_f32<LT>(x), sc));
+  }
+};
+
+template <typename CT, typename LT, int CODEC, bool SCATTER>
+__global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileLaunch p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr int G = 16 / sizeof(CT);  // tokens per 16-byte cache vector
+  constexpr int NG = kTT / G;
+  constexpr int VL = 16 / sizeof(LT);  // elements per 16-byte linear vector
+  using C = Codec<CT, LT, CODEC>;
+  __shared__ int64_t s_off[kTT];
+  __shared__ int s_packed[NG];
+  LT* tile = reinterpret_cast<LT*>(smem_raw);
+  const int HD = static_cast<int>(p.head_dim);
+  const int NH = static_cast<int>(p.num_heads);
+  const int HPS = p.heads_per_step;
+  const int pitch = HD + VL;            // smem row pitch (elements), keeps 16-byte alignment
+  const int head_tile = kTT * pitch;    // elements per head in the tile
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int64_t work = p.n_chunks * p.num_layers * p.n_kv;
+
+  for (int64_t w = blockIdx.x; w < work; w += gridDim.x) {
+    const int64_t chunk = w % p.n_chunks;
+    const int64_t rest = w / p.n_chunks;
+    const int64_t l = rest % p.num_layers;
+    const int kv = static_cast<int>(rest / p.num_layers);
+    const int64_t t0 = chunk * kTT;
+    const int cnt = static_cast<int>(min(static_cast<int64_t>(kTT), p.n_tokens - t0));
+    __syncthreads();  // the previous work item is done with s_off / tile
+    if (tid < kTT) {
+      int64_t off = -1;
+      if (tid < cnt) {
+        const int64_t s = load_index(p.slots, p.slots64, t0 + tid);
+        if (s >= 0 && s < p.num_slots) {
+          int64_t b, o;
+          split_slot(s, p.block_size, &b, &o);
+          off = b * p.c_sb + o;
+        }
+      }
+      s_off[tid] = off;
+    }
+    __syncthreads();
+    if (tid < NG) {
+      const int64_t o0 = s_off[tid * G];
+      bool ok = p.cache_vec && o0 >= 0 && (o0 % G) == 0;
+      for (int i = 1; ok && i < G; ++i) ok = (s_off[tid * G + i] == o0 + i);
+      s_packed[tid] = ok ? 1 : 0;
+    }
+    __syncthreads();
+
+    const CT* cache_l = reinterpret_cast<const CT*>(p.cache[kv]) + l * p.c_sl;
+    CT* cache_lw = reinterpret_cast<CT*>(p.cache[kv]) + l * p.c_sl;
+    LT* lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl + t0 * p.l_st;
+    const float* scl = CODEC ? p.scale[kv] : nullptr;
+
+    for (int h0 = 0; h0 < NH; h0 += HPS) {
+      const int nh = min(HPS, NH - h0);
+      if (!SCATTER) {
+        // (1) cache -> tile, group-fastest so a warp's packed loads cover whole cache rows
+        const int items = nh * NG * HD;
+        for (int it = tid; it < items; it += nthr) {
+          const int g = it % NG;
+          const int rem = it / NG;
+          const int d = rem % HD;
+          const int hh = rem / HD;
+          const int h = h0 + hh;
+          float sc = 1.f;
+          if (CODEC) sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? h : l * NH + h)];
+          const CT* ch = cache_l + h * p.c_sh + d * p.c_sd;
+          LT* trow = tile + hh * head_tile + (g * G) * pitch + d;
+          if (s_packed[g]) {
+            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(ch + s_off[g * G]));
+            const CT* e = reinterpret_cast<const CT*>(&raw);
+#pragma unroll
+            for (int i = 0; i < G; ++i) trow[i * pitch] = C::load(e[i], sc);
+          } else {
+#pragma unroll
+            for (int i = 0; i < G; ++i) {
+              const int64_t off = s_off[g * G + i];
+              trow[i * pitch] = off >= 0 ? C::load(ch[off], sc) : zero_of<LT>();
+            }
+          }
+        }
+        __syncthreads();
+        // (2) tile -> linear rows
+        if (p.lin_vec) {
+          const int vpr = HD / VL;
+          const int items2 = nh * cnt * vpr;
+          for (int it = tid; it < items2; it += nthr) {
+            const int c = it % vpr;
+            const int rem = it / vpr;
+            const int t = rem % cnt;
+            const int hh = rem / cnt;
+            uint4* dst = reinterpret_cast<uint4*>(lin_l + t * p.l_st + (h0 + hh) * p.l_sh + c * VL);
+            if (s_off[t] >= 0) {
+              *dst = *reinterpret_cast<const uint4*>(tile + hh * head_tile + t * pitch + c * VL);
+            } else if (p.fill_zero) {
+              *dst = make_uint4(0u, 0u, 0u, 0u);
+            }
+          }
+        } else {
+          const int items2 = nh * cnt * HD;
+          for (int it = tid; it < items2; it += nthr) {
+            const int d = it % HD;
+            const int rem = it / HD;
+            const int t = rem % cnt;
+            const int hh = rem / cnt;
+            LT* dst = lin_l + t * p.l_st + (h0 + hh) * p.l_sh + d;
+            if (s_off[t] >= 0) {
+              *dst = tile[hh * head_tile + t * pitch + d];
+            } else if (p.fill_zero) {
+              *dst = zero_of<LT>();
+            }
+          }
+        }
+        __syncthreads();
+      } else {
+        // (1) linear rows -> tile (only tokens that will be stored)
+        if (p.lin_vec) {
+          const int vpr = HD / VL;
+          const int items = nh * cnt * vpr;
+          for (int it = tid; it < items; it += nthr) {
+            const int c = it % vpr;
+            const int rem = it / vpr;
+            const int t = rem % cnt;
+            const int hh = rem / cnt;
+            if (s_off[t] < 0) continue;
+            *reinterpret_cast<uint4*>(tile + hh * head_tile + t * pitch + c * VL) =
+                __ldg(reinterpret_cast<const uint4*>(lin_l + t * p.l_st + (h0 + hh) * p.l_sh + c * VL));
+          }
+        } else {
+          const int items = nh * cnt * HD;
+          for (int it = tid; it < items; it += nthr) {
+            const int d = it % HD;
+            const int rem = it / HD;
+            const int t = rem % cnt;
+            const int hh = rem / cnt;
+            if (s_off[t] < 0) continue;
+            tile[hh * head_tile + t * pitch + d] = lin_l[t * p.l_st + (h0 + hh) * p.l_sh + d];
+          }
+        }
+        __syncthreads();
+        // (2) tile -> cache (+ FP8 encode)
+        const int items = nh * NG * HD;
+        for (int it = tid; it < items; it += nthr) {
+          const int g = it % NG;
+          const int rem = it / NG;
+          const int d = rem % HD;
+          const int hh = rem / HD;
+          const int h = h0 + hh;
+          float sc = 1.f;
+          if (CODEC) sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? h : l * NH + h)];
+          CT* ch = cache_lw + h * p.c_sh + d * p.c_sd;
+          const LT* trow = tile + hh * head_tile + (g * G) * pitch + d;
+          if (s_packed[g]) {
+            uint4 raw;
+            CT* e = reinterpret_cast<CT*>(&raw);
+#pragma unroll
+            for (int i = 0; i < G; ++i) e[i] = C::store(trow[i * pitch], sc);
+            *reinterpret_cast<uint4*>(ch + s_off[g * G]) = raw;
+          } else {
+#pragma unroll
+            for (int i = 0; i < G; ++i) {
+              const int64_t off = s_off[g * G + i];
+              if (off >= 0) ch[off] = C::store(trow[i * pitch], sc);
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+template <typename CT, typename LT, int CODEC, bool SCATTER>
+static int launch_tile(TileLaunch& p, cudaStream_t st) {
+  constexpr int VL = 16 / sizeof(LT);
+  const int threads = 256;
+  const size_t per_head = static_cast<size_t>(kTT) * (p.head_dim + VL) * sizeof(LT);
+  // Heads per step: keep ~24 KB of tile per CTA so each thread has several 16-byte accesses in flight.
+  int hps = static_cast<int>(std::max<size_t>(1, (24u << 10) / per_head));
+  hps = static_cast<int>(std::min<int64_t>(hps, p.num_heads));
+  p.heads_per_step = hps;
+  const size_t smem = per_head * hps;
+  auto kern = tile_kernel<CT, LT, CODEC, SCATTER>;
+  if (smem > (48u << 10)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_fail(e, "tile_kernel smem attribute");
+  }
+  const int64_t work = p.n_chunks * p.num_layers * p.n_kv;
+  const int grid = grid_for(reinterpret_cast<const void*>(kern), threads, smem, work);
+  if (grid <= 0) return MAK_OK;
+  kern<<<grid, threads, smem, st>>>(p);
+  return launch_status("tile_kernel");
+}
+
+struct TileCall {
+  const mak_paged_desc* cache;
+  const mak_linear_desc* lin;
+  const void* slots;
+  int32_t slot_dtype;
+  int32_t fill_zero;
+  const float* k_scale;
+  const float* v_scale;
+  int32_t scale_mode;
+  int32_t fp8_format;  // 0 = plain copy
+  bool scatter;
+};
+
+static int run_tile(const TileCall& c, cudaStream_t st, const char* name) {
+  const mak_paged_desc* pc = c.cache;
+  const mak_linear_desc* pl = c.lin;
+  if (!pc || !pl) return fail(MAK_E_INVALID, "%s: NULL descriptor", name);
+  if (pc->num_layers <= 0 || pc->num_blocks <= 0 || pc->num_heads <= 0 || pc->head_dim <= 0 || pc->block_size <= 0)
+    return fail(MAK_E_INVALID, "%s: all cache extents must be positive", name);
+  if (pl->num_tokens < 0) return fail(MAK_E_INVALID, "%s: negative token count", name);
+  if (pl->num_tokens == 0) return MAK_OK;
+  if (!c.slots || !valid_index_dtype(c.slot_dtype)) return fail(MAK_E_INVALID, "%s: slots must be int32/int64", name);
+  if (pc->head_dim > 4096) return fail(MAK_E_UNSUPPORTED, "%s: head_dim %lld > 4096", name, (long long)pc->head_dim);
+  const int n_kv = pc->v ? 2 : 1;
+  if (!pc->k || !pl->k || (n_kv == 2 && !pl->v)) return fail(MAK_E_INVALID, "%s: NULL data pointer", name);
+
+  const int ce = dtype_bytes(pc->dtype), le = dtype_bytes(pl->dtype);
+  if (c.fp8_format) {
+    if (pc->dtype != MAK_DT_U8) return fail(MAK_E_INVALID, "%s: FP8 cache must be stored as uint8", name);
+    if (pl->dtype != MAK_DT_F16 && pl->dtype != MAK_DT_BF16 && pl->dtype != MAK_DT_F32)
+      return fail(MAK_E_INVALID, "%s: FP8 linear dtype must be f16/bf16/f32", name);
+    if (!c.k_scale || (n_kv == 2 && !c.v_scale)) return fail(MAK_E_INVALID, "%s: NULL scale pointer", name);
+    if (c.scale_mode < MAK_SCALE_SCALAR || c.scale_mode > MAK_SCALE_PER_LAYER_HEAD)
+      return fail(MAK_E_INVALID, "%s: bad scale mode %d", name, c.scale_mode);
+  } else {
+    if (pc->dtype != pl->dtype || (ce != 2 && ce != 4))
+      return fail(MAK_E_INVALID, "%s: cache and linear dtypes must match (f16/bf16/f32)", name);
+  }
+  TileLaunch p;
+  memset(&p, 0, sizeof(p));
+  p.cache[0] = reinterpret_cast<uint64_t>(pc->k);
+  p.cache[1] = reinterpret_cast<uint64_t>(pc->v);
+  p.lin[0] = reinterpret_cast<uint64_t>(pl->k);
+  p.lin[1] = reinterpret_cast<uint64_t>(pl->v);
+  p.scale[0] = c.k_scale;
+  p.scale[1] = c.v_scale;
+  p.slots = c.slots;
+  p.c_sl = pc->stride_layer;
+  p.c_sb = pc->stride_block;
+  p.c_sh = pc->stride_head;
+  p.c_sd = pc->stride_dim;
+  p.l_sl = pl->stride_layer;
+  p.l_st = pl->stride_token;
+  p.l_sh = pl->stride_head;
+  p.num_layers = pc->num_layers;
+  p.num_heads = pc->num_heads;
+  p.head_dim = pc->head_dim;
+  p.block_size = pc->block_size;
+  p.num_slots = pc->num_blocks * pc->block_size;
+  p.n_tokens = pl->num_tokens;
+  p.n_chunks = (pl->num_tokens + kTT - 1) / kTT;
+  p.slots64 = c.slot_dtype == MAK_DT_I64;
+  p.n_kv = n_kv;
+  p.fill_zero = c.fill_zero ? 1 : 0;
+  p.scale_mode = c.scale_mode;
+  // 16-byte cache vectors need every cache address of a packed group aligned.
+  const int G = 16 / ce;
+  const uint64_t cbits = static_cast<uint64_t>(p.c_sl | p.c_sb | p.c_sh | p.c_sd) * ce;
+  p.cache_vec = aligned16(pc->k) && (n_kv == 1 || aligned16(pc->v)) && (cbits & 15u) == 0 && (pc->block_size % G) == 0;
+  const uint64_t lbits = static_cast<uint64_t>(p.l_sl | p.l_st | p.l_sh | pc->head_dim) * le;
+  p.lin_vec = aligned16(pl->k) && (n_kv == 1 || aligned16(pl->v)) && (lbits & 15u) == 0;
+
+  if (c.fp8_format == 0) {
+    if (ce == 2) return c.scatter ? launch_tile<uint16_t, uint16_t, 0, true>(p, st) : launch_tile<uint16_t, uint16_t, 0, false>(p, st);
+    return c.scatter ? launch_tile<uint32_t, uint32_t, 0, true>(p, st) : launch_tile<uint32_t, uint32_t, 0, false>(p, st);
+  }
+#define MAK_TILE_FP8(FMT)                                                                                              \
+  switch (pl->dtype) {                                                                                                 \
+    case MAK_DT_F16:                                                                                                   \
+      return c.scatter ? launch_tile<uint8_t, __half, FMT, true>(p, st) : launch_tile<uint8_t, __half, FMT, false>(p, st); \
+    case MAK_DT_BF16:                                                                                                  \
+      return c.scatter ? launch_tile<uint8_t, __nv_bfloat16, FMT, true>(p, st)                                         \
+                       : launch_tile<uint8_t, __nv_bfloat16, FMT, false>(p, st);                                       \
+    default:                                                                                                           \
+      return c.scatter ? launch_tile<uint8_t, float, FMT, true>(p, st) : launch_tile<uint8_t, float, FMT, false>(p, st); \
+  }
+  if (c.fp8_format == MAK_FP8_E4M3) {
+    MAK_TILE_FP8(MAK_FP8_E4M3)
+  } else if (c.fp8_format == MAK_FP8_E5M2) {
+    MAK_TILE_FP8(MAK_FP8_E5M2)
+  }
+#undef MAK_TILE_FP8
+  return fail(MAK_E_INVALID, "%s: unknown FP8 format %d", name, c.fp8_format);
+}
+
+static int tile_scatter(TileCall c, void* workspace, size_t ws_bytes, cudaStream_t st, const char* name) {
+  if (!c.lin || c.lin->num_tokens <= 0) return MAK_OK;
+  if (!c.slots || !valid_index_dtype(c.slot_dtype)) return fail(MAK_E_INVALID, "%s: slots must be int32/int64", name);
+  ScatterWs ws{};
+  int rc = carve_scatter_ws(workspace, ws_bytes, c.lin->num_tokens, &ws);
+  if (rc) return rc;
+  rc = resolve_last_writer(c.slots, c.slot_dtype, c.lin->num_tokens, ws, st);
+  if (rc) return rc;
+  c.slots = ws.eff;
+  c.slot_dtype = MAK_DT_I64;
+  c.scatter = true;
+  return run_tile(c, st, name);
+}
+
+}  // namespace mak
+
+using namespace mak;
+
+extern "C" {
+
+int mak_kv_paged_to_linear(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
+                           int32_t slot_dtype, int32_t fill_zero, void* stream) {
+  TileCall c{};
+  c.cache = cache;
+  c.lin = out;
+  c.slots = slots;
+  c.slot_dtype = slot_dtype;
+  c.fill_zero = fill_zero;
+  return run_tile(c, as_stream(stream), "mak_kv_paged_to_linear");
+}
+
+int mak_kv_linear_to_paged(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                           int32_t slot_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  TileCall c{};
+  c.cache = cache;
+  c.lin = in;
+  c.slots = slots;
+  c.slot_dtype = slot_dtype;
+  return tile_scatter(c, workspace, workspace_bytes, as_stream(stream), "mak_kv_linear_to_paged");
+}
+
+int mak_kv_paged_fp8_to_linear(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
+                               int32_t slot_dtype, const float* k_scale, const float* v_scale, int32_t scale_mode,
+                               int32_t fp8_format, void* stream) {
+  if (fp8_format != MAK_FP8_E4M3 && fp8_format != MAK_FP8_E5M2)
+    return fail(MAK_E_INVALID, "mak_kv_paged_fp8_to_linear: unknown FP8 format %d", fp8_format);
+  TileCall c{};
+  c.cache = cache;
+  c.lin = out;
+  c.slots = slots;
+  c.slot_dtype = slot_dtype;
+  c.fill_zero = 1;
+  c.k_scale = k_scale;
+  c.v_scale = v_scale;
+  c.scale_mode = scale_mode;
+  c.fp8_format = fp8_format;
+  return run_tile(c, as_stream(stream), "mak_kv_paged_fp8_to_linear");
+}
+
+int mak_kv_linear_to_paged_fp8(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                               int32_t slot_dtype, const float* k_scale, const float* v_scale, int32_t scale_mode,
+                               int32_t fp8_format, void* workspace, size_t workspace_bytes, void* stream) {
+  if (fp8_format != MAK_FP8_E4M3 && fp8_format != MAK_FP8_E5M2)
+    return fail(MAK_E_INVALID, "mak_kv_linear_to_paged_fp8: unknown FP8 format %d", fp8_format);
+  TileCall c{};
+  c.cache = cache;
+  c.lin = in;
+  c.slots = slots;
+  c.slot_dtype = slot_dtype;
+  c.k_scale = k_scale;
+  c.v_scale = v_scale;
+  c.scale_mode = scale_mode;
+  c.fp8_format = fp8_format;
+  return tile_scatter(c, workspace, workspace_bytes, as_stream(stream), "mak_kv_linear_to_paged_fp8");
+}
+
+}  // extern "C"

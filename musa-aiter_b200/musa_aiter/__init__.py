@@ -1,0 +1,56 @@
+"""musa_aiter — B200-native (sm_100a) drop-in for the musa-aiter ``kvcache`` operator family.
+
+The public names below keep the reference's signatures (musa_aiter/__init__.py:31-133
+of musa-aiter v0.5.0).  Every data-moving call runs hand-written CUDA kernels from
+``lib/libmak_kvcache.so`` on the caller's current CUDA stream; CPU tensors are
+rejected (there is no CPU fallback).
+"""
+
+from .version import __version__
+from . import registry, dispatch
+from .ops.kv_transfer import (
+    build_native_fp8_kv_cache,
+    build_native_kv_transfer,
+    is_native_fp8_kv_cache_available,
+    is_native_fp8_kv_vectorized_available,
+    is_native_kv_transfer_available,
+    kv_linear_to_paged,
+    kv_linear_to_paged_fp8,
+    kv_linear_to_paged_fp8_multi_layer,
+    kv_linear_to_paged_multi_layer,
+    kv_merged_linear_to_paged,
+    kv_merged_linear_to_paged_fp8,
+    kv_merged_linear_to_paged_fp8_multi_layer,
+    kv_merged_linear_to_paged_multi_layer,
+    kv_mla_linear_to_paged,
+    kv_mla_linear_to_paged_multi_layer,
+    kv_paged_fp8_to_linear,
+    kv_paged_fp8_to_linear_multi_layer,
+    kv_paged_fp8_to_merged_linear,
+    kv_paged_fp8_to_merged_linear_multi_layer,
+    kv_paged_to_linear,
+    kv_paged_to_linear_multi_layer,
+    kv_paged_to_merged_linear,
+    kv_paged_to_merged_linear_multi_layer,
+    kv_paged_to_mla_linear,
+    kv_paged_to_mla_linear_multi_layer,
+    native_fp8_kv_cache_abi_version,
+    native_kv_transfer_abi_version,
+)
+from .ops.lmcache_kv_transfer import (
+    clear_native_lmcache_kv_transfer_cache,
+    is_native_lmcache_kv_transfer_available,
+    is_native_lmcache_two_x_nl_kv_transfer_available,
+    lmcache_kv_buffer_to_paged,
+    lmcache_kv_buffer_to_paged_mla,
+    lmcache_kv_buffer_to_paged_two_x_nl,
+    lmcache_kv_paged_to_buffer,
+    lmcache_kv_paged_to_buffer_two_x_nl,
+    lmcache_mla_buffer_to_paged,
+    lmcache_mla_paged_to_buffer,
+    lmcache_paged_to_kv_buffer,
+    lmcache_paged_to_kv_buffer_mla,
+    native_lmcache_kv_transfer_abi_version,
+)
+
+__all__ = [name for name in dir() if not name.startswith("_") and name not in ("registry", "dispatch", "ops", "version")]

@@ -1,0 +1,253 @@
+"""ctypes boundary to ``libmak_kvcache.so`` (the sm_100a kernel library).
+
+The reference loads its JIT-built MUSA library with ctypes and assigns
+``argtypes`` on every call (musa_aiter/ops/kv_transfer.py:4193-4206 notes the
+~17 us cost).  Here the library is loaded once per process, every prototype
+is bound once at load time, and calls go straight through.
+
+There is no fallback: if the library is missing or a call fails, a
+``RuntimeError`` carrying the library's own message is raised.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from ctypes import POINTER, c_int32, c_int64, c_size_t, c_uint64, c_void_p
+
+import torch
+
+from . import _build
+
+ABI_VERSION = 1
+
+MAK_DT_U8, MAK_DT_F16, MAK_DT_BF16, MAK_DT_F32, MAK_DT_I32, MAK_DT_I64 = range(6)
+MAK_FP8_E4M3, MAK_FP8_E5M2 = 1, 2
+MAK_SCALE_SCALAR, MAK_SCALE_PER_HEAD, MAK_SCALE_PER_LAYER_HEAD = 0, 1, 2
+
+_DTYPE_CODES = {
+    torch.uint8: MAK_DT_U8,
+    torch.float16: MAK_DT_F16,
+    torch.bfloat16: MAK_DT_BF16,
+    torch.float32: MAK_DT_F32,
+    torch.int32: MAK_DT_I32,
+    torch.int64: MAK_DT_I64,
+}
+for _name in ("float8_e4m3fn", "float8_e5m2"):
+    if hasattr(torch, _name):
+        _DTYPE_CODES[getattr(torch, _name)] = MAK_DT_U8
+
+
+class PagedDesc(ctypes.Structure):
+    """``mak_paged_desc``: block-size-innermost cache ``[L][NB][NH][HD][BS]``."""
+
+    _fields_ = [
+        ("k", c_void_p),
+        ("v", c_void_p),
+        ("num_layers", c_int64),
+        ("num_blocks", c_int64),
+        ("num_heads", c_int64),
+        ("head_dim", c_int64),
+        ("block_size", c_int64),
+        ("stride_layer", c_int64),
+        ("stride_block", c_int64),
+        ("stride_head", c_int64),
+        ("stride_dim", c_int64),
+        ("dtype", c_int32),
+        ("reserved", c_int32),
+    ]
+
+
+class LinearDesc(ctypes.Structure):
+    """``mak_linear_desc``: token-major ``[L][T][NH][HD]`` buffers."""
+
+    _fields_ = [
+        ("k", c_void_p),
+        ("v", c_void_p),
+        ("num_tokens", c_int64),
+        ("stride_layer", c_int64),
+        ("stride_token", c_int64),
+        ("stride_head", c_int64),
+        ("dtype", c_int32),
+        ("reserved", c_int32),
+    ]
+
+
+class RowsDesc(ctypes.Structure):
+    """``mak_rows_desc``: planes of rows (strides in bytes)."""
+
+    _fields_ = [
+        ("plane_ptrs", POINTER(c_uint64)),
+        ("num_planes", c_int64),
+        ("rows_per_block", c_int64),
+        ("block_stride", c_int64),
+        ("row_stride", c_int64),
+        ("num_rows", c_int64),
+    ]
+
+
+_PROTOTYPES = {
+    "mak_abi_version": (c_int32, []),
+    "mak_last_error": (ctypes.c_char_p, []),
+    "mak_device_sm_count": (c_int32, []),
+    "mak_launch_count": (c_uint64, []),
+    "mak_slot_max": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_void_p]),
+    "mak_scatter_workspace_bytes": (c_size_t, [c_int64]),
+    "mak_resolve_last_writer": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "mak_build_slot_mapping": (
+        c_int32,
+        [c_void_p, c_int32, c_int64, c_void_p, c_int32, c_int64, c_int64, c_int64, c_void_p, c_void_p],
+    ),
+    "mak_kv_paged_to_linear": (c_int32, [POINTER(PagedDesc), POINTER(LinearDesc), c_void_p, c_int32, c_int32, c_void_p]),
+    "mak_kv_linear_to_paged": (
+        c_int32,
+        [POINTER(LinearDesc), POINTER(PagedDesc), c_void_p, c_int32, c_void_p, c_size_t, c_void_p],
+    ),
+    "mak_kv_paged_fp8_to_linear": (
+        c_int32,
+        [POINTER(PagedDesc), POINTER(LinearDesc), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p],
+    ),
+    "mak_kv_linear_to_paged_fp8": (
+        c_int32,
+        [
+            POINTER(LinearDesc),
+            POINTER(PagedDesc),
+            c_void_p,
+            c_int32,
+            c_void_p,
+            c_void_p,
+            c_int32,
+            c_int32,
+            c_void_p,
+            c_size_t,
+            c_void_p,
+        ],
+    ),
+    "mak_rows_gather": (
+        c_int32,
+        [POINTER(RowsDesc), POINTER(RowsDesc), POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int32, c_void_p],
+    ),
+    "mak_rows_scatter": (
+        c_int32,
+        [
+            POINTER(RowsDesc),
+            POINTER(RowsDesc),
+            POINTER(c_int64),
+            c_int64,
+            c_void_p,
+            c_int32,
+            c_int64,
+            c_int64,
+            c_void_p,
+            c_size_t,
+            c_void_p,
+        ],
+    ),
+    "mak_rows_copy": (
+        c_int32,
+        [
+            POINTER(RowsDesc),
+            POINTER(RowsDesc),
+            POINTER(c_int64),
+            c_int64,
+            c_void_p,
+            c_int32,
+            c_void_p,
+            c_int32,
+            c_int64,
+            c_void_p,
+            c_size_t,
+            c_void_p,
+        ],
+    ),
+}
+
+_LOCK = threading.Lock()
+_LIB: ctypes.CDLL | None = None
+_LOAD_ERROR: str | None = None
+
+
+def library_path() -> str:
+    return os.environ.get("MUSA_AITER_KVCACHE_LIB", str(_build.LIB_PATH))
+
+
+def load() -> ctypes.CDLL:
+    """Load and bind the kernel library once; raise RuntimeError if it is unavailable."""
+    global _LIB, _LOAD_ERROR
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        path = library_path()
+        if not os.path.exists(path):
+            _LOAD_ERROR = f"{path} not found: build it with musa_aiter.build_native_kv_transfer()"
+            raise RuntimeError(f"musa_aiter kvcache native library missing: {_LOAD_ERROR}")
+        lib = ctypes.CDLL(path)
+        for name, (restype, argtypes) in _PROTOTYPES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        version = lib.mak_abi_version()
+        if version != ABI_VERSION:
+            raise RuntimeError(f"musa_aiter kvcache native library ABI {version} != expected {ABI_VERSION}")
+        _LIB = lib
+        return lib
+
+
+def is_available() -> bool:
+    try:
+        load()
+        return True
+    except Exception:
+        return False
+
+
+def launch_count() -> int:
+    """Kernels launched by the library so far (host-side counter)."""
+    return int(load().mak_launch_count())
+
+
+def exported_symbols() -> list[str]:
+    return list(_PROTOTYPES)
+
+
+def check(rc: int, op: str) -> None:
+    if rc != 0:
+        msg = load().mak_last_error().decode(errors="replace")
+        raise RuntimeError(f"{op}: native kernel library returned {rc}: {msg}")
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODES[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype for the kvcache native library: {dtype}") from None
+
+
+def stream_ptr(device: torch.device) -> c_void_p:
+    """Current CUDA stream of ``device`` (the reference passes stream 0 in places;
+    this backend always honours the caller's current stream)."""
+    return c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def ptr(t: torch.Tensor | None) -> c_void_p:
+    return c_void_p(t.data_ptr() if t is not None else 0)
+
+
+def workspace(n_items: int, device: torch.device) -> tuple[torch.Tensor, int]:
+    """Scatter workspace from torch's caching allocator (stream-ordered reuse is safe)."""
+    nbytes = int(load().mak_scatter_workspace_bytes(int(n_items)))
+    return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
+
+
+def plane_array(ptrs: list[int]):
+    arr = (c_uint64 * max(1, len(ptrs)))(*ptrs)
+    return arr
+
+
+def rows_desc(ptrs: list[int], rows_per_block: int, block_stride: int, row_stride: int, num_rows: int):
+    arr = plane_array(ptrs)
+    desc = RowsDesc(ctypes.cast(arr, POINTER(c_uint64)), len(ptrs), rows_per_block, block_stride, row_stride, num_rows)
+    return desc, arr  # keep arr alive alongside desc

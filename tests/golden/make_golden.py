@@ -1,0 +1,337 @@
+"""Generate golden vectors for the kvcache oracle by running the reference itself.
+
+Usage (in a container that holds the reference source tree)::
+
+    MUSA_AITER_REF=/path/to/musa-aiter python tests/golden/make_golden.py
+
+The script imports the reference ``musa_aiter`` package (pure PyTorch on CPU),
+feeds it seeded inputs and stores inputs + outputs in ``tests/golden/*.npz``.
+``tests/test_oracle_golden.py`` replays every case through ``oracle.kv_oracle``
+and requires bit-identical results.  bfloat16 tensors are stored as uint16 bit
+patterns, FP8 caches as raw uint8.
+
+Families:
+- tile.npz    kv_paged_to_linear / kv_linear_to_paged (+ multi-layer, merged)
+- fp8.npz     exhaustive FP8 encode (all 65536 bf16 and fp16 inputs), edge fp32
+              inputs, all 256 codes decoded, multi-layer scale forms
+- rows.npz    LMCache 6-D / list / SGLang MP two_x_nl / MLA buffers, MLA flat caches
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+sys.dont_write_bytecode = True
+REF = os.environ.get("MUSA_AITER_REF", "/root/reference")
+if REF not in sys.path:
+    sys.path.insert(0, REF)
+
+import torch  # noqa: E402
+
+import musa_aiter as ref  # noqa: E402  (the reference package, not this repo's)
+
+assert str(Path(ref.__file__).resolve()).startswith(str(Path(REF).resolve())), ref.__file__
+
+OUT = Path(__file__).resolve().parent
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16)
+    if t.dtype in (torch.float8_e4m3fn, torch.float8_e5m2):
+        return t.view(torch.uint8).numpy()
+    return t.numpy()
+
+
+class Store:
+    def __init__(self) -> None:
+        self.d: dict[str, np.ndarray] = {}
+
+    def put(self, key: str, value) -> None:
+        assert key not in self.d, key
+        if isinstance(value, torch.Tensor):
+            value = to_np(value)
+        self.d[key] = np.asarray(value)
+
+    def save(self, name: str) -> None:
+        np.savez_compressed(OUT / name, **self.d)
+        print(f"wrote {name}: {len(self.d)} arrays")
+
+
+def gen(seed: int) -> torch.Generator:
+    g = torch.Generator()
+    g.manual_seed(seed)
+    return g
+
+
+def randn(shape, dtype, g):
+    return torch.randn(shape, generator=g, dtype=torch.float32).to(dtype)
+
+
+DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+
+
+# ---------------------------------------------------------------------------
+def make_tile() -> None:
+    st = Store()
+    nb, nh, hd, bs = 5, 2, 8, 4
+    for dname, dt in DTYPES.items():
+        g = gen(10)
+        kc = randn((nb, nh, hd, bs), dt, g)
+        vc = randn((nb, nh, hd, bs), dt, g)
+        slots = torch.tensor([0, 5, 19, -1, 7, 3, -4, 12, 13, 14, 15, 16], dtype=torch.int64)
+        p = f"gather/{dname}"
+        st.put(f"{p}/k_cache", kc)
+        st.put(f"{p}/v_cache", vc)
+        st.put(f"{p}/slots", slots)
+        ok, ov = ref.kv_paged_to_linear(kc, vc, slots)
+        st.put(f"{p}/out_k", ok)
+        st.put(f"{p}/out_v", ov)
+        # preserve mode into prefilled buffers
+        pk = torch.full((slots.numel(), nh, hd), 3.0, dtype=dt)
+        pv = torch.full((slots.numel(), nh, hd), -2.0, dtype=dt)
+        ref.kv_paged_to_linear(kc, vc, slots, fill_skipped="preserve", out_k=pk, out_v=pv)
+        st.put(f"{p}/preserve_k", pk)
+        st.put(f"{p}/preserve_v", pv)
+        # scatter with duplicate slots (last writer wins) and negative slots
+        sslots = torch.tensor([3, 9, -1, 3, 17, 0, 9, 19, -2, 3], dtype=torch.int32)
+        kl = randn((sslots.numel(), nh, hd), dt, g)
+        vl = randn((sslots.numel(), nh, hd), dt, g)
+        kd = torch.zeros_like(kc)
+        vd = torch.full_like(vc, 1.5)
+        ref.kv_linear_to_paged(kl, vl, kd, vd, sslots)
+        q = f"scatter/{dname}"
+        st.put(f"{q}/k_lin", kl)
+        st.put(f"{q}/v_lin", vl)
+        st.put(f"{q}/slots", sslots)
+        st.put(f"{q}/k_cache", kd)
+        st.put(f"{q}/v_cache", vd)
+        # multi-layer gather + scatter
+        nl = 3
+        kc3 = randn((nl, nb, nh, hd, bs), dt, g)
+        vc3 = randn((nl, nb, nh, hd, bs), dt, g)
+        ok3, ov3 = ref.kv_paged_to_linear_multi_layer(kc3, vc3, slots)
+        r = f"gather_ml/{dname}"
+        st.put(f"{r}/k_cache", kc3)
+        st.put(f"{r}/v_cache", vc3)
+        st.put(f"{r}/slots", slots)
+        st.put(f"{r}/out_k", ok3)
+        st.put(f"{r}/out_v", ov3)
+        kl3 = randn((nl, sslots.numel(), nh, hd), dt, g)
+        vl3 = randn((nl, sslots.numel(), nh, hd), dt, g)
+        kd3 = torch.zeros_like(kc3)
+        vd3 = torch.zeros_like(vc3)
+        ref.kv_linear_to_paged_multi_layer(kl3, vl3, kd3, vd3, sslots)
+        r = f"scatter_ml/{dname}"
+        st.put(f"{r}/k_lin", kl3)
+        st.put(f"{r}/v_lin", vl3)
+        st.put(f"{r}/slots", sslots)
+        st.put(f"{r}/k_cache", kd3)
+        st.put(f"{r}/v_cache", vd3)
+        # merged layouts
+        merged = ref.kv_paged_to_merged_linear(kc, vc, slots)
+        st.put(f"merged/{dname}/gather", merged)
+        merged_ml = ref.kv_paged_to_merged_linear_multi_layer(kc3, vc3, slots)
+        st.put(f"merged/{dname}/gather_ml", merged_ml)
+        ml_in = randn((sslots.numel(), 2, nh, hd), dt, g)
+        kd = torch.zeros_like(kc)
+        vd = torch.zeros_like(vc)
+        ref.kv_merged_linear_to_paged(ml_in, kd, vd, sslots)
+        st.put(f"merged/{dname}/scatter_in", ml_in)
+        st.put(f"merged/{dname}/scatter_k", kd)
+        st.put(f"merged/{dname}/scatter_v", vd)
+    st.save("tile.npz")
+
+
+# ---------------------------------------------------------------------------
+def _fp8_store(st: Store, key: str, k_lin, v_lin, nb, bs, k_scale, v_scale, fmt, slots=None):
+    t, nh, hd = k_lin.shape
+    kc = torch.zeros((nb, nh, hd, bs), dtype=torch.uint8)
+    vc = torch.zeros((nb, nh, hd, bs), dtype=torch.uint8)
+    if slots is None:
+        slots = torch.arange(t, dtype=torch.int64)
+    ref.kv_linear_to_paged_fp8(k_lin, v_lin, kc, vc, slots, k_scale, v_scale, fp8_format=fmt)
+    st.put(f"{key}/k_lin", k_lin)
+    st.put(f"{key}/v_lin", v_lin)
+    st.put(f"{key}/slots", slots)
+    st.put(f"{key}/k_scale", torch.as_tensor(k_scale, dtype=torch.float32))
+    st.put(f"{key}/v_scale", torch.as_tensor(v_scale, dtype=torch.float32))
+    st.put(f"{key}/k_cache", kc)
+    st.put(f"{key}/v_cache", vc)
+
+
+def make_fp8() -> None:
+    st = Store()
+    all16 = torch.arange(65536, dtype=torch.int32).to(torch.int16)
+    bf = all16.view(torch.bfloat16).reshape(512, 4, 32)
+    hf = all16.view(torch.float16).reshape(512, 4, 32)
+    scale_sets = [
+        (1.0, [0.5, 1.0, 3.75, 0.0123]),
+        (0.0371, [448.0 / 7.0, 2.0**-10, 1e-3, 117.0]),
+    ]
+    for fmt in ("e4m3", "e5m2"):
+        for i, (ks, vs) in enumerate(scale_sets):
+            _fp8_store(st, f"enc_bf16/{fmt}/{i}", bf, bf.flip(0), 32, 16, ks, vs, fmt)
+        _fp8_store(st, f"enc_f16/{fmt}/0", hf, hf.flip(0), 32, 16, scale_sets[1][0], scale_sets[0][1], fmt)
+    # fp32 edge values: specials, ties around the top codes and the min-normal boundaries
+    specials = [0.0, -0.0, float("inf"), float("-inf"), float("nan"), 448.0, 464.0, 464.0001, 479.9, 480.0, 480.1,
+                1e30, -1e30, 57344.0, 61439.996, 61440.0, 61440.004, 65536.0, 114688.0, 114687.9, 2e5,
+                2.0**-6, 2.0**-6 * 0.99999994, 2.0**-7, 2.0**-14, 2.0**-14 * 0.99999994, 2.0**-15, 2.0**-9 * 1.5,
+                0.3125, 0.34375, 1.0625, 1.125, 1.1875, 15.5, 240.0, 248.0, 256.0, 3.0e-5]
+    g = gen(20)
+    mags = torch.exp2(torch.rand(4096 - 2 * len(specials), generator=g) * 60.0 - 30.0)
+    signs = torch.where(torch.rand(mags.numel(), generator=g) < 0.5, -1.0, 1.0)
+    vals = torch.cat([torch.tensor(specials), -torch.tensor(specials), mags * signs]).to(torch.float32)
+    x32 = vals.reshape(32, 4, 32)
+    for fmt in ("e4m3", "e5m2"):
+        _fp8_store(st, f"enc_f32/{fmt}/0", x32, x32 * 3.0, 2, 16, 1.0, [1.0, 0.5, 2.0, 1.0 / 3.0], fmt)
+    # decode every code: cache holds codes 0..255 at slots 0..255 for [NB=16, NH=1, HD=16, BS=16]
+    codes = torch.arange(256, dtype=torch.int32).to(torch.uint8)
+    nb, nh, hd, bs = 4, 2, 8, 16
+    cache = codes.repeat(4).reshape(nb, nh, hd, bs).contiguous()
+    slots = torch.tensor([0, 1, 2, 3, -1, 17, 18, 33, 60, 63, 47, -3], dtype=torch.int64)
+    for fmt in ("e4m3", "e5m2"):
+        for oname, odt in DTYPES.items():
+            for j, (ks, vs) in enumerate([(1.0, [0.25, 3.0]), (0.0371, 1.7)]):
+                ok, ov = ref.kv_paged_fp8_to_linear(cache, cache.flip(0).contiguous(), slots, ks, vs, out_dtype=odt, fp8_format=fmt)
+                p = f"dec/{fmt}/{oname}/{j}"
+                st.put(f"{p}/k_scale", torch.as_tensor(ks, dtype=torch.float32))
+                st.put(f"{p}/v_scale", torch.as_tensor(vs, dtype=torch.float32))
+                st.put(f"{p}/out_k", ok)
+                st.put(f"{p}/out_v", ov)
+    st.put("dec/k_cache", cache)
+    st.put("dec/v_cache", cache.flip(0).contiguous())
+    st.put("dec/slots", slots)
+    # multi-layer: [L, NH] scales, duplicates and negative slots, bf16 and fp16 input
+    nl, nb, nh, hd, bs = 3, 4, 2, 16, 16
+    sl = torch.tensor([5, 6, 7, -1, 5, 40, 63, 0, 1, 2, 3, 4, 8, 9, 10, 11, 12, 13, 14, 15], dtype=torch.int64)
+    for fmt in ("e4m3", "e5m2"):
+        for lname, ldt in (("bfloat16", torch.bfloat16), ("float16", torch.float16), ("float32", torch.float32)):
+            g = gen(30)
+            kl = (randn((nl, sl.numel(), nh, hd), torch.float32, g) * 2.0).to(ldt)
+            vl = (randn((nl, sl.numel(), nh, hd), torch.float32, g) * 2.0).to(ldt)
+            ks = torch.rand((nl, nh), generator=g) * 0.02 + 0.001
+            vs = 0.0173
+            kc = torch.zeros((nl, nb, nh, hd, bs), dtype=torch.uint8)
+            vc = torch.zeros((nl, nb, nh, hd, bs), dtype=torch.uint8)
+            ref.kv_linear_to_paged_fp8_multi_layer(kl, vl, kc, vc, sl, ks, vs, fp8_format=fmt)
+            p = f"ml/{fmt}/{lname}"
+            st.put(f"{p}/k_lin", kl)
+            st.put(f"{p}/v_lin", vl)
+            st.put(f"{p}/k_scale", ks)
+            st.put(f"{p}/v_scale", torch.tensor(vs, dtype=torch.float32))
+            st.put(f"{p}/k_cache", kc)
+            st.put(f"{p}/v_cache", vc)
+            ok, ov = ref.kv_paged_fp8_to_linear_multi_layer(kc, vc, sl, ks, vs, out_dtype=ldt, fp8_format=fmt)
+            st.put(f"{p}/out_k", ok)
+            st.put(f"{p}/out_v", ov)
+    st.put("ml/slots", sl)
+    st.save("fp8.npz")
+
+
+# ---------------------------------------------------------------------------
+def make_rows() -> None:
+    st = Store()
+    nl, nb, bs, nh, hs = 3, 4, 4, 2, 8
+    h = nh * hs
+    gslots = torch.tensor([0, 3, 5, -1, 15, 7, 8, 9, 10, -2], dtype=torch.int64)
+    sslots = torch.tensor([2, 14, -1, 2, 6, 0, 14, 11], dtype=torch.int64)
+    for dname, dt in DTYPES.items():
+        g = gen(40)
+        # 6-D legacy layout
+        paged = randn((nl, 2, nb, bs, nh, hs), dt, g)
+        buf = torch.empty(2, nl, gslots.numel(), h, dtype=dt)
+        ref.lmcache_paged_to_kv_buffer(paged, buf, gslots)
+        p = f"six_d/{dname}"
+        st.put(f"{p}/paged", paged)
+        st.put(f"{p}/gather", buf)
+        src = randn((2, nl, sslots.numel(), h), dt, g)
+        dst = torch.full((nl, 2, nb, bs, nh, hs), 0.25, dtype=dt)
+        ref.lmcache_kv_buffer_to_paged(src, dst, sslots)
+        st.put(f"{p}/scatter_src", src)
+        st.put(f"{p}/scatter_dst", dst)
+        # list layout [2, NB, BS, NH, HS] per layer, memory with extra tail tokens
+        caches = [randn((2, nb, bs, nh, hs), dt, g) for _ in range(nl)]
+        mem = torch.full((2, nl, gslots.numel() + 3, h), 9.0, dtype=dt)
+        ref.lmcache_kv_paged_to_buffer(caches, mem, gslots, bs, nh, hs)
+        p = f"list/{dname}"
+        st.put(f"{p}/caches", torch.stack(caches))
+        st.put(f"{p}/gather", mem)
+        msrc = randn((2, nl, sslots.numel() + 2, h), dt, g)
+        dcaches = [torch.zeros((2, nb, bs, nh, hs), dtype=dt) for _ in range(nl)]
+        ref.lmcache_kv_buffer_to_paged(msrc, dcaches, sslots, 2, bs, nh, hs)
+        st.put(f"{p}/scatter_src", msrc)
+        st.put(f"{p}/scatter_dst", torch.stack(dcaches))
+        # SGLang MP 2 x NL x [NB, BS, NH, HS]
+        two = [[randn((nb, bs, nh, hs), dt, g) for _ in range(nl)] for _ in range(2)]
+        mem2 = torch.full((2, nl, gslots.numel(), h), 4.0, dtype=dt)
+        ref.lmcache_kv_paged_to_buffer_two_x_nl(two, mem2, gslots, bs, nh, hs)
+        p = f"two_x_nl/{dname}"
+        st.put(f"{p}/caches", torch.stack([torch.stack(x) for x in two]))
+        st.put(f"{p}/gather", mem2)
+        msrc2 = randn((2, nl, sslots.numel() + 1, h), dt, g)
+        dtwo = [[torch.full((nb, bs, nh, hs), -1.0, dtype=dt) for _ in range(nl)] for _ in range(2)]
+        ref.lmcache_kv_buffer_to_paged_two_x_nl(msrc2, dtwo, sslots, 1, bs, nh, hs)
+        st.put(f"{p}/scatter_src", msrc2)
+        st.put(f"{p}/scatter_dst", torch.stack([torch.stack(x) for x in dtwo]))
+        # MLA buffer [NL, T, HS] <-> [NL, NB, BS, HS]
+        hsm = 12
+        mpaged = randn((nl, nb, bs, hsm), dt, g)
+        mbuf = torch.full((nl, gslots.numel(), hsm), 5.0, dtype=dt)
+        ref.lmcache_paged_to_kv_buffer_mla(mpaged, mbuf, gslots)
+        p = f"mla/{dname}"
+        st.put(f"{p}/paged", mpaged)
+        st.put(f"{p}/gather", mbuf)
+        msrc3 = randn((nl, sslots.numel(), hsm), dt, g)
+        mdst = torch.zeros((nl, nb, bs, hsm), dtype=dt)
+        ref.lmcache_kv_buffer_to_paged_mla(msrc3, mdst, sslots)
+        st.put(f"{p}/scatter_src", msrc3)
+        st.put(f"{p}/scatter_dst", mdst)
+        # MLA list [1, NL, T, HS] <-> list of [NB, BS, HS]
+        mlist = [randn((nb, bs, hsm), dt, g) for _ in range(nl)]
+        mmem = torch.full((1, nl, gslots.numel() + 2, hsm), 7.0, dtype=dt)
+        ref.lmcache_mla_paged_to_buffer(mlist, mmem, gslots, bs, hsm)
+        p = f"mla_list/{dname}"
+        st.put(f"{p}/caches", torch.stack(mlist))
+        st.put(f"{p}/gather", mmem)
+        msrc4 = randn((1, nl, sslots.numel() + 1, hsm), dt, g)
+        mldst = [torch.zeros((nb, bs, hsm), dtype=dt) for _ in range(nl)]
+        ref.lmcache_mla_buffer_to_paged(msrc4, mldst, sslots, 1, bs, hsm)
+        st.put(f"{p}/scatter_src", msrc4)
+        st.put(f"{p}/scatter_dst", torch.stack(mldst))
+        # MLA flat asymmetric caches (kv_dim 12, pe_dim 4), single and multi layer
+        kvc = randn((nl, nb, bs, 12), dt, g)
+        pec = randn((nl, nb, bs, 4), dt, g)
+        okv, ope = ref.kv_paged_to_mla_linear(kvc[0], pec[0], gslots)
+        p = f"mla_flat/{dname}"
+        st.put(f"{p}/kv_cache", kvc)
+        st.put(f"{p}/pe_cache", pec)
+        st.put(f"{p}/gather_kv", okv)
+        st.put(f"{p}/gather_pe", ope)
+        okv3, ope3 = ref.kv_paged_to_mla_linear_multi_layer(kvc, pec, gslots)
+        st.put(f"{p}/gather_ml_kv", okv3)
+        st.put(f"{p}/gather_ml_pe", ope3)
+        lkv = randn((nl, sslots.numel(), 12), dt, g)
+        lpe = randn((nl, sslots.numel(), 4), dt, g)
+        dkv = torch.zeros_like(kvc)
+        dpe = torch.zeros_like(pec)
+        ref.kv_mla_linear_to_paged_multi_layer(lkv, lpe, dkv, dpe, sslots)
+        st.put(f"{p}/scatter_kv_in", lkv)
+        st.put(f"{p}/scatter_pe_in", lpe)
+        st.put(f"{p}/scatter_kv", dkv)
+        st.put(f"{p}/scatter_pe", dpe)
+    st.put("gslots", gslots)
+    st.put("sslots", sslots)
+    st.save("rows.npz")
+
+
+if __name__ == "__main__":
+    torch.manual_seed(0)
+    make_tile()
+    make_fp8()
+    make_rows()

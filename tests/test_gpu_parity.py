@@ -1,0 +1,383 @@
+"""GPU parity: the sm_100a kernels (through the public ``musa_aiter`` API, which
+calls the C ABI) against the reference's own outputs (golden vectors) and
+against the CPU oracle on larger seeded inputs.  Every comparison is
+bit-exact (integer/byte work and the FP8 codec given the same scales)."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import musa_aiter as ma
+from oracle import kv_oracle as O
+
+from ._util import TORCH_OF, first_diff, same_bits, to_np, to_torch
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+DTYPES = ("float32", "float16", "bfloat16")
+
+
+@pytest.fixture(scope="module")
+def tile():
+    return np.load(GOLDEN / "tile.npz")
+
+
+@pytest.fixture(scope="module")
+def fp8():
+    return np.load(GOLDEN / "fp8.npz")
+
+
+@pytest.fixture(scope="module")
+def rows():
+    return np.load(GOLDEN / "rows.npz")
+
+
+def T(a, dt=None):
+    return to_torch(a, dt)
+
+
+def full(shape, value, dt):
+    return torch.full(shape, value, dtype=TORCH_OF[dt], device="cuda")
+
+
+def eq(a, b, what=""):
+    assert same_bits(a, b), f"{what}: {first_diff(a, b)}"
+
+
+# ---------------------------------------------------------------------------
+# golden replay: tile family
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_golden_tile(cuda_device, tile, dt):
+    p = f"gather/{dt}"
+    kc, vc, sl = T(tile[f"{p}/k_cache"], dt), T(tile[f"{p}/v_cache"], dt), T(tile[f"{p}/slots"])
+    ok, ov = ma.kv_paged_to_linear(kc, vc, sl)
+    eq(ok, tile[f"{p}/out_k"], "gather k")
+    eq(ov, tile[f"{p}/out_v"], "gather v")
+    pk = full(tuple(ok.shape), 3.0, dt)
+    pv = full(tuple(ov.shape), -2.0, dt)
+    ma.kv_paged_to_linear(kc, vc, sl, fill_skipped="preserve", out_k=pk, out_v=pv)
+    eq(pk, tile[f"{p}/preserve_k"], "preserve k")
+    eq(pv, tile[f"{p}/preserve_v"], "preserve v")
+
+    q = f"scatter/{dt}"
+    kd = torch.zeros_like(kc)
+    vd = full(tuple(vc.shape), 1.5, dt)
+    ma.kv_linear_to_paged(T(tile[f"{q}/k_lin"], dt), T(tile[f"{q}/v_lin"], dt), kd, vd, T(tile[f"{q}/slots"]))
+    eq(kd, tile[f"{q}/k_cache"], "scatter k")
+    eq(vd, tile[f"{q}/v_cache"], "scatter v")
+
+    r = f"gather_ml/{dt}"
+    kc3, vc3 = T(tile[f"{r}/k_cache"], dt), T(tile[f"{r}/v_cache"], dt)
+    ok3, ov3 = ma.kv_paged_to_linear_multi_layer(kc3, vc3, T(tile[f"{r}/slots"]))
+    eq(ok3, tile[f"{r}/out_k"], "ml gather k")
+    eq(ov3, tile[f"{r}/out_v"], "ml gather v")
+    s = f"scatter_ml/{dt}"
+    kd3, vd3 = torch.zeros_like(kc3), torch.zeros_like(vc3)
+    ma.kv_linear_to_paged_multi_layer(T(tile[f"{s}/k_lin"], dt), T(tile[f"{s}/v_lin"], dt), kd3, vd3, T(tile[f"{s}/slots"]))
+    eq(kd3, tile[f"{s}/k_cache"], "ml scatter k")
+    eq(vd3, tile[f"{s}/v_cache"], "ml scatter v")
+
+    eq(ma.kv_paged_to_merged_linear(kc, vc, sl), tile[f"merged/{dt}/gather"], "merged gather")
+    eq(ma.kv_paged_to_merged_linear_multi_layer(kc3, vc3, sl), tile[f"merged/{dt}/gather_ml"], "merged ml gather")
+    kd, vd = torch.zeros_like(kc), torch.zeros_like(vc)
+    ma.kv_merged_linear_to_paged(T(tile[f"merged/{dt}/scatter_in"], dt), kd, vd, T(tile[f"scatter/{dt}/slots"]))
+    eq(kd, tile[f"merged/{dt}/scatter_k"], "merged scatter k")
+    eq(vd, tile[f"merged/{dt}/scatter_v"], "merged scatter v")
+
+
+# ---------------------------------------------------------------------------
+# golden replay: FP8 codec
+# ---------------------------------------------------------------------------
+
+
+def _enc(fp8, key, fmt, dt):
+    kc = torch.zeros(fp8[f"{key}/k_cache"].shape, dtype=torch.uint8, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks = torch.from_numpy(fp8[f"{key}/k_scale"]).cuda()
+    vs = torch.from_numpy(fp8[f"{key}/v_scale"]).cuda()
+    ma.kv_linear_to_paged_fp8(T(fp8[f"{key}/k_lin"], dt), T(fp8[f"{key}/v_lin"], dt), kc, vc, T(fp8[f"{key}/slots"]), ks, vs,
+                              fp8_format=fmt)
+    eq(kc, fp8[f"{key}/k_cache"], f"{key} k")
+    eq(vc, fp8[f"{key}/v_cache"], f"{key} v")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+def test_golden_fp8_encode_exhaustive(cuda_device, fp8, fmt):
+    for i in range(2):
+        _enc(fp8, f"enc_bf16/{fmt}/{i}", fmt, "bfloat16")
+    _enc(fp8, f"enc_f16/{fmt}/0", fmt, "float16")
+    _enc(fp8, f"enc_f32/{fmt}/0", fmt, "float32")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", DTYPES)
+def test_golden_fp8_decode_all_codes(cuda_device, fp8, fmt, dt):
+    kc, vc, sl = T(fp8["dec/k_cache"]), T(fp8["dec/v_cache"]), T(fp8["dec/slots"])
+    for j in range(2):
+        p = f"dec/{fmt}/{dt}/{j}"
+        ks = torch.from_numpy(fp8[f"{p}/k_scale"]).cuda()
+        vs = torch.from_numpy(fp8[f"{p}/v_scale"]).cuda()
+        ok, ov = ma.kv_paged_fp8_to_linear(kc, vc, sl, ks, vs, out_dtype=TORCH_OF[dt], fp8_format=fmt)
+        eq(ok, fp8[f"{p}/out_k"], p + " k")
+        eq(ov, fp8[f"{p}/out_v"], p + " v")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", DTYPES)
+def test_golden_fp8_multi_layer(cuda_device, fp8, fmt, dt):
+    p = f"ml/{fmt}/{dt}"
+    sl = T(fp8["ml/slots"])
+    ks = torch.from_numpy(fp8[f"{p}/k_scale"]).cuda()
+    vs = torch.from_numpy(fp8[f"{p}/v_scale"]).cuda()
+    kc = torch.zeros(fp8[f"{p}/k_cache"].shape, dtype=torch.uint8, device="cuda")
+    vc = torch.zeros_like(kc)
+    ma.kv_linear_to_paged_fp8_multi_layer(T(fp8[f"{p}/k_lin"], dt), T(fp8[f"{p}/v_lin"], dt), kc, vc, sl, ks, vs, fp8_format=fmt)
+    eq(kc, fp8[f"{p}/k_cache"], p + " store k")
+    eq(vc, fp8[f"{p}/v_cache"], p + " store v")
+    ok, ov = ma.kv_paged_fp8_to_linear_multi_layer(kc, vc, sl, ks, vs, out_dtype=TORCH_OF[dt], fp8_format=fmt)
+    eq(ok, fp8[f"{p}/out_k"], p + " load k")
+    eq(ov, fp8[f"{p}/out_v"], p + " load v")
+
+
+# ---------------------------------------------------------------------------
+# golden replay: row family (LMCache / SGLang MP / MLA)
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_golden_lmcache(cuda_device, rows, dt):
+    gs, ss = T(rows["gslots"]), T(rows["sslots"])
+    nl, nb, bs, nh, hs = 3, 4, 4, 2, 8
+    p = f"six_d/{dt}"
+    buf = full(rows[f"{p}/gather"].shape, 13.0, dt)
+    assert ma.lmcache_paged_to_kv_buffer(T(rows[f"{p}/paged"], dt), buf, gs) is True
+    eq(buf, rows[f"{p}/gather"], "6-D gather")
+    dst = full(rows[f"{p}/scatter_dst"].shape, 0.25, dt)
+    assert ma.lmcache_kv_buffer_to_paged(T(rows[f"{p}/scatter_src"], dt), dst, ss) is True
+    eq(dst, rows[f"{p}/scatter_dst"], "6-D scatter")
+
+    p = f"list/{dt}"
+    caches = list(T(rows[f"{p}/caches"], dt).unbind(0))
+    mem = full(rows[f"{p}/gather"].shape, 9.0, dt)
+    assert ma.lmcache_kv_paged_to_buffer(caches, mem, gs, bs, nh, hs) is True
+    eq(mem, rows[f"{p}/gather"], "list gather")
+    dcaches = [torch.zeros_like(c).contiguous() for c in caches]
+    assert ma.lmcache_kv_buffer_to_paged(T(rows[f"{p}/scatter_src"], dt), dcaches, ss, 2, bs, nh, hs) is True
+    eq(torch.stack(dcaches), rows[f"{p}/scatter_dst"], "list scatter")
+
+    p = f"two_x_nl/{dt}"
+    two_t = T(rows[f"{p}/caches"], dt)
+    two = [[two_t[kv, layer].contiguous() for layer in range(nl)] for kv in range(2)]
+    mem = full(rows[f"{p}/gather"].shape, 4.0, dt)
+    assert ma.lmcache_kv_paged_to_buffer(two, mem, gs, bs, nh, hs) is True
+    eq(mem, rows[f"{p}/gather"], "two_x_nl gather")
+    dtwo = [[full((nb, bs, nh, hs), -1.0, dt) for _ in range(nl)] for _ in range(2)]
+    assert ma.lmcache_kv_buffer_to_paged_two_x_nl(T(rows[f"{p}/scatter_src"], dt), dtwo, ss, 1, bs, nh, hs) is True
+    eq(torch.stack([torch.stack(x) for x in dtwo]), rows[f"{p}/scatter_dst"], "two_x_nl scatter")
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_golden_mla(cuda_device, rows, dt):
+    gs, ss = T(rows["gslots"]), T(rows["sslots"])
+    p = f"mla/{dt}"
+    buf = full(rows[f"{p}/gather"].shape, 5.0, dt)
+    assert ma.lmcache_paged_to_kv_buffer_mla(T(rows[f"{p}/paged"], dt), buf, gs) is True
+    eq(buf, rows[f"{p}/gather"], "mla gather")
+    dst = full(rows[f"{p}/scatter_dst"].shape, 0.0, dt)
+    assert ma.lmcache_kv_buffer_to_paged_mla(T(rows[f"{p}/scatter_src"], dt), dst, ss) is True
+    eq(dst, rows[f"{p}/scatter_dst"], "mla scatter")
+
+    p = f"mla_list/{dt}"
+    caches = [c.contiguous() for c in T(rows[f"{p}/caches"], dt).unbind(0)]
+    mem = full(rows[f"{p}/gather"].shape, 7.0, dt)
+    assert ma.lmcache_mla_paged_to_buffer(caches, mem, gs, 4, 12) is True
+    eq(mem, rows[f"{p}/gather"], "mla list gather")
+    dl = [torch.zeros_like(c) for c in caches]
+    assert ma.lmcache_mla_buffer_to_paged(T(rows[f"{p}/scatter_src"], dt), dl, ss, 1, 4, 12) is True
+    eq(torch.stack(dl), rows[f"{p}/scatter_dst"], "mla list scatter")
+
+    p = f"mla_flat/{dt}"
+    kvc, pec = T(rows[f"{p}/kv_cache"], dt), T(rows[f"{p}/pe_cache"], dt)
+    okv, ope = ma.kv_paged_to_mla_linear(kvc[0], pec[0], gs)
+    eq(okv, rows[f"{p}/gather_kv"], "mla flat kv")
+    eq(ope, rows[f"{p}/gather_pe"], "mla flat pe")
+    okv3, ope3 = ma.kv_paged_to_mla_linear_multi_layer(kvc, pec, gs)
+    eq(okv3, rows[f"{p}/gather_ml_kv"], "mla flat ml kv")
+    eq(ope3, rows[f"{p}/gather_ml_pe"], "mla flat ml pe")
+    dkv, dpe = torch.zeros_like(kvc), torch.zeros_like(pec)
+    assert ma.kv_mla_linear_to_paged_multi_layer(T(rows[f"{p}/scatter_kv_in"], dt), T(rows[f"{p}/scatter_pe_in"], dt),
+                                                 dkv, dpe, ss) is True
+    eq(dkv, rows[f"{p}/scatter_kv"], "mla flat scatter kv")
+    eq(dpe, rows[f"{p}/scatter_pe"], "mla flat scatter pe")
+
+
+# ---------------------------------------------------------------------------
+# larger seeded cases against the oracle
+# ---------------------------------------------------------------------------
+
+
+def block_table_slots(lens, nb, bs, gen) -> torch.Tensor:
+    """Per-sequence block tables drawn from one permutation (distinct blocks), as in the bench configs."""
+    perm = torch.randperm(nb, generator=gen)
+    slots, used = [], 0
+    for n in lens:
+        nblk = (n + bs - 1) // bs
+        bt = perm[used: used + nblk]
+        used += nblk
+        pos = torch.arange(n)
+        slots.append(bt[pos // bs] * bs + pos % bs)
+    return torch.cat(slots).to(torch.int64)
+
+
+@pytest.mark.parametrize("dt", ("float16", "bfloat16"))
+def test_config1_tile_round_trip_vs_oracle(cuda_device, dt):
+    """Config 1 shapes ([256,16,8,128] caches permuted to [NB,NH,HD,BS]), sequences {100,513,1024,2047}."""
+    g = torch.Generator().manual_seed(1)
+    nb, bs, nh, hd = 256, 16, 8, 128
+    slots = block_table_slots([100, 513, 1024, 2047], nb, bs, g)
+    kc = torch.randn((nb, nh, hd, bs), generator=g).to(TORCH_OF[dt])
+    vc = torch.randn((nb, nh, hd, bs), generator=g).to(TORCH_OF[dt])
+    ok, ov = ma.kv_paged_to_linear(kc.cuda(), vc.cuda(), slots.cuda())
+    rk, rv = O.kv_paged_to_linear(to_np(kc), to_np(vc), slots.numpy())
+    eq(ok, rk, "cfg1 gather k")
+    eq(ov, rv, "cfg1 gather v")
+    kd = torch.zeros_like(kc).cuda()
+    vd = torch.zeros_like(vc).cuda()
+    ma.kv_linear_to_paged(ok, ov, kd, vd, slots.cuda())
+    touched = slots.numpy()
+    b, o = touched // bs, touched % bs
+    assert same_bits(to_np(kd)[b, :, :, o], to_np(kc)[b, :, :, o])
+    assert same_bits(to_np(vd)[b, :, :, o], to_np(vc)[b, :, :, o])
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_random_slots_tile_multi_layer_vs_oracle(cuda_device, dt):
+    """Random slots with negatives and duplicates, odd head_dim and block_size (element paths)."""
+    g = torch.Generator().manual_seed(7)
+    for (nl, nb, nh, hd, bs, t) in [(3, 40, 3, 24, 16, 300), (2, 17, 2, 13, 5, 101), (4, 64, 8, 128, 16, 1000)]:
+        kc = torch.randn((nl, nb, nh, hd, bs), generator=g).to(TORCH_OF[dt])
+        vc = torch.randn((nl, nb, nh, hd, bs), generator=g).to(TORCH_OF[dt])
+        slots = torch.randint(-2, nb * bs, (t,), generator=g)
+        ok, ov = ma.kv_paged_to_linear_multi_layer(kc.cuda(), vc.cuda(), slots.cuda())
+        rk, rv = O.kv_paged_to_linear_multi_layer(to_np(kc), to_np(vc), slots.numpy())
+        eq(ok, rk, f"gather {nl,nb,nh,hd,bs}")
+        eq(ov, rv, f"gather {nl,nb,nh,hd,bs}")
+        kl = torch.randn((nl, t, nh, hd), generator=g).to(TORCH_OF[dt])
+        vl = torch.randn((nl, t, nh, hd), generator=g).to(TORCH_OF[dt])
+        kd, vd = kc.clone().cuda(), vc.clone().cuda()
+        ma.kv_linear_to_paged_multi_layer(kl.cuda(), vl.cuda(), kd, vd, slots.to(torch.int32).cuda())
+        rkc, rvc = to_np(kc), to_np(vc)
+        O.kv_linear_to_paged_multi_layer(to_np(kl), to_np(vl), rkc, rvc, slots.numpy())
+        eq(kd, rkc, "scatter k")
+        eq(vd, rvc, "scatter v")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+def test_config3_fp8_random_slots_vs_oracle(cuda_device, fmt):
+    """Config 3 style: randn*2 bf16, random unique slots, per-layer-head (E4M3) / scalar (E5M2) scales."""
+    g = torch.Generator().manual_seed(3)
+    nl, nb, nh, hd, bs, t = 4, 512, 8, 128, 16, 256
+    kl = (torch.randn((nl, t, nh, hd), generator=g) * 2.0).to(torch.bfloat16)
+    vl = (torch.randn((nl, t, nh, hd), generator=g) * 2.0).to(torch.bfloat16)
+    slots = torch.randperm(nb * bs, generator=g)[:t]
+    if fmt == "e4m3":
+        ks = kl.float().abs().amax(dim=(1, 3)) / 448.0  # [L, NH]
+        vs = vl.float().abs().amax(dim=(1, 3)) / 448.0
+    else:
+        ks = kl.float().abs().amax() / 57344.0
+        vs = vl.float().abs().amax() / 57344.0
+    kc = torch.zeros((nl, nb, nh, hd, bs), dtype=torch.uint8, device="cuda")
+    vc = torch.zeros_like(kc)
+    ma.kv_linear_to_paged_fp8_multi_layer(kl.cuda(), vl.cuda(), kc, vc, slots.cuda(), ks.cuda(), vs.cuda(), fp8_format=fmt)
+    rkc = np.zeros(kc.shape, np.uint8)
+    rvc = np.zeros(vc.shape, np.uint8)
+    O.kv_linear_to_paged_fp8_multi_layer(to_np(kl), to_np(vl), rkc, rvc, slots.numpy(), ks.numpy(), vs.numpy(), fp8_format=fmt)
+    eq(kc, rkc, "fp8 store k")
+    eq(vc, rvc, "fp8 store v")
+    ok, ov = ma.kv_paged_fp8_to_linear_multi_layer(kc, vc, slots.cuda(), ks.cuda(), vs.cuda(), out_dtype=torch.bfloat16, fp8_format=fmt)
+    rk, rv = O.kv_paged_fp8_to_linear_multi_layer(rkc, rvc, slots.numpy(), ks.numpy(), vs.numpy(), out_dtype="bfloat16", fp8_format=fmt)
+    eq(ok, rk, "fp8 load k")
+    eq(ov, rv, "fp8 load v")
+
+
+def test_fp8_block_table_slots_packed_path(cuda_device):
+    """Block-table slots (full 16-token runs) exercise the 16-byte FP8 vector path."""
+    g = torch.Generator().manual_seed(5)
+    nb, nh, hd, bs = 128, 4, 64, 16
+    slots = block_table_slots([37, 160, 301], nb, bs, g)
+    t = slots.numel()
+    kl = torch.randn((t, nh, hd), generator=g).to(torch.float16)
+    vl = torch.randn((t, nh, hd), generator=g).to(torch.float16)
+    ks = torch.rand(nh, generator=g) * 0.01 + 0.002
+    kc = torch.zeros((nb, nh, hd, bs), dtype=torch.uint8, device="cuda")
+    vc = torch.zeros_like(kc)
+    ma.kv_linear_to_paged_fp8(kl.cuda(), vl.cuda(), kc, vc, slots.cuda(), ks.cuda(), 0.004)
+    rkc, rvc = np.zeros(kc.shape, np.uint8), np.zeros(vc.shape, np.uint8)
+    O.kv_linear_to_paged_fp8(kl.numpy(), vl.numpy(), rkc, rvc, slots.numpy(), ks.numpy(), np.float32(0.004), lin_dtype="float16")
+    eq(kc, rkc, "fp8 packed store k")
+    eq(vc, rvc, "fp8 packed store v")
+    ok, ov = ma.kv_paged_fp8_to_linear(kc, vc, slots.cuda(), ks.cuda(), 0.004, out_dtype=torch.float32)
+    rk, rv = O.kv_paged_fp8_to_linear(rkc, rvc, slots.numpy(), ks.numpy(), np.float32(0.004), out_dtype="float32")
+    eq(ok, rk, "fp8 packed load k")
+    eq(ov, rv, "fp8 packed load v")
+
+
+def test_lmcache_list_config2_subset_vs_oracle(cuda_device):
+    """Config 2 geometry (8 heads x 128, BS 16) on a reduced cache: list gather/scatter, one launch."""
+    g = torch.Generator().manual_seed(2)
+    nl, nb, bs, nh, hs = 4, 2048, 16, 8, 128
+    lens = torch.randint(256, 4097, (6,), generator=g).tolist()
+    slots = block_table_slots(lens, nb, bs, g)
+    t = slots.numel()
+    caches = [torch.randn((2, nb, bs, nh, hs), generator=g).to(torch.bfloat16) for _ in range(nl)]
+    mem = torch.empty((2, nl, t, nh * hs), dtype=torch.bfloat16, device="cuda")
+    dcaches = [c.cuda() for c in caches]
+    assert ma.lmcache_kv_paged_to_buffer(dcaches, mem, slots.cuda(), bs, nh, hs) is True
+    ref = np.zeros((2, nl, t, nh * hs), np.uint16)
+    O.lmcache_list_paged_to_buffer([to_np(c) for c in caches], ref, slots.numpy())
+    eq(mem, ref, "list gather")
+    fresh = [torch.zeros_like(c) for c in dcaches]
+    assert ma.lmcache_kv_buffer_to_paged(mem, fresh, slots.cuda(), 0, bs, nh, hs) is True
+    for c_src, c_dst in zip(dcaches, fresh):
+        flat_s = c_src.view(2, nb * bs, nh * hs)[:, slots.cuda()]
+        flat_d = c_dst.view(2, nb * bs, nh * hs)[:, slots.cuda()]
+        assert torch.equal(flat_s.view(torch.int16), flat_d.view(torch.int16))
+
+
+def test_current_stream_is_used(cuda_device):
+    """Kernels run on the caller's current stream (op_tests/test_phase5_musa.py:608-639 checks the same)."""
+    nb, bs, nh, hs, nl = 64, 16, 2, 64, 2
+    caches = [torch.randn((2, nb, bs, nh, hs), device="cuda", dtype=torch.float16) for _ in range(nl)]
+    slots = torch.arange(200, device="cuda")
+    mem = torch.empty((2, nl, 200, nh * hs), device="cuda", dtype=torch.float16)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ma.lmcache_kv_paged_to_buffer(caches, mem, slots, bs, nh, hs)
+        ev = torch.cuda.Event()
+        ev.record(s)
+    ev.synchronize()
+    expect = torch.stack([torch.stack([c[kv].reshape(-1, nh * hs)[:200] for c in caches]) for kv in range(2)])
+    assert torch.equal(mem, expect)
+
+
+def test_empty_and_out_of_range(cuda_device):
+    kc = torch.randn((4, 2, 8, 4), device="cuda")
+    vc = torch.randn((4, 2, 8, 4), device="cuda")
+    ok, ov = ma.kv_paged_to_linear(kc, vc, torch.empty(0, dtype=torch.int64, device="cuda"))
+    assert ok.shape == (0, 2, 8)
+    with pytest.raises(ValueError, match="out of bounds"):
+        ma.kv_paged_to_linear(kc, vc, torch.tensor([0, 16], device="cuda"))
+    with pytest.raises(ValueError, match="out of bounds"):
+        ma.kv_linear_to_paged(torch.zeros((1, 2, 8), device="cuda"), torch.zeros((1, 2, 8), device="cuda"), kc, vc,
+                              torch.tensor([99], device="cuda"))
+    all_neg = torch.full((5,), -1, device="cuda")
+    ok, _ = ma.kv_paged_to_linear(kc, vc, all_neg)
+    assert torch.count_nonzero(ok) == 0

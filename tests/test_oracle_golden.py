@@ -1,0 +1,211 @@
+"""Pin the CPU oracle to the reference: replay the golden vectors (recorded by
+running the reference itself, see tests/golden/make_golden.py) through
+``oracle.kv_oracle`` and require bit-identical results."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import kv_oracle as O
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+DTYPES = ("float32", "float16", "bfloat16")
+
+
+@pytest.fixture(scope="module")
+def tile():
+    return np.load(GOLDEN / "tile.npz")
+
+
+@pytest.fixture(scope="module")
+def fp8():
+    return np.load(GOLDEN / "fp8.npz")
+
+
+@pytest.fixture(scope="module")
+def rows():
+    return np.load(GOLDEN / "rows.npz")
+
+
+def same_bits(a: np.ndarray, b: np.ndarray) -> bool:
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    return a.shape == b.shape and a.dtype.itemsize == b.dtype.itemsize and a.tobytes() == b.tobytes()
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_tile_gather_scatter(tile, dt):
+    p = f"gather/{dt}"
+    ok, ov = O.kv_paged_to_linear(tile[f"{p}/k_cache"], tile[f"{p}/v_cache"], tile[f"{p}/slots"])
+    assert same_bits(ok, tile[f"{p}/out_k"]) and same_bits(ov, tile[f"{p}/out_v"])
+    pk = np.full_like(ok, 0)
+    pv = np.full_like(ov, 0)
+    pk[...] = O.from_f32(np.full(pk.shape, 3.0, np.float32), dt)
+    pv[...] = O.from_f32(np.full(pv.shape, -2.0, np.float32), dt)
+    O.kv_paged_to_linear(tile[f"{p}/k_cache"], tile[f"{p}/v_cache"], tile[f"{p}/slots"], fill_skipped="preserve", out_k=pk, out_v=pv)
+    assert same_bits(pk, tile[f"{p}/preserve_k"]) and same_bits(pv, tile[f"{p}/preserve_v"])
+
+    q = f"scatter/{dt}"
+    kd = np.zeros_like(tile[f"{p}/k_cache"])
+    vd = np.zeros_like(tile[f"{p}/v_cache"])
+    vd[...] = O.from_f32(np.full(vd.shape, 1.5, np.float32), dt)
+    O.kv_linear_to_paged(tile[f"{q}/k_lin"], tile[f"{q}/v_lin"], kd, vd, tile[f"{q}/slots"])
+    assert same_bits(kd, tile[f"{q}/k_cache"]) and same_bits(vd, tile[f"{q}/v_cache"])
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_tile_multi_layer_and_merged(tile, dt):
+    r = f"gather_ml/{dt}"
+    ok, ov = O.kv_paged_to_linear_multi_layer(tile[f"{r}/k_cache"], tile[f"{r}/v_cache"], tile[f"{r}/slots"])
+    assert same_bits(ok, tile[f"{r}/out_k"]) and same_bits(ov, tile[f"{r}/out_v"])
+    merged_ml = np.stack([ok, ov], axis=2)
+    assert same_bits(merged_ml, tile[f"merged/{dt}/gather_ml"])
+    g = f"gather/{dt}"
+    k1, v1 = O.kv_paged_to_linear(tile[f"{g}/k_cache"], tile[f"{g}/v_cache"], tile[f"{g}/slots"])
+    assert same_bits(np.stack([k1, v1], axis=1), tile[f"merged/{dt}/gather"])
+
+    s = f"scatter_ml/{dt}"
+    kd = np.zeros_like(tile[f"{r}/k_cache"])
+    vd = np.zeros_like(tile[f"{r}/v_cache"])
+    O.kv_linear_to_paged_multi_layer(tile[f"{s}/k_lin"], tile[f"{s}/v_lin"], kd, vd, tile[f"{s}/slots"])
+    assert same_bits(kd, tile[f"{s}/k_cache"]) and same_bits(vd, tile[f"{s}/v_cache"])
+
+    m_in = tile[f"merged/{dt}/scatter_in"]
+    kd = np.zeros_like(tile[f"{g}/k_cache"])
+    vd = np.zeros_like(tile[f"{g}/v_cache"])
+    O.kv_linear_to_paged(m_in[:, 0], m_in[:, 1], kd, vd, tile[f"scatter/{dt}/slots"])
+    assert same_bits(kd, tile[f"merged/{dt}/scatter_k"]) and same_bits(vd, tile[f"merged/{dt}/scatter_v"])
+
+
+def _enc_case(fp8, key, fmt, lin_dtype):
+    kc = np.zeros_like(fp8[f"{key}/k_cache"])
+    vc = np.zeros_like(fp8[f"{key}/v_cache"])
+    O.kv_linear_to_paged_fp8(
+        fp8[f"{key}/k_lin"], fp8[f"{key}/v_lin"], kc, vc, fp8[f"{key}/slots"],
+        fp8[f"{key}/k_scale"], fp8[f"{key}/v_scale"], fp8_format=fmt, lin_dtype=lin_dtype,
+    )
+    assert same_bits(kc, fp8[f"{key}/k_cache"]), key
+    assert same_bits(vc, fp8[f"{key}/v_cache"]), key
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+def test_fp8_encode_exhaustive(fp8, fmt):
+    for i in range(2):
+        _enc_case(fp8, f"enc_bf16/{fmt}/{i}", fmt, "bfloat16")
+    _enc_case(fp8, f"enc_f16/{fmt}/0", fmt, "float16")
+    _enc_case(fp8, f"enc_f32/{fmt}/0", fmt, "float32")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", DTYPES)
+def test_fp8_decode_all_codes(fp8, fmt, dt):
+    for j in range(2):
+        p = f"dec/{fmt}/{dt}/{j}"
+        ok, ov = O.kv_paged_fp8_to_linear(
+            fp8["dec/k_cache"], fp8["dec/v_cache"], fp8["dec/slots"], fp8[f"{p}/k_scale"], fp8[f"{p}/v_scale"],
+            out_dtype=dt, fp8_format=fmt,
+        )
+        assert same_bits(ok, fp8[f"{p}/out_k"]) and same_bits(ov, fp8[f"{p}/out_v"]), p
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", DTYPES)
+def test_fp8_multi_layer(fp8, fmt, dt):
+    p = f"ml/{fmt}/{dt}"
+    kc = np.zeros_like(fp8[f"{p}/k_cache"])
+    vc = np.zeros_like(fp8[f"{p}/v_cache"])
+    O.kv_linear_to_paged_fp8_multi_layer(
+        fp8[f"{p}/k_lin"], fp8[f"{p}/v_lin"], kc, vc, fp8["ml/slots"], fp8[f"{p}/k_scale"], fp8[f"{p}/v_scale"],
+        fp8_format=fmt, lin_dtype=dt,
+    )
+    assert same_bits(kc, fp8[f"{p}/k_cache"]) and same_bits(vc, fp8[f"{p}/v_cache"])
+    ok, ov = O.kv_paged_fp8_to_linear_multi_layer(
+        fp8[f"{p}/k_cache"], fp8[f"{p}/v_cache"], fp8["ml/slots"], fp8[f"{p}/k_scale"], fp8[f"{p}/v_scale"],
+        out_dtype=dt, fp8_format=fmt,
+    )
+    assert same_bits(ok, fp8[f"{p}/out_k"]) and same_bits(ov, fp8[f"{p}/out_v"])
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_lmcache_rows(rows, dt):
+    gs, ss = rows["gslots"], rows["sslots"]
+    # 6-D
+    p = f"six_d/{dt}"
+    paged = rows[f"{p}/paged"]
+    buf = np.zeros_like(rows[f"{p}/gather"])
+    O.lmcache_paged_to_kv_buffer(paged, buf, gs)
+    assert same_bits(buf, rows[f"{p}/gather"])
+    dst = np.empty_like(rows[f"{p}/scatter_dst"])
+    dst[...] = O.from_f32(np.full(dst.shape, 0.25, np.float32), dt)
+    O.lmcache_kv_buffer_to_paged(rows[f"{p}/scatter_src"], dst, ss)
+    assert same_bits(dst, rows[f"{p}/scatter_dst"])
+    # list
+    p = f"list/{dt}"
+    caches = list(rows[f"{p}/caches"])
+    mem = np.empty_like(rows[f"{p}/gather"])
+    mem[...] = O.from_f32(np.full(mem.shape, 9.0, np.float32), dt)
+    O.lmcache_list_paged_to_buffer(caches, mem, gs)
+    assert same_bits(mem, rows[f"{p}/gather"])
+    dcaches = [np.zeros_like(c) for c in caches]
+    O.lmcache_list_buffer_to_paged(rows[f"{p}/scatter_src"], dcaches, ss, skip_prefix=2)
+    assert same_bits(np.stack(dcaches), rows[f"{p}/scatter_dst"])
+    # two_x_nl
+    p = f"two_x_nl/{dt}"
+    two = [list(x) for x in rows[f"{p}/caches"]]
+    mem = np.zeros_like(rows[f"{p}/gather"])
+    O.lmcache_two_x_nl_paged_to_buffer(two, mem, gs)
+    assert same_bits(mem, rows[f"{p}/gather"])
+    dtwo = [[np.empty_like(c) for c in x] for x in two]
+    for x in dtwo:
+        for c in x:
+            c[...] = O.from_f32(np.full(c.shape, -1.0, np.float32), dt)
+    O.lmcache_two_x_nl_buffer_to_paged(rows[f"{p}/scatter_src"], dtwo, ss, skip_prefix=1)
+    assert same_bits(np.stack([np.stack(x) for x in dtwo]), rows[f"{p}/scatter_dst"])
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_mla_rows(rows, dt):
+    gs, ss = rows["gslots"], rows["sslots"]
+    p = f"mla/{dt}"
+    buf = np.zeros_like(rows[f"{p}/gather"])
+    O.lmcache_paged_to_kv_buffer_mla(rows[f"{p}/paged"], buf, gs)
+    assert same_bits(buf, rows[f"{p}/gather"])
+    dst = np.zeros_like(rows[f"{p}/scatter_dst"])
+    O.lmcache_kv_buffer_to_paged_mla(rows[f"{p}/scatter_src"], dst, ss)
+    assert same_bits(dst, rows[f"{p}/scatter_dst"])
+    p = f"mla_list/{dt}"
+    caches = list(rows[f"{p}/caches"])
+    mem = np.zeros_like(rows[f"{p}/gather"])
+    O.lmcache_mla_paged_to_buffer(caches, mem, gs)
+    assert same_bits(mem, rows[f"{p}/gather"])
+    dl = [np.zeros_like(c) for c in caches]
+    O.lmcache_mla_buffer_to_paged(rows[f"{p}/scatter_src"], dl, ss, skip_prefix=1)
+    assert same_bits(np.stack(dl), rows[f"{p}/scatter_dst"])
+    p = f"mla_flat/{dt}"
+    kvc, pec = rows[f"{p}/kv_cache"], rows[f"{p}/pe_cache"]
+    okv, ope = O.kv_paged_to_mla_linear(kvc[0], pec[0], gs)
+    assert same_bits(okv, rows[f"{p}/gather_kv"]) and same_bits(ope, rows[f"{p}/gather_pe"])
+    okv3 = np.stack([O.kv_paged_to_mla_linear(kvc[i], pec[i], gs)[0] for i in range(kvc.shape[0])])
+    ope3 = np.stack([O.kv_paged_to_mla_linear(kvc[i], pec[i], gs)[1] for i in range(kvc.shape[0])])
+    assert same_bits(okv3, rows[f"{p}/gather_ml_kv"]) and same_bits(ope3, rows[f"{p}/gather_ml_pe"])
+    dkv = np.zeros_like(kvc)
+    dpe = np.zeros_like(pec)
+    for i in range(kvc.shape[0]):
+        O.kv_mla_linear_to_paged(rows[f"{p}/scatter_kv_in"][i], rows[f"{p}/scatter_pe_in"][i], dkv[i], dpe[i], ss)
+    assert same_bits(dkv, rows[f"{p}/scatter_kv"]) and same_bits(dpe, rows[f"{p}/scatter_pe"])
+
+
+def test_last_writer_mask_matches_sequential_loop():
+    rng = np.random.default_rng(3)
+    slots = rng.integers(-3, 20, size=500)
+    keep = O.last_writer_mask(slots)
+    seen = {}
+    for t, s in enumerate(slots):
+        if s >= 0:
+            seen[int(s)] = t
+    expected = np.zeros_like(keep)
+    expected[list(seen.values())] = True
+    assert np.array_equal(keep, expected)

@@ -249,6 +249,27 @@ MAK_API int mak_rows_scatter(const mak_rows_desc* linear, const mak_rows_desc* p
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Allocation-free row scatter.  No counterpart in the reference: it exists for
+ * callers that cannot call cudaMalloc (a serving engine that reserved its HBM
+ * up front and scatters inside its step loop, or a foreign-language caller
+ * holding only raw pointers from another framework's allocator).  Same
+ * semantics as mak_rows_scatter, but the duplicate-slot scratch lives in a
+ * static device array inside the library (about 2.5 MiB on every GPU that
+ * loads the library, held until exit), so no workspace is passed.
+ * - At most MAK_STATIC_SCATTER_MAX_SLOTS slots per call; larger calls return
+ *   MAK_E_UNSUPPORTED without launching anything.
+ * - The first call on a device looks up the array's device address for that
+ *   device; make that first call before any stream capture.
+ * - Every call shares the one array: calls that may overlap on the GPU (other
+ *   streams, other host threads) race and must be serialised by the caller.
+ * - Allocates nothing: no cudaMalloc, cudaFree or allocating library routine.
+ */
+#define MAK_STATIC_SCATTER_MAX_SLOTS 65536
+MAK_API int mak_rows_scatter_static(const mak_rows_desc* linear, const mak_rows_desc* paged, const int64_t* row_bytes,
+                                    int64_t row_bytes0, const void* slots, int32_t slot_dtype, int64_t n_slots,
+                                    int64_t skip_prefix, void* stream);
+
+/*
  * Indexed row copy: dst row dst_idx[i] = src row src_idx[i] for i < n, on
  * every plane pair.  A NULL index array means the identity (i).  Negative
  * indices on either side skip the item; rows out of range are skipped.  Duplicate destinations: the last i wins (needs workspace).

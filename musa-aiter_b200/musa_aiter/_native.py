@@ -144,6 +144,10 @@ _PROTOTYPES = {
             c_void_p,
         ],
     ),
+    "mak_rows_scatter_static": (
+        c_int32,
+        [POINTER(RowsDesc), POINTER(RowsDesc), POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int64, c_void_p],
+    ),
     "mak_rows_copy": (
         c_int32,
         [

@@ -172,6 +172,15 @@ MAK_API int mak_build_slot_mapping(const void* block_tables, int32_t bt_dtype, i
                            int32_t len_dtype, int64_t batch, int64_t max_seq, int64_t block_size, int64_t* slots,
                            void* stream);
 
+/*
+ * Dense slot vector from CSR-style token indices (SGLang Triton decode layout):
+ *   slots[b*max_seq + s] = s < min(indptr[b+1] - indptr[b], max_seq) ? indices[indptr[b] + s] : -1.
+ * Replaces the per-sequence index_select loop of musa_aiter/ops/kv_transfer.py:1291-1366
+ * and musa_aiter_kv_triton_indexed_to_dense_* (csrc/kvcache/kv_transfer_float.mu:88-167).
+ */
+MAK_API int mak_build_indexed_slots(const void* indptr, int32_t indptr_dtype, const void* indices, int32_t indices_dtype,
+                                    int64_t n_indices, int64_t batch, int64_t max_seq, int64_t* slots, void* stream);
+
 /* ---- tile family ([L][NB][NH][HD][BS] caches) --------------------------- */
 
 /*
@@ -281,6 +290,46 @@ MAK_API int mak_rows_copy(const mak_rows_desc* src, const mak_rows_desc* dst, co
                   const void* src_idx, int32_t src_idx_dtype, const void* dst_idx, int32_t dst_idx_dtype, int64_t n,
                   void* workspace, size_t workspace_bytes, void* stream);
 
+
+/*
+ * DSV4 MLA / blocked-scale staging <-> paged byte-block transfer: one launch
+ * for every layer and block of a batch.  Arguments and semantics follow
+ * lmcache_kv_strided_block_transfer (musa_aiter/ops/lmcache_kv_transfer.py:1294-1403,
+ * csrc/kvcache/kv_transfer_float.mu:3281-3405): staging [NL][staging_tokens][row_bytes],
+ * paged_ptrs a HOST array of NL device page bases, block_ids a DEVICE int64
+ * vector; mode 0 plain rows, mode 1 values-then-scales per block (here
+ * value_bytes + scale_bytes must equal row_bytes); direction 0 staging -> paged,
+ * 1 paged -> staging.  Negative block ids are skipped.
+ */
+MAK_API int mak_lmcache_strided_block_transfer(void* staging, const uint64_t* paged_ptrs, const int64_t* block_ids,
+                                               int64_t direction, int64_t num_layers, int64_t idx_start, int64_t n_valid,
+                                               int64_t offset_in_object, int64_t staging_tokens, int64_t block_size,
+                                               int64_t row_bytes, int64_t paged_block_stride, int64_t mode,
+                                               int64_t value_bytes, int64_t scale_bytes, void* stream);
+
+/* ---- CacheGen-style codec ------------------------------------------------ */
+
+/*
+ * min and max of a float tensor (f16/bf16/f32, n > 0) into out_minmax[0..1]
+ * (device float[2]); device-only, no host sync.
+ */
+MAK_API int mak_minmax(const void* x, int32_t dtype, int64_t n, float* out_minmax, void* stream);
+
+/*
+ * Uniform-bin encode with the reference's arithmetic (musa_aiter/ops/kv_transfer.py:1111-1172):
+ * scale = (1 / (max - min)) * (num_bins - 1) in fp32, code = clamp(round_half_even((x - min) * scale)),
+ * counts[num_bins] (device uint64) = histogram of the codes, cdf[num_bins + 1]
+ * (device float) = [0, cumsum(counts) / n] accumulated sequentially in fp32.
+ * minmax is the device output of mak_minmax.  Replaces musa_aiter_kv_cachegen_encode_float
+ * (csrc/kvcache/kv_transfer_float.mu:828-866) and the host bincount.
+ */
+MAK_API int mak_cachegen_encode(const void* x, int32_t dtype, int64_t n, const float* minmax, int32_t num_bins,
+                                uint8_t* codes, uint64_t* counts, float* cdf, void* stream);
+
+/* out[i] = codebook[codes[i]] converted to out_dtype (RNE).  Replaces
+ * musa_aiter_kv_cachegen_decode_float (csrc/kvcache/kv_transfer_float.mu:868-905). */
+MAK_API int mak_cachegen_decode(const uint8_t* codes, int64_t n, const void* codebook, int32_t codebook_dtype,
+                                int32_t num_bins, void* out, int32_t out_dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,191 @@
+// Staging <-> paged byte-block transfer for DSV4 MLA / blocked-scale groups,
+// and the indptr/indices -> dense slot builder.
+//
+// Strided block transfer (reference semantics: csrc/kvcache/kv_transfer_float.mu:3281-3405).
+// Staging is [NL][staging_tokens][row_bytes]; block p of the batch covers staging
+// tokens offset_in_object + p*BS + t and paged block block_ids[idx_start + p]:
+//   mode 0: paged row t at  block*stride + t*row_bytes;
+//   mode 1: each staging row is [value_bytes | scale_bytes]; the paged page keeps
+//           all values first (block*stride + t*value_bytes) then all scales
+//           (block*stride + BS*value_bytes + t*scale_bytes).
+// direction 0 writes the paged pages, 1 reads them into staging.  One warp moves
+// one token row with the widest vector every address allows; all layers go in
+// one launch.  Negative block ids are skipped.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace mak {
+
+constexpr int kStridedLayers = 256;
+
+struct StridedLaunch {
+  uint64_t layers[kStridedLayers];
+  uint8_t* staging;
+  const int64_t* block_ids;
+  int64_t idx_start, n_valid, offset_in_object, staging_tokens, block_size, row_bytes, block_stride;
+  int64_t value_bytes, scale_bytes;
+  int32_t direction, mode, num_layers, layer_base;
+};
+
+template <int VEC>
+struct VecOf;
+template <>
+struct VecOf<16> { using T = uint4; };
+template <>
+struct VecOf<8> { using T = uint2; };
+template <>
+struct VecOf<4> { using T = uint32_t; };
+
+template <int VEC>
+__device__ __forceinline__ void copy_span(uint8_t* dst, const uint8_t* src, int64_t bytes, int lane) {
+  using V = typename VecOf<VEC>::T;
+  const int64_t nv = bytes / VEC;
+  V* d = reinterpret_cast<V*>(dst);
+  const V* s = reinterpret_cast<const V*>(src);
+  for (int64_t v0 = lane; v0 < nv; v0 += 32 * 4) {
+    V r[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v0 + 32 * u < nv) r[u] = s[v0 + 32 * u];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v0 + 32 * u < nv) d[v0 + 32 * u] = r[u];
+  }
+}
+
+template <int VEC>
+__global__ void __launch_bounds__(256) strided_block_kernel(const __grid_constant__ StridedLaunch p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = static_cast<int64_t>(p.num_layers) * p.n_valid * p.block_size;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < rows; w += nwarps) {
+    const int64_t t = w % p.block_size;
+    const int64_t rest = w / p.block_size;
+    const int64_t blk_i = rest % p.n_valid;
+    const int layer = static_cast<int>(rest / p.n_valid);
+    const int64_t blk = p.block_ids[p.idx_start + blk_i];
+    if (blk < 0) continue;
+    uint8_t* staged = p.staging + ((static_cast<int64_t>(p.layer_base + layer) * p.staging_tokens) + p.offset_in_object +
+                                   blk_i * p.block_size + t) * p.row_bytes;
+    uint8_t* page = reinterpret_cast<uint8_t*>(p.layers[layer]) + blk * p.block_stride;
+    if (p.mode == 0) {
+      uint8_t* paged = page + t * p.row_bytes;
+      if (p.direction == 0) copy_span<VEC>(paged, staged, p.row_bytes, lane);
+      else copy_span<VEC>(staged, paged, p.row_bytes, lane);
+    } else {
+      uint8_t* pv = page + t * p.value_bytes;
+      uint8_t* ps = page + p.block_size * p.value_bytes + t * p.scale_bytes;
+      if (p.direction == 0) {
+        copy_span<VEC>(pv, staged, p.value_bytes, lane);
+        copy_span<VEC>(ps, staged + p.value_bytes, p.scale_bytes, lane);
+      } else {
+        copy_span<VEC>(staged, pv, p.value_bytes, lane);
+        copy_span<VEC>(staged + p.value_bytes, ps, p.scale_bytes, lane);
+      }
+    }
+  }
+}
+
+template <int VEC>
+static int launch_strided(const StridedLaunch& p, cudaStream_t st) {
+  const int threads = 256;
+  const int64_t rows = static_cast<int64_t>(p.num_layers) * p.n_valid * p.block_size;
+  const int grid = grid_for(reinterpret_cast<const void*>(strided_block_kernel<VEC>), threads, 0, (rows + 7) / 8);
+  if (grid <= 0) return MAK_OK;
+  strided_block_kernel<VEC><<<grid, threads, 0, st>>>(p);
+  return launch_status("strided_block_kernel");
+}
+
+// slot[b*S + s] = s < min(max(indptr[b+1] - indptr[b], 0), S) ? indices[indptr[b] + s] : -1
+__global__ void indexed_slots_kernel(const void* indptr, int ip64, const void* indices, int ix64, int64_t n_indices,
+                                     int64_t batch, int64_t max_seq, int64_t* slots) {
+  const int64_t total = batch * max_seq;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / max_seq, s = i - b * max_seq;
+    const int64_t start = load_index(indptr, ip64, b);
+    const int64_t end = load_index(indptr, ip64, b + 1);
+    const int64_t len = end > start ? end - start : 0;
+    int64_t out = -1;
+    if (s < len && start + s >= 0 && start + s < n_indices) out = load_index(indices, ix64, start + s);
+    slots[i] = out;
+  }
+}
+
+}  // namespace mak
+
+using namespace mak;
+
+extern "C" {
+
+int mak_lmcache_strided_block_transfer(void* staging, const uint64_t* paged_ptrs, const int64_t* block_ids,
+                                       int64_t direction, int64_t num_layers, int64_t idx_start, int64_t n_valid,
+                                       int64_t offset_in_object, int64_t staging_tokens, int64_t block_size,
+                                       int64_t row_bytes, int64_t paged_block_stride, int64_t mode, int64_t value_bytes,
+                                       int64_t scale_bytes, void* stream) {
+  const char* name = "mak_lmcache_strided_block_transfer";
+  if (!staging || !paged_ptrs || !block_ids) return fail(MAK_E_INVALID, "%s: NULL pointer", name);
+  if (num_layers <= 0 || num_layers > MAK_MAX_PLANES) return fail(MAK_E_INVALID, "%s: bad num_layers %lld", name, (long long)num_layers);
+  if (n_valid <= 0 || block_size <= 0 || staging_tokens <= 0 || idx_start < 0)
+    return fail(MAK_E_INVALID, "%s: n_valid, block_size and staging_tokens must be positive", name);
+  if (row_bytes <= 0 || (row_bytes & 3) != 0) return fail(MAK_E_INVALID, "%s: row_bytes must be a positive multiple of 4", name);
+  if (paged_block_stride <= 0) return fail(MAK_E_INVALID, "%s: paged_block_stride must be positive", name);
+  if (direction != 0 && direction != 1) return fail(MAK_E_INVALID, "%s: direction must be 0 or 1", name);
+  if (mode != 0 && mode != 1) return fail(MAK_E_INVALID, "%s: mode must be 0 or 1", name);
+  if (mode == 1 && (value_bytes <= 0 || scale_bytes <= 0 || (value_bytes & 3) || (scale_bytes & 3) ||
+                    value_bytes + scale_bytes != row_bytes))
+    return fail(MAK_E_INVALID, "%s: mode 1 needs value_bytes + scale_bytes == row_bytes, both multiples of 4", name);
+  if (offset_in_object < 0 || offset_in_object + n_valid * block_size > staging_tokens)
+    return fail(MAK_E_INVALID, "%s: block range exceeds the staging object", name);
+  uint64_t bits = reinterpret_cast<uint64_t>(staging) | static_cast<uint64_t>(row_bytes) |
+                  static_cast<uint64_t>(paged_block_stride);
+  if (mode == 1) bits |= static_cast<uint64_t>(value_bytes) | static_cast<uint64_t>(scale_bytes);
+  for (int64_t l = 0; l < num_layers; ++l) {
+    if (paged_ptrs[l] == 0) return fail(MAK_E_INVALID, "%s: layer %lld pointer is NULL", name, (long long)l);
+    bits |= paged_ptrs[l];
+  }
+  const int vec = (bits & 15u) == 0 ? 16 : ((bits & 7u) == 0 ? 8 : 4);
+  cudaStream_t st = as_stream(stream);
+  for (int64_t l0 = 0; l0 < num_layers; l0 += kStridedLayers) {
+    StridedLaunch p;
+    memset(&p, 0, sizeof(p));
+    const int64_t nl = std::min<int64_t>(kStridedLayers, num_layers - l0);
+    for (int64_t l = 0; l < nl; ++l) p.layers[l] = paged_ptrs[l0 + l];
+    p.staging = static_cast<uint8_t*>(staging);
+    p.block_ids = block_ids;
+    p.idx_start = idx_start;
+    p.n_valid = n_valid;
+    p.offset_in_object = offset_in_object;
+    p.staging_tokens = staging_tokens;
+    p.block_size = block_size;
+    p.row_bytes = row_bytes;
+    p.block_stride = paged_block_stride;
+    p.value_bytes = value_bytes;
+    p.scale_bytes = scale_bytes;
+    p.direction = static_cast<int32_t>(direction);
+    p.mode = static_cast<int32_t>(mode);
+    p.num_layers = static_cast<int32_t>(nl);
+    p.layer_base = static_cast<int32_t>(l0);
+    int rc = vec == 16 ? launch_strided<16>(p, st) : (vec == 8 ? launch_strided<8>(p, st) : launch_strided<4>(p, st));
+    if (rc) return rc;
+  }
+  return MAK_OK;
+}
+
+int mak_build_indexed_slots(const void* indptr, int32_t indptr_dtype, const void* indices, int32_t indices_dtype,
+                            int64_t n_indices, int64_t batch, int64_t max_seq, int64_t* slots, void* stream) {
+  if (!valid_index_dtype(indptr_dtype) || !valid_index_dtype(indices_dtype))
+    return fail(MAK_E_INVALID, "mak_build_indexed_slots: index dtypes must be int32 or int64");
+  if (batch < 0 || max_seq < 0 || n_indices < 0) return fail(MAK_E_INVALID, "mak_build_indexed_slots: bad sizes");
+  const int64_t total = batch * max_seq;
+  if (total == 0) return MAK_OK;
+  if (!indptr || !slots || (n_indices > 0 && !indices)) return fail(MAK_E_INVALID, "mak_build_indexed_slots: NULL pointer");
+  const int threads = 256;
+  const int grid = grid_for(reinterpret_cast<const void*>(indexed_slots_kernel), threads, 0, (total + threads - 1) / threads);
+  indexed_slots_kernel<<<grid, threads, 0, as_stream(stream)>>>(indptr, indptr_dtype == MAK_DT_I64, indices,
+                                                                indices_dtype == MAK_DT_I64, n_indices, batch, max_seq,
+                                                                slots);
+  return launch_status("indexed_slots_kernel");
+}
+
+}  // extern "C"

@@ -148,6 +148,17 @@ _PROTOTYPES = {
         c_int32,
         [POINTER(RowsDesc), POINTER(RowsDesc), POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int64, c_void_p],
     ),
+    "mak_build_indexed_slots": (
+        c_int32,
+        [c_void_p, c_int32, c_void_p, c_int32, c_int64, c_int64, c_int64, c_void_p, c_void_p],
+    ),
+    "mak_lmcache_strided_block_transfer": (
+        c_int32,
+        [c_void_p, POINTER(c_uint64), c_void_p] + [c_int64] * 12 + [c_void_p],
+    ),
+    "mak_minmax": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_void_p]),
+    "mak_cachegen_encode": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "mak_cachegen_decode": (c_int32, [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p]),
     "mak_rows_copy": (
         c_int32,
         [

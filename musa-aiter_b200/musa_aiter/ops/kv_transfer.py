@@ -997,3 +997,713 @@ def kv_mla_linear_to_paged_multi_layer(
         _mla_scatter(k_pe_linear, k_pe_cache, slots, layered=True, op=name, ws=ws)
     emit_native(name, kv_linear, "sm100a row scatter (MLA flat, all layers)")
     return True
+
+
+# ---------------------------------------------------------------------------
+# Flash-style dense [B, S, NH, HD] layouts (musa_aiter/ops/kv_transfer.py:1527-1795)
+# ---------------------------------------------------------------------------
+
+
+def _index_tensor_ok(t: torch.Tensor) -> bool:
+    return t.dtype in (torch.int16, torch.int32, torch.int64)
+
+
+def _flash_block_check(bt_cpu: torch.Tensor, lens_cpu: torch.Tensor, nb: int, bs: int, name: str) -> None:
+    """First invalid block id among the blocks each sequence needs, in sequence-major order."""
+    if bt_cpu.numel() == 0 or lens_cpu.numel() == 0:
+        return
+    needed = (lens_cpu.clamp(min=0) + bs - 1) // bs
+    cols = torch.arange(bt_cpu.shape[1]).unsqueeze(0)
+    used = cols < needed.unsqueeze(1)
+    bad = used & ((bt_cpu < 0) | (bt_cpu >= nb))
+    if bool(bad.any()):
+        idx = int(torch.nonzero(bad.flatten())[0])
+        raise ValueError(f"{name}: invalid block id {int(bt_cpu.flatten()[idx])}")
+
+
+def _dense_slots(block_tables: torch.Tensor, seq_lens: torch.Tensor, bs: int, dense_len: int) -> torch.Tensor:
+    from .kv_transfer_plan import build_slot_mapping
+
+    return build_slot_mapping(block_tables, seq_lens, bs, max_seq_len=dense_len)
+
+
+def kv_load_and_reshape_flash(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    *,
+    max_seq_len: int | None = None,
+    out_k: torch.Tensor | None = None,
+    out_v: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Paged ``[NB, NH, HD, BS]`` caches -> dense ``[B, S, NH, HD]`` (zero padding).
+
+    Slots come from the block tables on the device (``mak_build_slot_mapping``)
+    and one tile-gather launch moves every sequence.  Reference: kv_transfer.py:1527-1622.
+    """
+    name = "kv_load_and_reshape_flash"
+    nb, nh, hd, bs = _validate_paged_shapes(key_cache, value_cache, name=name)
+    if block_tables.dim() != 2:
+        raise ValueError(f"{name}: block_tables must be [batch, max_blocks]")
+    if seq_lens.dim() != 1 or seq_lens.shape[0] != block_tables.shape[0]:
+        raise ValueError(f"{name}: seq_lens must be [batch]")
+    if key_cache.device != value_cache.device or block_tables.device != key_cache.device or seq_lens.device != key_cache.device:
+        raise ValueError(f"{name}: all tensors must be on the same device")
+    if not _index_tensor_ok(block_tables):
+        raise ValueError(f"{name}: block_tables must use an integer dtype")
+    if not _index_tensor_ok(seq_lens):
+        raise ValueError(f"{name}: seq_lens must use an integer dtype")
+    batch = int(block_tables.shape[0])
+    lens_cpu = seq_lens.to(device="cpu", dtype=torch.long)
+    if lens_cpu.numel() > 0 and int(lens_cpu.min()) < 0:
+        raise ValueError(f"{name}: seq_lens must be non-negative")
+    inferred = int(lens_cpu.max()) if lens_cpu.numel() > 0 else 0
+    dense_len = inferred if max_seq_len is None else int(max_seq_len)
+    if dense_len < inferred:
+        raise ValueError(f"{name}: max_seq_len is smaller than seq_lens max")
+    if (dense_len + bs - 1) // bs > int(block_tables.shape[1]):
+        raise ValueError(f"{name}: block_tables does not contain enough columns")
+    shape = (batch, dense_len, nh, hd)
+    for o, c, w in ((out_k, key_cache, "out_k"), (out_v, value_cache, "out_v")):
+        if o is not None and (tuple(o.shape) != shape or o.dtype != c.dtype or o.device != c.device):
+            raise ValueError(f"{name}: {w} must match [B, S, kv_heads, head_dim] dtype/device")
+    _flash_block_check(block_tables.to(device="cpu", dtype=torch.long), lens_cpu, nb, bs, name)
+    require_cuda(name, key_cache, value_cache, block_tables, seq_lens, out_k, out_v)
+    ok = out_k if out_k is not None else torch.empty(shape, dtype=key_cache.dtype, device=key_cache.device)
+    ov = out_v if out_v is not None else torch.empty(shape, dtype=value_cache.dtype, device=value_cache.device)
+    if batch * dense_len:
+        slots = _dense_slots(block_tables, seq_lens, bs, dense_len)
+        _tile_gather(key_cache, value_cache, slots, ok.view(batch * dense_len, nh, hd) if ok.is_contiguous() else ok.reshape(-1, nh, hd),
+                     ov.view(batch * dense_len, nh, hd) if ov.is_contiguous() else ov.reshape(-1, nh, hd),
+                     layered=False, fill_zero=True, op=name)
+    emit_native(name, key_cache, "sm100a device slot builder + tile gather (zero padding)")
+    return ok, ov
+
+
+def kv_reshape_and_cache_back_flash(
+    dense_k: torch.Tensor,
+    dense_v: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+) -> bool:
+    """Dense ``[B, S, NH, HD]`` -> paged caches at the block-table slots. Reference: kv_transfer.py:1625-1726."""
+    name = "kv_reshape_and_cache_back_flash"
+    if dense_k.dim() != 4 or dense_v.dim() != 4:
+        raise ValueError("dense Flash KV tensors must be [batch, seq, heads, head_dim]")
+    if dense_k.shape != dense_v.shape or dense_k.dtype != dense_v.dtype:
+        raise ValueError("dense K and V tensors must have matching shape and dtype")
+    if dense_k.device != dense_v.device:
+        raise ValueError("dense K and V tensors must be on the same device")
+    nb, nh, hd, bs = _validate_paged_shapes(key_cache, value_cache, name=name)
+    if key_cache.dtype != dense_k.dtype or value_cache.dtype != dense_v.dtype:
+        raise ValueError("dense and paged KV tensors must have matching dtypes")
+    if key_cache.device != dense_k.device or value_cache.device != dense_k.device:
+        raise ValueError("dense and paged KV tensors must be on the same device")
+    if tuple(dense_k.shape[2:]) != (nh, hd):
+        raise ValueError("dense KV head shape does not match paged cache")
+    if block_tables.dim() != 2:
+        raise ValueError(f"{name}: block_tables must be [batch, max_blocks]")
+    if seq_lens.dim() != 1 or seq_lens.shape[0] != block_tables.shape[0]:
+        raise ValueError(f"{name}: seq_lens must be [batch]")
+    if dense_k.shape[0] != block_tables.shape[0]:
+        raise ValueError(f"{name}: dense batch does not match block_tables")
+    if block_tables.device != dense_k.device or seq_lens.device != dense_k.device:
+        raise ValueError(f"{name}: all tensors must be on the same device")
+    if not _index_tensor_ok(block_tables):
+        raise ValueError(f"{name}: block_tables must use an integer dtype")
+    if not _index_tensor_ok(seq_lens):
+        raise ValueError(f"{name}: seq_lens must use an integer dtype")
+    lens_cpu = seq_lens.to(device="cpu", dtype=torch.long)
+    bt_cpu = block_tables.to(device="cpu", dtype=torch.long)
+    batch, dense_len = int(dense_k.shape[0]), int(dense_k.shape[1])
+    for b in range(batch):
+        n = int(lens_cpu[b])
+        if n < 0 or n > dense_len:
+            raise ValueError(f"{name}: seq_lens exceeds dense sequence length")
+        need = (n + bs - 1) // bs
+        if need > int(block_tables.shape[1]):
+            raise ValueError(f"{name}: block_tables does not contain enough columns")
+        row = bt_cpu[b, :need]
+        bad = (row < 0) | (row >= nb)
+        if bool(bad.any()):
+            raise ValueError(f"{name}: invalid block id {int(row[torch.nonzero(bad)[0]])}")
+    require_cuda(name, dense_k, dense_v, key_cache, value_cache, block_tables, seq_lens)
+    if batch * dense_len:
+        slots = _dense_slots(block_tables, seq_lens, bs, dense_len)
+        _tile_scatter(dense_k.reshape(-1, nh, hd), dense_v.reshape(-1, nh, hd), key_cache, value_cache, slots,
+                      layered=False, op=name)
+    emit_native(name, dense_k, "sm100a device slot builder + tile scatter")
+    return True
+
+
+def kv_load_and_dequantize_fp8_flash(
+    key_cache_fp8: torch.Tensor,
+    value_cache_fp8: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    k_scale: torch.Tensor | float,
+    v_scale: torch.Tensor | float,
+    *,
+    max_seq_len: int | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+    fp8_format: Literal["e4m3", "e5m2"] = "e4m3",
+    out_k: torch.Tensor | None = None,
+    out_v: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """FP8 paged caches -> dense dequantized ``[B, S, NH, HD]`` in one fused launch. Reference: kv_transfer.py:1729-1795."""
+    name = "kv_load_and_dequantize_fp8_flash"
+    fmt = _normalize_fp8_format(fp8_format)
+    nb, nh, hd, bs = _validate_paged_shapes(key_cache_fp8, value_cache_fp8, name=name)
+    if block_tables.dim() != 2:
+        raise ValueError(f"{name}: block_tables must be [batch, max_blocks]")
+    if seq_lens.dim() != 1 or seq_lens.shape[0] != block_tables.shape[0]:
+        raise ValueError(f"{name}: seq_lens must be [batch]")
+    if key_cache_fp8.device != value_cache_fp8.device or block_tables.device != key_cache_fp8.device or seq_lens.device != key_cache_fp8.device:
+        raise ValueError(f"{name}: all tensors must be on the same device")
+    if not _index_tensor_ok(block_tables) or not _index_tensor_ok(seq_lens):
+        raise ValueError(f"{name}: block_tables and seq_lens must be integer tensors")
+    batch = int(block_tables.shape[0])
+    lens_cpu = seq_lens.to(device="cpu", dtype=torch.long)
+    if lens_cpu.numel() > 0 and int(lens_cpu.min()) < 0:
+        raise ValueError(f"{name}: seq_lens must be non-negative")
+    inferred = int(lens_cpu.max()) if lens_cpu.numel() > 0 else 0
+    dense_len = inferred if max_seq_len is None else int(max_seq_len)
+    if dense_len < inferred:
+        raise ValueError(f"{name}: max_seq_len is smaller than seq_lens max")
+    if (dense_len + bs - 1) // bs > int(block_tables.shape[1]):
+        raise ValueError(f"{name}: block_tables does not contain enough columns")
+    shape = (batch, dense_len, nh, hd)
+    for o, w in ((out_k, "out_k"), (out_v, "out_v")):
+        if o is not None and (tuple(o.shape) != shape or o.dtype is not out_dtype or o.device != key_cache_fp8.device):
+            raise ValueError(f"{name}: {w} must match [B, S, kv_heads, head_dim] dtype/device")
+    _flash_block_check(block_tables.to(device="cpu", dtype=torch.long), lens_cpu, nb, bs, name)
+    _validate_fp8_cache_tensor(key_cache_fp8, name=f"{name} key_cache_fp8")
+    _validate_fp8_cache_tensor(value_cache_fp8, name=f"{name} value_cache_fp8")
+    require_cuda(name, key_cache_fp8, value_cache_fp8, block_tables, seq_lens, out_k, out_v)
+    ok = out_k if out_k is not None else torch.empty(shape, dtype=out_dtype, device=key_cache_fp8.device)
+    ov = out_v if out_v is not None else torch.empty(shape, dtype=out_dtype, device=key_cache_fp8.device)
+    if batch * dense_len:
+        ks = _ensure_fp8_scale(k_scale, device=key_cache_fp8.device, name="k_scale", num_heads=nh)
+        vs = _ensure_fp8_scale(v_scale, device=key_cache_fp8.device, name="v_scale", num_heads=nh)
+        ksa, vsa, mode = _scale_args(ks, vs, 1, nh)
+        slots = _dense_slots(block_tables, seq_lens, bs, dense_len)
+        _tile_gather(_u8_view(key_cache_fp8), _u8_view(value_cache_fp8), slots, ok.reshape(-1, nh, hd), ov.reshape(-1, nh, hd),
+                     layered=False, fill_zero=True, op=name, fp8=(ksa, vsa, mode, _FMT_CODE[fmt]))
+    emit_native(name, key_cache_fp8, f"sm100a fused FP8 {fmt} dense dequantize gather")
+    return ok, ov
+
+
+def kv_triton_indexed_to_dense(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    kv_indptr: torch.Tensor,
+    kv_indices: torch.Tensor,
+    *,
+    max_seq_len: int,
+    out_k: torch.Tensor | None = None,
+    out_v: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """SGLang token pool ``[Ntok, NH, HD]`` + CSR indices -> dense ``[B, S, NH, HD]`` (zero padding).
+
+    No host sync: the dense slot vector is built on the device
+    (``mak_build_indexed_slots``) and one row-gather launch moves K and V.
+    Reference: kv_transfer.py:1291-1366.
+    """
+    name = "kv_triton_indexed_to_dense"
+    if key_cache.dim() != 3 or value_cache.dim() != 3:
+        raise ValueError(f"{name}: key/value cache must be [tokens, kv_heads, head_dim]")
+    if key_cache.shape != value_cache.shape or key_cache.dtype != value_cache.dtype or key_cache.device != value_cache.device:
+        raise ValueError(f"{name}: key/value cache shape, dtype, and device must match")
+    if kv_indptr.dim() != 1 or kv_indptr.numel() < 2:
+        raise ValueError(f"{name}: kv_indptr must be [batch + 1]")
+    if kv_indices.dim() != 1:
+        raise ValueError(f"{name}: kv_indices must be 1-D")
+    if kv_indptr.device != key_cache.device or kv_indices.device != key_cache.device:
+        raise ValueError(f"{name}: all tensors must be on the same device")
+    if not _index_tensor_ok(kv_indptr) or not _index_tensor_ok(kv_indices):
+        raise ValueError(f"{name}: indices must use integer dtype")
+    batch = int(kv_indptr.shape[0] - 1)
+    dense_len = int(max_seq_len)
+    if dense_len < 0:
+        raise ValueError(f"{name}: max_seq_len must be non-negative")
+    ntok, nh, hd = map(int, key_cache.shape)
+    shape = (batch, dense_len, nh, hd)
+    for o, c, w in ((out_k, key_cache, "out_k"), (out_v, value_cache, "out_v")):
+        if o is not None and (tuple(o.shape) != shape or o.dtype != c.dtype or o.device != c.device or not o.is_contiguous()):
+            raise ValueError(f"{name}: {w} must match [B, S, kv_heads, head_dim] dtype/device and be contiguous")
+    require_cuda(name, key_cache, value_cache, kv_indptr, kv_indices, out_k, out_v)
+    ok = out_k if out_k is not None else torch.empty(shape, dtype=key_cache.dtype, device=key_cache.device)
+    ov = out_v if out_v is not None else torch.empty(shape, dtype=value_cache.dtype, device=key_cache.device)
+    total = batch * dense_len
+    if total:
+        lib = _native.load()
+        ip, ip_code = kernel_slots(kv_indptr)
+        ix, ix_code = kernel_slots(kv_indices)
+        slots = torch.empty(total, dtype=torch.int64, device=key_cache.device)
+        stream = _native.stream_ptr(key_cache.device)
+        _native.check(lib.mak_build_indexed_slots(_native.ptr(ip), ip_code, _native.ptr(ix), ix_code, ix.numel(), batch,
+                                                  dense_len, _native.ptr(slots), stream), name)
+        kc, _ = _as_unit_inner(key_cache)
+        vc, _ = _as_unit_inner(value_cache)
+        if kc.stride(1) != hd or vc.stride(1) != hd:
+            kc, vc = kc.contiguous(), vc.contiguous()
+        e = kc.element_size()
+        pd, pa = _native.rows_desc([kc.data_ptr(), vc.data_ptr()], 1, kc.stride(0) * e, 0, ntok)
+        ld, la = _native.rows_desc([ok.data_ptr(), ov.data_ptr()], 1, nh * hd * e, 0, total)
+        _native.check(lib.mak_rows_gather(ctypes.byref(pd), ctypes.byref(ld), None, nh * hd * e, _native.ptr(slots),
+                                          _native.MAK_DT_I64, total, 1, stream), name)
+    emit_native(name, key_cache, "sm100a device CSR slot builder + row gather")
+    return ok, ov
+
+
+# ---------------------------------------------------------------------------
+# whole-block copies (musa_aiter/ops/kv_transfer.py:1871-2091)
+# ---------------------------------------------------------------------------
+
+
+def _validate_block_copy_shapes(src_k, src_v, dst_k, dst_v, *, name: str) -> tuple[int, int, bool]:
+    if src_k.shape != src_v.shape:
+        raise ValueError(f"{name}: source key/value cache shapes must match")
+    if dst_k.shape != dst_v.shape:
+        raise ValueError(f"{name}: destination key/value cache shapes must match")
+    if src_k.dim() not in (4, 5) or dst_k.dim() != src_k.dim():
+        raise ValueError(f"{name}: caches must be 4-D single-layer or 5-D multi-layer paged tensors")
+    if src_k.dtype != src_v.dtype or dst_k.dtype != dst_v.dtype:
+        raise ValueError(f"{name}: key/value dtype pairs must match")
+    if src_k.dtype != dst_k.dtype:
+        raise ValueError(f"{name}: source and destination dtypes must match")
+    if src_k.dim() == 4:
+        if src_k.shape[1:] != dst_k.shape[1:]:
+            raise ValueError(f"{name}: single-layer cache tails must match")
+        return int(src_k.shape[0]), int(dst_k.shape[0]), False
+    if src_k.shape[0] != dst_k.shape[0] or src_k.shape[2:] != dst_k.shape[2:]:
+        raise ValueError(f"{name}: multi-layer cache layer count and tails must match")
+    return int(src_k.shape[1]), int(dst_k.shape[1]), True
+
+
+def _ensure_block_mapping_pairs(block_mapping: torch.Tensor, *, src_blocks: int, dst_blocks: int, name: str) -> torch.Tensor:
+    if block_mapping.dim() != 2 or block_mapping.shape[1] != 2:
+        raise ValueError(f"{name}: block_mapping must be [num_pairs, 2] with source and destination block ids")
+    if not _index_tensor_ok(block_mapping):
+        raise ValueError(f"{name}: block_mapping must use an integer dtype")
+    pairs = block_mapping.to(device="cpu", dtype=torch.long)
+    if pairs.numel() == 0:
+        return pairs
+    valid = (pairs[:, 0] >= 0) & (pairs[:, 1] >= 0)
+    if not bool(valid.any()):
+        return pairs
+    src_max = int(pairs[valid, 0].max())
+    dst_max = int(pairs[valid, 1].max())
+    if src_max >= src_blocks:
+        raise ValueError(f"{name}: source block index {src_max} out of bounds for {src_blocks} blocks")
+    if dst_max >= dst_blocks:
+        raise ValueError(f"{name}: destination block index {dst_max} out of bounds for {dst_blocks} blocks")
+    return pairs
+
+
+def _block_planes(k: torch.Tensor, v: torch.Tensor, multi_layer: bool):
+    """One plane per (kv, layer); a row is one whole block (its [NH, HD, BS] tail must be contiguous)."""
+    e = k.element_size()
+    planes = []
+    for t in (k, v):
+        if multi_layer:
+            planes += [t.data_ptr() + l * t.stride(0) * e for l in range(t.shape[0])]
+        else:
+            planes.append(t.data_ptr())
+    bdim = 1 if multi_layer else 0
+    return planes, k.stride(bdim) * e, int(k.shape[bdim])
+
+
+def _block_tail_contiguous(t: torch.Tensor, multi_layer: bool) -> bool:
+    tail = t[0, 0] if multi_layer else t[0]
+    return tail.is_contiguous()
+
+
+def _copy_blocks(src_k, src_v, dst_k, dst_v, pairs_dev: torch.Tensor, multi_layer: bool, name: str) -> None:
+    lib = _native.load()
+    for t in (src_k, src_v, dst_k, dst_v):
+        if not _block_tail_contiguous(t, multi_layer) or (multi_layer and t.stride(0) % 1):
+            raise ValueError(f"{name}: each cache block must be contiguous")
+    if src_k.stride() != src_v.stride() or dst_k.stride() != dst_v.stride():
+        raise ValueError(f"{name}: key and value caches must share strides")
+    sp, s_bstride, s_nb = _block_planes(src_k, src_v, multi_layer)
+    dp, d_bstride, d_nb = _block_planes(dst_k, dst_v, multi_layer)
+    tail = src_k[0, 0] if multi_layer else src_k[0]
+    row = tail.numel() * src_k.element_size()
+    src_idx = pairs_dev[:, 0].contiguous()
+    dst_idx = torch.where(src_idx >= 0, pairs_dev[:, 1], torch.full_like(src_idx, -1)).contiguous()
+    n = int(src_idx.numel())
+    ws, nbytes = _native.workspace(n, dst_k.device)
+    sd, sa = _native.rows_desc(sp, 1, s_bstride, 0, s_nb)
+    dd, da = _native.rows_desc(dp, 1, d_bstride, 0, d_nb)
+    rc = lib.mak_rows_copy(ctypes.byref(sd), ctypes.byref(dd), None, row, _native.ptr(src_idx), _native.MAK_DT_I64,
+                           _native.ptr(dst_idx), _native.MAK_DT_I64, n, _native.ptr(ws), nbytes,
+                           _native.stream_ptr(dst_k.device))
+    _native.check(rc, name)
+
+
+def kv_copy_paged_blocks(
+    src_key_cache: torch.Tensor,
+    src_value_cache: torch.Tensor,
+    dst_key_cache: torch.Tensor,
+    dst_value_cache: torch.Tensor,
+    block_mapping: torch.Tensor,
+) -> int:
+    """Copy whole blocks by ``[P, 2]`` (src, dst) pairs for 1 or L layers; returns the valid-pair count.
+
+    Every (kv, layer) plane goes in one row-engine launch (a block is one row).
+    Reference: kv_transfer.py:2035-2091.
+    """
+    name = "kv_copy_paged_blocks"
+    src_blocks, dst_blocks, multi = _validate_block_copy_shapes(src_key_cache, src_value_cache, dst_key_cache,
+                                                                dst_value_cache, name=name)
+    pairs = _ensure_block_mapping_pairs(block_mapping, src_blocks=src_blocks, dst_blocks=dst_blocks, name=name)
+    require_cuda(name, src_key_cache, src_value_cache, dst_key_cache, dst_value_cache)
+    count = int(((pairs[:, 0] >= 0) & (pairs[:, 1] >= 0)).sum()) if pairs.numel() else 0
+    if count:
+        dev_pairs = block_mapping.to(device=dst_key_cache.device, dtype=torch.int64)
+        _copy_blocks(src_key_cache, src_value_cache, dst_key_cache, dst_value_cache, dev_pairs, multi, name)
+    emit_native(name, dst_key_cache, "sm100a row engine, one block per row")
+    return count
+
+
+def kv_copy_paged_blocks_fp8(
+    src_key_cache_fp8: torch.Tensor,
+    src_value_cache_fp8: torch.Tensor,
+    dst_key_cache_fp8: torch.Tensor,
+    dst_value_cache_fp8: torch.Tensor,
+    block_mapping: torch.Tensor,
+) -> int:
+    """Raw FP8 (uint8 / float8) block copy. Reference: kv_transfer.py:1871-1906."""
+    name = "kv_copy_paged_blocks_fp8"
+    src_blocks, dst_blocks, multi = _validate_block_copy_shapes(src_key_cache_fp8, src_value_cache_fp8, dst_key_cache_fp8,
+                                                                dst_value_cache_fp8, name=name)
+    for t in (src_key_cache_fp8, src_value_cache_fp8, dst_key_cache_fp8, dst_value_cache_fp8):
+        _validate_fp8_cache_tensor(t, name=name)
+    pairs = _ensure_block_mapping_pairs(block_mapping, src_blocks=src_blocks, dst_blocks=dst_blocks, name=name)
+    require_cuda(name, src_key_cache_fp8, src_value_cache_fp8, dst_key_cache_fp8, dst_value_cache_fp8)
+    count = int(((pairs[:, 0] >= 0) & (pairs[:, 1] >= 0)).sum()) if pairs.numel() else 0
+    if count:
+        dev_pairs = block_mapping.to(device=dst_key_cache_fp8.device, dtype=torch.int64)
+        _copy_blocks(_u8_view(src_key_cache_fp8), _u8_view(src_value_cache_fp8), _u8_view(dst_key_cache_fp8),
+                     _u8_view(dst_value_cache_fp8), dev_pairs, multi, name)
+    emit_native(name, dst_key_cache_fp8, "sm100a row engine, one FP8 block per row")
+    return count
+
+
+# ---------------------------------------------------------------------------
+# DSV4 opaque byte rows (musa_aiter/ops/kv_transfer.py:4411-4736)
+# ---------------------------------------------------------------------------
+
+import threading as _threading  # noqa: E402
+import time as _time  # noqa: E402
+from dataclasses import dataclass as _dataclass  # noqa: E402
+
+from .kv_layout import KVLayoutSpec, KVScaleKind  # noqa: E402
+
+
+@_dataclass(frozen=True)
+class InterleavedFp8Layout:
+    """DSV4 interleaved FP8 block-scale page row: ``[value region][scale region]``.
+
+    Same fields and checks as the reference descriptor (kv_transfer.py:4411-4452).
+    """
+
+    value_bytes: int
+    scale_bytes: int
+    scale_granularity: int
+
+    def __post_init__(self) -> None:
+        if self.value_bytes <= 0 or self.scale_bytes <= 0:
+            raise ValueError("InterleavedFp8Layout: value_bytes and scale_bytes must be positive")
+        if self.scale_granularity <= 0:
+            raise ValueError("InterleavedFp8Layout: scale_granularity must be positive")
+
+    @property
+    def item_bytes(self) -> int:
+        return self.value_bytes + self.scale_bytes
+
+    def as_kv_layout_spec(self, *, num_layers: int, num_blocks: int, block_size: int, dtype_name: str = "uint8") -> KVLayoutSpec:
+        return KVLayoutSpec.dsv4(num_layers=num_layers, num_blocks=num_blocks, block_size=block_size,
+                                 row_bytes=self.item_bytes, block_stride_bytes=self.item_bytes * block_size,
+                                 dtype_name=dtype_name, scale_kind=KVScaleKind.BLOCKED, value_bytes=self.value_bytes,
+                                 scale_bytes=self.scale_bytes)
+
+
+@_dataclass
+class PoolSpec:
+    """One pool of a DSV4 multi-pool copy: per-layer uint8 ``[pages, item_bytes]`` tensors."""
+
+    src_ptrs: list
+    dst_ptrs: list
+    item_bytes: int
+
+
+_stats_lock = _threading.Lock()
+_stats = {"pinned_calls": 0, "unpinned_calls": 0, "pinned_bytes": 0, "unpinned_bytes": 0,
+          "pinned_ns_total": 0, "unpinned_ns_total": 0}
+
+
+def kv_transfer_stats() -> dict:
+    """Pinned vs unpinned call counts, bytes and host-side ns of the byte-row copies."""
+    with _stats_lock:
+        return dict(_stats)
+
+
+def reset_kv_transfer_stats() -> None:
+    with _stats_lock:
+        for k in _stats:
+            _stats[k] = 0
+
+
+def _record_stats(src: torch.Tensor, dst: torch.Tensor, rows: int, item_bytes: int, ns: int) -> None:
+    host = src if src.device.type == "cpu" else (dst if dst.device.type == "cpu" else None)
+    pinned = host is None or bool(host.is_pinned())
+    key = "pinned" if pinned else "unpinned"
+    with _stats_lock:
+        _stats[f"{key}_calls"] += 1
+        _stats[f"{key}_bytes"] += rows * item_bytes
+        _stats[f"{key}_ns_total"] += ns
+
+
+def _check_row_indices(indices: torch.Tensor, num_rows: int, name: str) -> None:
+    """Host indices are range-checked eagerly (IndexError); device indices are guarded in the kernel."""
+    if indices.numel() == 0 or indices.device.type != "cpu":
+        return
+    idx = indices.to(torch.long)
+    lo, hi = int(idx.min()), int(idx.max())
+    if lo < 0:
+        raise IndexError(f"{name} row index {lo} is negative")
+    if hi >= num_rows:
+        raise IndexError(f"{name} row index {hi} out of bounds for {num_rows} rows")
+
+
+def _validate_rows_args(src, dst, src_indices, dst_indices, *, name: str) -> int:
+    if not isinstance(src, torch.Tensor) or not isinstance(dst, torch.Tensor):
+        raise TypeError(f"{name}: src and dst must be torch.Tensor")
+    if src.dtype is not torch.uint8 or dst.dtype is not torch.uint8:
+        raise ValueError(f"{name}: src and dst must be uint8 byte rows, got src={src.dtype}, dst={dst.dtype}")
+    if src.dim() != 2 or dst.dim() != 2:
+        raise ValueError(f"{name}: src and dst must be [rows, item_bytes]")
+    item = int(src.shape[1])
+    if int(dst.shape[1]) != item:
+        raise ValueError(f"{name}: src and dst item_bytes must match, got src={item}, dst={int(dst.shape[1])}")
+    if item <= 0:
+        raise ValueError(f"{name}: item_bytes must be positive")
+    for ix in (src_indices, dst_indices):
+        if not (isinstance(ix, torch.Tensor) and ix.dim() == 1 and _index_tensor_ok(ix)):
+            raise ValueError(f"{name}: indices must use an integer dtype")
+    if src_indices.numel() != dst_indices.numel():
+        raise ValueError(f"{name}: src_indices and dst_indices must have the same length")
+    _check_row_indices(src_indices, int(src.shape[0]), f"{name}: src")
+    _check_row_indices(dst_indices, int(dst.shape[0]), f"{name}: dst")
+    return item
+
+
+def _addressable(t: torch.Tensor) -> bool:
+    """The GPU can address CUDA tensors and pinned host tensors (unified addressing)."""
+    return t.device.type == "cuda" or (t.device.type == "cpu" and bool(t.is_pinned()))
+
+
+def _rows_copy_planes(srcs: list[torch.Tensor], dsts: list[torch.Tensor], src_indices, dst_indices, name: str) -> None:
+    """dst[l][dst_idx[i]] = src[l][src_idx[i]] for every plane pair, one launch."""
+    lib = _native.load()
+    s0, d0 = srcs[0], dsts[0]
+    dev = s0.device if s0.device.type == "cuda" else d0.device
+    if dev.type != "cuda":
+        raise RuntimeError(f"{name}: at least one side must be a CUDA tensor")
+    for side, first in ((srcs, s0), (dsts, d0)):
+        for t in side:
+            if not _addressable(t):
+                raise RuntimeError(f"{name}: host tensors must be pinned for the GPU to address them")
+            if t.stride(1) != 1 or t.stride() != first.stride() or t.shape[0] != first.shape[0]:
+                raise ValueError(f"{name}: byte rows must be contiguous and share one geometry per side")
+    si, sc = kernel_slots(src_indices.to(dev))
+    di, dc = kernel_slots(dst_indices.to(dev))
+    n = int(si.numel())
+    if n == 0:
+        return
+    ws, nbytes = _native.workspace(n, dev)
+    sd, sa = _native.rows_desc([t.data_ptr() for t in srcs], 1, s0.stride(0), 0, int(s0.shape[0]))
+    dd, da = _native.rows_desc([t.data_ptr() for t in dsts], 1, d0.stride(0), 0, int(d0.shape[0]))
+    rc = lib.mak_rows_copy(ctypes.byref(sd), ctypes.byref(dd), None, int(s0.shape[1]), _native.ptr(si), sc,
+                           _native.ptr(di), dc, n, _native.ptr(ws), nbytes, _native.stream_ptr(dev))
+    _native.check(rc, name)
+
+
+def kv_copy_paged_rows(
+    src: torch.Tensor,
+    dst: torch.Tensor,
+    src_indices: torch.Tensor,
+    dst_indices: torch.Tensor,
+    *,
+    layout: InterleavedFp8Layout | None = None,
+) -> None:
+    """``dst[dst_indices[i]] = src[src_indices[i]]`` for uint8 byte rows (DSV4 pages).
+
+    Host index tensors are range-checked (IndexError); device indices are guarded
+    in the kernel and out-of-range rows are skipped, as in the reference
+    (kv_transfer.py:4518-4557).  Source or destination may be pinned host memory.
+    """
+    name = "kv_copy_paged_rows"
+    item = _validate_rows_args(src, dst, src_indices, dst_indices, name=name)
+    if layout is not None and layout.item_bytes != item:
+        raise ValueError(f"{name}: layout.item_bytes={layout.item_bytes} != tensor row width {item}")
+    t0 = _time.perf_counter_ns()
+    _rows_copy_planes([src], [dst], src_indices, dst_indices, name)
+    _record_stats(src, dst, int(src_indices.numel()), item, _time.perf_counter_ns() - t0)
+    emit_native(name, src, "sm100a row engine (DSV4 byte rows)")
+
+
+def _validate_layer_table(src_ptrs, dst_ptrs, src_indices, dst_indices, *, name: str) -> int:
+    if not isinstance(src_ptrs, (list, tuple)) or not isinstance(dst_ptrs, (list, tuple)):
+        raise TypeError(f"{name}: src_ptrs and dst_ptrs must be lists of tensors")
+    if len(src_ptrs) == 0 or len(dst_ptrs) == 0:
+        raise ValueError(f"{name}: ptr-tables must be non-empty")
+    if len(src_ptrs) != len(dst_ptrs):
+        raise ValueError(f"{name}: src/dst layer counts must match, got {len(src_ptrs)} vs {len(dst_ptrs)}")
+    item = int(src_ptrs[0].shape[1])
+    for layer, (s, d) in enumerate(zip(src_ptrs, dst_ptrs)):
+        _validate_rows_args(s, d, src_indices, dst_indices, name=f"{name}[layer{layer}]")
+        if int(d.shape[1]) != item:
+            raise ValueError(f"{name}: layer {layer} item_bytes mismatch, expected {item}, got {int(d.shape[1])}")
+    return item
+
+
+def kv_copy_paged_rows_layer_table(src_ptrs, dst_ptrs, src_indices: torch.Tensor, dst_indices: torch.Tensor) -> None:
+    """All layers' byte-row copies in one launch (plane pointers in the kernel parameters).
+
+    Reference: kv_transfer.py:4588-4616.
+    """
+    name = "kv_copy_paged_rows_layer_table"
+    item = _validate_layer_table(src_ptrs, dst_ptrs, src_indices, dst_indices, name=name)
+    t0 = _time.perf_counter_ns()
+    _rows_copy_planes(list(src_ptrs), list(dst_ptrs), src_indices, dst_indices, name)
+    _record_stats(src_ptrs[0], dst_ptrs[0], int(src_indices.numel()) * len(src_ptrs), item, _time.perf_counter_ns() - t0)
+    emit_native(name, src_ptrs[0], f"sm100a row engine ({len(src_ptrs)} layers, item_bytes={item}, one launch)")
+
+
+def kv_copy_paged_rows_multi_pool(pools: list[PoolSpec], indices: torch.Tensor, *, direction: Literal["H2D", "D2H"]) -> None:
+    """Pools sharing one page-index vector (DSV4 KV/SWA/C4/C128/indexer/state), H2D or D2H.
+
+    Pinned host pools are addressed by the kernel directly; a pageable host
+    pool cannot be addressed by the GPU, so its rows are staged through a
+    pinned bounce buffer (the host-side index copy runs on the CPU there).
+    Reference: kv_transfer.py:4619-4660.
+    """
+    name = "kv_copy_paged_rows_multi_pool"
+    if direction not in ("H2D", "D2H"):
+        raise ValueError(f"{name}: direction must be 'H2D' or 'D2H', got {direction!r}")
+    if not isinstance(pools, (list, tuple)) or len(pools) == 0:
+        raise ValueError(f"{name}: pools must be a non-empty list of PoolSpec")
+    for i, pool in enumerate(pools):
+        if not isinstance(pool, PoolSpec):
+            raise TypeError(f"{name}: pools[{i}] must be PoolSpec")
+        item = _validate_layer_table(pool.src_ptrs, pool.dst_ptrs, indices, indices, name=f"{name}[pool{i}]")
+        if pool.item_bytes != item:
+            raise ValueError(f"{name}: pools[{i}].item_bytes={pool.item_bytes} != tensor row width {item}")
+    for pool in pools:
+        t0 = _time.perf_counter_ns()
+        srcs, dsts = list(pool.src_ptrs), list(pool.dst_ptrs)
+        if all(_addressable(t) for t in srcs + dsts):
+            _rows_copy_planes(srcs, dsts, indices, indices, name)
+        else:
+            for s, d in zip(srcs, dsts):
+                _staged_rows_copy(s, d, indices, name)
+        _record_stats(srcs[0], dsts[0], int(indices.numel()) * len(srcs), pool.item_bytes, _time.perf_counter_ns() - t0)
+    emit_native(name, pools[0].dst_ptrs[0] if direction == "H2D" else pools[0].src_ptrs[0],
+                f"sm100a row engine ({len(pools)} pools, direction={direction})")
+
+
+def _staged_rows_copy(src: torch.Tensor, dst: torch.Tensor, indices: torch.Tensor, name: str) -> None:
+    """Copy rows where one side is pageable host memory, through a pinned bounce buffer."""
+    rows = indices.to(torch.long)
+    n = int(rows.numel())
+    if n == 0:
+        return
+    if src.device.type == "cpu" and not src.is_pinned():
+        bounce = torch.empty((n, src.shape[1]), dtype=torch.uint8, pin_memory=True)
+        torch.index_select(src, 0, rows.cpu(), out=bounce)
+        ident = torch.arange(n, device=dst.device if dst.device.type == "cuda" else "cpu")
+        _rows_copy_planes([bounce], [dst], ident, rows.to(ident.device), name)
+    else:
+        bounce = torch.empty((n, dst.shape[1]), dtype=torch.uint8, pin_memory=True)
+        dev = src.device
+        ident = torch.arange(n, device=dev)
+        _rows_copy_planes([src], [bounce], rows.to(dev), ident, name)
+        torch.cuda.current_stream(dev).synchronize()
+        dst.index_copy_(0, rows.cpu(), bounce)
+
+
+# ---------------------------------------------------------------------------
+# CacheGen-style codec (musa_aiter/ops/kv_transfer.py:1111-1217)
+# ---------------------------------------------------------------------------
+
+
+def kv_cachegen_encode(tensor: torch.Tensor, *, num_bins: int = 256) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Uniform-bin uint8 encode with codebook and empirical CDF; the codes and
+    the histogram/CDF are computed on the device (one min/max read-back for the
+    codebook, as in the reference).  Reference: kv_transfer.py:1111-1172."""
+    name = "kv_cachegen_encode"
+    if num_bins < 2 or num_bins > 256:
+        raise ValueError(f"{name}: num_bins must be in [2, 256]")
+    if not tensor.is_floating_point():
+        raise ValueError(f"{name}: tensor must use a floating dtype")
+    require_cuda(name, tensor)
+    dev = tensor.device
+    if tensor.numel() == 0:
+        return (torch.empty_like(tensor, dtype=torch.uint8), torch.zeros(num_bins, dtype=torch.float32, device=dev),
+                torch.zeros(num_bins + 1, dtype=torch.float32, device=dev))
+    if tensor.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        tensor = tensor.float()
+    x = tensor.contiguous()
+    lib = _native.load()
+    stream = _native.stream_ptr(dev)
+    code = _native.dtype_code(x.dtype)
+    mm = torch.empty(2, dtype=torch.float32, device=dev)
+    _native.check(lib.mak_minmax(_native.ptr(x), code, x.numel(), _native.ptr(mm), stream), name)
+    lo, hi = mm.tolist()
+    if lo == hi:
+        cdf = torch.zeros(num_bins + 1, dtype=torch.float32, device=dev)
+        cdf[1:] = 1.0
+        return (torch.zeros_like(tensor, dtype=torch.uint8), torch.full((num_bins,), lo, dtype=torch.float32, device=dev), cdf)
+    codes = torch.empty(x.shape, dtype=torch.uint8, device=dev)
+    counts = torch.empty(num_bins, dtype=torch.int64, device=dev)
+    cdf = torch.empty(num_bins + 1, dtype=torch.float32, device=dev)
+    _native.check(lib.mak_cachegen_encode(_native.ptr(x), code, x.numel(), _native.ptr(mm), num_bins, _native.ptr(codes),
+                                          _native.ptr(counts), _native.ptr(cdf), stream), name)
+    codebook = torch.linspace(lo, hi, num_bins, dtype=torch.float32, device=dev)
+    emit_native(name, tensor, "sm100a min/max + encode/histogram + CDF kernels")
+    return codes, codebook, cdf
+
+
+def kv_cachegen_decode(encoded: torch.Tensor, codebook: torch.Tensor, *, dtype: torch.dtype | None = None) -> torch.Tensor:
+    """``codebook[encoded]`` (optionally cast to ``dtype``). Reference: kv_transfer.py:1175-1217."""
+    name = "kv_cachegen_decode"
+    if encoded.dtype != torch.uint8:
+        raise ValueError(f"{name}: encoded must be uint8")
+    if codebook.dim() != 1 or codebook.numel() < 2 or codebook.numel() > 256:
+        raise ValueError(f"{name}: codebook must be 1-D with 2..256 bins")
+    if codebook.device != encoded.device:
+        raise ValueError(f"{name}: encoded and codebook must be on same device")
+    if not codebook.is_floating_point():
+        raise ValueError(f"{name}: codebook must use a floating dtype")
+    if encoded.numel() > 0 and int(encoded.max().item()) >= int(codebook.numel()):
+        raise ValueError(f"{name}: encoded bin exceeds codebook size")
+    require_cuda(name, encoded, codebook)
+    out_dtype = codebook.dtype if dtype is None else dtype
+    cb = codebook if codebook.dtype in (torch.float16, torch.bfloat16, torch.float32) else codebook.float()
+    cb = cb.contiguous()
+    enc = encoded.contiguous()
+    work_dtype = out_dtype if out_dtype in (torch.float16, torch.bfloat16, torch.float32) else torch.float32
+    out = torch.empty(enc.shape, dtype=work_dtype, device=enc.device)
+    if enc.numel():
+        rc = _native.load().mak_cachegen_decode(_native.ptr(enc), enc.numel(), _native.ptr(cb), _native.dtype_code(cb.dtype),
+                                                cb.numel(), _native.ptr(out), _native.dtype_code(work_dtype),
+                                                _native.stream_ptr(enc.device))
+        _native.check(rc, name)
+    emit_native(name, encoded, "sm100a codebook decode")
+    return out if work_dtype == out_dtype else out.to(out_dtype)

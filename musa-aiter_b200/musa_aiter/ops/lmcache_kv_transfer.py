@@ -531,3 +531,60 @@ def lmcache_mla_paged_to_buffer(
     _gather("lmcache_mla_paged_to_buffer", list(kvcaches), [memory_tensor[0, i] for i in range(len(kvcaches))], slot_mapping)
     emit_native("lmcache_mla_paged_to_buffer", memory_tensor, "sm100a row gather (MLA list, one launch)")
     return True
+
+
+def lmcache_kv_strided_block_transfer(
+    staging: "torch.Tensor | int",
+    paged_ptrs: list[int],
+    block_ids: torch.Tensor,
+    direction: int,
+    num_layers: int,
+    idx_start: int,
+    n_valid: int,
+    offset_in_object: int,
+    staging_tokens: int,
+    block_size: int,
+    row_bytes: int,
+    paged_block_stride: int,
+    mode: int,
+    value_bytes: int = 0,
+    scale_bytes: int = 0,
+) -> bool:
+    """Staging ``[NL, staging_tokens, row_bytes]`` <-> padded paged pages, all layers in one launch.
+
+    Reference contract (lmcache_kv_transfer.py:1294-1403): mode 0 plain rows,
+    mode 1 per-block values-then-scales; direction 0 staging -> paged, 1 back.
+    Invalid arguments return False (the caller picks another path) instead of
+    raising; ``block_ids`` must be a contiguous CUDA int64 tensor and
+    ``paged_ptrs`` a host list of per-layer page base addresses.  In mode 1
+    ``value_bytes + scale_bytes`` must equal ``row_bytes``.
+    """
+    if num_layers <= 0 or n_valid <= 0 or block_size <= 0 or staging_tokens <= 0:
+        return False
+    if row_bytes <= 0 or row_bytes % 4 != 0 or mode not in (0, 1) or int(direction) not in (0, 1):
+        return False
+    if mode == 1 and (value_bytes <= 0 or scale_bytes <= 0 or value_bytes % 4 or scale_bytes % 4
+                      or value_bytes + scale_bytes != row_bytes):
+        return False
+    if not isinstance(paged_ptrs, (list, tuple)) or len(paged_ptrs) != num_layers:
+        return False
+    if not isinstance(block_ids, torch.Tensor) or block_ids.dtype is not torch.int64 or block_ids.device.type != "cuda" \
+            or not block_ids.is_contiguous():
+        return False
+    if idx_start < 0 or idx_start + n_valid > int(block_ids.numel()):
+        return False
+    staging_ptr = int(staging.data_ptr()) if isinstance(staging, torch.Tensor) else int(staging)
+    if staging_ptr <= 0:
+        return False
+    lib = _native.load()
+    arr = (ctypes.c_uint64 * num_layers)(*map(int, paged_ptrs))
+    with torch.cuda.device(block_ids.device):
+        rc = lib.mak_lmcache_strided_block_transfer(
+            ctypes.c_void_p(staging_ptr), arr, _native.ptr(block_ids), int(direction), int(num_layers), int(idx_start),
+            int(n_valid), int(offset_in_object), int(staging_tokens), int(block_size), int(row_bytes),
+            int(paged_block_stride), int(mode), int(value_bytes), int(scale_bytes), _native.stream_ptr(block_ids.device),
+        )
+    if rc != 0:
+        return False
+    emit_native("lmcache_kv_strided_block_transfer", block_ids, f"sm100a strided block transfer mode={mode} dir={direction}")
+    return True

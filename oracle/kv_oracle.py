@@ -451,3 +451,194 @@ def kv_mla_linear_to_paged(kv_lin, pe_lin, kv_cache, pe_cache, slots) -> None:
     nb, bs, _ = kv_cache.shape
     rows_scatter(kv_lin, kv_cache.reshape(nb * bs, -1), slots)
     rows_scatter(pe_lin, pe_cache.reshape(nb * bs, -1), slots)
+
+
+# ---------------------------------------------------------------------------
+# Flash dense layouts (musa_aiter/ops/kv_transfer.py:1527-1795)
+# ---------------------------------------------------------------------------
+
+
+def flash_slots(block_tables: np.ndarray, seq_lens: np.ndarray, block_size: int, dense_len: int) -> np.ndarray:
+    """Per-sequence slot building of kv_transfer.py:1779-1791: [B * dense_len], -1 past seq_len."""
+    bt = np.asarray(block_tables, dtype=np.int64)
+    lens = np.asarray(seq_lens, dtype=np.int64)
+    b = bt.shape[0]
+    out = np.full((b, dense_len), -1, dtype=np.int64)
+    pos = np.arange(dense_len)
+    for i in range(b):
+        n = int(lens[i])
+        blk = bt[i, pos[:n] // block_size]
+        out[i, :n] = blk * block_size + pos[:n] % block_size
+    return out.reshape(-1)
+
+
+def kv_load_and_reshape_flash(k_cache, v_cache, block_tables, seq_lens, max_seq_len=None):
+    """kv_transfer.py:1527-1622: dense [B, S, NH, HD] with zero padding."""
+    nb, nh, hd, bs = k_cache.shape
+    lens = np.asarray(seq_lens, dtype=np.int64)
+    dense = int(lens.max()) if max_seq_len is None and lens.size else int(max_seq_len or 0)
+    slots = flash_slots(block_tables, lens, bs, dense)
+    ok, ov = kv_paged_to_linear(k_cache, v_cache, slots)
+    b = lens.shape[0]
+    return ok.reshape(b, dense, nh, hd), ov.reshape(b, dense, nh, hd)
+
+
+def kv_reshape_and_cache_back_flash(dense_k, dense_v, k_cache, v_cache, block_tables, seq_lens) -> None:
+    """kv_transfer.py:1625-1726: scatter the first seq_len rows of every sequence (last writer wins)."""
+    b, dense, nh, hd = dense_k.shape
+    bs = k_cache.shape[3]
+    slots = flash_slots(block_tables, seq_lens, bs, dense)
+    kv_linear_to_paged(dense_k.reshape(b * dense, nh, hd), dense_v.reshape(b * dense, nh, hd), k_cache, v_cache, slots)
+
+
+def kv_load_and_dequantize_fp8_flash(k8, v8, block_tables, seq_lens, k_scale, v_scale, *, max_seq_len=None,
+                                     out_dtype="bfloat16", fp8_format="e4m3"):
+    """kv_transfer.py:1729-1795."""
+    nb, nh, hd, bs = k8.shape
+    lens = np.asarray(seq_lens, dtype=np.int64)
+    dense = int(lens.max()) if max_seq_len is None and lens.size else int(max_seq_len or 0)
+    slots = flash_slots(block_tables, lens, bs, dense)
+    ok, ov = kv_paged_fp8_to_linear(k8, v8, slots, k_scale, v_scale, out_dtype=out_dtype, fp8_format=fp8_format)
+    b = lens.shape[0]
+    return ok.reshape(b, dense, nh, hd), ov.reshape(b, dense, nh, hd)
+
+
+def kv_triton_indexed_to_dense(k_cache, v_cache, indptr, indices, max_seq_len):
+    """kv_transfer.py:1291-1366: rows indices[indptr[b] + s] for s < min(len_b, S), zeros elsewhere."""
+    indptr = np.asarray(indptr, dtype=np.int64)
+    indices = np.asarray(indices, dtype=np.int64)
+    b = indptr.shape[0] - 1
+    ntok, nh, hd = k_cache.shape
+    ok = np.zeros((b, max_seq_len, nh, hd), dtype=k_cache.dtype)
+    ov = np.zeros_like(ok)
+    for i in range(b):
+        n = min(max(int(indptr[i + 1] - indptr[i]), 0), max_seq_len)
+        if n <= 0:
+            continue
+        rows = indices[indptr[i]: indptr[i] + n]
+        ok[i, :n] = k_cache[rows]
+        ov[i, :n] = v_cache[rows]
+    return ok, ov
+
+
+# ---------------------------------------------------------------------------
+# block copies and DSV4 byte rows (kv_transfer.py:1871-2091, 4518-4736)
+# ---------------------------------------------------------------------------
+
+
+def kv_copy_paged_blocks(src_k, src_v, dst_k, dst_v, pairs) -> int:
+    """Copy whole blocks pair by pair in order (later pairs overwrite earlier ones); returns the count."""
+    pairs = np.asarray(pairs, dtype=np.int64).reshape(-1, 2)
+    multi = src_k.ndim == 5
+    copied = 0
+    for s, d in pairs:
+        if s < 0 or d < 0:
+            continue
+        if multi:
+            dst_k[:, d] = src_k[:, s]
+            dst_v[:, d] = src_v[:, s]
+        else:
+            dst_k[d] = src_k[s]
+            dst_v[d] = src_v[s]
+        copied += 1
+    return copied
+
+
+def kv_copy_paged_rows(src: np.ndarray, dst: np.ndarray, src_idx, dst_idx) -> None:
+    """dst.index_copy_(0, dst_idx, src.index_select(0, src_idx)) with in-order overwrite."""
+    si = np.asarray(src_idx, dtype=np.int64)
+    di = np.asarray(dst_idx, dtype=np.int64)
+    keep = last_writer_mask(di)
+    dst[di[keep]] = src[si[keep]]
+
+
+def hicache_transfer(src_k, dst_k, src_v, dst_v, src_idx, dst_idx, src_layout, dst_layout, start_layer, num_layers):
+    """musa_aiter/ops/hicache_transfer.py:254-340: per (page pair, layer) row copies, -1 skips."""
+    si = np.asarray(src_idx, dtype=np.int64)
+    di = np.asarray(dst_idx, dtype=np.int64)
+
+    def row(t, layout, layer, page):
+        return (layer, page) if layout == "layer_first" else (page, layer)
+
+    for s, d in zip(si, di):
+        if s < 0 or d < 0:
+            continue
+        for layer in range(start_layer, start_layer + num_layers):
+            dst_k[row(dst_k, dst_layout, layer, d)] = src_k[row(src_k, src_layout, layer, s)]
+            if src_v is not None:
+                dst_v[row(dst_v, dst_layout, layer, d)] = src_v[row(src_v, src_layout, layer, s)]
+
+
+def hicache_direct(src_layers, dst_layers, src_idx, dst_idx, page_size: int) -> None:
+    """hicache_transfer.py:531-580: per page, ``page_size`` rows from the page's first index."""
+    si = np.asarray(src_idx, dtype=np.int64).reshape(-1, page_size)[:, 0]
+    di = np.asarray(dst_idx, dtype=np.int64).reshape(-1, page_size)[:, 0]
+    for s, d in zip(si, di):
+        for src, dst in zip(src_layers, dst_layers):
+            dst[d: d + page_size] = src[s: s + page_size]
+
+
+# ---------------------------------------------------------------------------
+# CacheGen codec (kv_transfer.py:1111-1217)
+# ---------------------------------------------------------------------------
+
+
+def kv_cachegen_encode(x_f32: np.ndarray, num_bins: int = 256):
+    """Codes, codebook and CDF.  scale = reciprocal(max - min) * (bins - 1) in fp32 (PyTorch's
+    ``int / tensor``); codes = clamp(round_half_even((x - min) * scale)); CDF = [0, cumsum(counts) / n]
+    accumulated in fp32.  The codebook is torch.linspace on the host (the reference's call)."""
+    import torch
+
+    x = np.asarray(x_f32, dtype=np.float32)
+    n = x.size
+    if n == 0:
+        return np.zeros(x.shape, np.uint8), np.zeros(num_bins, np.float32), np.zeros(num_bins + 1, np.float32)
+    lo, hi = np.float32(x.min()), np.float32(x.max())
+    if lo == hi:
+        cdf = np.zeros(num_bins + 1, np.float32)
+        cdf[1:] = 1.0
+        return np.zeros(x.shape, np.uint8), np.full(num_bins, lo, np.float32), cdf
+    with np.errstate(divide="ignore"):
+        scale = np.float32(np.float32(1.0) / np.float32(hi - lo)) * np.float32(num_bins - 1)
+    q = np.rint(((x - lo).astype(np.float32) * np.float32(scale)).astype(np.float32))
+    codes = np.clip(q, 0, num_bins - 1).astype(np.uint8)
+    counts = np.bincount(codes.reshape(-1), minlength=num_bins).astype(np.float32)
+    cdf = np.zeros(num_bins + 1, np.float32)
+    cdf[1:] = np.cumsum(counts, dtype=np.float32) / np.float32(n)
+    codebook = torch.linspace(float(lo), float(hi), num_bins, dtype=torch.float32).numpy()
+    return codes, codebook, cdf
+
+
+def kv_cachegen_decode(codes: np.ndarray, codebook: np.ndarray) -> np.ndarray:
+    return np.asarray(codebook)[np.asarray(codes).astype(np.int64)]
+
+
+# ---------------------------------------------------------------------------
+# DSV4 strided block transfer (restated from csrc/kvcache/kv_transfer_float.mu:3281-3405;
+# the reference has no PyTorch path for it, so this restatement is pinned by reading only)
+# ---------------------------------------------------------------------------
+
+
+def strided_block_transfer(staging: np.ndarray, pages: list[np.ndarray], block_ids, direction: int, idx_start: int,
+                           n_valid: int, offset_in_object: int, block_size: int, row_bytes: int, block_stride: int,
+                           mode: int, value_bytes: int = 0, scale_bytes: int = 0) -> None:
+    """staging: uint8 [NL, staging_tokens, row_bytes]; pages: per-layer uint8 flat page arrays."""
+    ids = np.asarray(block_ids, dtype=np.int64)
+    for layer, page in enumerate(pages):
+        for p in range(n_valid):
+            blk = int(ids[idx_start + p])
+            if blk < 0:
+                continue
+            for t in range(block_size):
+                st = staging[layer, offset_in_object + p * block_size + t]
+                base = blk * block_stride
+                if mode == 0:
+                    spans = [(base + t * row_bytes, 0, row_bytes)]
+                else:
+                    spans = [(base + t * value_bytes, 0, value_bytes),
+                             (base + block_size * value_bytes + t * scale_bytes, value_bytes, scale_bytes)]
+                for poff, soff, nbytes in spans:
+                    if direction == 0:
+                        page[poff: poff + nbytes] = st[soff: soff + nbytes]
+                    else:
+                        st[soff: soff + nbytes] = page[poff: poff + nbytes]

@@ -15,6 +15,8 @@ Families:
 - fp8.npz     exhaustive FP8 encode (all 65536 bf16 and fp16 inputs), edge fp32
               inputs, all 256 codes decoded, multi-layer scale forms
 - rows.npz    LMCache 6-D / list / SGLang MP two_x_nl / MLA buffers, MLA flat caches
+- misc.npz    Flash dense load / cache-back / FP8 dequant, Triton-indexed dense gather,
+              block copies, DSV4 byte rows, HiCache transfers, CacheGen codec
 """
 
 from __future__ import annotations
@@ -330,8 +332,171 @@ def make_rows() -> None:
     st.save("rows.npz")
 
 
+def make_misc() -> None:
+    st = Store()
+    nb, nh, hd, bs = 12, 2, 8, 4
+    for dname, dt in DTYPES.items():
+        g = gen(50)
+        kc = randn((nb, nh, hd, bs), dt, g)
+        vc = randn((nb, nh, hd, bs), dt, g)
+        bt = torch.tensor([[3, 7, 1, 0], [5, 2, 11, 9], [8, 4, 0, 0]], dtype=torch.int32)
+        lens = torch.tensor([10, 13, 4], dtype=torch.int64)
+        ok, ov = ref.kv_load_and_reshape_flash(kc, vc, bt, lens, max_seq_len=15)
+        p = f"flash/{dname}"
+        st.put(f"{p}/k_cache", kc)
+        st.put(f"{p}/v_cache", vc)
+        st.put(f"{p}/out_k", ok)
+        st.put(f"{p}/out_v", ov)
+        dk = randn((3, 15, nh, hd), dt, g)
+        dv = randn((3, 15, nh, hd), dt, g)
+        kd, vd = kc.clone(), vc.clone()
+        ref.kv_reshape_and_cache_back_flash(dk, dv, kd, vd, bt, lens)
+        st.put(f"{p}/dense_k", dk)
+        st.put(f"{p}/dense_v", dv)
+        st.put(f"{p}/back_k", kd)
+        st.put(f"{p}/back_v", vd)
+        # triton-indexed dense gather from a token pool
+        pool_k = randn((40, nh, hd), dt, g)
+        pool_v = randn((40, nh, hd), dt, g)
+        indptr = torch.tensor([0, 5, 5, 17, 20], dtype=torch.int64)
+        indices = torch.randperm(40, generator=g)[:20].to(torch.int32)
+        tk, tv = ref.ops.kv_transfer.kv_triton_indexed_to_dense(pool_k, pool_v, indptr, indices, max_seq_len=9)
+        q = f"triton/{dname}"
+        st.put(f"{q}/pool_k", pool_k)
+        st.put(f"{q}/pool_v", pool_v)
+        st.put(f"{q}/indices", indices)
+        st.put(f"{q}/out_k", tk)
+        st.put(f"{q}/out_v", tv)
+        # block copies, single and multi layer, with a duplicate destination and skipped pairs
+        pairs = torch.tensor([[1, 4], [6, 0], [-1, 3], [2, 4], [9, -1], [11, 7]], dtype=torch.int64)
+        src3 = randn((3, nb, nh, hd, bs), dt, g)
+        srcv3 = randn((3, nb, nh, hd, bs), dt, g)
+        dst3 = torch.zeros((3, 8, nh, hd, bs), dtype=dt)
+        dstv3 = torch.zeros((3, 8, nh, hd, bs), dtype=dt)
+        n3 = ref.kv_copy_paged_blocks(src3, srcv3, dst3, dstv3, pairs)
+        r = f"blocks/{dname}"
+        st.put(f"{r}/src_k", src3)
+        st.put(f"{r}/src_v", srcv3)
+        st.put(f"{r}/dst_k", dst3)
+        st.put(f"{r}/dst_v", dstv3)
+        st.put(f"{r}/count", torch.tensor(n3))
+        d1k = torch.zeros((8, nh, hd, bs), dtype=dt)
+        d1v = torch.zeros((8, nh, hd, bs), dtype=dt)
+        n1 = ref.kv_copy_paged_blocks(src3[0], srcv3[0], d1k, d1v, pairs)
+        st.put(f"{r}/dst1_k", d1k)
+        st.put(f"{r}/dst1_v", d1v)
+        st.put(f"{r}/count1", torch.tensor(n1))
+    st.put("flash/block_tables", torch.tensor([[3, 7, 1, 0], [5, 2, 11, 9], [8, 4, 0, 0]], dtype=torch.int32))
+    st.put("flash/seq_lens", torch.tensor([10, 13, 4], dtype=torch.int64))
+    st.put("triton/indptr", torch.tensor([0, 5, 5, 17, 20], dtype=torch.int64))
+    st.put("blocks/pairs", torch.tensor([[1, 4], [6, 0], [-1, 3], [2, 4], [9, -1], [11, 7]], dtype=torch.int64))
+    # FP8 flash dequant
+    g = gen(51)
+    k8 = torch.randint(0, 256, (nb, nh, hd, 16), generator=g, dtype=torch.int32).to(torch.uint8)
+    v8 = torch.randint(0, 256, (nb, nh, hd, 16), generator=g, dtype=torch.int32).to(torch.uint8)
+    bt8 = torch.tensor([[3, 7], [5, 2], [8, 0]], dtype=torch.int64)
+    lens8 = torch.tensor([20, 32, 5], dtype=torch.int64)
+    for fmt in ("e4m3", "e5m2"):
+        ok, ov = ref.kv_load_and_dequantize_fp8_flash(k8, v8, bt8, lens8, 0.03, [0.5, 0.25], out_dtype=torch.bfloat16, fp8_format=fmt)
+        st.put(f"fp8flash/{fmt}/out_k", ok)
+        st.put(f"fp8flash/{fmt}/out_v", ov)
+    st.put("fp8flash/k8", k8)
+    st.put("fp8flash/v8", v8)
+    st.put("fp8flash/bt", bt8)
+    st.put("fp8flash/lens", lens8)
+    # DSV4 byte rows with odd widths and a duplicate destination
+    for width in (1, 24, 1729):
+        src = torch.randint(0, 256, (30, width), generator=g, dtype=torch.int32).to(torch.uint8)
+        dst = torch.randint(0, 256, (25, width), generator=g, dtype=torch.int32).to(torch.uint8)
+        si = torch.tensor([0, 5, 29, 7, 7, 13, 2], dtype=torch.int64)
+        di = torch.tensor([3, 24, 0, 3, 11, 17, 8], dtype=torch.int32)
+        d2 = dst.clone()
+        ref.kv_copy_paged_rows(src, d2, si, di)
+        st.put(f"rows/{width}/src", src)
+        st.put(f"rows/{width}/dst", dst)
+        st.put(f"rows/{width}/out", d2)
+    st.put("rows/si", torch.tensor([0, 5, 29, 7, 7, 13, 2], dtype=torch.int64))
+    st.put("rows/di", torch.tensor([3, 24, 0, 3, 11, 17, 8], dtype=torch.int32))
+    # HiCache: layer-first / page-first, K+V and MLA, per-layer and all-layer
+    L, P, item = 3, 10, 16
+    hsrc_k = randn((L, P, item), torch.float16, g)
+    hsrc_v = randn((L, P, item), torch.float16, g)
+    hpf_k = randn((P, L, item), torch.float16, g)
+    hpf_v = randn((P, L, item), torch.float16, g)
+    si = torch.tensor([4, -1, 9, 0, 4], dtype=torch.int64)
+    di = torch.tensor([1, 2, 7, 5, 3], dtype=torch.int64)
+    st.put("hicache/lf_k", hsrc_k)
+    st.put("hicache/lf_v", hsrc_v)
+    st.put("hicache/pf_k", hpf_k)
+    st.put("hicache/pf_v", hpf_v)
+    st.put("hicache/si", si)
+    st.put("hicache/di", di)
+    outs = {}
+    dk, dv = torch.zeros_like(hsrc_k), torch.zeros_like(hsrc_v)
+    ref.hicache_transfer_kv_per_layer(hsrc_k, dk, hsrc_v, dv, si, di, layer_id=1)
+    outs["per_layer"] = (dk, dv)
+    dk, dv = torch.zeros_like(hsrc_k), torch.zeros_like(hsrc_v)
+    ref.hicache_transfer_kv_per_layer_pf_lf(hpf_k, dk, hpf_v, dv, si, di, layer_id=2)
+    outs["per_layer_pf_lf"] = (dk, dv)
+    dk, dv = torch.zeros_like(hsrc_k), torch.zeros_like(hsrc_v)
+    ref.hicache_transfer_kv_all_layer(hsrc_k, dk, hsrc_v, dv, si, di)
+    outs["all_layer"] = (dk, dv)
+    dk, dv = torch.zeros_like(hpf_k), torch.zeros_like(hpf_v)
+    ref.hicache_transfer_kv_all_layer_lf_pf(hsrc_k, dk, hsrc_v, dv, si, di)
+    outs["all_layer_lf_pf"] = (dk, dv)
+    dm = torch.zeros_like(hsrc_k)
+    ref.hicache_transfer_kv_per_layer_mla(hsrc_k, dm, si, di, layer_id=0)
+    outs["mla_per_layer"] = (dm,)
+    dm = torch.zeros_like(hsrc_k)
+    ref.hicache_transfer_kv_per_layer_mla_pf_lf(hpf_k, dm, si, di, layer_id=1)
+    outs["mla_pf_lf"] = (dm,)
+    dm = torch.zeros_like(hsrc_k)
+    ref.hicache_transfer_kv_all_layer_mla(hsrc_k, dm, si, di)
+    outs["mla_all"] = (dm,)
+    dm = torch.zeros_like(hpf_k)
+    ref.hicache_transfer_kv_all_layer_mla_lf_pf(hsrc_k, dm, si, di)
+    outs["mla_all_lf_pf"] = (dm,)
+    for key, ts in outs.items():
+        for j, t in enumerate(ts):
+            st.put(f"hicache/out/{key}/{j}", t)
+    # direct page ranges (page 4): note only each page's first index is used
+    tok_src = [randn((24, 2, 8), torch.bfloat16, g) for _ in range(2)]
+    tok_dst = [torch.zeros((20, 2, 8), dtype=torch.bfloat16) for _ in range(2)]
+    dsi = torch.tensor([8, 9, 10, 11, 0, 1, 2, 3, 16, 99, 5, 5], dtype=torch.int64)
+    ddi = torch.tensor([4, 5, 6, 7, 12, 13, 14, 15, 0, 0, 0, 0], dtype=torch.int64)
+    ref.hicache_transfer_kv_direct(tok_src, tok_dst, dsi, ddi, 4)
+    st.put("hicache/direct/src", torch.stack(tok_src))
+    st.put("hicache/direct/out", torch.stack(tok_dst))
+    st.put("hicache/direct/si", dsi)
+    st.put("hicache/direct/di", ddi)
+    # CacheGen codec
+    for cname, (shape, cdt, bins) in {
+        "f32_256": ((33, 7), torch.float32, 256),
+        "bf16_256": ((5, 16, 9), torch.bfloat16, 256),
+        "f16_16": ((64, 3), torch.float16, 16),
+        "f32_2": ((17,), torch.float32, 2),
+    }.items():
+        x = (torch.randn(shape, generator=g) * 3.0 + 0.5).to(cdt)
+        enc, cb, cdf = ref.kv_cachegen_encode(x, num_bins=bins)
+        dec = ref.kv_cachegen_decode(enc, cb, dtype=cdt)
+        p = f"cachegen/{cname}"
+        st.put(f"{p}/x", x)
+        st.put(f"{p}/enc", enc)
+        st.put(f"{p}/codebook", cb)
+        st.put(f"{p}/cdf", cdf)
+        st.put(f"{p}/dec", dec)
+    const = torch.full((4, 4), 2.5, dtype=torch.float32)
+    enc, cb, cdf = ref.kv_cachegen_encode(const, num_bins=8)
+    st.put("cachegen/const/x", const)
+    st.put("cachegen/const/enc", enc)
+    st.put("cachegen/const/codebook", cb)
+    st.put("cachegen/const/cdf", cdf)
+    st.save("misc.npz")
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     make_tile()
     make_fp8()
     make_rows()
+    make_misc()

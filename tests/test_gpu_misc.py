@@ -1,0 +1,222 @@
+"""GPU parity for the rest of the kvcache family: Flash dense layouts, the
+Triton-indexed dense gather, block copies, DSV4 byte rows, HiCache transfers,
+the CacheGen codec and the DSV4 strided block transfer — against the
+reference's golden vectors and the CPU oracle, bit for bit."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import musa_aiter as ma
+from oracle import kv_oracle as O
+
+from ._util import TORCH_OF, first_diff, same_bits, to_np, to_torch
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+DTYPES = ("float32", "float16", "bfloat16")
+
+
+@pytest.fixture(scope="module")
+def misc():
+    return np.load(GOLDEN / "misc.npz")
+
+
+def T(a, dt=None):
+    return to_torch(a, dt)
+
+
+def eq(a, b, what=""):
+    assert same_bits(a, b), f"{what}: {first_diff(a, b)}"
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_golden_flash_triton_blocks(cuda_device, misc, dt):
+    p = f"flash/{dt}"
+    kc, vc = T(misc[f"{p}/k_cache"], dt), T(misc[f"{p}/v_cache"], dt)
+    bt, lens = T(misc["flash/block_tables"]), T(misc["flash/seq_lens"])
+    ok, ov = ma.kv_load_and_reshape_flash(kc, vc, bt, lens, max_seq_len=15)
+    eq(ok, misc[f"{p}/out_k"], "flash load k")
+    eq(ov, misc[f"{p}/out_v"], "flash load v")
+    kd, vd = kc.clone(), vc.clone()
+    assert ma.kv_reshape_and_cache_back_flash(T(misc[f"{p}/dense_k"], dt), T(misc[f"{p}/dense_v"], dt), kd, vd, bt, lens) is True
+    eq(kd, misc[f"{p}/back_k"], "flash back k")
+    eq(vd, misc[f"{p}/back_v"], "flash back v")
+
+    q = f"triton/{dt}"
+    tk, tv = ma.kv_triton_indexed_to_dense(T(misc[f"{q}/pool_k"], dt), T(misc[f"{q}/pool_v"], dt), T(misc["triton/indptr"]),
+                                           T(misc[f"{q}/indices"]), max_seq_len=9)
+    eq(tk, misc[f"{q}/out_k"], "triton k")
+    eq(tv, misc[f"{q}/out_v"], "triton v")
+
+    r = f"blocks/{dt}"
+    sk, sv = T(misc[f"{r}/src_k"], dt), T(misc[f"{r}/src_v"], dt)
+    dk = torch.zeros(misc[f"{r}/dst_k"].shape, dtype=TORCH_OF[dt], device="cuda")
+    dv = torch.zeros_like(dk)
+    n = ma.kv_copy_paged_blocks(sk, sv, dk, dv, T(misc["blocks/pairs"]))
+    assert n == int(misc[f"{r}/count"])
+    eq(dk, misc[f"{r}/dst_k"], "blocks ml k")
+    eq(dv, misc[f"{r}/dst_v"], "blocks ml v")
+    dk1 = torch.zeros(misc[f"{r}/dst1_k"].shape, dtype=TORCH_OF[dt], device="cuda")
+    dv1 = torch.zeros_like(dk1)
+    n1 = ma.kv_copy_paged_blocks(sk[0], sv[0], dk1, dv1, torch.from_numpy(misc["blocks/pairs"]))  # host mapping
+    assert n1 == int(misc[f"{r}/count1"])
+    eq(dk1, misc[f"{r}/dst1_k"], "blocks k")
+    eq(dv1, misc[f"{r}/dst1_v"], "blocks v")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+def test_golden_fp8_flash(cuda_device, misc, fmt):
+    ok, ov = ma.kv_load_and_dequantize_fp8_flash(T(misc["fp8flash/k8"]), T(misc["fp8flash/v8"]), T(misc["fp8flash/bt"]),
+                                                 T(misc["fp8flash/lens"]), 0.03, [0.5, 0.25], out_dtype=torch.bfloat16,
+                                                 fp8_format=fmt)
+    eq(ok, misc[f"fp8flash/{fmt}/out_k"], "fp8 flash k")
+    eq(ov, misc[f"fp8flash/{fmt}/out_v"], "fp8 flash v")
+
+
+def test_golden_rows_and_hicache(cuda_device, misc):
+    for width in (1, 24, 1729):
+        d = T(misc[f"rows/{width}/dst"])
+        ma.kv_copy_paged_rows(T(misc[f"rows/{width}/src"]), d, T(misc["rows/si"]), T(misc["rows/di"]))
+        eq(d, misc[f"rows/{width}/out"], f"rows {width}")
+    lf_k, lf_v = T(misc["hicache/lf_k"]), T(misc["hicache/lf_v"])
+    pf_k, pf_v = T(misc["hicache/pf_k"]), T(misc["hicache/pf_v"])
+    si, di = T(misc["hicache/si"]), T(misc["hicache/di"])
+    z = torch.zeros_like
+    dk, dv = z(lf_k), z(lf_v)
+    ma.hicache_transfer_kv_per_layer(lf_k, dk, lf_v, dv, si, di, layer_id=1)
+    eq(dk, misc["hicache/out/per_layer/0"], "per_layer k")
+    eq(dv, misc["hicache/out/per_layer/1"], "per_layer v")
+    dk, dv = z(lf_k), z(lf_v)
+    ma.hicache_transfer_kv_per_layer_pf_lf(pf_k, dk, pf_v, dv, si, di, layer_id=2)
+    eq(dk, misc["hicache/out/per_layer_pf_lf/0"], "pf_lf k")
+    eq(dv, misc["hicache/out/per_layer_pf_lf/1"], "pf_lf v")
+    dk, dv = z(lf_k), z(lf_v)
+    ma.hicache_transfer_kv_all_layer(lf_k, dk, lf_v, dv, si, di)
+    eq(dk, misc["hicache/out/all_layer/0"], "all k")
+    dk, dv = z(pf_k), z(pf_v)
+    ma.hicache_transfer_kv_all_layer_lf_pf(lf_k, dk, lf_v, dv, si, di)
+    eq(dk, misc["hicache/out/all_layer_lf_pf/0"], "lf_pf k")
+    eq(dv, misc["hicache/out/all_layer_lf_pf/1"], "lf_pf v")
+    dm = z(lf_k)
+    ma.hicache_transfer_kv_per_layer_mla(lf_k, dm, si, di, layer_id=0)
+    eq(dm, misc["hicache/out/mla_per_layer/0"], "mla per layer")
+    dm = z(lf_k)
+    ma.hicache_transfer_kv_per_layer_mla_pf_lf(pf_k, dm, si, di, layer_id=1)
+    eq(dm, misc["hicache/out/mla_pf_lf/0"], "mla pf_lf")
+    dm = z(lf_k)
+    ma.hicache_transfer_kv_all_layer_mla(lf_k, dm, si, di)
+    eq(dm, misc["hicache/out/mla_all/0"], "mla all")
+    dm = z(pf_k)
+    ma.hicache_transfer_kv_all_layer_mla_lf_pf(lf_k, dm, si, di)
+    eq(dm, misc["hicache/out/mla_all_lf_pf/0"], "mla lf_pf")
+    src = [t.contiguous() for t in T(misc["hicache/direct/src"], "bfloat16").unbind(0)]
+    dst = [torch.zeros((20, 2, 8), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    ma.hicache_transfer_kv_direct(src, dst, T(misc["hicache/direct/si"]), T(misc["hicache/direct/di"]), 4)
+    eq(torch.stack(dst), misc["hicache/direct/out"], "direct")
+
+
+def test_hicache_pinned_host_pool(cuda_device):
+    """Device pages -> pinned host pool and back (the HiCache offload direction), one launch each."""
+    g = torch.Generator(device="cuda").manual_seed(4)
+    dev_k = torch.randn((4, 64, 128), device="cuda", generator=g).to(torch.bfloat16)
+    dev_v = torch.randn((4, 64, 128), device="cuda", generator=g).to(torch.bfloat16)
+    host_k = torch.zeros((4, 80, 128), dtype=torch.bfloat16, pin_memory=True)
+    host_v = torch.zeros((4, 80, 128), dtype=torch.bfloat16, pin_memory=True)
+    si = torch.randperm(64, device="cuda")[:40]
+    di = torch.randperm(80, device="cuda")[:40]
+    ma.hicache_transfer_kv_all_layer(dev_k, host_k, dev_v, host_v, si, di)
+    torch.cuda.synchronize()
+    assert torch.equal(host_k[:, di.cpu()].view(torch.int16), dev_k[:, si].cpu().view(torch.int16))
+    back_k, back_v = torch.zeros_like(dev_k), torch.zeros_like(dev_v)
+    ma.hicache_transfer_kv_all_layer(host_k, back_k, host_v, back_v, di, si)
+    torch.cuda.synchronize()
+    assert torch.equal(back_v[:, si].view(torch.int16), dev_v[:, si].view(torch.int16))
+
+
+def test_golden_cachegen(cuda_device, misc):
+    for name, dt in (("f32_256", "float32"), ("bf16_256", "bfloat16"), ("f16_16", "float16"), ("f32_2", "float32"), ("const", "float32")):
+        p = f"cachegen/{name}"
+        x = T(misc[f"{p}/x"], dt)
+        bins = misc[f"{p}/codebook"].shape[0]
+        enc, cb, cdf = ma.kv_cachegen_encode(x, num_bins=bins)
+        eq(enc, misc[f"{p}/enc"], name + " codes")
+        eq(cb, misc[f"{p}/codebook"], name + " codebook")
+        eq(cdf, misc[f"{p}/cdf"], name + " cdf")
+        if f"{p}/dec" in misc:
+            eq(ma.kv_cachegen_decode(enc, cb, dtype=TORCH_OF[dt]), misc[f"{p}/dec"], name + " decode")
+
+
+def test_cachegen_large_vs_oracle(cuda_device):
+    g = torch.Generator().manual_seed(9)
+    x = (torch.randn((3, 1000, 257), generator=g) * 5.0).to(torch.bfloat16)
+    enc, cb, cdf = ma.kv_cachegen_encode(x.cuda(), num_bins=256)
+    renc, rcb, rcdf = O.kv_cachegen_encode(O.to_f32(to_np(x), "bfloat16"), 256)
+    eq(enc, renc, "codes")
+    eq(cdf, rcdf, "cdf")
+    eq(cb, rcb, "codebook")
+
+
+@pytest.mark.parametrize("mode", (0, 1))
+def test_strided_block_transfer_vs_oracle(cuda_device, mode):
+    """DSV4 staging <-> padded pages, both directions, vs the restated kernel semantics."""
+    g = torch.Generator().manual_seed(12 + mode)
+    nl, nb, bs = 3, 20, 8
+    value_bytes, scale_bytes = (0, 0) if mode == 0 else (576, 16)
+    row = 592 if mode == 0 else value_bytes + scale_bytes
+    stride = bs * row + 64  # padded pages
+    pages = [torch.randint(0, 256, (nb * stride,), generator=g, dtype=torch.int32).to(torch.uint8) for _ in range(nl)]
+    staging = torch.randint(0, 256, (nl, 50, row), generator=g, dtype=torch.int32).to(torch.uint8)
+    block_ids = torch.tensor([7, 3, -1, 12, 0, 19], dtype=torch.int64)
+    idx_start, n_valid, offset = 1, 4, 9
+    dpages = [p.cuda() for p in pages]
+    dstaging = staging.cuda()
+    ok = ma.lmcache_kv_strided_block_transfer(dstaging, [p.data_ptr() for p in dpages], block_ids.cuda(), 0, nl, idx_start,
+                                              n_valid, offset, 50, bs, row, stride, mode, value_bytes, scale_bytes)
+    assert ok is True
+    rpages = [p.numpy().copy() for p in pages]
+    O.strided_block_transfer(staging.numpy(), rpages, block_ids.numpy(), 0, idx_start, n_valid, offset, bs, row, stride,
+                             mode, value_bytes, scale_bytes)
+    for a, b in zip(dpages, rpages):
+        eq(a, b, "staging->paged")
+    out = torch.zeros_like(dstaging)
+    ok = ma.lmcache_kv_strided_block_transfer(out, [p.data_ptr() for p in dpages], block_ids.cuda(), 1, nl, idx_start,
+                                              n_valid, offset, 50, bs, row, stride, mode, value_bytes, scale_bytes)
+    assert ok is True
+    rout = np.zeros(out.shape, np.uint8)
+    O.strided_block_transfer(rout, rpages, block_ids.numpy(), 1, idx_start, n_valid, offset, bs, row, stride, mode,
+                             value_bytes, scale_bytes)
+    eq(out, rout, "paged->staging")
+    assert ma.lmcache_kv_strided_block_transfer(out, [0] * 2, block_ids.cuda(), 1, nl, 0, 1, 0, 50, bs, row, stride, mode) is False
+
+
+def test_flash_random_vs_oracle(cuda_device):
+    g = torch.Generator().manual_seed(21)
+    nb, nh, hd, bs = 64, 4, 64, 16
+    kc = torch.randn((nb, nh, hd, bs), generator=g).to(torch.float16)
+    vc = torch.randn((nb, nh, hd, bs), generator=g).to(torch.float16)
+    lens = torch.tensor([0, 17, 130, 64, 5])
+    bt = torch.stack([torch.randperm(nb, generator=g)[:12] for _ in range(5)]).to(torch.int32)
+    ok, ov = ma.kv_load_and_reshape_flash(kc.cuda(), vc.cuda(), bt.cuda(), lens.cuda())
+    rk, rv = O.kv_load_and_reshape_flash(kc.numpy(), vc.numpy(), bt.numpy(), lens.numpy())
+    eq(ok, rk, "flash k")
+    eq(ov, rv, "flash v")
+
+
+def test_kv_copy_paged_rows_layer_table_and_oob(cuda_device):
+    g = torch.Generator().manual_seed(30)
+    layers = 5
+    srcs = [torch.randint(0, 256, (100, 1728), generator=g, dtype=torch.int32).to(torch.uint8).cuda() for _ in range(layers)]
+    dsts = [torch.zeros((90, 1728), dtype=torch.uint8, device="cuda") for _ in range(layers)]
+    si = torch.tensor([1, 50, 99, 3, 150], device="cuda")  # 150 is out of range: skipped on the device path
+    di = torch.tensor([0, 89, 10, 11, 12], device="cuda")
+    ma.kv_copy_paged_rows_layer_table(srcs, dsts, si, di)
+    for s, d in zip(srcs, dsts):
+        assert torch.equal(d[di[:4]], s[si[:4]])
+        assert torch.count_nonzero(d[12]) == 0
+    with pytest.raises(IndexError):
+        ma.kv_copy_paged_rows(srcs[0], dsts[0], torch.tensor([150]), torch.tensor([0]))

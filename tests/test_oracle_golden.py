@@ -209,3 +209,82 @@ def test_last_writer_mask_matches_sequential_loop():
     expected = np.zeros_like(keep)
     expected[list(seen.values())] = True
     assert np.array_equal(keep, expected)
+
+
+@pytest.fixture(scope="module")
+def misc():
+    return np.load(GOLDEN / "misc.npz")
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+def test_flash_triton_blocks(misc, dt):
+    p = f"flash/{dt}"
+    bt, lens = misc["flash/block_tables"], misc["flash/seq_lens"]
+    ok, ov = O.kv_load_and_reshape_flash(misc[f"{p}/k_cache"], misc[f"{p}/v_cache"], bt, lens, max_seq_len=15)
+    assert same_bits(ok, misc[f"{p}/out_k"]) and same_bits(ov, misc[f"{p}/out_v"])
+    kd, vd = misc[f"{p}/k_cache"].copy(), misc[f"{p}/v_cache"].copy()
+    O.kv_reshape_and_cache_back_flash(misc[f"{p}/dense_k"], misc[f"{p}/dense_v"], kd, vd, bt, lens)
+    assert same_bits(kd, misc[f"{p}/back_k"]) and same_bits(vd, misc[f"{p}/back_v"])
+    q = f"triton/{dt}"
+    tk, tv = O.kv_triton_indexed_to_dense(misc[f"{q}/pool_k"], misc[f"{q}/pool_v"], misc["triton/indptr"], misc[f"{q}/indices"], 9)
+    assert same_bits(tk, misc[f"{q}/out_k"]) and same_bits(tv, misc[f"{q}/out_v"])
+    r = f"blocks/{dt}"
+    dk = np.zeros_like(misc[f"{r}/dst_k"])
+    dv = np.zeros_like(misc[f"{r}/dst_v"])
+    n = O.kv_copy_paged_blocks(misc[f"{r}/src_k"], misc[f"{r}/src_v"], dk, dv, misc["blocks/pairs"])
+    assert n == int(misc[f"{r}/count"]) and same_bits(dk, misc[f"{r}/dst_k"]) and same_bits(dv, misc[f"{r}/dst_v"])
+    dk1 = np.zeros_like(misc[f"{r}/dst1_k"])
+    dv1 = np.zeros_like(misc[f"{r}/dst1_v"])
+    n1 = O.kv_copy_paged_blocks(misc[f"{r}/src_k"][0], misc[f"{r}/src_v"][0], dk1, dv1, misc["blocks/pairs"])
+    assert n1 == int(misc[f"{r}/count1"]) and same_bits(dk1, misc[f"{r}/dst1_k"]) and same_bits(dv1, misc[f"{r}/dst1_v"])
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+def test_fp8_flash(misc, fmt):
+    ok, ov = O.kv_load_and_dequantize_fp8_flash(misc["fp8flash/k8"], misc["fp8flash/v8"], misc["fp8flash/bt"],
+                                                misc["fp8flash/lens"], np.float32(0.03), np.array([0.5, 0.25], np.float32),
+                                                out_dtype="bfloat16", fp8_format=fmt)
+    assert same_bits(ok, misc[f"fp8flash/{fmt}/out_k"]) and same_bits(ov, misc[f"fp8flash/{fmt}/out_v"])
+
+
+def test_rows_and_hicache(misc):
+    for width in (1, 24, 1729):
+        d = misc[f"rows/{width}/dst"].copy()
+        O.kv_copy_paged_rows(misc[f"rows/{width}/src"], d, misc["rows/si"], misc["rows/di"])
+        assert same_bits(d, misc[f"rows/{width}/out"]), width
+    lf_k, lf_v, pf_k, pf_v = misc["hicache/lf_k"], misc["hicache/lf_v"], misc["hicache/pf_k"], misc["hicache/pf_v"]
+    si, di = misc["hicache/si"], misc["hicache/di"]
+    cases = {
+        "per_layer": (lf_k, lf_v, "layer_first", "layer_first", 1, 1, lf_k.shape),
+        "per_layer_pf_lf": (pf_k, pf_v, "page_first", "layer_first", 2, 1, lf_k.shape),
+        "all_layer": (lf_k, lf_v, "layer_first", "layer_first", 0, 3, lf_k.shape),
+        "all_layer_lf_pf": (lf_k, lf_v, "layer_first", "page_first", 0, 3, pf_k.shape),
+        "mla_per_layer": (lf_k, None, "layer_first", "layer_first", 0, 1, lf_k.shape),
+        "mla_pf_lf": (pf_k, None, "page_first", "layer_first", 1, 1, lf_k.shape),
+        "mla_all": (lf_k, None, "layer_first", "layer_first", 0, 3, lf_k.shape),
+        "mla_all_lf_pf": (lf_k, None, "layer_first", "page_first", 0, 3, pf_k.shape),
+    }
+    for key, (sk, sv, sl, dl, start, num, dshape) in cases.items():
+        dk = np.zeros(dshape, np.float16)
+        dv = np.zeros(dshape, np.float16) if sv is not None else None
+        O.hicache_transfer(sk, dk, sv, dv, si, di, sl, dl, start, num)
+        assert same_bits(dk, misc[f"hicache/out/{key}/0"]), key
+        if sv is not None:
+            assert same_bits(dv, misc[f"hicache/out/{key}/1"]), key
+    src = list(misc["hicache/direct/src"])
+    dst = [np.zeros((20, 2, 8), np.uint16) for _ in range(2)]
+    O.hicache_direct(src, dst, misc["hicache/direct/si"], misc["hicache/direct/di"], 4)
+    assert same_bits(np.stack(dst), misc["hicache/direct/out"])
+
+
+def test_cachegen(misc):
+    for name, dt in (("f32_256", "float32"), ("bf16_256", "bfloat16"), ("f16_16", "float16"), ("f32_2", "float32"), ("const", "float32")):
+        p = f"cachegen/{name}"
+        x = O.to_f32(misc[f"{p}/x"], dt)
+        bins = misc[f"{p}/codebook"].shape[0]
+        enc, cb, cdf = O.kv_cachegen_encode(x, bins)
+        assert same_bits(enc, misc[f"{p}/enc"]), name
+        assert same_bits(cb, misc[f"{p}/codebook"]), name
+        assert same_bits(cdf, misc[f"{p}/cdf"]), name
+        if f"{p}/dec" in misc:
+            assert same_bits(O.from_f32(O.kv_cachegen_decode(enc, cb), dt), misc[f"{p}/dec"]), name

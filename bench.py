@@ -52,10 +52,14 @@ def parse_args():
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--layers", type=int, default=32, help="layers per rank (32 = configs[1])")
     ap.add_argument("--blocks", type=int, default=32768)
-    ap.add_argument("--requests", type=int, default=64)
+    ap.add_argument("--requests", type=int, default=None, help="requests (default 64 for cfg2, 128 cfg4, 256 cfg5)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-requests", type=int, default=8, help="requests in the bounded CPU sample")
+    ap.add_argument("--workload", default="cfg2",
+                    choices=("cfg2", "cfg1", "cfg1-tile", "cfg2-tile", "cfg3-e4m3", "cfg3-e5m2", "cfg4", "cfg5"),
+                    help="cfg2 (default) is the headline; the others measure the remaining configs")
+    ap.add_argument("--tokens", type=int, default=8192, help="cfg3 batch tokens (256 decode / 8192 prefill)")
     return ap.parse_args()
 
 
@@ -472,10 +476,197 @@ def run_e2e(args, dev, caches, mem, slots_cpu, P, gather, scatter, barrier, worl
     }
 
 
+# ---------------------------------------------------------------------------
+# the other configs (device GB/s and roofline; cfg2 above carries the e2e and CPU legs)
+# ---------------------------------------------------------------------------
+
+
+def _fresh_block_slots(lens: list[int], nb: int, bs: int, seed: int = 1) -> list[torch.Tensor]:
+    """Per-request slots whose block ids are distinct within a request, drawn afresh per request."""
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for n in lens:
+        k = (n + bs - 1) // bs
+        bt = torch.randperm(nb, generator=g)[:k]
+        pos = torch.arange(n)
+        out.append((bt[pos // bs] * bs + pos % bs).to(torch.int64))
+    return out
+
+
+def setup_workload(args, dev, rank):
+    """Returns (config dict, bytes per step, step callable, kernel label)."""
+    import musa_aiter as ma
+
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    w = args.workload
+    if w in ("cfg1", "cfg1-tile"):
+        nb, bs, nh, hs = 256, 16, 8, 128
+        slots = block_slots([100, 513, 1024, 2047], nb).to(dev)
+        t = int(slots.numel())
+        if w == "cfg1":
+            k = torch.randn((nb, bs, nh, hs), device=dev, generator=g).half()
+            v = torch.randn((nb, bs, nh, hs), device=dev, generator=g).half()
+            mem = torch.empty((2, 1, t, nh * hs), dtype=torch.float16, device=dev)
+
+            def step():
+                ma.lmcache_kv_paged_to_buffer_two_x_nl([[k], [v]], mem, slots, bs, nh, hs)
+                ma.lmcache_kv_buffer_to_paged_two_x_nl(mem, [[k], [v]], slots, 0, bs, nh, hs)
+            label = "rows_kernel (two_x_nl NL=1)"
+        else:
+            k = torch.randn((nb, nh, hs, bs), device=dev, generator=g).half()
+            v = torch.randn((nb, nh, hs, bs), device=dev, generator=g).half()
+            ok = torch.empty((t, nh, hs), dtype=torch.float16, device=dev)
+            ov = torch.empty_like(ok)
+
+            def step():
+                ma.kv_paged_to_linear(k, v, slots, out_k=ok, out_v=ov)
+                ma.kv_linear_to_paged(ok, ov, k, v, slots)
+            label = "tile_kernel (kv_paged_to_linear / kv_linear_to_paged)"
+        cfg = {"workload": f"{w}: fp16 [256,16,8,128] K/V, sequences 100/513/1024/2047 (T={t}), gather + scatter back",
+               "tokens": t}
+        return cfg, 4 * 2 * t * nh * hs * 2, step, label
+    if w == "cfg2-tile":
+        nl, nb, bs, nh, hd = args.layers, args.blocks, BS, NH, HS
+        lens = request_lengths(args.requests)
+        slots = block_slots(lens, nb).to(dev)
+        t = int(slots.numel())
+        k = torch.empty((nl, nb, nh, hd, bs), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        v = torch.empty_like(k).normal_(generator=g)
+        buf = torch.empty((2, nl, t, nh, hd), dtype=torch.bfloat16, device=dev)
+
+        def step():
+            ma.kv_paged_to_linear_multi_layer(k, v, slots, out_k=buf[0], out_v=buf[1])
+            ma.kv_linear_to_paged_multi_layer(buf[0], buf[1], k, v, slots)
+        cfg = {"workload": "cfg2-tile: [L,NB,NH,HD,BS] bf16 caches <-> [2,L,T,NH,HD] buffer, multi-layer gather + scatter",
+               "layers_per_rank": nl, "num_blocks": nb, "tokens": t}
+        return cfg, 4 * payload_bytes(nl, t), step, "tile_kernel (multi-layer, all layers one launch)"
+    if w.startswith("cfg3"):
+        fmt = w.split("-")[1]
+        nl, nb, bs, nh, hd, t = args.layers, args.blocks, BS, NH, HS, args.tokens
+        gc = torch.Generator().manual_seed(1)
+        slots = torch.randperm(nb * bs, generator=gc)[:t].to(dev)
+        kl = (torch.randn((nl, t, nh, hd), device=dev, generator=g) * 2.0).to(torch.bfloat16)
+        vl = (torch.randn((nl, t, nh, hd), device=dev, generator=g) * 2.0).to(torch.bfloat16)
+        if fmt == "e4m3":
+            ks = kl.float().abs().amax(dim=(1, 3)) / 448.0
+            vs = vl.float().abs().amax(dim=(1, 3)) / 448.0
+        else:
+            ks = kl.float().abs().amax() / 57344.0
+            vs = vl.float().abs().amax() / 57344.0
+        k8 = torch.zeros((nl, nb, nh, hd, bs), dtype=torch.uint8, device=dev)
+        v8 = torch.zeros_like(k8)
+        ok = torch.empty_like(kl)
+        ov = torch.empty_like(vl)
+
+        def step():
+            ma.kv_linear_to_paged_fp8_multi_layer(kl, vl, k8, v8, slots, ks, vs, fp8_format=fmt)
+            ma.kv_paged_fp8_to_linear_multi_layer(k8, v8, slots, ks, vs, out_dtype=torch.bfloat16, fp8_format=fmt,
+                                                  out_k=ok, out_v=ov)
+        cfg = {"workload": f"{w}: bf16 [L,T,8,128] -> FP8 {fmt} [L,NB,8,128,16] cache (random unique slots) and back",
+               "layers_per_rank": nl, "num_blocks": nb, "tokens": t,
+               "scale": "per-layer-head amax/448" if fmt == "e4m3" else "scalar amax/57344"}
+        return cfg, 2 * nl * t * nh * hd * 6, step, "tile_kernel FP8 (fused quantize-scatter / gather-dequant)"
+    if w == "cfg4":
+        nl, nb, bs, nh, hs = 10, 8192, 64, 8, 128
+        g2 = torch.Generator().manual_seed(2)
+        lens = torch.randint(1024, 32769, (args.requests,), generator=g2).tolist()
+        per_req = [s.to(dev) for s in _fresh_block_slots(lens, nb, bs)]
+        caches = [[torch.empty((nb, bs, nh, hs), dtype=torch.bfloat16, device=dev).normal_(generator=g) for _ in range(nl)]
+                  for _ in range(2)]
+        mem_full = torch.empty((2, nl, max(lens), nh * hs), dtype=torch.bfloat16, device=dev)
+        mems = [mem_full[:, :, :n] for n in lens]
+
+        def step():
+            for sl, mem in zip(per_req, mems):
+                ma.lmcache_kv_paged_to_buffer_two_x_nl(caches, mem, sl, bs, nh, hs)
+                ma.lmcache_kv_buffer_to_paged_two_x_nl(mem, caches, sl, 0, bs, nh, hs)
+        tot = sum(lens)
+        cfg = {"workload": "cfg4: SGLang MP 2 x 10 x [8192,64,8,128] bf16 (one GPU's layer shard of NL=80), per-request gather + scatter",
+               "requests": len(lens), "tokens": tot}
+        return cfg, 4 * 2 * nl * tot * nh * hs * 2, step, "rows_kernel (2 x NL planes per launch)"
+    if w == "cfg5":
+        nl, nb, bs, kvd, ped = 8, 16384, 64, 512, 64
+        g2 = torch.Generator().manual_seed(2)
+        nreq = args.requests
+        lens = torch.randint(512, 16385, (nreq,), generator=g2).tolist()
+        per_req = [s.to(dev) for s in _fresh_block_slots(lens, nb, bs)]
+        kvc = torch.empty((nl, nb, bs, kvd), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        pec = torch.empty((nl, nb, bs, ped), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+
+        def step():
+            for sl in per_req:
+                okv, ope = ma.kv_paged_to_mla_linear_multi_layer(kvc, pec, sl)
+                ma.kv_mla_linear_to_paged_multi_layer(okv, ope, kvc, pec, sl)
+        tot = sum(lens)
+        cfg = {"workload": "cfg5: MLA flat caches [8,16384,64,512]+[8,16384,64,64] bf16 (one GPU's shard of 61 layers), per-request gather + scatter",
+               "requests": nreq, "tokens": tot}
+        return cfg, 4 * nl * tot * (kvd + ped) * 2, step, "rows_kernel (MLA latent + rope rows)"
+    raise ValueError(w)
+
+
+def run_workload(args) -> None:
+    import torch.distributed as dist
+
+    from musa_aiter import _native
+
+    os.environ.setdefault("MUSA_AITER_SKIP_VALIDATION", "1")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    cfg, nbytes, step, label = setup_workload(args, dev, rank)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    stream = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = _native.launch_count()
+    sampler.start()
+    a.record(stream)
+    for _ in range(args.steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    launches = _native.launch_count() - l0
+    ms = a.elapsed_time(b) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    peak, kind = load_peak()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(world * gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
+            "frac_of_8tbs": round(gbs / 8000.0, 4),
+            "roofline": {"bound": "hbm", "kernel": label, "achieved": round(gbs, 2), "peak": peak,
+                         "peak_source": f"{kind} hbm_gbs", "unit": "GB/s", "frac": round(gbs / peak, 4), "traffic": None,
+                         "note": "whole-step algorithmic bytes / step time (plan kernels included)"},
+            "gpu_launches": int(launches), "clocks": clocks, "validation": "off in the timed loop (MUSA_AITER_SKIP_VALIDATION=1)",
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
+    if args.requests is None:
+        args.requests = {"cfg4": 128, "cfg5": 256}.get(args.workload, 64)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "cfg2":
+        run_workload(args)
     else:
         run_native(args)
 

@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 
 #include "common.cuh"
@@ -54,12 +55,39 @@ int sm_count() {
   return n;
 }
 
-int grid_for(const void* kernel, int threads, size_t smem, int64_t work_ctas) {
-  if (work_ctas <= 0) return 0;
+namespace {
+struct OccKey {
+  const void* kernel;
+  int threads;
+  size_t smem;
+  bool operator<(const OccKey& o) const {
+    if (kernel != o.kernel) return kernel < o.kernel;
+    if (threads != o.threads) return threads < o.threads;
+    return smem < o.smem;
+  }
+};
+std::map<OccKey, int> g_occ;
+std::mutex g_occ_mu;
+}  // namespace
+
+int blocks_per_sm(const void* kernel, int threads, size_t smem) {
+  const OccKey key{kernel, threads, smem};
+  {
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    auto it = g_occ.find(key);
+    if (it != g_occ.end()) return it->second;
+  }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm <= 0)
     per_sm = 1;
-  const int64_t cap = static_cast<int64_t>(per_sm) * sm_count();
+  std::lock_guard<std::mutex> lk(g_occ_mu);
+  g_occ[key] = per_sm;
+  return per_sm;
+}
+
+int grid_for(const void* kernel, int threads, size_t smem, int64_t work_ctas) {
+  if (work_ctas <= 0) return 0;
+  const int64_t cap = static_cast<int64_t>(blocks_per_sm(kernel, threads, smem)) * sm_count();
   return static_cast<int>(work_ctas < cap ? work_ctas : cap);
 }
 

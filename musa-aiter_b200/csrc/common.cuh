@@ -31,6 +31,8 @@ inline int dtype_bytes(int32_t dt) {
 // Grid size for a grid-stride kernel: enough CTAs for `work_ctas` units of
 // work, capped at the number of CTAs that fit on the device at once.
 int grid_for(const void* kernel, int threads, size_t smem, int64_t work_ctas);
+// Resident CTAs per SM for a kernel launch shape (queried once, then cached).
+int blocks_per_sm(const void* kernel, int threads, size_t smem);
 
 // Scatter workspace layout: [hash keys C x u64][hash vals C x i64][eff n x i64]
 struct ScatterWs {

@@ -2,17 +2,20 @@
 // innermost ([L][NB][NH][HD][BS], the musa-aiter paged layout of
 // musa_aiter/ops/kv_transfer.py:2987-3000) and token-major rows ([L][T][NH][HD]).
 //
-// A CTA owns a chunk of kTT consecutive tokens of one (layer, kv) plane and
-// walks the heads a few at a time.  Tokens whose slots form an aligned run of
-// G = 16 / sizeof(cache element) consecutive offsets inside one block are
-// "packed": for each head_dim index d the CTA moves all G of them with one
-// 16-byte access of the cache row [d][o0 .. o0+G).  The [token][d] <-> [d][token]
-// transpose happens in shared memory; the token-major side always moves in
-// 16-byte vectors.  Unpacked tokens (random slots, partial blocks, skipped
-// slots) fall back to element accesses, so any slot mapping is handled.
+// Main path (tile_seg_kernel): a warp takes a window of tokens of one (kv,
+// layer) plane, splits the window's slot mapping into segments (runs of
+// consecutive slots inside one block) with ballots, and moves each segment
+// through 16-byte chunks of the cache rows ([d][o0 .. o0 + G)), transposing
+// in registers.  Long segments (>= G tokens: block-table traffic) and short
+// ones (random slots, run ends) are handled by two instantiations launched
+// back to back, so the short, latency-bound path runs at high occupancy while
+// the long path keeps the registers its transposes need.
 //
-// FP8 caches (raw uint8) fuse the musa-aiter reference codec into the
-// transpose: decode(byte) * scale on gather, encode(x / scale) on scatter
+// Fallback (tile_kernel): any head_dim / block_size / alignment, through a
+// shared-memory transpose of 32-token chunks.
+//
+// FP8 caches (raw uint8) fuse the musa-aiter reference codec into the moves:
+// decode(byte) * scale on gather, encode(x / scale) on scatter
 // (musa_aiter/ops/kv_transfer.py:2161-2200).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -34,6 +37,7 @@ struct TileLaunch {
   int64_t l_sl, l_st, l_sh;        // linear strides (elements); head_dim stride is 1
   int64_t num_layers, num_heads, head_dim, block_size, num_slots, n_tokens, n_chunks;
   int32_t slots64, n_kv, fill_zero, cache_vec, lin_vec, scale_mode, heads_per_step;
+  int32_t window;  // tokens per warp window of the segment kernel (8, 16 or 32)
 };
 
 // ---- element conversions (round-to-nearest-even everywhere) ---------------
@@ -311,13 +315,245 @@ __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileL
 }
 
 // ---------------------------------------------------------------------------
+// Segment tile kernel (the main path).
+//
+// A warp owns a window of 32 tokens of one (kv, layer) plane.  It loads the
+// window's slots (plus the next 32, since runs may cross the window end), and
+// finds "segments": runs of tokens whose slots are consecutive inside one
+// cache block, capped at 32 tokens and cut at offsets that are multiples of
+// min(block_size, 32) so every segment stays chunk-aligned in slot space.  The
+// warp handles every segment that STARTS in its window, whole.  Per segment the
+// lanes split the (head, head_dim-group) units; a unit moves R head_dim rows
+// (R = 16 / sizeof(linear element)) through the 16-byte cache chunks (G =
+// 16 / sizeof(cache element) offsets each) that the segment touches:
+//   gather : R chunk loads, then one 16-byte token row per covered column;
+//   scatter: for a fully covered chunk, G token-row loads then R chunk stores;
+//            for a partially covered chunk, element stores (no read-modify-
+//            write, so concurrent segments of one block never race).
+// No shared memory, no block barriers; FP8 codecs run in registers.
+// ---------------------------------------------------------------------------
+// MODE 1 handles segments of at least G tokens (plus zero rows), MODE 2 the shorter ones;
+// the two are launched back to back so each keeps the register budget its path needs.
+template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE>
+__global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg_kernel(const __grid_constant__ TileLaunch p) {
+  constexpr int G = 16 / sizeof(CT);
+  constexpr int R = 16 / sizeof(LT);
+  using C = Codec<CT, LT, CODEC>;
+  const int lane = threadIdx.x & 31;
+  const int upr = static_cast<int>(p.head_dim) / R;
+  const int NH = static_cast<int>(p.num_heads);
+  const int units = NH * upr;
+  const int64_t cap = p.block_size < 32 ? p.block_size : 32;
+  const int plane = blockIdx.y;
+  const int64_t l = plane % p.num_layers;
+  const int kv = plane / static_cast<int>(p.num_layers);
+  const CT* cache_r = reinterpret_cast<const CT*>(p.cache[kv]) + l * p.c_sl;
+  CT* cache_w = reinterpret_cast<CT*>(p.cache[kv]) + l * p.c_sl;
+  LT* lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl;
+  const float* scl = CODEC ? p.scale[kv] : nullptr;
+  const int W = p.window;
+  const uint32_t wmask = W >= 32 ? 0xffffffffu : ((1u << W) - 1u);
+  const int64_t windows = (p.n_tokens + W - 1) / W;
+  const int64_t wstride = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < windows; w += wstride) {
+    const int64_t t0 = w * W;
+    // Slots of tokens t0 + lane (A) and t0 + 32 + lane (B), as (block element offset, in-block offset).
+    int64_t offA = -1, offB = -1, sA = -1, sB = -1, oA = 0, oB = 0;
+    {
+      const int64_t ta = t0 + lane, tb = t0 + 32 + lane;
+      if (ta < p.n_tokens) sA = load_index(p.slots, p.slots64, ta);
+      if (tb < p.n_tokens) sB = load_index(p.slots, p.slots64, tb);
+      if (sA >= p.num_slots) sA = -1;
+      if (sB >= p.num_slots) sB = -1;
+      int64_t b;
+      if (sA >= 0) { split_slot(sA, p.block_size, &b, &oA); offA = b * p.c_sb + oA; }
+      if (sB >= 0) { split_slot(sB, p.block_size, &b, &oB); offB = b * p.c_sb + oB; }
+    }
+    int64_t sPrev = -1;  // slot of token t0 - 1 (for lane 0)
+    if (lane == 0 && t0 > 0) {
+      sPrev = load_index(p.slots, p.slots64, t0 - 1);
+      if (sPrev >= p.num_slots) sPrev = -1;
+    }
+    const int64_t upA = __shfl_up_sync(0xffffffffu, sA, 1);
+    const int64_t lastA = __shfl_sync(0xffffffffu, sA, 31);
+    int64_t upB = __shfl_up_sync(0xffffffffu, sB, 1);
+    const int64_t prevA = lane == 0 ? sPrev : upA;
+    const int64_t prevB = lane == 0 ? lastA : upB;
+    const bool startA = sA >= 0 && (prevA < 0 || sA != prevA + 1 || (oA % cap) == 0);
+    const bool startB = sB >= 0 && (prevB < 0 || sB != prevB + 1 || (oB % cap) == 0);
+    const uint32_t mStartA = __ballot_sync(0xffffffffu, startA);  // segments starting at t0 + lane
+    const uint64_t bound = static_cast<uint64_t>(mStartA) |
+                           (static_cast<uint64_t>(__ballot_sync(0xffffffffu, startB)) << 32) |
+                           ~(static_cast<uint64_t>(__ballot_sync(0xffffffffu, sA >= 0)) |
+                             (static_cast<uint64_t>(__ballot_sync(0xffffffffu, sB >= 0)) << 32));
+    // zero rows for skipped tokens of this window (gather, fill mode)
+    if (MODE == 1 && !SCATTER && p.fill_zero) {
+      uint32_t mZero = ~__ballot_sync(0xffffffffu, sA >= 0) & wmask;
+      const int64_t left = p.n_tokens - t0;
+      if (left < 32) mZero &= (1u << left) - 1u;
+      while (mZero) {
+        const int q = __ffs(mZero) - 1;
+        mZero &= mZero - 1;
+        for (int u = lane; u < units; u += 32) {
+          const int h = u / upr, dg = u - h * upr;
+          *reinterpret_cast<uint4*>(lin_l + (t0 + q) * p.l_st + h * p.l_sh + dg * R) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+    }
+    uint32_t mSeg = mStartA & wmask;  // the warp owns the segments that start inside its window
+    while (mSeg) {
+      const int q = __ffs(mSeg) - 1;
+      mSeg &= mSeg - 1;
+      const uint64_t rest = bound >> (q + 1);
+      const int len = rest ? (__ffsll(static_cast<long long>(rest))) : (64 - q);
+      const int64_t soff = __shfl_sync(0xffffffffu, offA, q);  // element offset of the segment's first slot
+      const int o_s = static_cast<int>(__shfl_sync(0xffffffffu, oA, q));
+      const int64_t ts = t0 + q;
+      const int64_t cbase = soff - o_s;  // block start (element offset)
+      if ((MODE == 1) != (len >= G)) continue;
+      if (len < G) {
+        // Short segment (random slots, run ends): one element per item, head_dim fastest
+        // across lanes, so a warp instruction touches consecutive cache rows (whole
+        // sectors per instruction) and a contiguous piece of the token row; four items
+        // per lane in flight.
+        const int hd = static_cast<int>(p.head_dim);
+        const int per_col = NH * hd;
+        const int items = per_col * len;
+        for (int base = 0; base < items; base += 128) {
+          CT cv[4];
+          LT lv[4];
+          int64_t ck[4];
+          LT* lk[4];
+          float sck[4];
+          bool ok[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int it = base + k * 32 + lane;
+            ok[k] = it < items;
+            const int j = ok[k] ? it / per_col : 0;
+            const int hdid = ok[k] ? it - j * per_col : 0;
+            const int h = hdid / hd, d = hdid - h * hd;
+            sck[k] = 1.f;
+            if (CODEC) sck[k] = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? h : l * NH + h)];
+            ck[k] = cbase + h * p.c_sh + static_cast<int64_t>(d) * p.c_sd + o_s + j;
+            lk[k] = lin_l + (ts + j) * p.l_st + h * p.l_sh + d;
+            if (ok[k]) {
+              if (!SCATTER) cv[k] = cache_r[ck[k]];
+              else lv[k] = lk[k][0];
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (!ok[k]) continue;
+            if (!SCATTER) lk[k][0] = C::load(cv[k], sck[k]);
+            else cache_w[ck[k]] = C::store(lv[k], sck[k]);
+          }
+        }
+        continue;
+      }
+      const int c_first = o_s / G, nch = (o_s + len - 1) / G - c_first + 1;
+      // (unit, chunk) items: neighbouring lanes take neighbouring chunks of one unit, so one
+      // warp instruction covers whole 32-byte sectors of a cache row.
+      for (int it = lane; it < units * nch; it += 32) {
+        const int u = it / nch;
+        const int c = c_first + (it - u * nch);
+        const int h = u / upr, dg = u - h * upr;
+        float sc = 1.f;
+        if (CODEC) sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? h : l * NH + h)];
+        const int64_t row0 = cbase + h * p.c_sh + static_cast<int64_t>(dg) * R * p.c_sd;
+        LT* lrow = lin_l + ts * p.l_st + h * p.l_sh + dg * R;  // token ts, head h, head_dim dg*R
+        const int col0 = c * G;
+        const int lo = max(col0, o_s), hi = min(col0 + G, o_s + len);  // covered columns [lo, hi)
+        if (lo == col0 && hi == col0 + G) {
+          if (!SCATTER) {
+            uint4 rows[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) rows[r] = __ldg(reinterpret_cast<const uint4*>(cache_r + row0 + r * p.c_sd + col0));
+#pragma unroll
+            for (int i = 0; i < G; ++i) {
+              uint4 outv;
+              LT* o = reinterpret_cast<LT*>(&outv);
+#pragma unroll
+              for (int r = 0; r < R; ++r) o[r] = C::load(reinterpret_cast<const CT*>(&rows[r])[i], sc);
+              *reinterpret_cast<uint4*>(lrow + (col0 + i - o_s) * p.l_st) = outv;
+            }
+          } else {
+            uint4 toks[G];
+#pragma unroll
+            for (int i = 0; i < G; ++i) toks[i] = __ldg(reinterpret_cast<const uint4*>(lrow + (col0 + i - o_s) * p.l_st));
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              uint4 v;
+              CT* e = reinterpret_cast<CT*>(&v);
+#pragma unroll
+              for (int i = 0; i < G; ++i) e[i] = C::store(reinterpret_cast<const LT*>(&toks[i])[r], sc);
+              *reinterpret_cast<uint4*>(cache_w + row0 + r * p.c_sd + col0) = v;
+            }
+          }
+        } else {
+          // partially covered chunk: element accesses on the cache side, 16-byte token rows
+#pragma unroll 1
+          for (int col = lo; col < hi; ++col) {
+            LT* trow = lrow + (col - o_s) * p.l_st;
+            if (!SCATTER) {
+              uint4 outv;
+              LT* o = reinterpret_cast<LT*>(&outv);
+#pragma unroll
+              for (int r = 0; r < R; ++r) o[r] = C::load(cache_r[row0 + r * p.c_sd + col], sc);
+              *reinterpret_cast<uint4*>(trow) = outv;
+            } else {
+              const uint4 tv = __ldg(reinterpret_cast<const uint4*>(trow));
+              const LT* x = reinterpret_cast<const LT*>(&tv);
+#pragma unroll
+              for (int r = 0; r < R; ++r) cache_w[row0 + r * p.c_sd + col] = C::store(x[r], sc);
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE>
+static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
+  const int threads = 256;
+  const int64_t planes = p.num_layers * p.n_kv;
+  auto kern = tile_seg_kernel<CT, LT, CODEC, SCATTER, MODE>;
+  const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kern), threads, 0);
+  // Narrower windows when 32-token windows would not give every resident warp a few windows
+  // (short batches; runs of random slots are one token each, so parallelism comes from windows).
+  const int64_t resident_warps = static_cast<int64_t>(per_sm) * sm_count() * (threads / 32);
+  p.window = 32;
+  while (p.window > 8 && (p.n_tokens + p.window - 1) / p.window * planes < 4 * resident_warps) p.window /= 2;
+  const int64_t windows = (p.n_tokens + p.window - 1) / p.window;
+  // About 4 device-fulls of CTAs, spread over the planes; each CTA walks windows grid-stride.
+  const int64_t target = static_cast<int64_t>(per_sm) * sm_count() * 4;
+  int64_t gx = std::max<int64_t>(1, target / planes);
+  gx = std::min<int64_t>(gx, (windows + (threads / 32) - 1) / (threads / 32));
+  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(planes));
+  kern<<<grid, threads, 0, st>>>(p);
+  return launch_status("tile_seg_kernel");
+}
+
+template <typename CT, typename LT, int CODEC, bool SCATTER>
+static int launch_tile_segments(TileLaunch& p, cudaStream_t st) {
+  int rc = launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 1>(p, st);
+  if (rc) return rc;
+  return launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 2>(p, st);
+}
+
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 static int launch_tile(TileLaunch& p, cudaStream_t st) {
   constexpr int VL = 16 / sizeof(LT);
+  // Segment path: 16-byte chunks on both sides; needs aligned chunks and whole linear vectors.
+  if (p.lin_vec && p.cache_vec && p.head_dim % VL == 0 && p.num_layers * p.n_kv <= 65535)
+    return launch_tile_segments<CT, LT, CODEC, SCATTER>(p, st);
   const int threads = 256;
   const size_t per_head = static_cast<size_t>(kTT) * (p.head_dim + VL) * sizeof(LT);
   // Heads per step: keep ~24 KB of tile per CTA so each thread has several 16-byte accesses in flight.

@@ -57,7 +57,12 @@ def kernel_slots(slots: torch.Tensor) -> tuple[torch.Tensor, int]:
 
 
 def validation_enabled() -> bool:
-    return os.environ.get("MUSA_AITER_SKIP_SLOT_VALIDATION", "0") not in {"1", "true", "TRUE", "yes", "YES"}
+    """Device-side validation reads (slot bounds, FP8 scale checks) are on unless
+    ``MUSA_AITER_SKIP_VALIDATION=1`` (alias ``MUSA_AITER_SKIP_SLOT_VALIDATION``) is set;
+    with them off no host sync happens and the kernels skip out-of-range slots."""
+    off = {"1", "true", "TRUE", "yes", "YES"}
+    return os.environ.get("MUSA_AITER_SKIP_VALIDATION", "0") not in off and \
+        os.environ.get("MUSA_AITER_SKIP_SLOT_VALIDATION", "0") not in off
 
 
 def slot_max(slots: torch.Tensor) -> int:
@@ -79,7 +84,7 @@ def check_slots_in_bounds(slots: torch.Tensor, nb: int, bs: int, name: str) -> N
     """musa_aiter/ops/kv_transfer.py:3020-3028: raise before touching any data.
 
     On CUDA this is one reduction kernel plus an 8-byte read-back (the reference
-    does two ``.item()`` syncs); ``MUSA_AITER_SKIP_SLOT_VALIDATION=1`` skips it,
+    does two ``.item()`` syncs); ``MUSA_AITER_SKIP_VALIDATION=1`` skips it,
     in which case out-of-range slots are skipped by the kernels instead.
     """
     if slots.device.type == "cuda" and not validation_enabled():

@@ -32,6 +32,7 @@ from ._common import (
     require_cuda,
     same_geometry,
     unit_inner,
+    validation_enabled,
 )
 
 __all__ = [
@@ -522,8 +523,9 @@ def _validate_fp8_cache_tensor(tensor: torch.Tensor, *, name: str) -> None:
 def _ensure_fp8_scale(scale, *, device: torch.device, name: str, num_heads: int, num_layers: int | None = None) -> torch.Tensor:
     """musa_aiter/ops/kv_transfer.py:2110-2121: positive finite scalar, [NH] or [L, NH]."""
     scale_tensor = torch.as_tensor(scale, dtype=torch.float32, device=device)
-    if not bool(torch.isfinite(scale_tensor).all()) or float(scale_tensor.min().item()) <= 0.0:
-        raise ValueError(f"{name}: FP8 scale must be positive and finite")
+    if scale_tensor.device.type != "cuda" or validation_enabled():
+        if not bool(torch.isfinite(scale_tensor).all()) or float(scale_tensor.min().item()) <= 0.0:
+            raise ValueError(f"{name}: FP8 scale must be positive and finite")
     if scale_tensor.numel() == 1:
         return scale_tensor.reshape(())
     if scale_tensor.dim() == 1 and int(scale_tensor.shape[0]) == num_heads:

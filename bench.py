@@ -275,7 +275,7 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": config_block(args, int(block_slots(request_lengths(args.requests), args.blocks).numel()), 1),
+        "config": config_block(args, int(block_slots(request_lengths(args.requests), args.blocks).numel()), world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

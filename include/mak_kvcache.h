@@ -307,6 +307,32 @@ MAK_API int mak_lmcache_strided_block_transfer(void* staging, const uint64_t* pa
                                                int64_t row_bytes, int64_t paged_block_stride, int64_t mode,
                                                int64_t value_bytes, int64_t scale_bytes, void* stream);
 
+/* ---- host <-> device byte-copy batch --------------------------------------- */
+
+typedef struct mak_copy_entry {
+  uint64_t dst;  /* destination address (device, or pinned host) */
+  uint64_t src;  /* source address (device, or pinned host) */
+  uint64_t size; /* bytes */
+} mak_copy_entry;
+
+#define MAK_COPY_AUTO 0   /* copy engine for entries >= engine_threshold, one kernel for the rest */
+#define MAK_COPY_ENGINE 1 /* every entry on the copy engines (SMs stay free for compute) */
+#define MAK_COPY_KERNEL 2 /* every entry through the batch-copy kernel */
+
+/*
+ * Submit a batch of byte copies on one stream, in order, without synchronising.
+ * Host sides must be pinned (the kernel addresses them through unified
+ * addressing); engine_threshold <= 0 means 4 MiB.  Replaces the MUSA
+ * batched-copy submission of csrc/kvcache/lmcache_musa_batch_copy_ext.cpp:208-259
+ * (no batched-memcpy runtime call is used: small entries are batched into
+ * kernel launches of up to 128 entries instead).
+ */
+MAK_API int mak_memcpy_batch(const mak_copy_entry* entries, int64_t n, int32_t mode, int64_t engine_threshold,
+                             void* stream);
+
+/* CUDA runtime and driver versions the library sees (lmcache_musa_batch_copy_ext.cpp:177-206). */
+MAK_API int mak_runtime_versions(int32_t* runtime_version, int32_t* driver_version);
+
 /* ---- CacheGen-style codec ------------------------------------------------ */
 
 /*

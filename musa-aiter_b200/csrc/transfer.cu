@@ -1,5 +1,6 @@
 // Staging <-> paged byte-block transfer for DSV4 MLA / blocked-scale groups,
-// and the indptr/indices -> dense slot builder.
+// the indptr/indices -> dense slot builder, and the host <-> device byte-copy
+// batch (LMCache direct transfer).
 //
 // Strided block transfer (reference semantics: csrc/kvcache/kv_transfer_float.mu:3281-3405).
 // Staging is [NL][staging_tokens][row_bytes]; block p of the batch covers staging
@@ -112,6 +113,45 @@ __global__ void indexed_slots_kernel(const void* indptr, int ip64, const void* i
   }
 }
 
+// ---------------------------------------------------------------------------
+// Byte-copy batch.  Small entries go through one kernel that reads/writes the
+// pinned host side directly (unified addressing): CTA rows are entries, CTA
+// columns split an entry, 4 independent 16-byte vectors per thread in flight.
+// Large entries (or every entry when the caller wants the SMs free) go to the
+// copy engines with one cudaMemcpyAsync each.
+// ---------------------------------------------------------------------------
+constexpr int kBatchEntries = 128;
+
+struct BatchLaunch {
+  mak_copy_entry e[kBatchEntries];
+  int32_t n;
+};
+
+__global__ void __launch_bounds__(256) batch_copy_kernel(const __grid_constant__ BatchLaunch p) {
+  const mak_copy_entry& e = p.e[blockIdx.y];
+  const uint64_t bits = e.dst | e.src | e.size;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if ((bits & 15u) == 0) {
+    const uint4* s = reinterpret_cast<const uint4*>(e.src);
+    uint4* d = reinterpret_cast<uint4*>(e.dst);
+    const int64_t n = static_cast<int64_t>(e.size / 16);
+    for (int64_t i0 = tid; i0 < n; i0 += nthr * 4) {
+      uint4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * nthr < n) r[u] = s[i0 + u * nthr];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (i0 + u * nthr < n) d[i0 + u * nthr] = r[u];
+    }
+  } else {
+    const uint8_t* s = reinterpret_cast<const uint8_t*>(e.src);
+    uint8_t* d = reinterpret_cast<uint8_t*>(e.dst);
+    for (int64_t i = tid; i < static_cast<int64_t>(e.size); i += nthr) d[i] = s[i];
+  }
+}
+
 }  // namespace mak
 
 using namespace mak;
@@ -169,6 +209,56 @@ int mak_lmcache_strided_block_transfer(void* staging, const uint64_t* paged_ptrs
     int rc = vec == 16 ? launch_strided<16>(p, st) : (vec == 8 ? launch_strided<8>(p, st) : launch_strided<4>(p, st));
     if (rc) return rc;
   }
+  return MAK_OK;
+}
+
+int mak_memcpy_batch(const mak_copy_entry* entries, int64_t n, int32_t mode, int64_t engine_threshold, void* stream) {
+  if (n < 0 || (n > 0 && entries == nullptr)) return fail(MAK_E_INVALID, "mak_memcpy_batch: bad entry array");
+  if (mode < MAK_COPY_AUTO || mode > MAK_COPY_KERNEL) return fail(MAK_E_INVALID, "mak_memcpy_batch: bad mode %d", mode);
+  cudaStream_t st = as_stream(stream);
+  if (engine_threshold <= 0) engine_threshold = 4 << 20;
+  BatchLaunch L;
+  memset(&L, 0, sizeof(L));
+  uint64_t largest = 0;
+  auto flush = [&]() -> int {
+    if (L.n == 0) return MAK_OK;
+    const int threads = 256;
+    const uint64_t per_cta = static_cast<uint64_t>(threads) * 16 * 4;
+    const unsigned gx = static_cast<unsigned>(std::min<uint64_t>(64, (largest + per_cta - 1) / per_cta));
+    batch_copy_kernel<<<dim3(std::max(1u, gx), L.n), threads, 0, st>>>(L);
+    const int rc = launch_status("batch_copy_kernel");
+    L.n = 0;
+    largest = 0;
+    return rc;
+  };
+  for (int64_t i = 0; i < n; ++i) {
+    const mak_copy_entry& e = entries[i];
+    if (e.size == 0) continue;
+    if (e.dst == 0 || e.src == 0) return fail(MAK_E_INVALID, "mak_memcpy_batch: entry %lld has a NULL pointer", (long long)i);
+    const bool engine = mode == MAK_COPY_ENGINE || (mode == MAK_COPY_AUTO && e.size >= static_cast<uint64_t>(engine_threshold));
+    if (engine) {
+      cudaError_t err = cudaMemcpyAsync(reinterpret_cast<void*>(e.dst), reinterpret_cast<const void*>(e.src), e.size,
+                                        cudaMemcpyDefault, st);
+      if (err != cudaSuccess) return cuda_fail(err, "mak_memcpy_batch: cudaMemcpyAsync");
+      continue;
+    }
+    L.e[L.n++] = e;
+    largest = std::max<uint64_t>(largest, e.size);
+    if (L.n == kBatchEntries) {
+      int rc = flush();
+      if (rc) return rc;
+    }
+  }
+  return flush();
+}
+
+int mak_runtime_versions(int32_t* runtime_version, int32_t* driver_version) {
+  int rt = 0, drv = 0;
+  cudaError_t e = cudaRuntimeGetVersion(&rt);
+  if (e == cudaSuccess) e = cudaDriverGetVersion(&drv);
+  if (e != cudaSuccess) return cuda_fail(e, "mak_runtime_versions");
+  if (runtime_version) *runtime_version = rt;
+  if (driver_version) *driver_version = drv;
   return MAK_OK;
 }
 

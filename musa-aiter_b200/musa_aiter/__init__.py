@@ -80,6 +80,12 @@ from .ops.kv_transfer import (
     native_fp8_kv_cache_abi_version,
     native_kv_transfer_abi_version,
 )
+from .ops.lmcache_musa_batch_copy import (
+    is_native_lmcache_musa_batch_copy_available,
+    lmcache_musa_memcpy_batch_async,
+    native_lmcache_musa_batch_copy_abi_version,
+    native_lmcache_musa_batch_copy_runtime_versions,
+)
 from .ops.lmcache_kv_transfer import (
     clear_native_lmcache_kv_transfer_cache,
     is_native_lmcache_kv_transfer_available,

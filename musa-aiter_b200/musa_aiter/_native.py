@@ -25,6 +25,7 @@ ABI_VERSION = 1
 MAK_DT_U8, MAK_DT_F16, MAK_DT_BF16, MAK_DT_F32, MAK_DT_I32, MAK_DT_I64 = range(6)
 MAK_FP8_E4M3, MAK_FP8_E5M2 = 1, 2
 MAK_SCALE_SCALAR, MAK_SCALE_PER_HEAD, MAK_SCALE_PER_LAYER_HEAD = 0, 1, 2
+MAK_COPY_AUTO, MAK_COPY_ENGINE, MAK_COPY_KERNEL = 0, 1, 2
 
 _DTYPE_CODES = {
     torch.uint8: MAK_DT_U8,
@@ -72,6 +73,12 @@ class LinearDesc(ctypes.Structure):
         ("dtype", c_int32),
         ("reserved", c_int32),
     ]
+
+
+class CopyEntry(ctypes.Structure):
+    """``mak_copy_entry``: one byte copy of a batch."""
+
+    _fields_ = [("dst", c_uint64), ("src", c_uint64), ("size", c_uint64)]
 
 
 class RowsDesc(ctypes.Structure):
@@ -156,6 +163,8 @@ _PROTOTYPES = {
         c_int32,
         [c_void_p, POINTER(c_uint64), c_void_p] + [c_int64] * 12 + [c_void_p],
     ),
+    "mak_memcpy_batch": (c_int32, [POINTER(CopyEntry), c_int64, c_int32, c_int64, c_void_p]),
+    "mak_runtime_versions": (c_int32, [POINTER(c_int32), POINTER(c_int32)]),
     "mak_minmax": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_void_p]),
     "mak_cachegen_encode": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "mak_cachegen_decode": (c_int32, [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p]),

@@ -220,3 +220,32 @@ def test_kv_copy_paged_rows_layer_table_and_oob(cuda_device):
         assert torch.count_nonzero(d[12]) == 0
     with pytest.raises(IndexError):
         ma.kv_copy_paged_rows(srcs[0], dsts[0], torch.tensor([150]), torch.tensor([0]))
+
+
+def test_memcpy_batch_h2d_d2h(cuda_device):
+    """Small entries go through the batch kernel, large ones through the copy engines; offsets and
+    registration-boundary splits land every byte where the plan says."""
+    g = torch.Generator().manual_seed(40)
+    host = torch.randint(0, 256, (9 << 20,), generator=g, dtype=torch.int32).to(torch.uint8).pin_memory()
+    dev = torch.zeros(10 << 20, dtype=torch.uint8, device="cuda")
+    sizes = [100, 4096, 3, 8 << 20, 1000]
+    src_off = [0, 128, 7, 5000, (8 << 20) + 6000]
+    dst_off = [16, 4096, 9000, 1 << 20, (9 << 20) + 5]
+    assert ma.lmcache_musa_memcpy_batch_async([dev] * 5, [host] * 5, sizes, source_offsets=src_off,
+                                              destination_offsets=dst_off, pin_chunk_size=1 << 16) is True
+    torch.cuda.synchronize()
+    expect = torch.zeros_like(dev).cpu()
+    for s, so, do in zip(sizes, src_off, dst_off):
+        expect[do: do + s] = host[so: so + s]
+    assert torch.equal(dev.cpu(), expect)
+    back = torch.zeros(10 << 20, dtype=torch.uint8).pin_memory()
+    assert ma.lmcache_musa_memcpy_batch_async([back] * 5, [dev] * 5, sizes, source_offsets=dst_off,
+                                              destination_offsets=dst_off, prefer_overlap_with_compute=True,
+                                              max_batch_entries=2) is True
+    torch.cuda.synchronize()
+    for s, do in zip(sizes, dst_off):
+        assert torch.equal(back[do: do + s], expect[do: do + s])
+    with pytest.raises(ValueError, match="pinned"):
+        ma.lmcache_musa_memcpy_batch_async([dev], [torch.zeros(16, dtype=torch.uint8)], [16])
+    assert ma.lmcache_musa_memcpy_batch_async([dev], [dev], [16]) is False
+    assert ma.native_lmcache_musa_batch_copy_runtime_versions()[0] >= 12000

@@ -51,7 +51,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--layers", type=int, default=32, help="layers per rank (32 = configs[1])")
-    ap.add_argument("--blocks", type=int, default=32768)
+    ap.add_argument("--blocks", type=int, default=None,
+                    help="cache blocks (default 32768 for cfg2/tile/FP8 workloads, 8192 cfg4, 16384 cfg5)")
     ap.add_argument("--requests", type=int, default=None, help="requests (default 64 for cfg2, 128 cfg4, 256 cfg5)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -567,7 +568,7 @@ def setup_workload(args, dev, rank):
                "scale": "per-layer-head amax/448" if fmt == "e4m3" else "scalar amax/57344"}
         return cfg, 2 * nl * t * nh * hd * 6, step, "tile_kernel FP8 (fused quantize-scatter / gather-dequant)"
     if w == "cfg4":
-        nl, nb, bs, nh, hs = 10, 8192, 64, 8, 128
+        nl, nb, bs, nh, hs = 10, args.blocks or 8192, 64, 8, 128
         g2 = torch.Generator().manual_seed(2)
         lens = torch.randint(1024, 32769, (args.requests,), generator=g2).tolist()
         per_req = [s.to(dev) for s in _fresh_block_slots(lens, nb, bs)]
@@ -582,10 +583,10 @@ def setup_workload(args, dev, rank):
                 ma.lmcache_kv_buffer_to_paged_two_x_nl(mem, caches, sl, 0, bs, nh, hs)
         tot = sum(lens)
         cfg = {"workload": "cfg4: SGLang MP 2 x 10 x [8192,64,8,128] bf16 (one GPU's layer shard of NL=80), per-request gather + scatter",
-               "requests": len(lens), "tokens": tot}
+               "requests": len(lens), "tokens": tot, "num_blocks": nb}
         return cfg, 4 * 2 * nl * tot * nh * hs * 2, step, "rows_kernel (2 x NL planes per launch)"
     if w == "cfg5":
-        nl, nb, bs, kvd, ped = 8, 16384, 64, 512, 64
+        nl, nb, bs, kvd, ped = 8, args.blocks or 16384, 64, 512, 64
         g2 = torch.Generator().manual_seed(2)
         nreq = args.requests
         lens = torch.randint(512, 16385, (nreq,), generator=g2).tolist()
@@ -599,7 +600,7 @@ def setup_workload(args, dev, rank):
                 ma.kv_mla_linear_to_paged_multi_layer(okv, ope, kvc, pec, sl)
         tot = sum(lens)
         cfg = {"workload": "cfg5: MLA flat caches [8,16384,64,512]+[8,16384,64,64] bf16 (one GPU's shard of 61 layers), per-request gather + scatter",
-               "requests": nreq, "tokens": tot}
+               "requests": nreq, "tokens": tot, "num_blocks": nb}
         return cfg, 4 * nl * tot * (kvd + ped) * 2, step, "rows_kernel (MLA latent + rope rows)"
     raise ValueError(w)
 
@@ -663,6 +664,8 @@ def main():
     args = parse_args()
     if args.requests is None:
         args.requests = {"cfg4": 128, "cfg5": 256}.get(args.workload, 64)
+    if args.blocks is None and (args.impl == "reference" or args.workload not in ("cfg4", "cfg5")):
+        args.blocks = 32768
     if args.impl == "reference":
         run_reference(args)
     elif args.workload != "cfg2":

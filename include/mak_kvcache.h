@@ -258,6 +258,24 @@ MAK_API int mak_rows_scatter(const mak_rows_desc* linear, const mak_rows_desc* p
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Grouped forms: `paged` and `linear` are arrays of n_groups (1..4)
+ * descriptors; group g's planes follow group g-1's, and row_bytes (if not NULL)
+ * gives one width per GROUP.  Lets planes of different geometry (e.g. the MLA
+ * latent cache and its rope cache) move in one launch with one slot resolution.
+ * Replaces the pair of per-cache launches the reference makes for MLA flat
+ * caches (musa_aiter_kv_paged_to_mla_linear_* / musa_aiter_kv_mla_linear_to_paged_*,
+ * csrc/kvcache/kv_transfer_float.mu:673-826, called twice from
+ * ops/kv_transfer.py:3841-4118); same semantics as mak_rows_gather / mak_rows_scatter.
+ */
+MAK_API int mak_rows_gatherv(const mak_rows_desc* paged, const mak_rows_desc* linear, int32_t n_groups,
+                             const int64_t* row_bytes, int64_t row_bytes0, const void* slots, int32_t slot_dtype,
+                             int64_t n_slots, int32_t fill_zero, void* stream);
+MAK_API int mak_rows_scatterv(const mak_rows_desc* linear, const mak_rows_desc* paged, int32_t n_groups,
+                              const int64_t* row_bytes, int64_t row_bytes0, const void* slots, int32_t slot_dtype,
+                              int64_t n_slots, int64_t skip_prefix, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/*
  * Allocation-free row scatter.  No counterpart in the reference: it exists for
  * callers that cannot call cudaMalloc (a serving engine that reserved its HBM
  * up front and scatters inside its step loop, or a foreign-language caller

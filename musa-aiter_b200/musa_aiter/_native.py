@@ -133,13 +133,13 @@ _PROTOTYPES = {
     ),
     "mak_rows_gather": (
         c_int32,
-        [POINTER(RowsDesc), POINTER(RowsDesc), POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int32, c_void_p],
+        [c_void_p, c_void_p, POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int32, c_void_p],
     ),
     "mak_rows_scatter": (
         c_int32,
         [
-            POINTER(RowsDesc),
-            POINTER(RowsDesc),
+            c_void_p,
+            c_void_p,
             POINTER(c_int64),
             c_int64,
             c_void_p,
@@ -151,9 +151,19 @@ _PROTOTYPES = {
             c_void_p,
         ],
     ),
+    "mak_rows_gatherv": (
+        c_int32,
+        [c_void_p, c_void_p, c_int32, POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int32,
+         c_void_p],
+    ),
+    "mak_rows_scatterv": (
+        c_int32,
+        [c_void_p, c_void_p, c_int32, POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int64,
+         c_void_p, c_size_t, c_void_p],
+    ),
     "mak_rows_scatter_static": (
         c_int32,
-        [POINTER(RowsDesc), POINTER(RowsDesc), POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int64, c_void_p],
+        [c_void_p, c_void_p, POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int64, c_void_p],
     ),
     "mak_build_indexed_slots": (
         c_int32,
@@ -171,8 +181,8 @@ _PROTOTYPES = {
     "mak_rows_copy": (
         c_int32,
         [
-            POINTER(RowsDesc),
-            POINTER(RowsDesc),
+            c_void_p,
+            c_void_p,
             POINTER(c_int64),
             c_int64,
             c_void_p,
@@ -250,14 +260,20 @@ def dtype_code(dtype: torch.dtype) -> int:
         raise ValueError(f"unsupported dtype for the kvcache native library: {dtype}") from None
 
 
-def stream_ptr(device: torch.device) -> c_void_p:
-    """Current CUDA stream of ``device`` (the reference passes stream 0 in places;
-    this backend always honours the caller's current stream)."""
-    return c_void_p(torch.cuda.current_stream(device).cuda_stream)
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 
 
-def ptr(t: torch.Tensor | None) -> c_void_p:
-    return c_void_p(t.data_ptr() if t is not None else 0)
+def stream_ptr(device: torch.device) -> int:
+    """Current CUDA stream of ``device`` as an address (the reference passes
+    stream 0 in places; this backend always honours the caller's current stream)."""
+    if _RAW_STREAM is not None:
+        idx = device.index
+        return _RAW_STREAM(idx if idx is not None else torch.cuda.current_device())
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return t.data_ptr() if t is not None else None
 
 
 def workspace(n_items: int, device: torch.device) -> tuple[torch.Tensor, int]:
@@ -271,7 +287,36 @@ def plane_array(ptrs: list[int]):
     return arr
 
 
+def rows_pack(*sides):
+    """One C buffer holding a ``mak_rows_desc`` per side followed by all plane pointer arrays.
+
+    Each side is ``(ptrs, rows_per_block, block_stride, row_stride, num_rows)``;
+    descriptor ``i`` starts at byte ``48 * i`` of the buffer (the struct is six
+    64-bit words).  Built with one slice assignment: constructing ctypes
+    Structures per call costs several microseconds more per launch."""
+    n = len(sides)
+    words = [0] * (6 * n)
+    tail: list[int] = []
+    for i, (ptrs, rpb, bstride, rstride, nrows) in enumerate(sides):
+        words[6 * i: 6 * i + 6] = (len(tail), len(ptrs), rpb, bstride, rstride, nrows)
+        tail += ptrs
+    buf = (c_int64 * (6 * n + max(1, len(tail))))()
+    pbase = ctypes.addressof(buf) + 48 * n
+    for i in range(n):
+        words[6 * i] = pbase + 8 * words[6 * i]
+    words += tail
+    buf[: len(words)] = words
+    return buf
+
+
+def rows_desc_array(sides):
+    """A C array of ``mak_rows_desc`` (one per group) for the grouped entry points;
+    returns ``(array, keepalive)``."""
+    buf = rows_pack(*sides)
+    return buf, buf
+
+
 def rows_desc(ptrs: list[int], rows_per_block: int, block_stride: int, row_stride: int, num_rows: int):
-    arr = plane_array(ptrs)
-    desc = RowsDesc(ctypes.cast(arr, POINTER(c_uint64)), len(ptrs), rows_per_block, block_stride, row_stride, num_rows)
-    return desc, arr  # keep arr alive alongside desc
+    """One ``mak_rows_desc`` (pass it with ``ctypes.byref``); returns ``(desc, keepalive)``."""
+    buf = rows_pack((ptrs, rows_per_block, block_stride, row_stride, num_rows))
+    return buf, buf

@@ -20,17 +20,19 @@ _INDEX_DTYPES = (torch.int16, torch.int32, torch.int64)
 def require_cuda(name: str, *tensors: torch.Tensor) -> torch.device:
     """All tensors must be CUDA tensors on one device: this backend has no CPU path."""
     dev = None
+    idx = -2
     for t in tensors:
         if t is None:
             continue
-        if t.device.type != "cuda":
+        if not t.is_cuda:
             raise RuntimeError(
                 f"{name}: the B200 kvcache backend runs on CUDA tensors only (got a {t.device} tensor); "
                 "there is no CPU fallback"
             )
         if dev is None:
             dev = t.device
-        elif t.device != dev:
+            idx = t.get_device()
+        elif t.get_device() != idx:
             raise ValueError(f"{name}: all tensors must be on the same device")
     _native.load()
     return dev

@@ -792,64 +792,78 @@ def kv_merged_linear_to_paged_fp8_multi_layer(
 # ---------------------------------------------------------------------------
 
 
-def _rows_side_paged(cache: torch.Tensor, layered: bool):
-    """Row-side descriptor of [L, NB, BS, W] (layered) or [NB, BS, W] with unit inner stride."""
+def _rows_side_paged(cache: torch.Tensor, layered: bool) -> tuple:
+    """Row geometry ``(ptrs, rows_per_block, block_stride, row_stride, num_rows)`` of
+    [L, NB, BS, W] (layered: one plane per layer) or [NB, BS, W], unit inner stride."""
     e = cache.element_size()
+    base = cache.data_ptr()
     if layered:
-        nl = cache.shape[0]
-        ptrs = [cache.data_ptr() + i * cache.stride(0) * e for i in range(nl)]
+        s0, sb, st = cache.stride()[:3]
+        ptrs = [base + i * s0 * e for i in range(cache.shape[0])]
         nb, bs = cache.shape[1], cache.shape[2]
-        sb, st = cache.stride(1), cache.stride(2)
     else:
-        ptrs = [cache.data_ptr()]
+        sb, st = cache.stride()[:2]
+        ptrs = [base]
         nb, bs = cache.shape[0], cache.shape[1]
-        sb, st = cache.stride(0), cache.stride(1)
-    return _native.rows_desc(ptrs, int(bs), int(sb * e), int(st * e), int(nb * bs))
+    return ptrs, int(bs), int(sb * e), int(st * e), int(nb * bs)
 
 
-def _rows_side_linear(buf: torch.Tensor, layered: bool):
-    """Row-side descriptor of [L, T, W] (layered) or [T, W]."""
+def _rows_side_linear(buf: torch.Tensor, layered: bool) -> tuple:
+    """Row geometry of [L, T, W] (layered) or [T, W]."""
     e = buf.element_size()
+    base = buf.data_ptr()
     if layered:
-        ptrs = [buf.data_ptr() + i * buf.stride(0) * e for i in range(buf.shape[0])]
-        t, st = buf.shape[1], buf.stride(1)
+        s0, st = buf.stride()[:2]
+        ptrs = [base + i * s0 * e for i in range(buf.shape[0])]
+        t = buf.shape[1]
     else:
-        ptrs = [buf.data_ptr()]
+        ptrs = [base]
         t, st = buf.shape[0], buf.stride(0)
-    return _native.rows_desc(ptrs, 1, int(st * e), 0, int(t))
+    return ptrs, 1, int(st * e), 0, int(t)
 
 
-def _mla_gather(cache: torch.Tensor, slots: torch.Tensor, out: torch.Tensor, *, layered: bool, op: str) -> None:
+def _mla_pair_gather(kv_cache: torch.Tensor, pe_cache: torch.Tensor, slots: torch.Tensor, okv: torch.Tensor,
+                     ope: torch.Tensor, *, layered: bool, op: str) -> None:
+    """Latent and rope caches -> linear rows in ONE launch (two plane geometries, one slot vector)."""
     lib = _native.load()
-    cache, _ = _as_unit_inner(cache)
-    work, tmp = _as_unit_inner(out)
+    c1, _ = _as_unit_inner(kv_cache)
+    c2, _ = _as_unit_inner(pe_cache)
+    w1, t1 = _as_unit_inner(okv)
+    w2, t2 = _as_unit_inner(ope)
     ks, code = kernel_slots(slots)
-    pd, pa = _rows_side_paged(cache, layered)
-    ld, la = _rows_side_linear(work, layered)
-    rb = cache.shape[-1] * cache.element_size()
-    rc = lib.mak_rows_gather(ctypes.byref(pd), ctypes.byref(ld), None, rb, _native.ptr(ks), code, ks.numel(), 1,
-                             _native.stream_ptr(cache.device))
+    buf = _native.rows_pack(_rows_side_paged(c1, layered), _rows_side_paged(c2, layered),
+                            _rows_side_linear(w1, layered), _rows_side_linear(w2, layered))
+    base = ctypes.addressof(buf)
+    rb = (ctypes.c_int64 * 2)(c1.shape[-1] * c1.element_size(), c2.shape[-1] * c2.element_size())
+    rc = lib.mak_rows_gatherv(base, base + 96, 2, rb, 0, ks.data_ptr(), code, ks.numel(), 1, _native.stream_ptr(c1.device))
     _native.check(rc, op)
-    if tmp:
-        out.copy_(work)
+    if t1:
+        okv.copy_(w1)
+    if t2:
+        ope.copy_(w2)
 
 
-def _mla_scatter(lin: torch.Tensor, cache: torch.Tensor, slots: torch.Tensor, *, layered: bool, op: str, ws=None) -> None:
+def _mla_pair_scatter(kv_linear: torch.Tensor, pe_linear: torch.Tensor, kv_cache: torch.Tensor, pe_cache: torch.Tensor,
+                      slots: torch.Tensor, *, layered: bool, op: str) -> None:
+    """Linear rows -> latent and rope caches in ONE launch with one last-writer resolution."""
     lib = _native.load()
-    lin, _ = _as_unit_inner(lin)
-    work, tmp = _as_unit_inner(cache)
+    l1, _ = _as_unit_inner(kv_linear)
+    l2, _ = _as_unit_inner(pe_linear)
+    w1, t1 = _as_unit_inner(kv_cache)
+    w2, t2 = _as_unit_inner(pe_cache)
     ks, code = kernel_slots(slots)
-    pd, pa = _rows_side_paged(work, layered)
-    ld, la = _rows_side_linear(lin, layered)
-    rb = cache.shape[-1] * cache.element_size()
-    if ws is None:
-        ws = _native.workspace(ks.numel(), cache.device)
-    buf, nbytes = ws
-    rc = lib.mak_rows_scatter(ctypes.byref(ld), ctypes.byref(pd), None, rb, _native.ptr(ks), code, ks.numel(), 0,
-                              _native.ptr(buf), nbytes, _native.stream_ptr(cache.device))
+    buf = _native.rows_pack(_rows_side_linear(l1, layered), _rows_side_linear(l2, layered),
+                            _rows_side_paged(w1, layered), _rows_side_paged(w2, layered))
+    base = ctypes.addressof(buf)
+    rb = (ctypes.c_int64 * 2)(w1.shape[-1] * w1.element_size(), w2.shape[-1] * w2.element_size())
+    ws, nbytes = _native.workspace(ks.numel(), w1.device)
+    rc = lib.mak_rows_scatterv(base, base + 96, 2, rb, 0, ks.data_ptr(), code, ks.numel(), 0, ws.data_ptr(), nbytes,
+                               _native.stream_ptr(w1.device))
     _native.check(rc, op)
-    if tmp:
-        cache.copy_(work)
+    if t1:
+        kv_cache.copy_(w1)
+    if t2:
+        pe_cache.copy_(w2)
 
 
 def _validate_flat_paged_shapes(first_cache, second_cache, *, name: str) -> tuple[int, int, int, int]:
@@ -905,8 +919,7 @@ def kv_paged_to_mla_linear(
     if okv.dtype != kv_cache.dtype or ope.dtype != k_pe_cache.dtype:
         raise ValueError(f"{name}: output dtypes must match caches")
     if tcount:
-        _mla_gather(kv_cache, slots, okv, layered=False, op=name)
-        _mla_gather(k_pe_cache, slots, ope, layered=False, op=name)
+        _mla_pair_gather(kv_cache, k_pe_cache, slots, okv, ope, layered=False, op=name)
     emit_native(name, kv_cache, "sm100a row gather (MLA flat)")
     return okv, ope
 
@@ -936,9 +949,7 @@ def kv_mla_linear_to_paged(
         raise ValueError(f"{name}: dtypes must match caches")
     require_cuda(name, kv_linear, k_pe_linear, kv_cache, k_pe_cache, slots)
     if tcount:
-        ws = _native.workspace(tcount, kv_cache.device)
-        _mla_scatter(kv_linear, kv_cache, slots, layered=False, op=name, ws=ws)
-        _mla_scatter(k_pe_linear, k_pe_cache, slots, layered=False, op=name, ws=ws)
+        _mla_pair_scatter(kv_linear, k_pe_linear, kv_cache, k_pe_cache, slots, layered=False, op=name)
     emit_native(name, kv_linear, "sm100a row scatter (MLA flat)")
 
 
@@ -961,8 +972,7 @@ def kv_paged_to_mla_linear_multi_layer(
     okv = torch.empty((nl, t, kv_dim), dtype=kv_cache.dtype, device=kv_cache.device)
     ope = torch.empty((nl, t, pe_dim), dtype=k_pe_cache.dtype, device=kv_cache.device)
     if t:
-        _mla_gather(kv_cache, slots, okv, layered=True, op=name)
-        _mla_gather(k_pe_cache, slots, ope, layered=True, op=name)
+        _mla_pair_gather(kv_cache, k_pe_cache, slots, okv, ope, layered=True, op=name)
     emit_native(name, kv_cache, "sm100a row gather (MLA flat, all layers)")
     return okv, ope
 
@@ -994,9 +1004,7 @@ def kv_mla_linear_to_paged_multi_layer(
     check_slots_in_bounds(slots, nb, bs, name)
     require_cuda(name, kv_linear, k_pe_linear, kv_cache, k_pe_cache, slots)
     if tcount:
-        ws = _native.workspace(tcount, kv_cache.device)
-        _mla_scatter(kv_linear, kv_cache, slots, layered=True, op=name, ws=ws)
-        _mla_scatter(k_pe_linear, k_pe_cache, slots, layered=True, op=name, ws=ws)
+        _mla_pair_scatter(kv_linear, k_pe_linear, kv_cache, k_pe_cache, slots, layered=True, op=name)
     emit_native(name, kv_linear, "sm100a row scatter (MLA flat, all layers)")
     return True
 

@@ -157,6 +157,84 @@ def _scatter(op: str, linear: list[torch.Tensor], paged: list[torch.Tensor], slo
     _native.check(rc, op)
 
 
+# Fast descriptors: plane pointers computed from a base pointer and strides (or
+# read straight off a list of uniform tensors) with no per-plane tensor views.
+# Each returns None when the layout needs the general path above.
+
+
+def _stacked_buffer_side(buf: torch.Tensor, n0: int, n1: int) -> tuple | None:
+    """``[n0, n1, T, row]`` buffer -> planes (i0, i1) in i0-major order, token rows of ``row`` elements."""
+    if not _rows_contiguous(buf, 3):
+        return None
+    e = buf.element_size()
+    s0, s1, st = buf.stride()[:3]
+    base = buf.data_ptr()
+    ptrs = [base + (i0 * s0 + i1 * s1) * e for i0 in range(n0) for i1 in range(n1)]
+    return ptrs, 1, st * e, 0, int(buf.shape[2])
+
+
+def _layer_buffer_side(buf: torch.Tensor) -> tuple | None:
+    """``[NL, T, row]`` buffer -> one plane per layer."""
+    if not _rows_contiguous(buf, 2):
+        return None
+    e = buf.element_size()
+    s0, st = buf.stride()[:2]
+    base = buf.data_ptr()
+    return [base + i * s0 * e for i in range(buf.shape[0])], 1, st * e, 0, int(buf.shape[1])
+
+
+def _stacked_cache_side(cache: torch.Tensor, plane_offsets: list[int], nb_dim: int, dtype: torch.dtype) -> tuple | None:
+    """Planes at element offsets ``plane_offsets`` of ``cache``; blocks and slots on dims ``nb_dim``, ``nb_dim+1``."""
+    if cache.dtype != dtype or not _rows_contiguous(cache, nb_dim + 2):
+        return None
+    e = cache.element_size()
+    base = cache.data_ptr()
+    st = cache.stride()
+    nb, bs = int(cache.shape[nb_dim]), int(cache.shape[nb_dim + 1])
+    return [base + o * e for o in plane_offsets], bs, st[nb_dim] * e, st[nb_dim + 1] * e, nb * bs
+
+
+def _list_cache_side(caches: list[torch.Tensor], plane_offsets: list[int], nb_dim: int, dtype: torch.dtype) -> tuple | None:
+    """Uniform list of caches (same shape, strides and ``dtype``), each giving the planes at ``plane_offsets``."""
+    first = caches[0]
+    shape, stride = first.shape, first.stride()
+    if first.dtype != dtype or not _rows_contiguous(first, nb_dim + 2):
+        return None
+    e = first.element_size()
+    ptrs = []
+    for o in plane_offsets:
+        for c in caches:
+            if c.stride() != stride or c.shape != shape or c.dtype != dtype:
+                return None
+            ptrs.append(c.data_ptr() + o * e)
+    nb, bs = int(shape[nb_dim]), int(shape[nb_dim + 1])
+    return ptrs, bs, stride[nb_dim] * e, stride[nb_dim + 1] * e, nb * bs
+
+
+def _fast_gather(op: str, paged: tuple, linear: tuple, row_bytes: int, slots: torch.Tensor, device) -> None:
+    lib = _native.load()
+    ks, code = kernel_slots(slots)
+    buf = _native.rows_pack(paged, linear)
+    base = ctypes.addressof(buf)
+    rc = lib.mak_rows_gather(base, base + 48, None, row_bytes, ks.data_ptr(), code, ks.numel(), 1,
+                             _native.stream_ptr(device))
+    _native.check(rc, op)
+
+
+def _fast_scatter(op: str, linear: tuple, paged: tuple, row_bytes: int, slots: torch.Tensor, skip_prefix: int,
+                  device) -> None:
+    if slots.numel() == 0:
+        return
+    lib = _native.load()
+    ks, code = kernel_slots(slots)
+    ws, nbytes = _native.workspace(ks.numel(), device)
+    buf = _native.rows_pack(linear, paged)
+    base = ctypes.addressof(buf)
+    rc = lib.mak_rows_scatter(base, base + 48, None, row_bytes, ks.data_ptr(), code, ks.numel(), int(skip_prefix),
+                              ws.data_ptr(), nbytes, _native.stream_ptr(device))
+    _native.check(rc, op)
+
+
 # ---------------------------------------------------------------------------
 # contract validation (musa_aiter/ops/lmcache_kv_transfer.py:323-544)
 # ---------------------------------------------------------------------------
@@ -346,9 +424,17 @@ def lmcache_kv_buffer_to_paged(
     nb, bs = int(paged_kv_cache.shape[2]), int(paged_kv_cache.shape[3])
     if not _rows_contiguous(paged_kv_cache, 4):
         raise ValueError("LMCache non-MLA paged_kv_cache token rows [NH, HS] must be contiguous")
-    paged = [paged_kv_cache[layer, kv].view(nb, bs, hidden) for kv in range(2) for layer in range(nl)]
-    linear = [kv_buffer[kv, layer] for kv in range(2) for layer in range(nl)]
-    _scatter("lmcache_kv_buffer_to_paged", linear, paged, slot_mapping, 0)
+    sl, skv = paged_kv_cache.stride()[:2]
+    offsets = [kv * skv + layer * sl for kv in range(2) for layer in range(nl)]
+    pside = _stacked_cache_side(paged_kv_cache, offsets, 2, kv_buffer.dtype)
+    lside = _stacked_buffer_side(kv_buffer, 2, nl)
+    if pside is not None and lside is not None:
+        _fast_scatter("lmcache_kv_buffer_to_paged", lside, pside, hidden * kv_buffer.element_size(), slot_mapping, 0,
+                      kv_buffer.device)
+    else:
+        paged = [paged_kv_cache[layer, kv].view(nb, bs, hidden) for kv in range(2) for layer in range(nl)]
+        linear = [kv_buffer[kv, layer] for kv in range(2) for layer in range(nl)]
+        _scatter("lmcache_kv_buffer_to_paged", linear, paged, slot_mapping, 0)
     emit_native("lmcache_kv_buffer_to_paged", kv_buffer, "sm100a row scatter (6-D cache, all layers)")
     return True
 
@@ -361,9 +447,17 @@ def lmcache_paged_to_kv_buffer(paged_kv_cache: torch.Tensor, kv_buffer: torch.Te
     nl = int(kv_buffer.shape[1])
     hidden = int(kv_buffer.shape[3])
     nb, bs = int(paged_kv_cache.shape[2]), int(paged_kv_cache.shape[3])
-    paged = [paged_kv_cache[layer, kv].reshape(nb, bs, hidden) for kv in range(2) for layer in range(nl)]
-    linear = [kv_buffer[kv, layer] for kv in range(2) for layer in range(nl)]
-    _gather("lmcache_paged_to_kv_buffer", paged, linear, slot_mapping)
+    sl, skv = paged_kv_cache.stride()[:2]
+    offsets = [kv * skv + layer * sl for kv in range(2) for layer in range(nl)]
+    pside = _stacked_cache_side(paged_kv_cache, offsets, 2, kv_buffer.dtype)
+    lside = _stacked_buffer_side(kv_buffer, 2, nl)
+    if pside is not None and lside is not None:
+        _fast_gather("lmcache_paged_to_kv_buffer", pside, lside, hidden * kv_buffer.element_size(), slot_mapping,
+                     kv_buffer.device)
+    else:
+        paged = [paged_kv_cache[layer, kv].reshape(nb, bs, hidden) for kv in range(2) for layer in range(nl)]
+        linear = [kv_buffer[kv, layer] for kv in range(2) for layer in range(nl)]
+        _gather("lmcache_paged_to_kv_buffer", paged, linear, slot_mapping)
     emit_native("lmcache_paged_to_kv_buffer", kv_buffer, "sm100a row gather (6-D cache, all layers)")
     return True
 
@@ -374,8 +468,14 @@ def lmcache_kv_buffer_to_paged_mla(kv_buffer: torch.Tensor, paged_kv_cache: torc
     _check_slot_dtype(slot_mapping, "LMCache MLA")
     require_cuda("lmcache_kv_buffer_to_paged_mla", kv_buffer, paged_kv_cache, slot_mapping)
     nl = int(kv_buffer.shape[0])
-    _scatter("lmcache_kv_buffer_to_paged_mla", [kv_buffer[i] for i in range(nl)], [paged_kv_cache[i] for i in range(nl)],
-             slot_mapping, 0)
+    pside = _stacked_cache_side(paged_kv_cache, [i * paged_kv_cache.stride(0) for i in range(nl)], 1, kv_buffer.dtype)
+    lside = _layer_buffer_side(kv_buffer)
+    if pside is not None and lside is not None:
+        _fast_scatter("lmcache_kv_buffer_to_paged_mla", lside, pside, int(kv_buffer.shape[2]) * kv_buffer.element_size(),
+                      slot_mapping, 0, kv_buffer.device)
+    else:
+        _scatter("lmcache_kv_buffer_to_paged_mla", [kv_buffer[i] for i in range(nl)],
+                 [paged_kv_cache[i] for i in range(nl)], slot_mapping, 0)
     emit_native("lmcache_kv_buffer_to_paged_mla", kv_buffer, "sm100a row scatter (MLA, all layers)")
     return True
 
@@ -386,8 +486,14 @@ def lmcache_paged_to_kv_buffer_mla(paged_kv_cache: torch.Tensor, kv_buffer: torc
     _check_slot_dtype(slot_mapping, "LMCache MLA")
     require_cuda("lmcache_paged_to_kv_buffer_mla", kv_buffer, paged_kv_cache, slot_mapping)
     nl = int(kv_buffer.shape[0])
-    _gather("lmcache_paged_to_kv_buffer_mla", [paged_kv_cache[i] for i in range(nl)], [kv_buffer[i] for i in range(nl)],
-            slot_mapping)
+    pside = _stacked_cache_side(paged_kv_cache, [i * paged_kv_cache.stride(0) for i in range(nl)], 1, kv_buffer.dtype)
+    lside = _layer_buffer_side(kv_buffer)
+    if pside is not None and lside is not None:
+        _fast_gather("lmcache_paged_to_kv_buffer_mla", pside, lside, int(kv_buffer.shape[2]) * kv_buffer.element_size(),
+                     slot_mapping, kv_buffer.device)
+    else:
+        _gather("lmcache_paged_to_kv_buffer_mla", [paged_kv_cache[i] for i in range(nl)],
+                [kv_buffer[i] for i in range(nl)], slot_mapping)
     emit_native("lmcache_paged_to_kv_buffer_mla", kv_buffer, "sm100a row gather (MLA, all layers)")
     return True
 
@@ -412,11 +518,18 @@ def lmcache_kv_paged_to_buffer(
     require_cuda("lmcache_kv_paged_to_buffer", memory_tensor, slot_mapping, *kvcaches)
     nl = len(kvcaches)
     hidden = num_heads * head_size
-    paged = [kvcaches[layer][kv].view(kvcaches[layer].shape[1], block_size, hidden) if kvcaches[layer][kv].is_contiguous()
-             else kvcaches[layer][kv].reshape(kvcaches[layer].shape[1], block_size, hidden)
-             for kv in range(2) for layer in range(nl)]
-    linear = [memory_tensor[kv, layer] for kv in range(2) for layer in range(nl)]
-    _gather("lmcache_kv_paged_to_buffer", paged, linear, slot_mapping)
+    skv = kvcaches[0].stride(0)
+    pside = _list_cache_side(kvcaches, [0, skv], 1, memory_tensor.dtype)
+    lside = _stacked_buffer_side(memory_tensor, 2, nl)
+    if pside is not None and lside is not None:
+        _fast_gather("lmcache_kv_paged_to_buffer", pside, lside, hidden * memory_tensor.element_size(), slot_mapping,
+                     memory_tensor.device)
+    else:
+        paged = [kvcaches[layer][kv].view(kvcaches[layer].shape[1], block_size, hidden) if kvcaches[layer][kv].is_contiguous()
+                 else kvcaches[layer][kv].reshape(kvcaches[layer].shape[1], block_size, hidden)
+                 for kv in range(2) for layer in range(nl)]
+        linear = [memory_tensor[kv, layer] for kv in range(2) for layer in range(nl)]
+        _gather("lmcache_kv_paged_to_buffer", paged, linear, slot_mapping)
     emit_native("lmcache_kv_paged_to_buffer", memory_tensor, "sm100a row gather (layer list, all layers, one launch)")
     return True
 
@@ -429,15 +542,21 @@ def _list_buffer_to_paged(memory_tensor, kvcaches, slot_mapping, skip_prefix_n_t
     require_cuda("lmcache_kv_buffer_to_paged", memory_tensor, slot_mapping, *kvcaches)
     nl = len(kvcaches)
     hidden = num_heads * head_size
-    paged = []
-    for kv in range(2):
-        for layer in range(nl):
-            plane = kvcaches[layer][kv]
-            if not _rows_contiguous(plane, 2):
-                raise ValueError("LMCache list non-MLA kvcache token rows must be contiguous")
-            paged.append(plane.view(plane.shape[0], block_size, hidden))
-    linear = [memory_tensor[kv, layer] for kv in range(2) for layer in range(nl)]
-    _scatter("lmcache_kv_buffer_to_paged", linear, paged, slot_mapping, skip_prefix_n_tokens)
+    pside = _list_cache_side(kvcaches, [0, kvcaches[0].stride(0)], 1, memory_tensor.dtype)
+    lside = _stacked_buffer_side(memory_tensor, 2, nl)
+    if pside is not None and lside is not None:
+        _fast_scatter("lmcache_kv_buffer_to_paged", lside, pside, hidden * memory_tensor.element_size(), slot_mapping,
+                      skip_prefix_n_tokens, memory_tensor.device)
+    else:
+        paged = []
+        for kv in range(2):
+            for layer in range(nl):
+                plane = kvcaches[layer][kv]
+                if not _rows_contiguous(plane, 2):
+                    raise ValueError("LMCache list non-MLA kvcache token rows must be contiguous")
+                paged.append(plane.view(plane.shape[0], block_size, hidden))
+        linear = [memory_tensor[kv, layer] for kv in range(2) for layer in range(nl)]
+        _scatter("lmcache_kv_buffer_to_paged", linear, paged, slot_mapping, skip_prefix_n_tokens)
     emit_native("lmcache_kv_buffer_to_paged", memory_tensor, "sm100a row scatter (layer list, all layers, one launch)")
     return True
 
@@ -459,14 +578,20 @@ def lmcache_kv_buffer_to_paged_two_x_nl(
     require_cuda("lmcache_kv_buffer_to_paged_two_x_nl", memory_tensor, slot_mapping, *kvcaches[0], *kvcaches[1])
     nl = len(kvcaches[0])
     hidden = num_heads * head_size
-    paged = []
-    for kv in range(2):
-        for cache in kvcaches[kv]:
-            if not _rows_contiguous(cache, 2):
-                raise ValueError("LMCache TWO_X_NL_X_NB_BS_NH_HS cache token rows must be contiguous")
-            paged.append(cache.view(cache.shape[0], block_size, hidden))
-    linear = [memory_tensor[kv, layer] for kv in range(2) for layer in range(nl)]
-    _scatter("lmcache_kv_buffer_to_paged_two_x_nl", linear, paged, slot_mapping, skip_prefix_n_tokens)
+    pside = _list_cache_side(kvcaches[0] + kvcaches[1], [0], 0, memory_tensor.dtype)
+    lside = _stacked_buffer_side(memory_tensor, 2, nl)
+    if pside is not None and lside is not None:
+        _fast_scatter("lmcache_kv_buffer_to_paged_two_x_nl", lside, pside, hidden * memory_tensor.element_size(),
+                      slot_mapping, skip_prefix_n_tokens, memory_tensor.device)
+    else:
+        paged = []
+        for kv in range(2):
+            for cache in kvcaches[kv]:
+                if not _rows_contiguous(cache, 2):
+                    raise ValueError("LMCache TWO_X_NL_X_NB_BS_NH_HS cache token rows must be contiguous")
+                paged.append(cache.view(cache.shape[0], block_size, hidden))
+        linear = [memory_tensor[kv, layer] for kv in range(2) for layer in range(nl)]
+        _scatter("lmcache_kv_buffer_to_paged_two_x_nl", linear, paged, slot_mapping, skip_prefix_n_tokens)
     emit_native("lmcache_kv_buffer_to_paged_two_x_nl", memory_tensor, "sm100a row scatter (2 x NL planes, one launch)")
     return True
 
@@ -484,13 +609,19 @@ def lmcache_kv_paged_to_buffer_two_x_nl(
     require_cuda("lmcache_kv_paged_to_buffer_two_x_nl", memory_tensor, slot_mapping, *kvcaches[0], *kvcaches[1])
     nl = len(kvcaches[0])
     hidden = num_heads * head_size
-    paged = []
-    for kv in range(2):
-        for cache in kvcaches[kv]:
-            paged.append(cache.view(cache.shape[0], block_size, hidden) if _rows_contiguous(cache, 2)
-                         else cache.reshape(cache.shape[0], block_size, hidden))
-    linear = [memory_tensor[kv, layer] for kv in range(2) for layer in range(nl)]
-    _gather("lmcache_kv_paged_to_buffer_two_x_nl", paged, linear, slot_mapping)
+    pside = _list_cache_side(kvcaches[0] + kvcaches[1], [0], 0, memory_tensor.dtype)
+    lside = _stacked_buffer_side(memory_tensor, 2, nl)
+    if pside is not None and lside is not None:
+        _fast_gather("lmcache_kv_paged_to_buffer_two_x_nl", pside, lside, hidden * memory_tensor.element_size(),
+                     slot_mapping, memory_tensor.device)
+    else:
+        paged = []
+        for kv in range(2):
+            for cache in kvcaches[kv]:
+                paged.append(cache.view(cache.shape[0], block_size, hidden) if _rows_contiguous(cache, 2)
+                             else cache.reshape(cache.shape[0], block_size, hidden))
+        linear = [memory_tensor[kv, layer] for kv in range(2) for layer in range(nl)]
+        _gather("lmcache_kv_paged_to_buffer_two_x_nl", paged, linear, slot_mapping)
     emit_native("lmcache_kv_paged_to_buffer_two_x_nl", memory_tensor, "sm100a row gather (2 x NL planes, one launch)")
     return True
 
@@ -511,8 +642,14 @@ def lmcache_mla_buffer_to_paged(
     for c in kvcaches:
         if not _rows_contiguous(c, 2):
             raise ValueError("LMCache list MLA kvcache token rows must be contiguous")
-    _scatter("lmcache_mla_buffer_to_paged", [memory_tensor[0, i] for i in range(len(kvcaches))], list(kvcaches),
-             slot_mapping, skip_prefix_n_tokens)
+    pside = _list_cache_side(list(kvcaches), [0], 0, memory_tensor.dtype)
+    lside = _stacked_buffer_side(memory_tensor, 1, len(kvcaches))
+    if pside is not None and lside is not None:
+        _fast_scatter("lmcache_mla_buffer_to_paged", lside, pside, int(memory_tensor.shape[3]) * memory_tensor.element_size(),
+                      slot_mapping, skip_prefix_n_tokens, memory_tensor.device)
+    else:
+        _scatter("lmcache_mla_buffer_to_paged", [memory_tensor[0, i] for i in range(len(kvcaches))], list(kvcaches),
+                 slot_mapping, skip_prefix_n_tokens)
     emit_native("lmcache_mla_buffer_to_paged", memory_tensor, "sm100a row scatter (MLA list, one launch)")
     return True
 
@@ -528,7 +665,14 @@ def lmcache_mla_paged_to_buffer(
     _validate_mla_list_contract(memory_tensor, kvcaches, slot_mapping, block_size, head_size)
     _check_slot_dtype(slot_mapping, "LMCache list MLA")
     require_cuda("lmcache_mla_paged_to_buffer", memory_tensor, slot_mapping, *kvcaches)
-    _gather("lmcache_mla_paged_to_buffer", list(kvcaches), [memory_tensor[0, i] for i in range(len(kvcaches))], slot_mapping)
+    pside = _list_cache_side(list(kvcaches), [0], 0, memory_tensor.dtype)
+    lside = _stacked_buffer_side(memory_tensor, 1, len(kvcaches))
+    if pside is not None and lside is not None:
+        _fast_gather("lmcache_mla_paged_to_buffer", pside, lside, int(memory_tensor.shape[3]) * memory_tensor.element_size(),
+                     slot_mapping, memory_tensor.device)
+    else:
+        _gather("lmcache_mla_paged_to_buffer", list(kvcaches), [memory_tensor[0, i] for i in range(len(kvcaches))],
+                slot_mapping)
     emit_native("lmcache_mla_paged_to_buffer", memory_tensor, "sm100a row gather (MLA list, one launch)")
     return True
 

@@ -58,7 +58,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-requests", type=int, default=8, help="requests in the bounded CPU sample")
     ap.add_argument("--workload", default="cfg2",
-                    choices=("cfg2", "cfg1", "cfg1-tile", "cfg2-tile", "cfg3-e4m3", "cfg3-e5m2", "cfg4", "cfg5"),
+                    choices=("cfg2", "cfg1", "cfg1-tile", "cfg2-tile", "cfg3-e4m3", "cfg3-e5m2", "cfg4", "cfg5",
+                             "cfg5-fp8"),
                     help="cfg2 (default) is the headline; the others measure the remaining configs")
     ap.add_argument("--tokens", type=int, default=8192, help="cfg3 batch tokens (256 decode / 8192 prefill)")
     return ap.parse_args()
@@ -602,6 +603,28 @@ def setup_workload(args, dev, rank):
         cfg = {"workload": "cfg5: MLA flat caches [8,16384,64,512]+[8,16384,64,64] bf16 (one GPU's shard of 61 layers), per-request gather + scatter",
                "requests": nreq, "tokens": tot, "num_blocks": nb}
         return cfg, 4 * nl * tot * (kvd + ped) * 2, step, "rows_kernel (MLA latent + rope rows)"
+    if w == "cfg5-fp8":
+        nl, nb, bs, kvd, ped = 8, args.blocks or 16384, 64, 512, 64
+        g2 = torch.Generator().manual_seed(2)
+        nreq = args.requests
+        lens = torch.randint(512, 16385, (nreq,), generator=g2).tolist()
+        per_req = [s.to(dev) for s in _fresh_block_slots(lens, nb, bs)]
+        row = ma.mla_fp8_row_bytes(kvd, ped)
+        cache = torch.zeros((nl, nb, bs, row), dtype=torch.uint8, device=dev)
+        kv_full = torch.empty((nl, max(lens), kvd), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        pe_full = torch.empty((nl, max(lens), ped), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        out_kv = torch.empty_like(kv_full)
+        out_pe = torch.empty_like(pe_full)
+
+        def step():
+            for sl, n in zip(per_req, lens):
+                ma.kv_mla_linear_to_paged_fp8_rows(kv_full[:, :n], pe_full[:, :n], cache, sl)
+                ma.kv_paged_fp8_rows_to_mla_linear(cache, sl, out_kv=out_kv[:, :n], out_k_pe=out_pe[:, :n])
+        tot = sum(lens)
+        cfg = {"workload": "cfg5-fp8: MLA latent+rope bf16 [8,T,512]+[8,T,64] <-> FP8 rows [8,16384,64,656] "
+                           "(E4M3, per-128 group scales), per-request fused quantise-scatter + gather-dequantise",
+               "requests": nreq, "tokens": tot, "num_blocks": nb}
+        return cfg, 2 * nl * tot * (2 * (kvd + ped) + row), step, "mla_fp8_store_kernel / mla_fp8_load_kernel"
     raise ValueError(w)
 
 
@@ -663,8 +686,8 @@ def run_workload(args) -> None:
 def main():
     args = parse_args()
     if args.requests is None:
-        args.requests = {"cfg4": 128, "cfg5": 256}.get(args.workload, 64)
-    if args.blocks is None and (args.impl == "reference" or args.workload not in ("cfg4", "cfg5")):
+        args.requests = {"cfg4": 128, "cfg5": 256, "cfg5-fp8": 256}.get(args.workload, 64)
+    if args.blocks is None and (args.impl == "reference" or args.workload not in ("cfg4", "cfg5", "cfg5-fp8")):
         args.blocks = 32768
     if args.impl == "reference":
         run_reference(args)

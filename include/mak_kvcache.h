@@ -375,6 +375,53 @@ MAK_API int mak_cachegen_encode(const void* x, int32_t dtype, int64_t n, const f
 MAK_API int mak_cachegen_decode(const uint8_t* codes, int64_t n, const void* codebook, int32_t codebook_dtype,
                                 int32_t num_bins, void* out, int32_t out_dtype, void* stream);
 
+/* ---- MLA FP8 rows with per-group scales ----------------------------------- */
+
+/*
+ * MLA latent + rope token rows of one or more layers:
+ *   kv[l][t][0..kv_dim)  and  pe[l][t][0..pe_dim), element strides given,
+ *   innermost stride 1, dtype MAK_DT_F16 or MAK_DT_BF16 (both tensors).
+ */
+typedef struct mak_mla_linear_desc {
+  void* kv;
+  void* pe;
+  int64_t num_layers;
+  int64_t num_tokens;
+  int64_t kv_dim;          /* 256, 512 or 1024: groups of 128 */
+  int64_t pe_dim;          /* multiple of 8, at most 256 */
+  int64_t kv_stride_layer; /* elements */
+  int64_t kv_stride_token;
+  int64_t pe_stride_layer;
+  int64_t pe_stride_token;
+  int32_t dtype;
+  int32_t reserved;
+} mak_mla_linear_desc;
+
+/*
+ * FP8 MLA cache row, one per token and layer (the DeepSeek MLA FP8 row):
+ *   [kv_dim FP8 codes][kv_dim/128 fp32 group scales][pe_dim rope elements, input dtype]
+ * e.g. 512 + 16 + 128 = 656 bytes.  Group g's scale is the amax of the finite
+ * |x| among its 128 values / fp8_max in fp32 (fp8_max 448 for E4M3, 57344 for
+ * E5M2), so every stored scale is finite,
+ * and each value is encoded with the musa-aiter FP8 rule as x / scale
+ * (musa_aiter/ops/kv_transfer.py:2161-2183; an all-zero group stores scale 0 and
+ * zero codes).  No reference counterpart: the reference only moves such rows as
+ * opaque bytes (kv_copy_paged_rows_layer_table, ops/kv_transfer.py:4588-4616;
+ * lmcache_kv_strided_block_transfer mode 1).  `cache` has one plane per layer,
+ * row width mak_mla_fp8_row_bytes(kv_dim, pe_dim).
+ *
+ * store: quantise and scatter, last writer wins for duplicate slots, negative or
+ *        out-of-range slots skipped; workspace = mak_scatter_workspace_bytes(n).
+ * load:  gather and dequantise (code * scale, RNE to the output dtype); rows of
+ *        negative or out-of-range slots become zeros.
+ */
+MAK_API int64_t mak_mla_fp8_row_bytes(int64_t kv_dim, int64_t pe_dim);
+MAK_API int mak_mla_fp8_rows_store(const mak_mla_linear_desc* lin, const mak_rows_desc* cache, const void* slots,
+                                   int32_t slot_dtype, int32_t fp8_format, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+MAK_API int mak_mla_fp8_rows_load(const mak_rows_desc* cache, const mak_mla_linear_desc* lin, const void* slots,
+                                  int32_t slot_dtype, int32_t fp8_format, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

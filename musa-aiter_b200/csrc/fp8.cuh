@@ -1,0 +1,131 @@
+// Element conversions and the musa-aiter FP8 codec shared by the tile engine
+// and the MLA FP8 row kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+#include "mak_kvcache.h"
+
+namespace mak {
+
+// ---- element conversions (round-to-nearest-even everywhere) ---------------
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+template <typename T>
+__device__ __forceinline__ T zero_of() {
+  T z;
+  memset(&z, 0, sizeof(T));
+  return z;
+}
+
+// ---- musa-aiter FP8 codec ---------------------------------------------------
+// Encoder semantics (musa_aiter/ops/kv_transfer.py:2161-2183): w = x / scale in
+// fp32; non-finite -> zero carrying the sign of (w < 0); |w| below the smallest
+// normal -> signed zero; |w| clamped to (2 - 2^-m) * 2^emax (480 for E4M3 with
+// exponent field 15 / mantissa 7, 114688 for E5M2 with exponent field 31); the
+// mantissa rounds half-to-even.  Inside the formats' standard finite range this
+// is exactly cvt.rn.satfinite; the extra top codes are handled explicitly.
+__device__ __forceinline__ uint32_t cvt_e4m3(float a) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(r) : "f"(a));
+  return r & 0xFFu;
+}
+__device__ __forceinline__ uint32_t cvt_e5m2(float a) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %1;" : "=h"(r) : "f"(a));
+  return r & 0xFFu;
+}
+
+template <int F>
+__device__ __forceinline__ uint8_t fp8_encode(float w) {
+  const uint32_t sign = (w < 0.f) ? 0x80u : 0u;
+  const float a = fabsf(w);
+  if (!(a <= 3.40282346638528859812e+38f)) return static_cast<uint8_t>(sign);  // inf / nan
+  if (F == MAK_FP8_E4M3) {
+    if (a < 0.015625f) return static_cast<uint8_t>(sign);  // below 2^-6
+    // 464 is the midpoint of 448 (mantissa 6) and 480 (mantissa 7): ties go to 448.
+    if (a > 464.f) return static_cast<uint8_t>(sign | 0x7Fu);
+    return static_cast<uint8_t>(sign | cvt_e4m3(a));
+  } else {
+    if (a < 6.103515625e-05f) return static_cast<uint8_t>(sign);  // below 2^-14
+    if (a >= 61440.f) {
+      // Exponent field 31: scale by 2^-16 (exact) into field 15, add 16 back.
+      const float y = fminf(a, 114688.f) * 1.52587890625e-05f;
+      return static_cast<uint8_t>(sign | (cvt_e5m2(y) + 0x40u));
+    }
+    return static_cast<uint8_t>(sign | cvt_e5m2(a));
+  }
+}
+
+// Two values at once, same rule as fp8_encode: one paired conversion, the
+// special ranges chosen per value with selects.  Returns code(w0) | code(w1) << 8.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float hi, float lo) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t cvt_e5m2x2(float hi, float lo) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <int F>
+__device__ __forceinline__ uint32_t fp8_encode2(float w0, float w1) {
+  const uint32_t s0 = (w0 < 0.f) ? 0x80u : 0u;
+  const uint32_t s1 = (w1 < 0.f) ? 0x80u : 0u;
+  const float a0 = fabsf(w0), a1 = fabsf(w1);
+  const bool fin0 = a0 <= 3.40282346638528859812e+38f, fin1 = a1 <= 3.40282346638528859812e+38f;
+  uint32_t c0, c1;
+  if (F == MAK_FP8_E4M3) {
+    const uint32_t c = cvt_e4m3x2(a1, a0);
+    c0 = (a0 > 464.f) ? 0x7Fu : (c & 0xFFu);
+    c1 = (a1 > 464.f) ? 0x7Fu : (c >> 8);
+    c0 = (fin0 && a0 >= 0.015625f) ? c0 : 0u;
+    c1 = (fin1 && a1 >= 0.015625f) ? c1 : 0u;
+  } else {
+    const bool top0 = a0 >= 61440.f, top1 = a1 >= 61440.f;
+    const float y0 = top0 ? fminf(a0, 114688.f) * 1.52587890625e-05f : a0;
+    const float y1 = top1 ? fminf(a1, 114688.f) * 1.52587890625e-05f : a1;
+    const uint32_t c = cvt_e5m2x2(y1, y0);
+    c0 = (c & 0xFFu) + (top0 ? 0x40u : 0u);
+    c1 = (c >> 8) + (top1 ? 0x40u : 0u);
+    c0 = (fin0 && a0 >= 6.103515625e-05f) ? c0 : 0u;
+    c1 = (fin1 && a1 >= 6.103515625e-05f) ? c1 : 0u;
+  }
+  return (s0 | c0) | ((s1 | c1) << 8);
+}
+
+// Decoder (musa_aiter/ops/kv_transfer.py:2186-2200): exponent field 0 -> 0,
+// otherwise (1 + m / 2^mb) * 2^(e - bias), all codes finite; built bit-exactly.
+template <int F>
+__device__ __forceinline__ float fp8_decode(uint32_t code) {
+  constexpr int mb = (F == MAK_FP8_E4M3) ? 3 : 2;
+  constexpr int bias = (F == MAK_FP8_E4M3) ? 7 : 15;
+  const uint32_t e = (code >> mb) & ((1u << (7 - mb)) - 1u);
+  const uint32_t m = code & ((1u << mb) - 1u);
+  uint32_t bits = e ? (((e - bias + 127u) << 23) | (m << (23 - mb))) : 0u;
+  bits |= (code & 0x80u) << 24;
+  return __uint_as_float(bits);
+}
+
+}  // namespace mak

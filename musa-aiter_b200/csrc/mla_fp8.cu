@@ -1,0 +1,359 @@
+// MLA FP8 rows with per-group scales: the latent part of a token (kv_dim
+// values) is quantised in groups of 128 with scale = amax / fp8_max (amax over
+// the group's finite values) and stored
+// next to its scales and the unquantised rope part, one row per token and
+// layer:  [kv_dim codes][kv_dim/128 fp32 scales][pe_dim rope elements].
+//
+// One warp per (token, layer): lane l owns E = kv_dim / 32 consecutive values
+// (16-byte loads), the group amax is a shuffle reduction over the 128 / E lanes
+// of a group, the codes leave as one E-byte store per lane.  The element codec
+// is the musa-aiter reference rule (fp8.cuh).  grid = (token warps, layers).
+#include <algorithm>
+
+#include "common.cuh"
+#include "fp8.cuh"
+
+namespace mak {
+
+constexpr int kMlaPlanes = 256;  // layers per launch
+constexpr int kMlaThreads = 256;
+
+struct MlaLaunch {
+  uint64_t cache[kMlaPlanes];
+  const unsigned char* kv;
+  const unsigned char* pe;
+  int64_t kv_sl, kv_st, pe_sl, pe_st;  // byte strides
+  int64_t rows_per_block, block_stride, row_stride, num_rows;
+  const void* idx;
+  int64_t num_tokens;
+  int32_t idx64;
+  int32_t lg_rows;    // log2(rows_per_block) or -1
+  int32_t kv_dim;
+  int32_t pe_bytes;   // rope bytes per row (multiple of 8)
+};
+
+__device__ __forceinline__ int64_t mla_row_offset(const MlaLaunch& p, int64_t r) {
+  if (p.rows_per_block == 1) return r * p.block_stride;
+  if (p.lg_rows >= 0) return (r >> p.lg_rows) * p.block_stride + (r & (p.rows_per_block - 1)) * p.row_stride;
+  int64_t b, o;
+  split_slot(r, p.rows_per_block, &b, &o);
+  return b * p.block_stride + o * p.row_stride;
+}
+
+// 16-bit element <-> fp32 through raw bits (keeps values in registers).
+template <typename T>
+__device__ __forceinline__ float bits_to_f32(uint32_t u);
+template <>
+__device__ __forceinline__ float bits_to_f32<__nv_bfloat16>(uint32_t u) { return __uint_as_float(u << 16); }
+template <>
+__device__ __forceinline__ float bits_to_f32<__half>(uint32_t u) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(u)));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t f32_to_bits(float x) {
+  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(x)));
+}
+template <>
+__device__ __forceinline__ uint32_t f32_to_bits<__half>(float x) {
+  return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(x)));
+}
+
+// Two fp32 values -> two RNE 16-bit elements in one conversion (lo = a, hi = b).
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  const __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+template <int F>
+__device__ __forceinline__ float fp8_max_of() {
+  return F == MAK_FP8_E4M3 ? 448.f : 57344.f;
+}
+
+// E bytes (8, 16 or 32) from/to a row, 8- or 16-byte accesses.
+template <int E>
+struct Bytes {
+  uint32_t w[E / 4];
+};
+
+template <int E>
+__device__ __forceinline__ void store_bytes(unsigned char* dst, const Bytes<E>& b) {
+  if (E == 8) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(b.w[0], b.w[1]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < E / 16; ++k)
+      reinterpret_cast<uint4*>(dst)[k] = make_uint4(b.w[4 * k], b.w[4 * k + 1], b.w[4 * k + 2], b.w[4 * k + 3]);
+  }
+}
+
+template <int E>
+__device__ __forceinline__ Bytes<E> load_bytes(const unsigned char* src) {
+  Bytes<E> b;
+  if (E == 8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(src);
+    b.w[0] = v.x;
+    b.w[1] = v.y;
+  } else {
+#pragma unroll
+    for (int k = 0; k < E / 16; ++k) {
+      const uint4 v = reinterpret_cast<const uint4*>(src)[k];
+      b.w[4 * k] = v.x;
+      b.w[4 * k + 1] = v.y;
+      b.w[4 * k + 2] = v.z;
+      b.w[4 * k + 3] = v.w;
+    }
+  }
+  return b;
+}
+
+template <typename T, int F, int E>
+__global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid_constant__ MlaLaunch p) {
+  constexpr int kLanesPerGroup = 128 / E;
+  const int lane = threadIdx.x & 31;
+  const int layer = blockIdx.y;
+  const int64_t step = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  unsigned char* plane = reinterpret_cast<unsigned char*>(p.cache[layer]);
+  const unsigned char* kv_layer = p.kv + layer * p.kv_sl;
+  const unsigned char* pe_layer = p.pe + layer * p.pe_sl;
+  for (int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < p.num_tokens; t += step) {
+    const int64_t dr = load_index(p.idx, p.idx64, t);
+    if (dr < 0 || dr >= p.num_rows) continue;
+    unsigned char* row = plane + mla_row_offset(p, dr);
+    // latent values of this lane
+    const uint4* src = reinterpret_cast<const uint4*>(kv_layer + t * p.kv_st + lane * E * 2);
+    float x[E];
+#pragma unroll
+    for (int k = 0; k < E / 8; ++k) {
+      const uint4 v = src[k];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[8 * k + 2 * j] = bits_to_f32<T>(w[j] & 0xFFFFu);
+        x[8 * k + 2 * j + 1] = bits_to_f32<T>(w[j] >> 16);
+      }
+    }
+    float amax = 0.f;  // over the finite values only: every stored scale is finite
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      const float a = fabsf(x[j]);
+      if (a <= 3.40282346638528859812e+38f) amax = fmaxf(amax, a);
+    }
+#pragma unroll
+    for (int o = 1; o < kLanesPerGroup; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = __fdiv_rn(amax, fp8_max_of<F>());
+    Bytes<E> codes;
+#pragma unroll
+    for (int j = 0; j < E / 4; ++j) {
+      const uint32_t lo = fp8_encode2<F>(__fdiv_rn(x[4 * j], scale), __fdiv_rn(x[4 * j + 1], scale));
+      const uint32_t hi = fp8_encode2<F>(__fdiv_rn(x[4 * j + 2], scale), __fdiv_rn(x[4 * j + 3], scale));
+      codes.w[j] = lo | (hi << 16);
+    }
+    store_bytes<E>(row + lane * E, codes);
+    if ((lane % kLanesPerGroup) == 0) reinterpret_cast<float*>(row + p.kv_dim)[lane / kLanesPerGroup] = scale;
+    // rope part, 8 bytes per lane
+    unsigned char* rope = row + p.kv_dim + (p.kv_dim / 128) * 4;
+    const unsigned char* pe_src = pe_layer + t * p.pe_st;
+    for (int b = lane * 8; b < p.pe_bytes; b += 256)
+      *reinterpret_cast<uint2*>(rope + b) = *reinterpret_cast<const uint2*>(pe_src + b);
+  }
+}
+
+template <typename T, int F, int E>
+__global__ void __launch_bounds__(kMlaThreads) mla_fp8_load_kernel(const __grid_constant__ MlaLaunch p,
+                                                                   unsigned char* kv_out, unsigned char* pe_out) {
+  constexpr int kLanesPerGroup = 128 / E;
+  const int lane = threadIdx.x & 31;
+  const int layer = blockIdx.y;
+  const int64_t step = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const unsigned char* plane = reinterpret_cast<const unsigned char*>(p.cache[layer]);
+  unsigned char* kv_layer = kv_out + layer * p.kv_sl;
+  unsigned char* pe_layer = pe_out + layer * p.pe_sl;
+  for (int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < p.num_tokens; t += step) {
+    const int64_t sr = load_index(p.idx, p.idx64, t);
+    const bool have = sr >= 0 && sr < p.num_rows;
+    uint4* dst = reinterpret_cast<uint4*>(kv_layer + t * p.kv_st + lane * E * 2);
+    unsigned char* pe_dst = pe_layer + t * p.pe_st;
+    if (!have) {
+#pragma unroll
+      for (int k = 0; k < E / 8; ++k) dst[k] = make_uint4(0u, 0u, 0u, 0u);
+      for (int b = lane * 8; b < p.pe_bytes; b += 256) *reinterpret_cast<uint2*>(pe_dst + b) = make_uint2(0u, 0u);
+      continue;
+    }
+    const unsigned char* row = plane + mla_row_offset(p, sr);
+    const Bytes<E> codes = load_bytes<E>(row + lane * E);
+    const float scale = reinterpret_cast<const float*>(row + p.kv_dim)[lane / kLanesPerGroup];
+#pragma unroll
+    for (int k = 0; k < E / 8; ++k) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i0 = 8 * k + 2 * j;
+        const uint32_t c0 = (codes.w[i0 >> 2] >> (8 * (i0 & 3))) & 0xFFu;
+        const uint32_t c1 = (codes.w[(i0 + 1) >> 2] >> (8 * ((i0 + 1) & 3))) & 0xFFu;
+        w[j] = pack2<T>(__fmul_rn(fp8_decode<F>(c0), scale), __fmul_rn(fp8_decode<F>(c1), scale));
+      }
+      dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    const unsigned char* rope = row + p.kv_dim + (p.kv_dim / 128) * 4;
+    for (int b = lane * 8; b < p.pe_bytes; b += 256)
+      *reinterpret_cast<uint2*>(pe_dst + b) = *reinterpret_cast<const uint2*>(rope + b);
+  }
+}
+
+static int64_t mla_row_bytes(int64_t kv_dim, int64_t pe_dim, int elem_bytes) {
+  return kv_dim + (kv_dim / 128) * 4 + pe_dim * elem_bytes;
+}
+
+// Shared argument checks; fills everything in `L` except cache pointers and idx.
+static int mla_prepare(const mak_mla_linear_desc* lin, const mak_rows_desc* cache, int32_t fp8_format, const char* name,
+                       MlaLaunch* L) {
+  if (lin == nullptr || cache == nullptr) return fail(MAK_E_INVALID, "%s: NULL descriptor", name);
+  if (lin->dtype != MAK_DT_BF16 && lin->dtype != MAK_DT_F16)
+    return fail(MAK_E_UNSUPPORTED, "%s: linear dtype must be float16 or bfloat16", name);
+  if (fp8_format != MAK_FP8_E4M3 && fp8_format != MAK_FP8_E5M2) return fail(MAK_E_INVALID, "%s: bad fp8 format", name);
+  if (lin->kv_dim != 256 && lin->kv_dim != 512 && lin->kv_dim != 1024)
+    return fail(MAK_E_UNSUPPORTED, "%s: kv_dim must be 256, 512 or 1024 (got %lld)", name, (long long)lin->kv_dim);
+  if (lin->pe_dim < 0 || lin->pe_dim % 8 != 0 || lin->pe_dim > 256)
+    return fail(MAK_E_UNSUPPORTED, "%s: pe_dim must be a multiple of 8 in [0, 256]", name);
+  if (lin->num_layers < 0 || lin->num_tokens < 0) return fail(MAK_E_INVALID, "%s: negative extents", name);
+  if (cache->num_planes != lin->num_layers)
+    return fail(MAK_E_INVALID, "%s: cache has %lld planes for %lld layers", name, (long long)cache->num_planes,
+                (long long)lin->num_layers);
+  if (cache->num_planes > 0 && cache->plane_ptrs == nullptr) return fail(MAK_E_INVALID, "%s: plane_ptrs is NULL", name);
+  if (cache->rows_per_block <= 0 || cache->num_rows < 0 || cache->block_stride < 0 || cache->row_stride < 0)
+    return fail(MAK_E_INVALID, "%s: bad cache row geometry", name);
+  const int e = 2;
+  const int64_t need = mla_row_bytes(lin->kv_dim, lin->pe_dim, e);
+  if ((cache->rows_per_block == 1 ? cache->block_stride : cache->row_stride) < need && cache->num_rows > 1)
+    return fail(MAK_E_INVALID, "%s: cache rows are narrower than the %lld-byte FP8 row", name, (long long)need);
+  const uint64_t kv_bits = reinterpret_cast<uintptr_t>(lin->kv) | static_cast<uint64_t>(lin->kv_stride_layer * e) |
+                           static_cast<uint64_t>(lin->kv_stride_token * e);
+  const uint64_t pe_bits = reinterpret_cast<uintptr_t>(lin->pe) | static_cast<uint64_t>(lin->pe_stride_layer * e) |
+                           static_cast<uint64_t>(lin->pe_stride_token * e);
+  if ((kv_bits & 15u) != 0) return fail(MAK_E_UNSUPPORTED, "%s: latent rows must be 16-byte aligned", name);
+  if (lin->pe_dim > 0 && (pe_bits & 7u) != 0) return fail(MAK_E_UNSUPPORTED, "%s: rope rows must be 8-byte aligned", name);
+  uint64_t c_bits = static_cast<uint64_t>(cache->block_stride) |
+                    (cache->rows_per_block > 1 ? static_cast<uint64_t>(cache->row_stride) : 0u);
+  for (int64_t q = 0; q < cache->num_planes; ++q) c_bits |= cache->plane_ptrs[q];
+  const uint64_t c_align = lin->kv_dim >= 512 ? 15u : 7u;
+  if ((c_bits & c_align) != 0)
+    return fail(MAK_E_UNSUPPORTED, "%s: cache rows must be %d-byte aligned", name, static_cast<int>(c_align + 1));
+  memset(L, 0, sizeof(*L));
+  L->kv = static_cast<const unsigned char*>(lin->kv);
+  L->pe = static_cast<const unsigned char*>(lin->pe);
+  L->kv_sl = lin->kv_stride_layer * e;
+  L->kv_st = lin->kv_stride_token * e;
+  L->pe_sl = lin->pe_stride_layer * e;
+  L->pe_st = lin->pe_stride_token * e;
+  L->rows_per_block = cache->rows_per_block;
+  L->block_stride = cache->block_stride;
+  L->row_stride = cache->row_stride;
+  L->num_rows = cache->num_rows;
+  int lg = -1;
+  if ((cache->rows_per_block & (cache->rows_per_block - 1)) == 0) {
+    lg = 0;
+    while ((int64_t{1} << lg) < cache->rows_per_block) ++lg;
+  }
+  L->lg_rows = lg;
+  L->num_tokens = lin->num_tokens;
+  L->kv_dim = static_cast<int32_t>(lin->kv_dim);
+  L->pe_bytes = static_cast<int32_t>(lin->pe_dim * e);
+  return MAK_OK;
+}
+
+template <bool STORE, typename T, int F, int E>
+static int launch_mla(MlaLaunch& L, int64_t layers, unsigned char* kv_out, unsigned char* pe_out, cudaStream_t st,
+                      const mak_rows_desc* cache) {
+  const void* kern = STORE ? reinterpret_cast<const void*>(mla_fp8_store_kernel<T, F, E>)
+                           : reinterpret_cast<const void*>(mla_fp8_load_kernel<T, F, E>);
+  const int64_t resident = static_cast<int64_t>(blocks_per_sm(kern, kMlaThreads, 0)) * sm_count();
+  for (int64_t l0 = 0; l0 < layers; l0 += kMlaPlanes) {
+    const int64_t nl = std::min<int64_t>(kMlaPlanes, layers - l0);
+    for (int64_t q = 0; q < nl; ++q) L.cache[q] = cache->plane_ptrs[l0 + q];
+    const int64_t want = (L.num_tokens + (kMlaThreads / 32) - 1) / (kMlaThreads / 32);
+    const int64_t cap = std::max<int64_t>(1, (4 * resident + nl - 1) / nl);
+    const dim3 grid(static_cast<unsigned>(std::min(want, cap)), static_cast<unsigned>(nl));
+    MlaLaunch P = L;
+    P.kv = L.kv + l0 * L.kv_sl;
+    P.pe = L.pe + l0 * L.pe_sl;
+    if (STORE) {
+      mla_fp8_store_kernel<T, F, E><<<grid, kMlaThreads, 0, st>>>(P);
+    } else {
+      mla_fp8_load_kernel<T, F, E><<<grid, kMlaThreads, 0, st>>>(P, kv_out + l0 * L.kv_sl, pe_out + l0 * L.pe_sl);
+    }
+    const int rc = launch_status(STORE ? "mla_fp8_store_kernel" : "mla_fp8_load_kernel");
+    if (rc) return rc;
+  }
+  return MAK_OK;
+}
+
+template <bool STORE, typename T, int F>
+static int dispatch_e(MlaLaunch& L, const mak_mla_linear_desc* lin, const mak_rows_desc* cache, cudaStream_t st) {
+  unsigned char* kv_out = static_cast<unsigned char*>(lin->kv);
+  unsigned char* pe_out = static_cast<unsigned char*>(lin->pe);
+  switch (lin->kv_dim) {
+    case 256: return launch_mla<STORE, T, F, 8>(L, lin->num_layers, kv_out, pe_out, st, cache);
+    case 512: return launch_mla<STORE, T, F, 16>(L, lin->num_layers, kv_out, pe_out, st, cache);
+    default: return launch_mla<STORE, T, F, 32>(L, lin->num_layers, kv_out, pe_out, st, cache);
+  }
+}
+
+template <bool STORE>
+static int dispatch(MlaLaunch& L, const mak_mla_linear_desc* lin, const mak_rows_desc* cache, int32_t fmt,
+                    cudaStream_t st) {
+  if (lin->dtype == MAK_DT_BF16) {
+    return fmt == MAK_FP8_E4M3 ? dispatch_e<STORE, __nv_bfloat16, MAK_FP8_E4M3>(L, lin, cache, st)
+                               : dispatch_e<STORE, __nv_bfloat16, MAK_FP8_E5M2>(L, lin, cache, st);
+  }
+  return fmt == MAK_FP8_E4M3 ? dispatch_e<STORE, __half, MAK_FP8_E4M3>(L, lin, cache, st)
+                             : dispatch_e<STORE, __half, MAK_FP8_E5M2>(L, lin, cache, st);
+}
+
+}  // namespace mak
+
+using namespace mak;
+
+extern "C" {
+
+int64_t mak_mla_fp8_row_bytes(int64_t kv_dim, int64_t pe_dim) { return mla_row_bytes(kv_dim, pe_dim, 2); }
+
+int mak_mla_fp8_rows_store(const mak_mla_linear_desc* lin, const mak_rows_desc* cache, const void* slots,
+                           int32_t slot_dtype, int32_t fp8_format, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  MlaLaunch L;
+  int rc = mla_prepare(lin, cache, fp8_format, "mak_mla_fp8_rows_store", &L);
+  if (rc) return rc;
+  if (lin->num_tokens == 0 || lin->num_layers == 0) return MAK_OK;
+  if (slots == nullptr || !valid_index_dtype(slot_dtype))
+    return fail(MAK_E_INVALID, "mak_mla_fp8_rows_store: slot vector must be int32 or int64");
+  cudaStream_t st = as_stream(stream);
+  ScatterWs ws{};
+  rc = carve_scatter_ws(workspace, workspace_bytes, lin->num_tokens, &ws);
+  if (rc) return rc;
+  rc = resolve_last_writer(slots, slot_dtype, lin->num_tokens, ws, st);
+  if (rc) return rc;
+  L.idx = ws.eff;
+  L.idx64 = 1;
+  return dispatch<true>(L, lin, cache, fp8_format, st);
+}
+
+int mak_mla_fp8_rows_load(const mak_rows_desc* cache, const mak_mla_linear_desc* lin, const void* slots,
+                          int32_t slot_dtype, int32_t fp8_format, void* stream) {
+  MlaLaunch L;
+  int rc = mla_prepare(lin, cache, fp8_format, "mak_mla_fp8_rows_load", &L);
+  if (rc) return rc;
+  if (lin->num_tokens == 0 || lin->num_layers == 0) return MAK_OK;
+  if (slots == nullptr || !valid_index_dtype(slot_dtype))
+    return fail(MAK_E_INVALID, "mak_mla_fp8_rows_load: slot vector must be int32 or int64");
+  L.idx = slots;
+  L.idx64 = slot_dtype == MAK_DT_I64;
+  return dispatch<false>(L, lin, cache, fp8_format, as_stream(stream));
+}
+
+}  // extern "C"

@@ -23,6 +23,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "fp8.cuh"
 
 namespace mak {
 
@@ -39,84 +40,6 @@ struct TileLaunch {
   int32_t slots64, n_kv, fill_zero, cache_vec, lin_vec, scale_mode, heads_per_step;
   int32_t window;  // tokens per warp window of the segment kernel (8, 16 or 32)
 };
-
-// ---- element conversions (round-to-nearest-even everywhere) ---------------
-template <typename T>
-__device__ __forceinline__ float to_f32(T x);
-template <>
-__device__ __forceinline__ float to_f32<float>(float x) { return x; }
-template <>
-__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
-template <>
-__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
-
-template <typename T>
-__device__ __forceinline__ T from_f32(float x);
-template <>
-__device__ __forceinline__ float from_f32<float>(float x) { return x; }
-template <>
-__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
-template <>
-__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
-
-template <typename T>
-__device__ __forceinline__ T zero_of() {
-  T z;
-  memset(&z, 0, sizeof(T));
-  return z;
-}
-
-// ---- musa-aiter FP8 codec ---------------------------------------------------
-// Encoder semantics (musa_aiter/ops/kv_transfer.py:2161-2183): w = x / scale in
-// fp32; non-finite -> zero carrying the sign of (w < 0); |w| below the smallest
-// normal -> signed zero; |w| clamped to (2 - 2^-m) * 2^emax (480 for E4M3 with
-// exponent field 15 / mantissa 7, 114688 for E5M2 with exponent field 31); the
-// mantissa rounds half-to-even.  Inside the formats' standard finite range this
-// is exactly cvt.rn.satfinite; the extra top codes are handled explicitly.
-__device__ __forceinline__ uint32_t cvt_e4m3(float a) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(r) : "f"(a));
-  return r & 0xFFu;
-}
-__device__ __forceinline__ uint32_t cvt_e5m2(float a) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %1;" : "=h"(r) : "f"(a));
-  return r & 0xFFu;
-}
-
-template <int F>
-__device__ __forceinline__ uint8_t fp8_encode(float w) {
-  const uint32_t sign = (w < 0.f) ? 0x80u : 0u;
-  const float a = fabsf(w);
-  if (!(a <= 3.40282346638528859812e+38f)) return static_cast<uint8_t>(sign);  // inf / nan
-  if (F == MAK_FP8_E4M3) {
-    if (a < 0.015625f) return static_cast<uint8_t>(sign);  // below 2^-6
-    // 464 is the midpoint of 448 (mantissa 6) and 480 (mantissa 7): ties go to 448.
-    if (a > 464.f) return static_cast<uint8_t>(sign | 0x7Fu);
-    return static_cast<uint8_t>(sign | cvt_e4m3(a));
-  } else {
-    if (a < 6.103515625e-05f) return static_cast<uint8_t>(sign);  // below 2^-14
-    if (a >= 61440.f) {
-      // Exponent field 31: scale by 2^-16 (exact) into field 15, add 16 back.
-      const float y = fminf(a, 114688.f) * 1.52587890625e-05f;
-      return static_cast<uint8_t>(sign | (cvt_e5m2(y) + 0x40u));
-    }
-    return static_cast<uint8_t>(sign | cvt_e5m2(a));
-  }
-}
-
-// Decoder (musa_aiter/ops/kv_transfer.py:2186-2200): exponent field 0 -> 0,
-// otherwise (1 + m / 2^mb) * 2^(e - bias), all codes finite; built bit-exactly.
-template <int F>
-__device__ __forceinline__ float fp8_decode(uint32_t code) {
-  constexpr int mb = (F == MAK_FP8_E4M3) ? 3 : 2;
-  constexpr int bias = (F == MAK_FP8_E4M3) ? 7 : 15;
-  const uint32_t e = (code >> mb) & ((1u << (7 - mb)) - 1u);
-  const uint32_t m = code & ((1u << mb) - 1u);
-  uint32_t bits = e ? (((e - bias + 127u) << 23) | (m << (23 - mb))) : 0u;
-  bits |= (code & 0x80u) << 24;
-  return __uint_as_float(bits);
-}
 
 template <typename CT, typename LT, int CODEC>
 struct Codec {

@@ -66,7 +66,9 @@ from .ops.kv_transfer import (
     kv_merged_linear_to_paged_fp8_multi_layer,
     kv_merged_linear_to_paged_multi_layer,
     kv_mla_linear_to_paged,
+    kv_mla_linear_to_paged_fp8_rows,
     kv_mla_linear_to_paged_multi_layer,
+    kv_paged_fp8_rows_to_mla_linear,
     kv_paged_fp8_to_linear,
     kv_paged_fp8_to_linear_multi_layer,
     kv_paged_fp8_to_merged_linear,
@@ -77,6 +79,7 @@ from .ops.kv_transfer import (
     kv_paged_to_merged_linear_multi_layer,
     kv_paged_to_mla_linear,
     kv_paged_to_mla_linear_multi_layer,
+    mla_fp8_row_bytes,
     native_fp8_kv_cache_abi_version,
     native_kv_transfer_abi_version,
 )

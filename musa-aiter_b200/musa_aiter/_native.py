@@ -75,6 +75,25 @@ class LinearDesc(ctypes.Structure):
     ]
 
 
+class MlaLinearDesc(ctypes.Structure):
+    """``mak_mla_linear_desc``: MLA latent ``[L][T][kv_dim]`` + rope ``[L][T][pe_dim]`` rows."""
+
+    _fields_ = [
+        ("kv", c_void_p),
+        ("pe", c_void_p),
+        ("num_layers", c_int64),
+        ("num_tokens", c_int64),
+        ("kv_dim", c_int64),
+        ("pe_dim", c_int64),
+        ("kv_stride_layer", c_int64),
+        ("kv_stride_token", c_int64),
+        ("pe_stride_layer", c_int64),
+        ("pe_stride_token", c_int64),
+        ("dtype", c_int32),
+        ("reserved", c_int32),
+    ]
+
+
 class CopyEntry(ctypes.Structure):
     """``mak_copy_entry``: one byte copy of a batch."""
 
@@ -178,6 +197,12 @@ _PROTOTYPES = {
     "mak_minmax": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_void_p]),
     "mak_cachegen_encode": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "mak_cachegen_decode": (c_int32, [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p]),
+    "mak_mla_fp8_row_bytes": (c_int64, [c_int64, c_int64]),
+    "mak_mla_fp8_rows_store": (
+        c_int32,
+        [POINTER(MlaLinearDesc), c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_size_t, c_void_p],
+    ),
+    "mak_mla_fp8_rows_load": (c_int32, [c_void_p, POINTER(MlaLinearDesc), c_void_p, c_int32, c_int32, c_void_p]),
     "mak_rows_copy": (
         c_int32,
         [

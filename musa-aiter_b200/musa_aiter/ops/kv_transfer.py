@@ -63,6 +63,9 @@ __all__ = [
     "kv_mla_linear_to_paged",
     "kv_paged_to_mla_linear_multi_layer",
     "kv_mla_linear_to_paged_multi_layer",
+    "mla_fp8_row_bytes",
+    "kv_mla_linear_to_paged_fp8_rows",
+    "kv_paged_fp8_rows_to_mla_linear",
 ]
 
 
@@ -1007,6 +1010,145 @@ def kv_mla_linear_to_paged_multi_layer(
         _mla_pair_scatter(kv_linear, k_pe_linear, kv_cache, k_pe_cache, slots, layered=True, op=name)
     emit_native(name, kv_linear, "sm100a row scatter (MLA flat, all layers)")
     return True
+
+
+# ---------------------------------------------------------------------------
+# MLA FP8 rows with per-group scales (no reference API: the reference moves
+# such rows only as opaque bytes, kv_transfer.py:4411-4452, 4588-4616)
+# ---------------------------------------------------------------------------
+
+MLA_FP8_GROUP = 128
+
+
+def mla_fp8_row_bytes(kv_dim: int = 512, pe_dim: int = 64) -> int:
+    """Bytes of one FP8 MLA row: ``kv_dim`` codes, ``kv_dim/128`` fp32 scales, ``pe_dim`` 16-bit rope values
+    (512 + 16 + 128 = 656 for DeepSeek MLA)."""
+    return int(kv_dim) + (int(kv_dim) // MLA_FP8_GROUP) * 4 + int(pe_dim) * 2
+
+
+def _mla_fp8_args(kv, pe, cache_rows, name):
+    """Normalise to layered views: kv [L,T,kvd], pe [L,T,ped], cache [L,NB,BS,row]."""
+    if kv.dim() not in (2, 3) or pe.dim() != kv.dim():
+        raise ValueError(f"{name}: latent and rope buffers must both be [T, dim] or [layers, T, dim]")
+    if cache_rows.dim() != kv.dim() + 1:
+        raise ValueError(f"{name}: cache must be [blocks, block_size, row_bytes] or [layers, blocks, block_size, row_bytes]")
+    if kv.dim() == 2:
+        kv, pe, cache_rows = kv.unsqueeze(0), pe.unsqueeze(0), cache_rows.unsqueeze(0)
+    if kv.shape[:2] != pe.shape[:2] or kv.shape[0] != cache_rows.shape[0]:
+        raise ValueError(f"{name}: layer and token counts of latent, rope and cache must agree")
+    if kv.dtype not in (torch.float16, torch.bfloat16) or pe.dtype != kv.dtype:
+        raise ValueError(f"{name}: latent and rope must share float16 or bfloat16")
+    if cache_rows.dtype is not torch.uint8:
+        raise ValueError(f"{name}: FP8 row cache storage must be torch.uint8")
+    kvd, ped = int(kv.shape[2]), int(pe.shape[2])
+    if kvd not in (256, 512, 1024):
+        raise ValueError(f"{name}: kv_dim must be 256, 512 or 1024 (groups of 128), got {kvd}")
+    if ped % 8 or ped > 256:
+        raise ValueError(f"{name}: pe_dim must be a multiple of 8 up to 256, got {ped}")
+    if int(cache_rows.shape[3]) != mla_fp8_row_bytes(kvd, ped):
+        raise ValueError(f"{name}: cache row is {int(cache_rows.shape[3])} bytes, expected {mla_fp8_row_bytes(kvd, ped)}")
+    return kv, pe, cache_rows
+
+
+def _mla_fp8_descs(kv, pe, cache_rows):
+    lin = _native.MlaLinearDesc(kv.data_ptr(), pe.data_ptr(), int(kv.shape[0]), int(kv.shape[1]), int(kv.shape[2]),
+                                int(pe.shape[2]), kv.stride(0), kv.stride(1), pe.stride(0), pe.stride(1),
+                                _native.dtype_code(kv.dtype), 0)
+    base = cache_rows.data_ptr()
+    s0, sb, st, _ = cache_rows.stride()
+    nb, bs = int(cache_rows.shape[1]), int(cache_rows.shape[2])
+    buf = _native.rows_pack(([base + i * s0 for i in range(cache_rows.shape[0])], bs, sb, st, nb * bs))
+    return lin, buf
+
+
+def _rows_ok(t: torch.Tensor, align: int) -> bool:
+    e = t.element_size()
+    return t.stride(-1) == 1 and (t.data_ptr() | (t.stride(0) * e) | (t.stride(1) * e)) % align == 0
+
+
+def kv_mla_linear_to_paged_fp8_rows(
+    kv_linear: torch.Tensor,
+    k_pe_linear: torch.Tensor,
+    cache_rows: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    *,
+    fp8_format: Literal["e4m3", "e5m2"] = "e4m3",
+) -> bool:
+    """Quantise MLA latent rows in groups of 128 and scatter them, with their scales and the rope part,
+    into FP8 row caches ``[NB, BS, row]`` / ``[L, NB, BS, row]`` (uint8, ``row = mla_fp8_row_bytes``).
+
+    Group scale = amax of the group's finite |x| / fp8_max (448 E4M3, 57344 E5M2); each value is encoded with the reference
+    FP8 rule as ``x / scale`` (kv_transfer.py:2161-2183).  Last writer wins for duplicate slots,
+    negative slots are skipped.  One fused launch (plus the duplicate-slot resolution) for all layers.
+    """
+    name = "kv_mla_linear_to_paged_fp8_rows"
+    fmt = _normalize_fp8_format(fp8_format)
+    kv, pe, cache = _mla_fp8_args(kv_linear, k_pe_linear, cache_rows, name)
+    tcount = int(kv.shape[1])
+    slots = ensure_slotmapping_vector(slot_mapping, expected_len=tcount, name=name)
+    if cache.stride(-1) != 1:
+        raise ValueError(f"{name}: cache rows must be contiguous")
+    require_cuda(name, kv, pe, cache, slots)
+    check_slots_in_bounds(slots, int(cache.shape[1]), int(cache.shape[2]), name)
+    if tcount and kv.shape[0]:
+        if not _rows_ok(kv, 16):
+            kv = kv.contiguous()
+        if not _rows_ok(pe, 8):
+            pe = pe.contiguous()
+        lib = _native.load()
+        ks, code = kernel_slots(slots)
+        lin, buf = _mla_fp8_descs(kv, pe, cache)
+        ws, nbytes = _native.workspace(tcount, kv.device)
+        _native.check(lib.mak_mla_fp8_rows_store(ctypes.byref(lin), ctypes.addressof(buf), ks.data_ptr(), code,
+                                                 _FMT_CODE[fmt], ws.data_ptr(), nbytes, _native.stream_ptr(kv.device)),
+                      name)
+    emit_native(name, kv_linear, "sm100a fused group-quantise + row scatter (MLA FP8 rows)")
+    return True
+
+
+def kv_paged_fp8_rows_to_mla_linear(
+    cache_rows: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    *,
+    kv_dim: int = 512,
+    pe_dim: int = 64,
+    out_dtype: torch.dtype = torch.bfloat16,
+    fp8_format: Literal["e4m3", "e5m2"] = "e4m3",
+    out_kv: torch.Tensor | None = None,
+    out_k_pe: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gather FP8 MLA rows and dequantise them (``code * scale`` in fp32, RNE to ``out_dtype``):
+    ``[NB, BS, row]`` -> ``[T, kv_dim]`` + ``[T, pe_dim]``, or ``[L, NB, BS, row]`` -> ``[L, T, ...]``.
+    Rows of negative slots are zero.  The rope part is returned bit-exact (stored in ``out_dtype``)."""
+    name = "kv_paged_fp8_rows_to_mla_linear"
+    fmt = _normalize_fp8_format(fp8_format)
+    layered = cache_rows.dim() == 4
+    tcount = int(slot_mapping.numel())
+    slots = ensure_slotmapping_vector(slot_mapping, expected_len=tcount, name=name)
+    lead = (int(cache_rows.shape[0]),) if layered else ()
+    okv = out_kv if out_kv is not None else torch.empty(lead + (tcount, kv_dim), dtype=out_dtype, device=cache_rows.device)
+    ope = out_k_pe if out_k_pe is not None else torch.empty(lead + (tcount, pe_dim), dtype=out_dtype, device=cache_rows.device)
+    if tuple(okv.shape) != lead + (tcount, kv_dim) or tuple(ope.shape) != lead + (tcount, pe_dim):
+        raise ValueError(f"{name}: output shapes must be {lead + (tcount, kv_dim)} and {lead + (tcount, pe_dim)}")
+    kv, pe, cache = _mla_fp8_args(okv, ope, cache_rows, name)
+    if cache.stride(-1) != 1:
+        raise ValueError(f"{name}: cache rows must be contiguous")
+    require_cuda(name, kv, pe, cache, slots)
+    check_slots_in_bounds(slots, int(cache.shape[1]), int(cache.shape[2]), name)
+    if tcount and kv.shape[0]:
+        work_kv = kv if _rows_ok(kv, 16) else torch.empty(kv.shape, dtype=kv.dtype, device=kv.device)
+        work_pe = pe if _rows_ok(pe, 8) else torch.empty(pe.shape, dtype=pe.dtype, device=pe.device)
+        lib = _native.load()
+        ks, code = kernel_slots(slots)
+        lin, buf = _mla_fp8_descs(work_kv, work_pe, cache)
+        _native.check(lib.mak_mla_fp8_rows_load(ctypes.addressof(buf), ctypes.byref(lin), ks.data_ptr(), code,
+                                                _FMT_CODE[fmt], _native.stream_ptr(kv.device)), name)
+        if work_kv is not kv:
+            kv.copy_(work_kv)
+        if work_pe is not pe:
+            pe.copy_(work_pe)
+    emit_native(name, cache_rows, "sm100a fused row gather + group dequantise (MLA FP8 rows)")
+    return okv, ope
 
 
 # ---------------------------------------------------------------------------

@@ -453,6 +453,78 @@ def kv_mla_linear_to_paged(kv_lin, pe_lin, kv_cache, pe_cache, slots) -> None:
     rows_scatter(pe_lin, pe_cache.reshape(nb * bs, -1), slots)
 
 
+# ---- MLA FP8 rows with per-group scales ----------------------------------------
+# Row = [kv_dim FP8 codes][kv_dim/128 fp32 scales][pe_dim rope elements, 2 B each].
+# Group scale = amax over the group's finite |x| (0 when none) / fp8_max in fp32,
+# so every stored scale is finite; the element rule is the pinned ``fp8_quantize_to_uint8`` above
+# (musa_aiter/ops/kv_transfer.py:2161-2183).  The grouping and byte layout are
+# this build's documented choice (the reference only moves such rows as opaque
+# bytes, kv_transfer.py:4411-4452, 4588-4616): parity for them is unpinned.
+
+MLA_FP8_GROUP = 128
+
+
+def mla_fp8_row_bytes(kv_dim: int, pe_dim: int) -> int:
+    return kv_dim + (kv_dim // MLA_FP8_GROUP) * 4 + pe_dim * 2
+
+
+def mla_fp8_group_scales(x_f32: np.ndarray, fp8_format: str) -> np.ndarray:
+    """``[..., kv_dim]`` fp32 -> ``[..., kv_dim / 128]`` fp32 scales."""
+    fmax = np.float32(448.0 if normalize_fp8_format(fp8_format) == "e4m3" else 57344.0)
+    x = np.asarray(x_f32, dtype=np.float32)
+    g = x.reshape(x.shape[:-1] + (x.shape[-1] // MLA_FP8_GROUP, MLA_FP8_GROUP))
+    a = np.abs(g)
+    a = np.where(np.isfinite(a), a, np.float32(0.0))
+    amax = np.max(a, axis=-1, initial=np.float32(0.0)).astype(np.float32)
+    return (amax / fmax).astype(np.float32)
+
+
+def mla_fp8_encode_rows(kv: np.ndarray, pe: np.ndarray, in_dtype: str, fp8_format: str) -> np.ndarray:
+    """Token rows ``[T, kv_dim]`` + ``[T, pe_dim]`` (in_dtype; bf16 as uint16 bits) -> ``[T, row]`` uint8."""
+    x = to_f32(kv, in_dtype)
+    t, kvd = x.shape
+    scales = mla_fp8_group_scales(x, fp8_format)
+    per_elem = np.repeat(scales, MLA_FP8_GROUP, axis=-1)
+    codes = fp8_quantize_to_uint8(x, per_elem, fp8_format)
+    pe = np.ascontiguousarray(pe)
+    pe_bytes = pe.view(np.uint8).reshape(t, pe.shape[-1] * pe.itemsize)
+    return np.concatenate([codes, np.ascontiguousarray(scales).view(np.uint8).reshape(t, -1), pe_bytes], axis=1)
+
+
+def mla_fp8_rows_store(kv: np.ndarray, pe: np.ndarray, cache_rows: np.ndarray, slots: np.ndarray, *,
+                       in_dtype: str, fp8_format: str = "e4m3") -> None:
+    """``[L, T, kv_dim]`` + ``[L, T, pe_dim]`` -> ``cache_rows[L, NB*BS, row]`` at ``slots`` (last writer wins;
+    negative / out-of-range slots skipped)."""
+    slots = np.asarray(slots, dtype=np.int64)
+    keep = last_writer_mask(slots) & (slots < cache_rows.shape[1])
+    t = np.nonzero(keep)[0]
+    for layer in range(kv.shape[0]):
+        rows = mla_fp8_encode_rows(kv[layer], pe[layer], in_dtype, fp8_format)
+        cache_rows[layer, slots[t]] = rows[t]
+
+
+def mla_fp8_rows_load(cache_rows: np.ndarray, slots: np.ndarray, *, kv_dim: int, pe_dim: int, out_dtype: str,
+                      fp8_format: str = "e4m3") -> tuple[np.ndarray, np.ndarray]:
+    """``cache_rows[L, NB*BS, row]`` at ``slots`` -> (``[L, T, kv_dim]``, ``[L, T, pe_dim]``) in out_dtype
+    (bf16 as uint16 bits); negative / out-of-range slots give zero rows."""
+    slots = np.asarray(slots, dtype=np.int64)
+    nl, nrows, _ = cache_rows.shape
+    ok = (slots >= 0) & (slots < nrows)
+    np_t = np.uint16 if out_dtype == "bfloat16" else np.float16
+    kv = np.zeros((nl, slots.shape[0], kv_dim), dtype=np_t)
+    pe = np.zeros((nl, slots.shape[0], pe_dim), dtype=np_t)
+    idx = np.nonzero(ok)[0]
+    g = kv_dim // MLA_FP8_GROUP
+    for layer in range(nl):
+        rows = cache_rows[layer, slots[idx]]
+        codes = rows[:, :kv_dim]
+        scales = np.ascontiguousarray(rows[:, kv_dim: kv_dim + 4 * g]).view(np.float32)
+        per_elem = np.repeat(scales, MLA_FP8_GROUP, axis=-1)
+        kv[layer, idx] = fp8_dequantize_from_uint8(codes, per_elem, fp8_format, out_dtype)
+        pe[layer, idx] = np.ascontiguousarray(rows[:, kv_dim + 4 * g: kv_dim + 4 * g + 2 * pe_dim]).view(np_t)
+    return kv, pe
+
+
 # ---------------------------------------------------------------------------
 # Flash dense layouts (musa_aiter/ops/kv_transfer.py:1527-1795)
 # ---------------------------------------------------------------------------

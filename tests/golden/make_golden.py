@@ -17,6 +17,11 @@ Families:
 - rows.npz    LMCache 6-D / list / SGLang MP two_x_nl / MLA buffers, MLA flat caches
 - misc.npz    Flash dense load / cache-back / FP8 dequant, Triton-indexed dense gather,
               block copies, DSV4 byte rows, HiCache transfers, CacheGen codec
+- mla_fp8.npz MLA latent rows encoded / decoded by the reference's FP8 element codec
+              (``_fp8_quantize_to_uint8`` / ``_fp8_dequantize_from_uint8``) with per-128
+              group scales amax/fp8_max (the group rule is this build's choice)
+
+``python tests/golden/make_golden.py mla_fp8`` regenerates one family only.
 """
 
 from __future__ import annotations
@@ -494,9 +499,40 @@ def make_misc() -> None:
     st.save("misc.npz")
 
 
+def make_mla_fp8() -> None:
+    """Per-group FP8 rows: values, group scales (amax over the finite |x| of the group, / fp8_max
+    in fp32), the reference's element encoder on x / scale, and its decoder times the stored scale."""
+    from musa_aiter.ops import kv_transfer as rk  # the reference module
+
+    st = Store()
+    g = gen(40)
+    t, kvd = 24, 512
+    x = randn((t, kvd), torch.float32, g) * torch.exp2(torch.randint(-12, 12, (t, 1), generator=g).float())
+    x[1, :128] = 0.0                                   # all-zero group -> scale 0
+    x[2, 5] = float("nan")                             # NaN ignored by the group amax
+    x[3, 130] = float("inf")                           # non-finite values do not enter the amax
+    x[4, 300:428] = -0.0
+    x[5, 0] = 1e-30                                    # tiny values beside a large one
+    x[5, 1] = 3.0e4
+    for dname, dt in (("bfloat16", torch.bfloat16), ("float16", torch.float16)):
+        xd = x.to(dt)
+        for fmt, fmax in (("e4m3", 448.0), ("e5m2", 57344.0)):
+            ax = xd.float().abs()
+            a = torch.where(torch.isfinite(ax), ax, torch.zeros_like(ax)).reshape(t, kvd // 128, 128).amax(-1)
+            scale = (a / torch.tensor(fmax, dtype=torch.float32)).to(torch.float32)
+            per = scale.repeat_interleave(128, dim=1)
+            codes = rk._fp8_quantize_to_uint8(xd, per, fmt)
+            dec = rk._fp8_dequantize_from_uint8(codes, per, fmt, dt)
+            p = f"{dname}/{fmt}"
+            st.put(f"{p}/x", xd)
+            st.put(f"{p}/scale", scale)
+            st.put(f"{p}/codes", codes)
+            st.put(f"{p}/dec", dec)
+    st.save("mla_fp8.npz")
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
-    make_tile()
-    make_fp8()
-    make_rows()
-    make_misc()
+    families = {"tile": make_tile, "fp8": make_fp8, "rows": make_rows, "misc": make_misc, "mla_fp8": make_mla_fp8}
+    for name in (sys.argv[1:] or list(families)):
+        families[name]()

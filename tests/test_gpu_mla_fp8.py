@@ -1,0 +1,152 @@
+"""GPU parity for the MLA FP8 row kernels (per-128 group scales, fused quantise +
+scatter and gather + dequantise) against the reference's FP8 element codec
+(golden vectors) and the CPU oracle.  Bit-exact: the scales come from the same
+fp32 division and every value goes through the same encode / decode rule."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import musa_aiter as ma
+from oracle import kv_oracle as O
+
+from ._util import first_diff, same_bits, to_np, to_torch
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TORCH = {"bfloat16": torch.bfloat16, "float16": torch.float16}
+
+
+def eq(got, want, what):
+    assert same_bits(got, want), f"{what}: {first_diff(got, want)}"
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN / "mla_fp8.npz")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", ("bfloat16", "float16"))
+def test_golden_group_codec(cuda_device, golden, dt, fmt):
+    p = f"{dt}/{fmt}"
+    x = to_torch(golden[f"{p}/x"], dt)
+    t = x.shape[0]
+    pe = torch.randn((t, 64), device="cuda").to(TORCH[dt])
+    row = ma.mla_fp8_row_bytes(512, 64)
+    cache = torch.full((4, 8, row), 0xEE, dtype=torch.uint8, device="cuda")
+    slots = torch.arange(t, device="cuda") + 3
+    assert ma.kv_mla_linear_to_paged_fp8_rows(x, pe, cache, slots, fp8_format=fmt) is True
+    rows = cache.view(32, row)[3: 3 + t]
+    eq(rows[:, :512], golden[f"{p}/codes"], "codes")
+    eq(rows[:, 512:528].contiguous().view(torch.float32), golden[f"{p}/scale"], "scales")
+    eq(rows[:, 528:].contiguous().view(TORCH[dt]), to_np(pe), "rope")
+    assert torch.all(cache.view(32, row)[:3] == 0xEE) and torch.all(cache.view(32, row)[3 + t:] == 0xEE)
+    okv, ope = ma.kv_paged_fp8_rows_to_mla_linear(cache, slots, out_dtype=TORCH[dt], fp8_format=fmt)
+    eq(okv, golden[f"{p}/dec"], "decoded latent")
+    eq(ope, to_np(pe), "rope round trip")
+
+
+def _oracle_cache(cache: torch.Tensor) -> np.ndarray:
+    c = cache.cpu().numpy()
+    return c.reshape(c.shape[0], -1, c.shape[-1]).copy()
+
+
+@pytest.mark.parametrize("kvd,ped", ((512, 64), (256, 32), (1024, 128), (512, 0)))
+@pytest.mark.parametrize("dt", ("bfloat16", "float16"))
+def test_random_multi_layer_vs_oracle(cuda_device, kvd, ped, dt):
+    g = torch.Generator().manual_seed(kvd + ped)
+    nl, nb, bs, t = 3, 12, 16, 90
+    x = (torch.randn((nl, t, kvd), generator=g) * torch.exp2(torch.randint(-8, 8, (nl, t, 1), generator=g).float()))
+    x = x.to(TORCH[dt])
+    pe = torch.randn((nl, t, ped), generator=g).to(TORCH[dt])
+    slots = torch.randint(-2, nb * bs, (t,), generator=g, dtype=torch.int64)
+    slots[10] = slots[70]  # duplicate: token 70 wins
+    row = ma.mla_fp8_row_bytes(kvd, ped)
+    cache0 = torch.randint(0, 256, (nl, nb, bs, row), generator=g, dtype=torch.uint8)
+    cache = cache0.cuda()
+    xs = x.cuda()
+    pes = pe.cuda()
+    assert ma.kv_mla_linear_to_paged_fp8_rows(xs, pes, cache, slots.cuda()) is True
+    want = _oracle_cache(cache0)
+    O.mla_fp8_rows_store(to_np(x), to_np(pe), want, slots.numpy(), in_dtype=dt)
+    eq(cache.view(nl, nb * bs, row), want, "store")
+    # load back from written rows (untouched rows hold random bytes, not FP8 rows), plus misses
+    lslots = torch.cat([slots[torch.randperm(t, generator=g)], torch.tensor([-1, -5])]).to(torch.int32)
+    okv, ope = ma.kv_paged_fp8_rows_to_mla_linear(cache, lslots.cuda(), kv_dim=kvd, pe_dim=ped, out_dtype=TORCH[dt])
+    rk, rp = O.mla_fp8_rows_load(want, lslots.numpy(), kv_dim=kvd, pe_dim=ped, out_dtype=dt)
+    eq(okv, rk, "load latent")
+    eq(ope, rp, "load rope")
+
+
+def test_flat_cache_strided_inputs_and_e5m2(cuda_device):
+    """Single-layer caches, latent rows read through a strided view, E5M2 codes."""
+    g = torch.Generator().manual_seed(77)
+    nb, bs, t = 9, 64, 200
+    big = (torch.randn((t, 640), generator=g) * 50).to(torch.bfloat16)
+    x = big[:, 64:576]  # 16-byte aligned rows with a 1280-byte token stride
+    pe = torch.randn((t, 64), generator=g).to(torch.bfloat16)
+    slots = torch.randperm(nb * bs, generator=g)[:t].to(torch.int64)
+    row = ma.mla_fp8_row_bytes()
+    cache = torch.zeros((nb, bs, row), dtype=torch.uint8, device="cuda")
+    assert ma.kv_mla_linear_to_paged_fp8_rows(big.cuda()[:, 64:576], pe.cuda(), cache, slots.cuda(), fp8_format="e5m2")
+    want = np.zeros((1, nb * bs, row), np.uint8)
+    O.mla_fp8_rows_store(to_np(x)[None], to_np(pe)[None], want, slots.numpy(), in_dtype="bfloat16", fp8_format="e5m2")
+    eq(cache.view(1, nb * bs, row), want, "store e5m2")
+    out_big = torch.full((t, 700), 9.0, dtype=torch.bfloat16, device="cuda")
+    okv, ope = ma.kv_paged_fp8_rows_to_mla_linear(cache, slots.cuda(), fp8_format="e5m2", out_kv=out_big[:, 8:520])
+    rk, rp = O.mla_fp8_rows_load(want, slots.numpy(), kv_dim=512, pe_dim=64, out_dtype="bfloat16", fp8_format="e5m2")
+    eq(okv, rk[0], "load e5m2 into a strided output")
+    eq(ope, rp[0], "rope")
+    assert torch.all(out_big[:, :8] == 9.0) and torch.all(out_big[:, 520:] == 9.0)
+
+
+def test_rejects_bad_rows(cuda_device):
+    x = torch.zeros((4, 512), dtype=torch.bfloat16, device="cuda")
+    pe = torch.zeros((4, 64), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="row is"):
+        ma.kv_mla_linear_to_paged_fp8_rows(x, pe, torch.zeros((2, 4, 600), dtype=torch.uint8, device="cuda"),
+                                           torch.arange(4, device="cuda"))
+    with pytest.raises(ValueError, match="kv_dim"):
+        ma.kv_mla_linear_to_paged_fp8_rows(x[:, :384], pe, torch.zeros((2, 4, 528), dtype=torch.uint8, device="cuda"),
+                                           torch.arange(4, device="cuda"))
+    with pytest.raises(ValueError, match="out of bounds"):
+        ma.kv_mla_linear_to_paged_fp8_rows(x, pe, torch.zeros((2, 4, 656), dtype=torch.uint8, device="cuda"),
+                                           torch.tensor([0, 1, 2, 8], device="cuda"))
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", ("bfloat16", "float16"))
+def test_every_input_under_fixed_group_amax(cuda_device, dt, fmt):
+    """Every finite 16-bit input value, quantised under several group scales: each group of 128
+    starts with its amax A, the other 127 values are all inputs with |x| <= A (exhaustive)."""
+    allv = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(TORCH[dt]).float()
+    allv = allv[torch.isfinite(allv)]
+    groups = []
+    for amax in (1.0, 3.0, 0.37, 448.0, 1.0e-3, 12345.0, 2.0**-20, 57344.0, 6.0e4):
+        a = torch.tensor(amax).to(TORCH[dt]).float()
+        vals = allv[allv.abs() <= a]
+        n = (vals.numel() + 126) // 127
+        pad = torch.zeros(n * 127 - vals.numel())
+        body = torch.cat([vals, pad]).reshape(n, 127)
+        groups.append(torch.cat([a.expand(n, 1), body], dim=1))
+    g = torch.cat(groups)
+    g = torch.cat([g, torch.zeros((-g.shape[0]) % 4, 128)])  # whole rows of 4 groups
+    x = g.reshape(-1, 512).to(TORCH[dt])
+    t = x.shape[0]
+    pe = torch.zeros((t, 64), dtype=TORCH[dt])
+    row = ma.mla_fp8_row_bytes()
+    nb = (t + 63) // 64
+    cache = torch.zeros((nb, 64, row), dtype=torch.uint8, device="cuda")
+    slots = torch.arange(t)
+    ma.kv_mla_linear_to_paged_fp8_rows(x.cuda(), pe.cuda(), cache, slots.cuda(), fp8_format=fmt)
+    want = np.zeros((1, nb * 64, row), np.uint8)
+    O.mla_fp8_rows_store(to_np(x)[None], to_np(pe)[None], want, slots.numpy(), in_dtype=dt, fp8_format=fmt)
+    eq(cache.view(1, nb * 64, row), want, f"{t} rows, every input")
+    okv, _ = ma.kv_paged_fp8_rows_to_mla_linear(cache, slots.cuda(), out_dtype=TORCH[dt], fp8_format=fmt)
+    rk, _ = O.mla_fp8_rows_load(want, slots.numpy(), kv_dim=512, pe_dim=64, out_dtype=dt, fp8_format=fmt)
+    eq(okv, rk[0], "decode")

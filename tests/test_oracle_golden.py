@@ -288,3 +288,28 @@ def test_cachegen(misc):
         assert same_bits(cdf, misc[f"{p}/cdf"]), name
         if f"{p}/dec" in misc:
             assert same_bits(O.from_f32(O.kv_cachegen_decode(enc, cb), dt), misc[f"{p}/dec"]), name
+
+
+# ---- MLA FP8 rows: the reference's element codec under per-128 group scales ----
+
+
+@pytest.fixture(scope="module")
+def mla_fp8():
+    return np.load(GOLDEN / "mla_fp8.npz")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", ("bfloat16", "float16"))
+def test_mla_fp8_rows_codec(mla_fp8, dt, fmt):
+    p = f"{dt}/{fmt}"
+    x = mla_fp8[f"{p}/x"]
+    x32 = O.to_f32(x, dt)
+    scales = O.mla_fp8_group_scales(x32, fmt)
+    assert scales.tobytes() == mla_fp8[f"{p}/scale"].tobytes()
+    pe = np.zeros((x.shape[0], 64), dtype=x.dtype)
+    rows = O.mla_fp8_encode_rows(x, pe, dt, fmt)
+    assert rows.shape == (x.shape[0], O.mla_fp8_row_bytes(512, 64))
+    assert np.array_equal(rows[:, :512], mla_fp8[f"{p}/codes"])
+    cache = rows[None]
+    kv, _ = O.mla_fp8_rows_load(cache, np.arange(x.shape[0]), kv_dim=512, pe_dim=64, out_dtype=dt, fp8_format=fmt)
+    assert kv[0].tobytes() == mla_fp8[f"{p}/dec"].tobytes()

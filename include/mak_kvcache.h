@@ -422,6 +422,22 @@ MAK_API int mak_mla_fp8_rows_store(const mak_mla_linear_desc* lin, const mak_row
 MAK_API int mak_mla_fp8_rows_load(const mak_rows_desc* cache, const mak_mla_linear_desc* lin, const void* slots,
                                   int32_t slot_dtype, int32_t fp8_format, void* stream);
 
+/* ---- peer mappings for block migration between GPUs of one node ----------- */
+
+/*
+ * No reference counterpart (the reference's communication layer raises for
+ * world_size != 1, musa_aiter/communication.py:55-56).  A receiving process
+ * exports a device pointer as the CUDA IPC handle of its allocation plus the
+ * offset inside it; the sending process imports it (opened once per handle and
+ * device, reference-counted) and moves blocks with mak_rows_copy, whose stores
+ * then land in the peer's memory.  mak_ipc_release drops one import.
+ * Handles are mak_ipc_handle_bytes() (64) bytes.
+ */
+MAK_API int mak_ipc_handle_bytes(void);
+MAK_API int mak_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+MAK_API int mak_ipc_import(const void* handle, int64_t offset, void** ptr_out);
+MAK_API int mak_ipc_release(const void* handle);
+
 #ifdef __cplusplus
 }
 #endif

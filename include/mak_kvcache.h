@@ -422,6 +422,58 @@ MAK_API int mak_mla_fp8_rows_store(const mak_mla_linear_desc* lin, const mak_row
 MAK_API int mak_mla_fp8_rows_load(const mak_rows_desc* cache, const mak_mla_linear_desc* lin, const void* slots,
                                   int32_t slot_dtype, int32_t fp8_format, void* stream);
 
+/* ---- rotary position embedding (the `cache` family) ----------------------- */
+
+/*
+ * Dtype codes: x_dtype / cos_dtype / sin_dtype are the operands; prod1_dtype is
+ * the promoted type of (x, cos), prod2_dtype of (x, sin), sum_dtype of the two
+ * products (torch type promotion; the caller computes them); out_dtype the
+ * result.  f16 / bf16 steps round to nearest-even after every operation.
+ */
+typedef struct mak_rope_dense_desc {
+  const void* x;
+  const void* cos;        /* broadcast to the output's leading dims by strides (0 = broadcast) */
+  const void* sin;
+  void* out;              /* contiguous [rows, 2 * half] */
+  int64_t rows;           /* product of the leading sizes */
+  int64_t half;           /* head_dim / 2 */
+  int64_t sizes[6];       /* leading sizes (ndim of them) */
+  int64_t x_strides[7];   /* leading strides, then [6] = stride along head_dim (elements) */
+  int64_t cos_strides[7]; /* leading strides, then [6] = stride along half */
+  int64_t sin_strides[7];
+  int32_t ndim;
+  int32_t interleaved;    /* 1: pairs (2j, 2j+1); 0: pairs (j, j + half) */
+  int32_t x_dtype, cos_dtype, sin_dtype, prod1_dtype, prod2_dtype, sum_dtype, out_dtype;
+  int32_t reserved;
+} mak_rope_dense_desc;
+
+/* out = rope(x, cos, sin).  Replaces apply_rope (musa_aiter/ops/cache.py:9-42). */
+MAK_API int mak_rope_dense(const mak_rope_dense_desc* desc, void* stream);
+
+typedef struct mak_rope_cache_desc {
+  void* cache;            /* key cache [num_blocks][num_heads][head_dim][block_size], rotated in place */
+  const void* cos;        /* [max_positions, half] (row stride) or [half] (cos_stride_row = 0) */
+  const void* sin;
+  const void* slots;      /* per token; negative = skip */
+  const void* positions;  /* per token, row of cos / sin */
+  int64_t n_tokens;
+  int64_t num_blocks, num_heads, head_dim, block_size;
+  int64_t stride_block, stride_head, stride_dim; /* elements; block offset stride 1 */
+  int64_t cos_stride_row, cos_stride_last, sin_stride_row, sin_stride_last;
+  int32_t slot_dtype, pos_dtype;
+  int32_t cache_dtype, cos_dtype, sin_dtype, prod1_dtype, prod2_dtype, sum_dtype;
+  int32_t interleaved;
+  int32_t reserved;
+} mak_rope_cache_desc;
+
+/*
+ * Rotate key_cache[block, :, :, offset] of every token in place with the cos /
+ * sin row of its position.  Slots must be distinct within one call (the caller
+ * splits repeated slots into successive calls, which keeps the reference's
+ * token order).  Replaces apply_rope_to_key_cache (musa_aiter/ops/cache.py:45-102).
+ */
+MAK_API int mak_rope_key_cache(const mak_rope_cache_desc* desc, void* stream);
+
 /* ---- peer mappings for block migration between GPUs of one node ----------- */
 
 /*

@@ -8,6 +8,7 @@ rejected (there is no CPU fallback).
 
 from .version import __version__
 from . import registry, dispatch
+from .ops.cache import apply_rope, apply_rope_to_key_cache, copy_to_kv_cache
 from .ops.kv_layout import KVFormatFacts, KVLayoutKind, KVLayoutSpec, KVOrganization, KVScaleKind
 from .ops.kv_transfer_plan import (
     KVTransferEntry,

@@ -198,6 +198,8 @@ _PROTOTYPES = {
     "mak_cachegen_encode": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "mak_cachegen_decode": (c_int32, [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p]),
     "mak_mla_fp8_row_bytes": (c_int64, [c_int64, c_int64]),
+    "mak_rope_dense": (c_int32, [c_void_p, c_void_p]),
+    "mak_rope_key_cache": (c_int32, [c_void_p, c_void_p]),
     "mak_ipc_handle_bytes": (c_int32, []),
     "mak_ipc_export": (c_int32, [c_void_p, c_void_p, POINTER(c_int64)]),
     "mak_ipc_import": (c_int32, [c_void_p, c_int64, POINTER(c_void_p)]),

@@ -114,3 +114,12 @@ _KVCACHE = [
 
 for _name, _status, _dtypes, _desc, _notes in _KVCACHE:
     register(OperatorCapability(_name, "kvcache", _status, _dtypes, ("cuda",), (BACKEND,), _desc, _notes, ("handwritten-cuda-sm100a",)))
+
+# The `cache` family entries the reference registers (musa_aiter/registry.py:85-86), the write-side
+# producers of the kvcache path.
+_CACHE = [
+    ("apply_rope", "b200", _FLOAT, "RoPE with the reference's per-operation rounding.", ()),
+    ("apply_rope_to_key_cache", "b200", _FLOAT, "Apply RoPE in place to selected paged key-cache slots.", ()),
+]
+for _name, _status, _dtypes, _desc, _notes in _CACHE:
+    register(OperatorCapability(_name, "cache", _status, _dtypes, ("cuda",), (BACKEND,), _desc, _notes, ("handwritten-cuda-sm100a",)))

@@ -526,6 +526,93 @@ def mla_fp8_rows_load(cache_rows: np.ndarray, slots: np.ndarray, *, kv_dim: int,
 
 
 # ---------------------------------------------------------------------------
+# `cache` family: RoPE and the KV-cache write (musa_aiter/ops/cache.py)
+# ---------------------------------------------------------------------------
+
+
+def promote_float(a: str, b: str, *, b_is_0dim: bool = False) -> str:
+    """torch's result type of a float tensor op between dtypes a and b (b a 0-dim tensor or not)."""
+    if b_is_0dim or a == b:
+        return a
+    if "float32" in (a, b):
+        return "float32"
+    return "float32"  # float16 with bfloat16
+
+
+def round_to(v: np.ndarray, dtype: str) -> np.ndarray:
+    """fp32 values rounded to nearest-even in ``dtype`` and back to fp32."""
+    v = np.asarray(v, dtype=np.float32)
+    if dtype == "float16":
+        with np.errstate(over="ignore"):
+            return v.astype(np.float16).astype(np.float32)
+    if dtype == "bfloat16":
+        return bf16_bits_to_f32(f32_to_bf16_bits(v))
+    return v
+
+
+def _op(a, b, dtype, fn):
+    with np.errstate(over="ignore", invalid="ignore"):
+        return round_to(fn(round_to(a, dtype), round_to(b, dtype)).astype(np.float32), dtype)
+
+
+def rope_pair(x1, x2, c, s, *, r1: str, r2: str, r3: str):
+    """(x1*cos - x2*sin, x1*sin + x2*cos) with torch's per-operation types (cache.py:35-42)."""
+    mul = np.multiply
+    p11, p22 = _op(x1, c, r1, mul), _op(x2, s, r2, mul)
+    p12, p21 = _op(x1, s, r2, mul), _op(x2, c, r1, mul)
+    return _op(p11, p22, r3, np.subtract), _op(p12, p21, r3, np.add)
+
+
+def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, *, x_dtype: str, cos_dtype: str, sin_dtype: str,
+               interleaved: bool = False) -> np.ndarray:
+    """``apply_rope`` (musa_aiter/ops/cache.py:9-42) on numpy inputs (bf16 as uint16 bits)."""
+    xf = to_f32(x, x_dtype)
+    cf = to_f32(cos, cos_dtype)
+    sf = to_f32(sin, sin_dtype)
+    r1 = promote_float(x_dtype, cos_dtype, b_is_0dim=np.ndim(cos) == 0)
+    r2 = promote_float(x_dtype, sin_dtype, b_is_0dim=np.ndim(sin) == 0)
+    r3 = promote_float(r1, r2)
+    half = xf.shape[-1] // 2
+    if interleaved:
+        x1, x2 = xf[..., 0::2], xf[..., 1::2]
+    else:
+        x1, x2 = xf[..., :half], xf[..., half:]
+    x1, x2, cf, sf = np.broadcast_arrays(x1, x2, cf, sf)
+    o1, o2 = rope_pair(x1, x2, cf, sf, r1=r1, r2=r2, r3=r3)
+    if interleaved:
+        out = np.stack((o1, o2), axis=-1).reshape(o1.shape[:-1] + (2 * half,))
+    else:
+        out = np.concatenate((o1, o2), axis=-1)
+    return from_f32(out, x_dtype)
+
+
+def apply_rope_to_key_cache(key_cache: np.ndarray, slots: np.ndarray, positions: np.ndarray, cos: np.ndarray,
+                            sin: np.ndarray, *, cache_dtype: str, cos_dtype: str, sin_dtype: str,
+                            interleaved: bool = False) -> None:
+    """In place on ``key_cache[NB, NH, HD, BS]``, token by token (musa_aiter/ops/cache.py:84-101)."""
+    bs = key_cache.shape[-1]
+    for t, slot in enumerate(np.asarray(slots, dtype=np.int64).tolist()):
+        if slot < 0:
+            continue
+        b, o = slot // bs, slot % bs
+        pos = int(positions[t])
+        crow = cos if cos.ndim == 1 else cos[pos]
+        srow = sin if sin.ndim == 1 else sin[pos]
+        key_cache[b, :, :, o] = apply_rope(key_cache[b, :, :, o], crow, srow, x_dtype=cache_dtype, cos_dtype=cos_dtype,
+                                           sin_dtype=sin_dtype, interleaved=interleaved)
+
+
+def copy_to_kv_cache(k: np.ndarray, v: np.ndarray, key_cache: np.ndarray, value_cache: np.ndarray, slots) -> None:
+    """musa_aiter/ops/cache.py:133-144: token loop, negative slots skipped, last writer wins."""
+    bs = key_cache.shape[-1]
+    for t, slot in enumerate(np.asarray(slots, dtype=np.int64).tolist()):
+        if slot < 0:
+            continue
+        key_cache[slot // bs, :, :, slot % bs] = k[t]
+        value_cache[slot // bs, :, :, slot % bs] = v[t]
+
+
+# ---------------------------------------------------------------------------
 # Flash dense layouts (musa_aiter/ops/kv_transfer.py:1527-1795)
 # ---------------------------------------------------------------------------
 

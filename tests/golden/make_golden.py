@@ -21,6 +21,9 @@ Families:
               (``_fp8_quantize_to_uint8`` / ``_fp8_dequantize_from_uint8``) with per-128
               group scales amax/fp8_max (the group rule is this build's choice)
 
+- cache.npz   apply_rope (dtype pairs, interleaved, broadcast shapes), apply_rope_to_key_cache
+              (1-D and 2-D tables, repeated slots), copy_to_kv_cache
+
 ``python tests/golden/make_golden.py mla_fp8`` regenerates one family only.
 """
 
@@ -531,8 +534,63 @@ def make_mla_fp8() -> None:
     st.save("mla_fp8.npz")
 
 
+def make_cache() -> None:
+    st = Store()
+    g = gen(50)
+    names = list(DTYPES)
+    for xn in names:
+        for cn in names:
+            for inter in (False, True):
+                x = (randn((3, 5, 4, 16), torch.float32, g) * 3.0).to(DTYPES[xn])
+                ang = torch.rand((5, 1, 8), generator=g) * 6.0
+                cos, sin = torch.cos(ang).to(DTYPES[cn]), torch.sin(ang).to(DTYPES[cn])
+                out = ref.apply_rope(x, cos, sin, interleaved=inter)
+                p = f"rope/{xn}/{cn}/{int(inter)}"
+                st.put(f"{p}/x", x)
+                st.put(f"{p}/cos", cos)
+                st.put(f"{p}/sin", sin)
+                st.put(f"{p}/out", out)
+    # mixed cos / sin dtypes and a broadcast that grows the output
+    x = (randn((4, 2, 8), torch.float32, g) * 2.0).to(torch.bfloat16)
+    cos = torch.cos(torch.rand((3, 1, 1, 4), generator=g) * 6.0).to(torch.float16)
+    sin = torch.sin(torch.rand((1, 4), generator=g) * 6.0).to(torch.float32)
+    st.put("rope_mixed/x", x)
+    st.put("rope_mixed/cos", cos)
+    st.put("rope_mixed/sin", sin)
+    st.put("rope_mixed/out", ref.apply_rope(x, cos, sin))
+    for cn in names:
+        dt = DTYPES[cn]
+        kc = (randn((4, 2, 8, 4), torch.float32, g) * 2.0).to(dt)
+        slots = torch.tensor([0, 6, -1, 13, 6, 15, 2], dtype=torch.int64)
+        positions = torch.tensor([0, 3, 1, 7, 2, 5, 9], dtype=torch.int64)
+        ang = torch.rand((10, 4), generator=g) * 6.0
+        cos2, sin2 = torch.cos(ang).to(dt), torch.sin(ang).to(dt)
+        p = f"rope_cache/{cn}"
+        st.put(f"{p}/cache_in", kc)
+        st.put(f"{p}/slots", slots)
+        st.put(f"{p}/positions", positions)
+        st.put(f"{p}/cos", cos2)
+        st.put(f"{p}/sin", sin2)
+        out2 = ref.apply_rope_to_key_cache(kc.clone(), slots, positions, cos2, sin2)
+        st.put(f"{p}/cache_out", out2)
+        out1 = ref.apply_rope_to_key_cache(kc.clone(), slots, positions, cos2[4], sin2[4], interleaved=True)
+        st.put(f"{p}/cache_out_1d_inter", out1)
+        k = randn((6, 2, 8), torch.float32, g).to(dt)
+        v = randn((6, 2, 8), torch.float32, g).to(dt)
+        kcc, vcc = torch.zeros((4, 2, 8, 4), dtype=dt), torch.zeros((4, 2, 8, 4), dtype=dt)
+        cslots = torch.tensor([0, 5, -1, 5, 15, 9], dtype=torch.int64)
+        ref.copy_to_kv_cache(k, v, kcc, vcc, cslots)
+        st.put(f"copy/{cn}/k", k)
+        st.put(f"copy/{cn}/v", v)
+        st.put(f"copy/{cn}/slots", cslots)
+        st.put(f"copy/{cn}/kc", kcc)
+        st.put(f"copy/{cn}/vc", vcc)
+    st.save("cache.npz")
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
-    families = {"tile": make_tile, "fp8": make_fp8, "rows": make_rows, "misc": make_misc, "mla_fp8": make_mla_fp8}
+    families = {"tile": make_tile, "fp8": make_fp8, "rows": make_rows, "misc": make_misc, "mla_fp8": make_mla_fp8,
+                "cache": make_cache}
     for name in (sys.argv[1:] or list(families)):
         families[name]()

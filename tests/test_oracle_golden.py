@@ -313,3 +313,49 @@ def test_mla_fp8_rows_codec(mla_fp8, dt, fmt):
     cache = rows[None]
     kv, _ = O.mla_fp8_rows_load(cache, np.arange(x.shape[0]), kv_dim=512, pe_dim=64, out_dtype=dt, fp8_format=fmt)
     assert kv[0].tobytes() == mla_fp8[f"{p}/dec"].tobytes()
+
+
+# ---- `cache` family: RoPE (per-operation rounding) and the KV-cache write -------
+
+
+@pytest.fixture(scope="module")
+def cache_g():
+    return np.load(GOLDEN / "cache.npz")
+
+
+CACHE_DT = ("float32", "float16", "bfloat16")
+
+
+@pytest.mark.parametrize("inter", (0, 1))
+@pytest.mark.parametrize("cn", CACHE_DT)
+@pytest.mark.parametrize("xn", CACHE_DT)
+def test_apply_rope_dtype_pairs(cache_g, xn, cn, inter):
+    p = f"rope/{xn}/{cn}/{inter}"
+    out = O.apply_rope(cache_g[f"{p}/x"], cache_g[f"{p}/cos"], cache_g[f"{p}/sin"], x_dtype=xn, cos_dtype=cn,
+                       sin_dtype=cn, interleaved=bool(inter))
+    assert out.tobytes() == cache_g[f"{p}/out"].tobytes()
+
+
+def test_apply_rope_mixed_and_growing_broadcast(cache_g):
+    out = O.apply_rope(cache_g["rope_mixed/x"], cache_g["rope_mixed/cos"], cache_g["rope_mixed/sin"],
+                       x_dtype="bfloat16", cos_dtype="float16", sin_dtype="float32")
+    assert out.shape == cache_g["rope_mixed/out"].shape
+    assert out.tobytes() == cache_g["rope_mixed/out"].tobytes()
+
+
+@pytest.mark.parametrize("cn", CACHE_DT)
+def test_rope_key_cache_and_copy(cache_g, cn):
+    p = f"rope_cache/{cn}"
+    kc = cache_g[f"{p}/cache_in"].copy()
+    O.apply_rope_to_key_cache(kc, cache_g[f"{p}/slots"], cache_g[f"{p}/positions"], cache_g[f"{p}/cos"],
+                              cache_g[f"{p}/sin"], cache_dtype=cn, cos_dtype=cn, sin_dtype=cn)
+    assert kc.tobytes() == cache_g[f"{p}/cache_out"].tobytes()
+    kc = cache_g[f"{p}/cache_in"].copy()
+    O.apply_rope_to_key_cache(kc, cache_g[f"{p}/slots"], cache_g[f"{p}/positions"], cache_g[f"{p}/cos"][4],
+                              cache_g[f"{p}/sin"][4], cache_dtype=cn, cos_dtype=cn, sin_dtype=cn, interleaved=True)
+    assert kc.tobytes() == cache_g[f"{p}/cache_out_1d_inter"].tobytes()
+    q = f"copy/{cn}"
+    kcc = np.zeros_like(cache_g[f"{q}/kc"])
+    vcc = np.zeros_like(cache_g[f"{q}/vc"])
+    O.copy_to_kv_cache(cache_g[f"{q}/k"], cache_g[f"{q}/v"], kcc, vcc, cache_g[f"{q}/slots"])
+    assert kcc.tobytes() == cache_g[f"{q}/kc"].tobytes() and vcc.tobytes() == cache_g[f"{q}/vc"].tobytes()

@@ -341,6 +341,46 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
         // sectors per instruction) and a contiguous piece of the token row; four items
         // per lane in flight.
         const int hd = static_cast<int>(p.head_dim);
+        if ((hd & 31) == 0) {
+          // head_dim a multiple of 32: lane = dim within a 32-dim group; every lane walks the
+          // same (token, head, group) sequence with carried counters (no divisions), eight
+          // elements in flight per lane.
+          const int mpr = hd >> 5;
+          const int steps = len * NH * mpr;
+          int j = 0, h = 0, m = 0;
+          for (int s0 = 0; s0 < steps; s0 += 8) {
+            CT cv[8];
+            LT lv[8];
+            int pk[8];  // (token << 16) | (head << 8) | group of each element in flight, -1 = none
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              pk[k] = -1;
+              if (s0 + k < steps) {
+                const int d = (m << 5) + lane;
+                pk[k] = (j << 16) | (h << 8) | m;
+                if (!SCATTER) cv[k] = cache_r[cbase + h * p.c_sh + static_cast<int64_t>(d) * p.c_sd + o_s + j];
+                else lv[k] = lin_l[(ts + j) * p.l_st + h * p.l_sh + d];
+                if (++m == mpr) {
+                  m = 0;
+                  if (++h == NH) {
+                    h = 0;
+                    ++j;
+                  }
+                }
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              if (pk[k] < 0) continue;
+              const int jj = pk[k] >> 16, hh = (pk[k] >> 8) & 0xFF, d = ((pk[k] & 0xFF) << 5) + lane;
+              float sc = 1.f;
+              if (CODEC) sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? hh : l * NH + hh)];
+              if (!SCATTER) lin_l[(ts + jj) * p.l_st + hh * p.l_sh + d] = C::load(cv[k], sc);
+              else cache_w[cbase + hh * p.c_sh + static_cast<int64_t>(d) * p.c_sd + o_s + jj] = C::store(lv[k], sc);
+            }
+          }
+          continue;
+        }
         const int per_col = NH * hd;
         const int items = per_col * len;
         for (int base = 0; base < items; base += 128) {

@@ -340,6 +340,21 @@ def rows_pack(*sides):
     return buf
 
 
+_PACK_CACHE: dict = {}
+_PACK_CACHE_MAX = 256
+
+
+def cached(key, build):
+    """Memoise a descriptor buffer for long-lived tensors (KV caches).  ``key`` must include every
+    pointer, shape and stride the buffer encodes, so a hit is always a valid descriptor."""
+    hit = _PACK_CACHE.get(key)
+    if hit is None:
+        if len(_PACK_CACHE) >= _PACK_CACHE_MAX:
+            _PACK_CACHE.clear()
+        hit = _PACK_CACHE[key] = build()
+    return hit
+
+
 def rows_desc_array(sides):
     """A C array of ``mak_rows_desc`` (one per group) for the grouped entry points;
     returns ``(array, keepalive)``."""

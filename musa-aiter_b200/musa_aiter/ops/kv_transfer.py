@@ -825,20 +825,31 @@ def _rows_side_linear(buf: torch.Tensor, layered: bool) -> tuple:
     return ptrs, 1, int(st * e), 0, int(t)
 
 
+def _mla_cache_side(c1: torch.Tensor, c2: torch.Tensor, layered: bool):
+    """(packed paged descriptors of the latent and rope caches, row widths), memoised per cache pair."""
+    key = ("mla", layered, c1.data_ptr(), c1.shape, c1.stride(), c1.dtype, c2.data_ptr(), c2.shape, c2.stride(), c2.dtype)
+
+    def build():
+        buf = _native.rows_pack(_rows_side_paged(c1, layered), _rows_side_paged(c2, layered))
+        rb = (ctypes.c_int64 * 2)(c1.shape[-1] * c1.element_size(), c2.shape[-1] * c2.element_size())
+        return buf, ctypes.addressof(buf), rb
+
+    return _native.cached(key, build)
+
+
 def _mla_pair_gather(kv_cache: torch.Tensor, pe_cache: torch.Tensor, slots: torch.Tensor, okv: torch.Tensor,
                      ope: torch.Tensor, *, layered: bool, op: str) -> None:
     """Latent and rope caches -> linear rows in ONE launch (two plane geometries, one slot vector)."""
     lib = _native.load()
-    c1, _ = _as_unit_inner(kv_cache)
-    c2, _ = _as_unit_inner(pe_cache)
+    c1 = kv_cache if kv_cache.stride(-1) == 1 else kv_cache.contiguous()
+    c2 = pe_cache if pe_cache.stride(-1) == 1 else pe_cache.contiguous()
     w1, t1 = _as_unit_inner(okv)
     w2, t2 = _as_unit_inner(ope)
     ks, code = kernel_slots(slots)
-    buf = _native.rows_pack(_rows_side_paged(c1, layered), _rows_side_paged(c2, layered),
-                            _rows_side_linear(w1, layered), _rows_side_linear(w2, layered))
-    base = ctypes.addressof(buf)
-    rb = (ctypes.c_int64 * 2)(c1.shape[-1] * c1.element_size(), c2.shape[-1] * c2.element_size())
-    rc = lib.mak_rows_gatherv(base, base + 96, 2, rb, 0, ks.data_ptr(), code, ks.numel(), 1, _native.stream_ptr(c1.device))
+    _, paged, rb = _mla_cache_side(c1, c2, layered)
+    lin = _native.rows_pack(_rows_side_linear(w1, layered), _rows_side_linear(w2, layered))
+    rc = lib.mak_rows_gatherv(paged, ctypes.addressof(lin), 2, rb, 0, ks.data_ptr(), code, ks.numel(), 1,
+                              _native.stream_ptr(c1.device))
     _native.check(rc, op)
     if t1:
         okv.copy_(w1)
@@ -855,13 +866,11 @@ def _mla_pair_scatter(kv_linear: torch.Tensor, pe_linear: torch.Tensor, kv_cache
     w1, t1 = _as_unit_inner(kv_cache)
     w2, t2 = _as_unit_inner(pe_cache)
     ks, code = kernel_slots(slots)
-    buf = _native.rows_pack(_rows_side_linear(l1, layered), _rows_side_linear(l2, layered),
-                            _rows_side_paged(w1, layered), _rows_side_paged(w2, layered))
-    base = ctypes.addressof(buf)
-    rb = (ctypes.c_int64 * 2)(w1.shape[-1] * w1.element_size(), w2.shape[-1] * w2.element_size())
+    _, paged, rb = _mla_cache_side(w1, w2, layered)
+    lin = _native.rows_pack(_rows_side_linear(l1, layered), _rows_side_linear(l2, layered))
     ws, nbytes = _native.workspace(ks.numel(), w1.device)
-    rc = lib.mak_rows_scatterv(base, base + 96, 2, rb, 0, ks.data_ptr(), code, ks.numel(), 0, ws.data_ptr(), nbytes,
-                               _native.stream_ptr(w1.device))
+    rc = lib.mak_rows_scatterv(ctypes.addressof(lin), paged, 2, rb, 0, ks.data_ptr(), code, ks.numel(), 0,
+                               ws.data_ptr(), nbytes, _native.stream_ptr(w1.device))
     _native.check(rc, op)
     if t1:
         kv_cache.copy_(w1)
@@ -964,10 +973,11 @@ def kv_paged_to_mla_linear_multi_layer(
     """Stacked ``[L, NB, BS, W]`` MLA caches -> ``[L, T, W]`` (reference kv_transfer.py:3982-4050)."""
     name = "kv_paged_to_mla_linear_multi_layer"
     nl, nb, bs, kv_dim, pe_dim = _validate_stacked_mla_shapes(kv_cache, k_pe_cache, name=name)
-    if k_pe_cache.dtype != kv_cache.dtype or k_pe_cache.device != kv_cache.device:
+    dev_id = kv_cache.get_device()
+    if k_pe_cache.dtype != kv_cache.dtype or k_pe_cache.get_device() != dev_id:
         raise ValueError(f"{name}: caches must share dtype and device")
     slots = ensure_slotmapping_vector(slot_mapping, expected_len=int(slot_mapping.numel()), name=name)
-    if slots.device != kv_cache.device:
+    if slots.get_device() != dev_id:
         raise ValueError(f"{name}: slot_mapping must share device")
     check_slots_in_bounds(slots, nb, bs, name)
     require_cuda(name, kv_cache, k_pe_cache, slots)
@@ -1000,7 +1010,8 @@ def kv_mla_linear_to_paged_multi_layer(
         raise ValueError(f"{name}: hidden dims must match caches")
     if kv_linear.dtype != kv_cache.dtype or k_pe_linear.dtype != k_pe_cache.dtype:
         raise ValueError(f"{name}: dtypes must match caches")
-    if any(t.device != kv_cache.device for t in (kv_linear, k_pe_linear, kv_cache, k_pe_cache, slot_mapping)):
+    dev_id = kv_cache.get_device()
+    if any(t.get_device() != dev_id for t in (kv_linear, k_pe_linear, k_pe_cache, slot_mapping)):
         raise ValueError(f"{name}: all tensors must share device")
     tcount = int(kv_linear.shape[1])
     slots = ensure_slotmapping_vector(slot_mapping, expected_len=tcount, name=name)
@@ -1054,11 +1065,15 @@ def _mla_fp8_descs(kv, pe, cache_rows):
     lin = _native.MlaLinearDesc(kv.data_ptr(), pe.data_ptr(), int(kv.shape[0]), int(kv.shape[1]), int(kv.shape[2]),
                                 int(pe.shape[2]), kv.stride(0), kv.stride(1), pe.stride(0), pe.stride(1),
                                 _native.dtype_code(kv.dtype), 0)
-    base = cache_rows.data_ptr()
-    s0, sb, st, _ = cache_rows.stride()
-    nb, bs = int(cache_rows.shape[1]), int(cache_rows.shape[2])
-    buf = _native.rows_pack(([base + i * s0 for i in range(cache_rows.shape[0])], bs, sb, st, nb * bs))
-    return lin, buf
+    key = ("mlafp8", cache_rows.data_ptr(), cache_rows.shape, cache_rows.stride())
+
+    def build():
+        base = cache_rows.data_ptr()
+        s0, sb, st, _ = cache_rows.stride()
+        nb, bs = int(cache_rows.shape[1]), int(cache_rows.shape[2])
+        return _native.rows_pack(([base + i * s0 for i in range(cache_rows.shape[0])], bs, sb, st, nb * bs))
+
+    return lin, _native.cached(key, build)
 
 
 def _rows_ok(t: torch.Tensor, align: int) -> bool:

@@ -293,7 +293,10 @@ def _contains_nested_cache_list(kvcaches: list[Any]) -> bool:
     return any(isinstance(axis_or_tensor, list) for axis_or_tensor in kvcaches)
 
 
-def _validate_two_x_nl_contract(memory_tensor, kvcaches, slot_mapping, skip_prefix_n_tokens, block_size, num_heads, head_size) -> None:
+def _validate_two_x_nl_contract(memory_tensor, kvcaches, slot_mapping, skip_prefix_n_tokens, block_size, num_heads,
+                                head_size) -> tuple | None:
+    """Reference checks (lmcache_kv_transfer.py:323-393); returns the caches' row-plane geometry when
+    they share one strided layout with contiguous token rows, else None."""
     name = "LMCache TWO_X_NL_X_NB_BS_NH_HS"
     if memory_tensor.dim() != 4 or int(memory_tensor.shape[0]) != 2:
         raise ValueError(f"{name} memory_tensor must be [2, NL, T, NH*HS]")
@@ -323,17 +326,32 @@ def _validate_two_x_nl_contract(memory_tensor, kvcaches, slot_mapping, skip_pref
     expected_shape = (num_blocks, block_size, num_heads, head_size)
     if num_blocks <= 0:
         raise ValueError(f"{name} num_blocks must be positive")
+    # One pass over the 2*NL caches: the reference's checks in its order, and (as a by-product)
+    # the plane pointers when every cache shares one strided layout with contiguous token rows.
+    mdt, mdev = memory_tensor.dtype, memory_tensor.get_device()
+    stride0 = first.stride()
+    uniform = _rows_contiguous(first, 2)
+    ptrs = []
     for kv_axis, layers in enumerate(kvcaches):
         for layer, cache in enumerate(layers):
-            if not isinstance(cache, torch.Tensor) or tuple(cache.shape) != expected_shape:
+            if not isinstance(cache, torch.Tensor) or cache.shape != expected_shape:
                 raise ValueError(f"{name} cache[{kv_axis}][{layer}] must have shape {expected_shape}")
-            if cache.dtype != memory_tensor.dtype:
+            if cache.dtype != mdt:
                 raise ValueError(f"{name} cache dtype must match memory_tensor")
-            if cache.device != memory_tensor.device:
+            if cache.get_device() != mdev:
                 raise ValueError(f"{name} caches and memory_tensor must share a device")
-    if slot_mapping.device != memory_tensor.device:
+            if uniform:
+                if cache.stride() == stride0:
+                    ptrs.append(cache.data_ptr())
+                else:
+                    uniform = False
+    if slot_mapping.get_device() != mdev:
         raise ValueError(f"{name} slot_mapping and data tensors must share a device")
     _validate_slots(slot_mapping, num_tokens=int(slot_mapping.numel()), num_blocks=num_blocks, block_size=block_size)
+    if not uniform:
+        return None
+    e = first.element_size()
+    return ptrs, block_size, stride0[0] * e, stride0[1] * e, num_blocks * block_size
 
 
 def _validate_non_mla_list_contract(memory_tensor, kvcaches, slot_mapping, block_size, num_heads, head_size) -> None:
@@ -574,11 +592,11 @@ def lmcache_kv_buffer_to_paged_two_x_nl(
 
     Reference: lmcache_kv_transfer.py:176-226 (memory token ``skip + t`` goes to ``slot_mapping[t]``).
     """
-    _validate_two_x_nl_contract(memory_tensor, kvcaches, slot_mapping, skip_prefix_n_tokens, block_size, num_heads, head_size)
-    require_cuda("lmcache_kv_buffer_to_paged_two_x_nl", memory_tensor, slot_mapping, *kvcaches[0], *kvcaches[1])
+    pside = _validate_two_x_nl_contract(memory_tensor, kvcaches, slot_mapping, skip_prefix_n_tokens, block_size, num_heads,
+                                        head_size)
+    require_cuda("lmcache_kv_buffer_to_paged_two_x_nl", memory_tensor, slot_mapping, kvcaches[0][0])
     nl = len(kvcaches[0])
     hidden = num_heads * head_size
-    pside = _list_cache_side(kvcaches[0] + kvcaches[1], [0], 0, memory_tensor.dtype)
     lside = _stacked_buffer_side(memory_tensor, 2, nl)
     if pside is not None and lside is not None:
         _fast_scatter("lmcache_kv_buffer_to_paged_two_x_nl", lside, pside, hidden * memory_tensor.element_size(),
@@ -605,11 +623,10 @@ def lmcache_kv_paged_to_buffer_two_x_nl(
     head_size: int,
 ) -> bool:
     """Gather SGLang MP caches into ``[2, NL, T, H]`` (whole buffer written; reference :229-269)."""
-    _validate_two_x_nl_contract(memory_tensor, kvcaches, slot_mapping, 0, block_size, num_heads, head_size)
-    require_cuda("lmcache_kv_paged_to_buffer_two_x_nl", memory_tensor, slot_mapping, *kvcaches[0], *kvcaches[1])
+    pside = _validate_two_x_nl_contract(memory_tensor, kvcaches, slot_mapping, 0, block_size, num_heads, head_size)
+    require_cuda("lmcache_kv_paged_to_buffer_two_x_nl", memory_tensor, slot_mapping, kvcaches[0][0])
     nl = len(kvcaches[0])
     hidden = num_heads * head_size
-    pside = _list_cache_side(kvcaches[0] + kvcaches[1], [0], 0, memory_tensor.dtype)
     lside = _stacked_buffer_side(memory_tensor, 2, nl)
     if pside is not None and lside is not None:
         _fast_gather("lmcache_kv_paged_to_buffer_two_x_nl", pside, lside, hidden * memory_tensor.element_size(),

@@ -11,7 +11,8 @@
  *
  * The library allocates no device memory.  Entry points that need scratch
  * memory (last-writer-wins resolution of duplicate destination slots) take a
- * caller-owned workspace whose size is given by `mak_scatter_workspace_bytes`.
+ * caller-owned workspace whose size is given by `mak_scatter_workspace_bytes`,
+ * or (the *_owned forms) a caller-kept owner table that persists across calls.
  *
  * Layout vocabulary (element strides unless stated otherwise):
  *   - "tile" caches keep block_size innermost: [L][NB][NH][HD][BS]
@@ -276,6 +277,24 @@ MAK_API int mak_rows_scatterv(const mak_rows_desc* linear, const mak_rows_desc* 
                               void* stream);
 
 /*
+ * mak_rows_scatterv with the last writer found through a caller-kept owner
+ * table instead of the per-call workspace hash: one marking kernel sets
+ * owner[slot] = max(owner[slot], epoch << 32 | token) and the copy moves a
+ * token only while the entry still carries its own tag, so a scatter is two
+ * launches (no memset, no resolve pass).  `owner` holds owner_rows uint64
+ * entries in device memory (owner_rows >= every group's paged num_rows), is
+ * zeroed once by the caller and then reused; every call on one table takes a
+ * larger epoch than the calls before it (1 .. 2^32-1; after that zero the table
+ * and restart at 1), and calls that share a table run in stream order (one
+ * table per stream).  n_slots < 2^32.  Same results as mak_rows_scatterv
+ * (reference semantics: musa_aiter/ops/kv_transfer.py:3092-3112, last token wins).
+ */
+MAK_API int mak_rows_scatterv_owned(const mak_rows_desc* linear, const mak_rows_desc* paged, int32_t n_groups,
+                                    const int64_t* row_bytes, int64_t row_bytes0, const void* slots,
+                                    int32_t slot_dtype, int64_t n_slots, int64_t skip_prefix, uint64_t* owner,
+                                    int64_t owner_rows, uint32_t epoch, void* stream);
+
+/*
  * Allocation-free row scatter.  No counterpart in the reference: it exists for
  * callers that cannot call cudaMalloc (a serving engine that reserved its HBM
  * up front and scatters inside its step loop, or a foreign-language caller
@@ -421,6 +440,25 @@ MAK_API int mak_mla_fp8_rows_store(const mak_mla_linear_desc* lin, const mak_row
                                    void* stream);
 MAK_API int mak_mla_fp8_rows_load(const mak_rows_desc* cache, const mak_mla_linear_desc* lin, const void* slots,
                                   int32_t slot_dtype, int32_t fp8_format, void* stream);
+/* store with the owner-table last-writer resolution of mak_rows_scatterv_owned
+ * (owner_rows >= cache->num_rows; same table and epoch rules). */
+MAK_API int mak_mla_fp8_rows_store_owned(const mak_mla_linear_desc* lin, const mak_rows_desc* cache,
+                                         const void* slots, int32_t slot_dtype, int32_t fp8_format, uint64_t* owner,
+                                         int64_t owner_rows, uint32_t epoch, void* stream);
+
+/*
+ * Self-check of the store's division-free quotient (a reciprocal per group and
+ * Markstein's correction step per value) against the IEEE fp32 division on this
+ * device: for the 2^23 scales 2^scale_exp * [1, 2) and every 16-bit input of
+ * elem_dtype (MAK_DT_BF16 / MAK_DT_F16) that a group with that scale can hold,
+ * adds to counts[0] the FP8 codes that differ and to counts[1] the quotients
+ * >= 2^-14 in magnitude that differ in any bit (device memory, 2 x uint64,
+ * zeroed by the caller).  Scales outside the fast range ([2^-60, 2^16]) take
+ * the IEEE division in the store and are not counted.  No reference
+ * counterpart: a test entry point.
+ */
+MAK_API int mak_fp8_quotient_selfcheck(int32_t elem_dtype, int32_t fp8_format, int32_t scale_exp, uint64_t* counts,
+                                       void* stream);
 
 /* ---- rotary position embedding (the `cache` family) ----------------------- */
 

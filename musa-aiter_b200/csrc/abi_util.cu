@@ -164,6 +164,29 @@ __global__ void hash_resolve_kernel(const void* slots, int is64, int64_t n, cons
   }
 }
 
+__global__ void owner_mark_kernel(const void* slots, int is64, int64_t n, unsigned long long* owner, int64_t rows,
+                                  unsigned long long tag_hi) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t s = load_index(slots, is64, i);
+    if (s >= 0 && s < rows) atomicMax(owner + s, tag_hi | static_cast<unsigned long long>(i));
+  }
+}
+
+int mark_owners(const void* slots, int32_t slot_dtype, int64_t n, uint64_t* owner, int64_t owner_rows, uint32_t epoch,
+                cudaStream_t st, const char* name) {
+  if (owner == nullptr || owner_rows < 0) return fail(MAK_E_INVALID, "%s: owner table is NULL", name);
+  if ((reinterpret_cast<uintptr_t>(owner) & 7u) != 0) return fail(MAK_E_INVALID, "%s: owner table must be 8-byte aligned", name);
+  if (epoch == 0) return fail(MAK_E_INVALID, "%s: epoch must be at least 1", name);
+  if (n >= (int64_t{1} << 32)) return fail(MAK_E_UNSUPPORTED, "%s: owner tables take fewer than 2^32 items", name);
+  if (n == 0) return MAK_OK;
+  const int threads = 256;
+  const int grid = grid_for(reinterpret_cast<const void*>(owner_mark_kernel), threads, 0, (n + threads - 1) / threads);
+  owner_mark_kernel<<<grid, threads, 0, st>>>(slots, slot_dtype == MAK_DT_I64, n,
+                                              reinterpret_cast<unsigned long long*>(owner), owner_rows,
+                                              static_cast<unsigned long long>(epoch) << 32);
+  return launch_status("owner_mark_kernel");
+}
+
 int64_t hash_capacity(int64_t n) {
   int64_t c = 64;
   while (c < 2 * n) c <<= 1;

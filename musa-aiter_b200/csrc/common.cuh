@@ -45,6 +45,11 @@ int64_t hash_capacity(int64_t n);
 int carve_scatter_ws(void* ws, size_t ws_bytes, int64_t n, ScatterWs* out);
 // Resolves duplicates of `slots` into ws.eff (last index wins).  Returns MAK_OK or error.
 int resolve_last_writer(const void* slots, int32_t slot_dtype, int64_t n, const ScatterWs& ws, cudaStream_t st);
+// Owner-table last-writer marking: owner[slot] = max(owner[slot], epoch << 32 | i)
+// for every in-range slot i < n (n < 2^32, epoch >= 1).  The consuming kernel
+// lets item i write only while owner[slot] still equals its own tag.
+int mark_owners(const void* slots, int32_t slot_dtype, int64_t n, uint64_t* owner, int64_t owner_rows, uint32_t epoch,
+                cudaStream_t st, const char* name);
 
 // ---- device helpers -----------------------------------------------------------
 __device__ __forceinline__ int64_t load_index(const void* p, int is64, int64_t i) {

@@ -89,10 +89,12 @@ __device__ __forceinline__ uint32_t cvt_e5m2x2(float hi, float lo) {
   return r;
 }
 
+// fp8_encode2 with the sign read from separate values (g0, g1): the sign of
+// w is the sign of g wherever the two differ only by rounding (see fast_quot).
 template <int F>
-__device__ __forceinline__ uint32_t fp8_encode2(float w0, float w1) {
-  const uint32_t s0 = (w0 < 0.f) ? 0x80u : 0u;
-  const uint32_t s1 = (w1 < 0.f) ? 0x80u : 0u;
+__device__ __forceinline__ uint32_t fp8_encode2s(float g0, float w0, float g1, float w1) {
+  const uint32_t s0 = (g0 < 0.f) ? 0x80u : 0u;
+  const uint32_t s1 = (g1 < 0.f) ? 0x80u : 0u;
   const float a0 = fabsf(w0), a1 = fabsf(w1);
   const bool fin0 = a0 <= 3.40282346638528859812e+38f, fin1 = a1 <= 3.40282346638528859812e+38f;
   uint32_t c0, c1;
@@ -115,6 +117,34 @@ __device__ __forceinline__ uint32_t fp8_encode2(float w0, float w1) {
   return (s0 | c0) | ((s1 | c1) << 8);
 }
 
+template <int F>
+__device__ __forceinline__ uint32_t fp8_encode2(float w0, float w1) {
+  return fp8_encode2s<F>(w0, w0, w1, w1);
+}
+
+// x / s rounded to nearest in fp32 without a division per value, by
+// Markstein's correction step (P. Markstein, "IA-64 and Elementary Functions",
+// 2000): with y = RN(1/s) and q0 = RN(x * y), q0 is within one ulp of x / s,
+// the remainder r = x - s * q0 is exact in one fma, and RN(q0 + r * y) is the
+// correctly rounded quotient, as long as r does not underflow.  For s in
+// [2^-60, 2^16] (fast_quot_ok) and |x / s| at most a few times the FP8
+// maximum, that holds wherever the FP8 code depends on the magnitude
+// (|x / s| >= 2^-14); below that only the sign and non-zero-ness of the
+// quotient reach the encoder, and q0 and q1 both keep them (|x / s| >= 2^-149
+// for every non-zero 16-bit x).  Non-finite x: q0 = x * y carries the IEEE
+// quotient's sign and class while q1 is nan, so callers read the sign from q0
+// (fp8_encode2s).  mak_fp8_quotient_selfcheck compares the path with the IEEE
+// division for every 16-bit input and every scale significand.
+struct FastQuot {
+  float q0, q1;
+};
+__device__ __forceinline__ bool fast_quot_ok(float s) { return s >= 0x1p-60f && s <= 0x1p16f; }
+__device__ __forceinline__ FastQuot fast_quot(float x, float s, float y) {
+  const float q0 = __fmul_rn(x, y);
+  const float r = __fmaf_rn(-q0, s, x);
+  return {q0, __fmaf_rn(r, y, q0)};
+}
+
 // Decoder (musa_aiter/ops/kv_transfer.py:2186-2200): exponent field 0 -> 0,
 // otherwise (1 + m / 2^mb) * 2^(e - bias), all codes finite; built bit-exactly.
 template <int F>
@@ -126,6 +156,21 @@ __device__ __forceinline__ float fp8_decode(uint32_t code) {
   uint32_t bits = e ? (((e - bias + 127u) << 23) | (m << (23 - mb))) : 0u;
   bits |= (code & 0x80u) << 24;
   return __uint_as_float(bits);
+}
+
+// The same decoder for a code held in the top byte of x (the low 24 bits zero,
+// as __byte_perm leaves it): the magnitude bits shift straight into the fp32
+// exponent and mantissa fields, the exponent bias is one add, and exponent
+// field 0 keeps only the sign.
+template <int F>
+__device__ __forceinline__ float fp8_decode_top(uint32_t x) {
+  constexpr int mb = (F == MAK_FP8_E4M3) ? 3 : 2;
+  constexpr int bias = (F == MAK_FP8_E4M3) ? 7 : 15;
+  constexpr uint32_t kMag = 0x7Fu << (23 - mb);
+  constexpr uint32_t kExp = ((1u << (7 - mb)) - 1u) << (24 + mb);
+  const uint32_t sign = x & 0x80000000u;
+  const uint32_t bits = (((x >> (1 + mb)) & kMag) + (static_cast<uint32_t>(127 - bias) << 23)) | sign;
+  return __uint_as_float((x & kExp) ? bits : sign);
 }
 
 }  // namespace mak

@@ -30,6 +30,9 @@ struct MlaLaunch {
   int32_t lg_rows;    // log2(rows_per_block) or -1
   int32_t kv_dim;
   int32_t pe_bytes;   // rope bytes per row (multiple of 8)
+  // store, owner-table mode: token t writes only while owner[row] == tag_hi | t
+  const unsigned long long* owner;
+  uint64_t tag_hi;
 };
 
 __device__ __forceinline__ int64_t mla_row_offset(const MlaLaunch& p, int64_t r) {
@@ -124,6 +127,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
   for (int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < p.num_tokens; t += step) {
     const int64_t dr = load_index(p.idx, p.idx64, t);
     if (dr < 0 || dr >= p.num_rows) continue;
+    if (p.owner != nullptr && __ldcg(p.owner + dr) != (p.tag_hi | static_cast<uint64_t>(t))) continue;
     unsigned char* row = plane + mla_row_offset(p, dr);
     // latent values of this lane
     const uint4* src = reinterpret_cast<const uint4*>(kv_layer + t * p.kv_st + lane * E * 2);
@@ -148,11 +152,22 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
     for (int o = 1; o < kLanesPerGroup; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float scale = __fdiv_rn(amax, fp8_max_of<F>());
     Bytes<E> codes;
+    if (fast_quot_ok(scale)) {
+      // one reciprocal per group, three fp32 operations per value (fp8.cuh)
+      const float y = __frcp_rn(scale);
 #pragma unroll
-    for (int j = 0; j < E / 4; ++j) {
-      const uint32_t lo = fp8_encode2<F>(__fdiv_rn(x[4 * j], scale), __fdiv_rn(x[4 * j + 1], scale));
-      const uint32_t hi = fp8_encode2<F>(__fdiv_rn(x[4 * j + 2], scale), __fdiv_rn(x[4 * j + 3], scale));
-      codes.w[j] = lo | (hi << 16);
+      for (int j = 0; j < E / 4; ++j) {
+        const FastQuot a = fast_quot(x[4 * j], scale, y), b = fast_quot(x[4 * j + 1], scale, y);
+        const FastQuot c = fast_quot(x[4 * j + 2], scale, y), d = fast_quot(x[4 * j + 3], scale, y);
+        codes.w[j] = fp8_encode2s<F>(a.q0, a.q1, b.q0, b.q1) | (fp8_encode2s<F>(c.q0, c.q1, d.q0, d.q1) << 16);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < E / 4; ++j) {
+        const uint32_t lo = fp8_encode2<F>(__fdiv_rn(x[4 * j], scale), __fdiv_rn(x[4 * j + 1], scale));
+        const uint32_t hi = fp8_encode2<F>(__fdiv_rn(x[4 * j + 2], scale), __fdiv_rn(x[4 * j + 3], scale));
+        codes.w[j] = lo | (hi << 16);
+      }
     }
     store_bytes<E>(row + lane * E, codes);
     if ((lane % kLanesPerGroup) == 0) reinterpret_cast<float*>(row + p.kv_dim)[lane / kLanesPerGroup] = scale;
@@ -193,10 +208,12 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_load_kernel(const __grid_
       uint32_t w[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int i0 = 8 * k + 2 * j;
-        const uint32_t c0 = (codes.w[i0 >> 2] >> (8 * (i0 & 3))) & 0xFFu;
-        const uint32_t c1 = (codes.w[(i0 + 1) >> 2] >> (8 * ((i0 + 1) & 3))) & 0xFFu;
-        w[j] = pack2<T>(__fmul_rn(fp8_decode<F>(c0), scale), __fmul_rn(fp8_decode<F>(c1), scale));
+        // codes 2j, 2j+1 of word 2k + j/2, each moved to the top byte
+        const uint32_t cw = codes.w[2 * k + (j >> 1)];
+        const int b = 2 * (j & 1);
+        const uint32_t x0 = __byte_perm(cw, 0u, 0x0444u | (b << 12));
+        const uint32_t x1 = __byte_perm(cw, 0u, 0x0444u | ((b + 1) << 12));
+        w[j] = pack2<T>(__fmul_rn(fp8_decode_top<F>(x0), scale), __fmul_rn(fp8_decode_top<F>(x1), scale));
       }
       dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
     }
@@ -315,6 +332,43 @@ static int dispatch(MlaLaunch& L, const mak_mla_linear_desc* lin, const mak_rows
                              : dispatch_e<STORE, __half, MAK_FP8_E5M2>(L, lin, cache, st);
 }
 
+// Self-check of the division-free quotient (fast_quot) against the IEEE fp32
+// division: thread k takes the scale s = 2^scale_exp * (1 + k / 2^23) and every
+// 16-bit input x of type T with |x| <= 2 * fp8_max * s (the inputs a group with
+// that scale can hold), and counts (a) FP8 codes that differ from
+// fp8_encode(x / s) and (b) quotients with |x / s| >= 2^-14 that differ in any
+// bit.  Only scales the store kernel sends down the fast path are tested.
+template <typename T, int F>
+__global__ void fp8_quotient_check_kernel(int scale_exp, unsigned long long* counts) {
+  const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= (1u << 23)) return;
+  const float s = __uint_as_float((static_cast<uint32_t>(scale_exp + 127) << 23) | k);
+  unsigned long long bad_code = 0, bad_quot = 0;
+  if (fast_quot_ok(s)) {
+    const float y = __frcp_rn(s);
+    const float lim = 2.f * fp8_max_of<F>() * s;
+    for (uint32_t u = 0; u < 65536u; u += 2) {
+      const float x0 = bits_to_f32<T>(u), x1 = bits_to_f32<T>(u + 1);
+      const FastQuot a = fast_quot(x0, s, y), b = fast_quot(x1, s, y);
+      const float w0 = __fdiv_rn(x0, s), w1 = __fdiv_rn(x1, s);
+      const uint32_t got = fp8_encode2s<F>(a.q0, a.q1, b.q0, b.q1);
+      const bool in0 = !(fabsf(x0) > lim), in1 = !(fabsf(x1) > lim);  // nan inputs stay in
+      bad_code += (in0 && (got & 0xFFu) != fp8_encode<F>(w0)) + (in1 && (got >> 8) != fp8_encode<F>(w1));
+      bad_quot += (in0 && fabsf(w0) >= 0x1p-14f && __float_as_uint(w0) != __float_as_uint(a.q1)) +
+                  (in1 && fabsf(w1) >= 0x1p-14f && __float_as_uint(w1) != __float_as_uint(b.q1));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    bad_code += __shfl_xor_sync(0xffffffffu, bad_code, o);
+    bad_quot += __shfl_xor_sync(0xffffffffu, bad_quot, o);
+  }
+  if ((threadIdx.x & 31) == 0 && (bad_code | bad_quot)) {
+    atomicAdd(counts, bad_code);
+    atomicAdd(counts + 1, bad_quot);
+  }
+}
+
 }  // namespace mak
 
 using namespace mak;
@@ -343,6 +397,29 @@ int mak_mla_fp8_rows_store(const mak_mla_linear_desc* lin, const mak_rows_desc* 
   return dispatch<true>(L, lin, cache, fp8_format, st);
 }
 
+int mak_mla_fp8_rows_store_owned(const mak_mla_linear_desc* lin, const mak_rows_desc* cache, const void* slots,
+                                 int32_t slot_dtype, int32_t fp8_format, uint64_t* owner, int64_t owner_rows,
+                                 uint32_t epoch, void* stream) {
+  const char* name = "mak_mla_fp8_rows_store_owned";
+  MlaLaunch L;
+  int rc = mla_prepare(lin, cache, fp8_format, name, &L);
+  if (rc) return rc;
+  if (lin->num_tokens == 0 || lin->num_layers == 0) return MAK_OK;
+  if (slots == nullptr || !valid_index_dtype(slot_dtype))
+    return fail(MAK_E_INVALID, "%s: slot vector must be int32 or int64", name);
+  if (owner_rows < cache->num_rows)
+    return fail(MAK_E_INVALID, "%s: owner table has %lld rows, the cache %lld", name, (long long)owner_rows,
+                (long long)cache->num_rows);
+  cudaStream_t st = as_stream(stream);
+  rc = mark_owners(slots, slot_dtype, lin->num_tokens, owner, owner_rows, epoch, st, name);
+  if (rc) return rc;
+  L.idx = slots;
+  L.idx64 = slot_dtype == MAK_DT_I64;
+  L.owner = reinterpret_cast<const unsigned long long*>(owner);
+  L.tag_hi = static_cast<uint64_t>(epoch) << 32;
+  return dispatch<true>(L, lin, cache, fp8_format, st);
+}
+
 int mak_mla_fp8_rows_load(const mak_rows_desc* cache, const mak_mla_linear_desc* lin, const void* slots,
                           int32_t slot_dtype, int32_t fp8_format, void* stream) {
   MlaLaunch L;
@@ -354,6 +431,27 @@ int mak_mla_fp8_rows_load(const mak_rows_desc* cache, const mak_mla_linear_desc*
   L.idx = slots;
   L.idx64 = slot_dtype == MAK_DT_I64;
   return dispatch<false>(L, lin, cache, fp8_format, as_stream(stream));
+}
+
+int mak_fp8_quotient_selfcheck(int32_t elem_dtype, int32_t fp8_format, int32_t scale_exp, uint64_t* counts,
+                               void* stream) {
+  if (counts == nullptr) return fail(MAK_E_INVALID, "mak_fp8_quotient_selfcheck: counts is NULL");
+  if (elem_dtype != MAK_DT_BF16 && elem_dtype != MAK_DT_F16)
+    return fail(MAK_E_UNSUPPORTED, "mak_fp8_quotient_selfcheck: element dtype must be float16 or bfloat16");
+  if (fp8_format != MAK_FP8_E4M3 && fp8_format != MAK_FP8_E5M2)
+    return fail(MAK_E_INVALID, "mak_fp8_quotient_selfcheck: bad fp8 format");
+  if (scale_exp < -126 || scale_exp > 127) return fail(MAK_E_INVALID, "mak_fp8_quotient_selfcheck: scale_exp out of range");
+  cudaStream_t st = as_stream(stream);
+  auto* c = reinterpret_cast<unsigned long long*>(counts);
+  const dim3 grid((1u << 23) / 256);
+  if (elem_dtype == MAK_DT_BF16) {
+    if (fp8_format == MAK_FP8_E4M3) fp8_quotient_check_kernel<__nv_bfloat16, MAK_FP8_E4M3><<<grid, 256, 0, st>>>(scale_exp, c);
+    else fp8_quotient_check_kernel<__nv_bfloat16, MAK_FP8_E5M2><<<grid, 256, 0, st>>>(scale_exp, c);
+  } else {
+    if (fp8_format == MAK_FP8_E4M3) fp8_quotient_check_kernel<__half, MAK_FP8_E4M3><<<grid, 256, 0, st>>>(scale_exp, c);
+    else fp8_quotient_check_kernel<__half, MAK_FP8_E5M2><<<grid, 256, 0, st>>>(scale_exp, c);
+  }
+  return launch_status("fp8_quotient_check_kernel");
 }
 
 }  // extern "C"

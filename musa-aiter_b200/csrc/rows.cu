@@ -59,6 +59,10 @@ struct RowLaunch {
   int32_t num_planes;
   int32_t zero_fill;    // write zeros where the source row is missing
   uint8_t lgchunk[kRowPlanes];  // log2 of each plane's chunk length (items per warp chunk, <= 32)
+  // Owner-table mode (dst_idx set): item i writes only while owner[dst] == tag_hi | i.
+  const unsigned long long* owner;
+  int64_t owner_rows;
+  uint64_t tag_hi;
 };
 static_assert(sizeof(RowLaunch) <= 4096, "row launch parameters must fit the classic 4 KB parameter block");
 
@@ -94,7 +98,14 @@ __device__ __forceinline__ void fetch_item(const RowLaunch& p, int64_t i, bool l
   if (!live) return;
   const bool indexed = i < p.n_items;
   if (p.dst_idx != nullptr) {
-    if (indexed) *dr = load_index(p.dst_idx, p.dst_idx64, i);
+    if (indexed) {
+      *dr = load_index(p.dst_idx, p.dst_idx64, i);
+      if (p.owner != nullptr) {
+        const int64_t r = *dr;
+        const bool own = r >= 0 && r < p.owner_rows && __ldcg(p.owner + r) == (p.tag_hi | static_cast<uint64_t>(i));
+        *dr = own ? r : -1;
+      }
+    }
   } else {
     *dr = i + p.dst_base;
   }
@@ -286,6 +297,9 @@ struct RowCall {
   int64_t src_base;
   int64_t dst_base;
   int32_t zero_fill;
+  const unsigned long long* owner;  // owner-table last-writer mode (see mak_rows_scatterv_owned)
+  int64_t owner_rows;
+  uint64_t tag_hi;
 };
 
 static int check_side(const mak_rows_desc* s, const char* name) {
@@ -392,6 +406,9 @@ static int run_rows(const RowCall& c, cudaStream_t st, const char* name) {
     L.dst_base = c.dst_base;
     L.num_planes = static_cast<int32_t>(np);
     L.zero_fill = c.zero_fill;
+    L.owner = c.owner;
+    L.owner_rows = c.owner_rows;
+    L.tag_hi = c.tag_hi;
     for (int64_t q = 0; q < np; ++q) L.lgchunk[q] = static_cast<uint8_t>(glg[L.sg[q]]);
     switch (vec) {
       case 16: rc = launch_rows_vec<16>(L, st); break;
@@ -476,6 +493,41 @@ int mak_rows_scatterv(const mak_rows_desc* linear, const mak_rows_desc* paged, i
   c.n_total = n_slots;
   c.src_base = skip_prefix;
   return run_rows(c, st, "mak_rows_scatter");
+}
+
+int mak_rows_scatterv_owned(const mak_rows_desc* linear, const mak_rows_desc* paged, int32_t n_groups,
+                            const int64_t* row_bytes, int64_t row_bytes0, const void* slots, int32_t slot_dtype,
+                            int64_t n_slots, int64_t skip_prefix, uint64_t* owner, int64_t owner_rows, uint32_t epoch,
+                            void* stream) {
+  const char* name = "mak_rows_scatterv_owned";
+  if (n_slots < 0 || (n_slots > 0 && slots == nullptr)) return fail(MAK_E_INVALID, "%s: bad slot vector", name);
+  if (n_slots == 0) return MAK_OK;
+  if (!valid_index_dtype(slot_dtype)) return fail(MAK_E_INVALID, "%s: slot dtype must be int32 or int64", name);
+  if (skip_prefix < 0) return fail(MAK_E_INVALID, "%s: skip_prefix must be non-negative", name);
+  if (paged == nullptr || n_groups < 1 || n_groups > kRowGroups) return fail(MAK_E_INVALID, "%s: bad descriptors", name);
+  for (int g = 0; g < n_groups; ++g)
+    if (paged[g].num_rows > owner_rows)
+      return fail(MAK_E_INVALID, "%s: owner table has %lld rows, group %d has %lld", name, (long long)owner_rows, g,
+                  (long long)paged[g].num_rows);
+  cudaStream_t st = as_stream(stream);
+  int rc = mark_owners(slots, slot_dtype, n_slots, owner, owner_rows, epoch, st, name);
+  if (rc) return rc;
+  RowCall c{};
+  c.src = linear;
+  c.dst = paged;
+  c.n_groups = n_groups;
+  c.group_row_bytes = n_groups > 1 ? row_bytes : nullptr;
+  c.row_bytes = n_groups > 1 ? nullptr : row_bytes;
+  c.row_bytes0 = row_bytes0;
+  c.dst_idx = slots;
+  c.dst_idx_dtype = slot_dtype;
+  c.n_items = n_slots;
+  c.n_total = n_slots;
+  c.src_base = skip_prefix;
+  c.owner = reinterpret_cast<const unsigned long long*>(owner);
+  c.owner_rows = owner_rows;
+  c.tag_hi = static_cast<uint64_t>(epoch) << 32;
+  return run_rows(c, st, name);
 }
 
 int mak_rows_copy(const mak_rows_desc* src, const mak_rows_desc* dst, const int64_t* row_bytes, int64_t row_bytes0,

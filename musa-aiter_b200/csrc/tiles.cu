@@ -50,7 +50,7 @@ struct Codec {
 template <typename LT>
 struct Codec<uint8_t, LT, MAK_FP8_E4M3> {
   __device__ static __forceinline__ LT load(uint8_t c, float sc) {
-    return from_f32<LT>(__fmul_rn(fp8_decode<MAK_FP8_E4M3>(c), sc));
+    return from_f32<LT>(__fmul_rn(fp8_decode_top<MAK_FP8_E4M3>(static_cast<uint32_t>(c) << 24), sc));
   }
   __device__ static __forceinline__ uint8_t store(LT x, float sc) {
     return fp8_encode<MAK_FP8_E4M3>(__fdiv_rn(to_f32<LT>(x), sc));
@@ -59,7 +59,7 @@ struct Codec<uint8_t, LT, MAK_FP8_E4M3> {
 template <typename LT>
 struct Codec<uint8_t, LT, MAK_FP8_E5M2> {
   __device__ static __forceinline__ LT load(uint8_t c, float sc) {
-    return from_f32<LT>(__fmul_rn(fp8_decode<MAK_FP8_E5M2>(c), sc));
+    return from_f32<LT>(__fmul_rn(fp8_decode_top<MAK_FP8_E5M2>(static_cast<uint32_t>(c) << 24), sc));
   }
   __device__ static __forceinline__ uint8_t store(LT x, float sc) {
     return fp8_encode<MAK_FP8_E5M2>(__fdiv_rn(to_f32<LT>(x), sc));

@@ -180,6 +180,11 @@ _PROTOTYPES = {
         [c_void_p, c_void_p, c_int32, POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int64,
          c_void_p, c_size_t, c_void_p],
     ),
+    "mak_rows_scatterv_owned": (
+        c_int32,
+        [c_void_p, c_void_p, c_int32, POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int64,
+         c_void_p, c_int64, ctypes.c_uint32, c_void_p],
+    ),
     "mak_rows_scatter_static": (
         c_int32,
         [c_void_p, c_void_p, POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int64, c_void_p],
@@ -209,6 +214,11 @@ _PROTOTYPES = {
         [POINTER(MlaLinearDesc), c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_size_t, c_void_p],
     ),
     "mak_mla_fp8_rows_load": (c_int32, [c_void_p, POINTER(MlaLinearDesc), c_void_p, c_int32, c_int32, c_void_p]),
+    "mak_mla_fp8_rows_store_owned": (
+        c_int32,
+        [POINTER(MlaLinearDesc), c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, ctypes.c_uint32, c_void_p],
+    ),
+    "mak_fp8_quotient_selfcheck": (c_int32, [c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "mak_rows_copy": (
         c_int32,
         [
@@ -311,6 +321,37 @@ def workspace(n_items: int, device: torch.device) -> tuple[torch.Tensor, int]:
     """Scatter workspace from torch's caching allocator (stream-ordered reuse is safe)."""
     nbytes = int(load().mak_scatter_workspace_bytes(int(n_items)))
     return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
+
+
+# Owner tables for the two-launch scatter (mak_rows_scatterv_owned): one zeroed
+# int64 vector per (device, stream), grown to the largest destination seen, and
+# the next epoch.  The lock makes epoch order equal enqueue order on a stream.
+_OWNER_LOCK = threading.Lock()
+_OWNERS: dict = {}
+_EPOCH_MAX = (1 << 32) - 1
+_OWNER_MAX_ROWS = 1 << 27  # 1 GiB of table; larger destinations take the workspace path
+
+
+def owned_scatter(device: torch.device, stream: int, rows: int, n: int, launch):
+    """Call ``launch(owner_ptr, owner_rows, epoch)`` with this stream's owner table and a fresh
+    epoch and return its status, or return None when the workspace path must be used instead
+    (stream capture: a captured epoch would be replayed; very large destinations or calls)."""
+    if rows > _OWNER_MAX_ROWS or n >= _EPOCH_MAX or torch.cuda.is_current_stream_capturing():
+        return None
+    key = (device.index, stream)
+    with _OWNER_LOCK:
+        ent = _OWNERS.get(key)
+        if ent is None or ent[1] < rows:
+            cap = max(rows, 2 * ent[1]) if ent is not None else max(rows, 1 << 16)
+            cap = min(cap, _OWNER_MAX_ROWS)
+            t = torch.zeros(cap, dtype=torch.int64, device=device)
+            ent = _OWNERS[key] = [t, cap, t.data_ptr(), 1]
+        epoch = ent[3]
+        if epoch > _EPOCH_MAX:
+            ent[0].zero_()
+            epoch = 1
+        ent[3] = epoch + 1
+        return launch(ent[2], ent[1], epoch)
 
 
 def plane_array(ptrs: list[int]):

@@ -868,9 +868,16 @@ def _mla_pair_scatter(kv_linear: torch.Tensor, pe_linear: torch.Tensor, kv_cache
     ks, code = kernel_slots(slots)
     _, paged, rb = _mla_cache_side(w1, w2, layered)
     lin = _native.rows_pack(_rows_side_linear(l1, layered), _rows_side_linear(l2, layered))
-    ws, nbytes = _native.workspace(ks.numel(), w1.device)
-    rc = lib.mak_rows_scatterv(ctypes.addressof(lin), paged, 2, rb, 0, ks.data_ptr(), code, ks.numel(), 0,
-                               ws.data_ptr(), nbytes, _native.stream_ptr(w1.device))
+    n = ks.numel()
+    dev = w1.device
+    sp = _native.stream_ptr(dev)
+    rows = w1.shape[-3] * w1.shape[-2]
+    rc = _native.owned_scatter(dev, sp, rows, n, lambda own, orows, epoch: lib.mak_rows_scatterv_owned(
+        ctypes.addressof(lin), paged, 2, rb, 0, ks.data_ptr(), code, n, 0, own, orows, epoch, sp))
+    if rc is None:
+        ws, nbytes = _native.workspace(n, dev)
+        rc = lib.mak_rows_scatterv(ctypes.addressof(lin), paged, 2, rb, 0, ks.data_ptr(), code, n, 0, ws.data_ptr(),
+                                   nbytes, sp)
     _native.check(rc, op)
     if t1:
         kv_cache.copy_(w1)
@@ -1113,10 +1120,16 @@ def kv_mla_linear_to_paged_fp8_rows(
         lib = _native.load()
         ks, code = kernel_slots(slots)
         lin, buf = _mla_fp8_descs(kv, pe, cache)
-        ws, nbytes = _native.workspace(tcount, kv.device)
-        _native.check(lib.mak_mla_fp8_rows_store(ctypes.byref(lin), ctypes.addressof(buf), ks.data_ptr(), code,
-                                                 _FMT_CODE[fmt], ws.data_ptr(), nbytes, _native.stream_ptr(kv.device)),
-                      name)
+        dev = kv.device
+        sp = _native.stream_ptr(dev)
+        rows = int(cache.shape[1]) * int(cache.shape[2])
+        rc = _native.owned_scatter(dev, sp, rows, tcount, lambda own, orows, epoch: lib.mak_mla_fp8_rows_store_owned(
+            ctypes.byref(lin), ctypes.addressof(buf), ks.data_ptr(), code, _FMT_CODE[fmt], own, orows, epoch, sp))
+        if rc is None:
+            ws, nbytes = _native.workspace(tcount, dev)
+            rc = lib.mak_mla_fp8_rows_store(ctypes.byref(lin), ctypes.addressof(buf), ks.data_ptr(), code,
+                                            _FMT_CODE[fmt], ws.data_ptr(), nbytes, sp)
+        _native.check(rc, name)
     emit_native(name, kv_linear, "sm100a fused group-quantise + row scatter (MLA FP8 rows)")
     return True
 

@@ -227,11 +227,17 @@ def _fast_scatter(op: str, linear: tuple, paged: tuple, row_bytes: int, slots: t
         return
     lib = _native.load()
     ks, code = kernel_slots(slots)
-    ws, nbytes = _native.workspace(ks.numel(), device)
+    n = ks.numel()
     buf = _native.rows_pack(linear, paged)
     base = ctypes.addressof(buf)
-    rc = lib.mak_rows_scatter(base, base + 48, None, row_bytes, ks.data_ptr(), code, ks.numel(), int(skip_prefix),
-                              ws.data_ptr(), nbytes, _native.stream_ptr(device))
+    sp = _native.stream_ptr(device)
+    skip = int(skip_prefix)
+    rc = _native.owned_scatter(device, sp, paged[4], n, lambda own, rows, epoch: lib.mak_rows_scatterv_owned(
+        base, base + 48, 1, None, row_bytes, ks.data_ptr(), code, n, skip, own, rows, epoch, sp))
+    if rc is None:
+        ws, nbytes = _native.workspace(n, device)
+        rc = lib.mak_rows_scatter(base, base + 48, None, row_bytes, ks.data_ptr(), code, n, skip, ws.data_ptr(),
+                                  nbytes, sp)
     _native.check(rc, op)
 
 

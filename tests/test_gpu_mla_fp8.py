@@ -127,13 +127,20 @@ def test_every_input_under_fixed_group_amax(cuda_device, dt, fmt):
     allv = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(TORCH[dt]).float()
     allv = allv[torch.isfinite(allv)]
     groups = []
-    for amax in (1.0, 3.0, 0.37, 448.0, 1.0e-3, 12345.0, 2.0**-20, 57344.0, 6.0e4):
+    # amax values put the group scale inside, at and outside the division-free range
+    # [2^-60, 2^16] of the store (fp8.cuh fast_quot); inf keeps every finite input in the
+    # group next to an infinite one
+    for amax in (1.0, 3.0, 0.37, 448.0, 1.0e-3, 12345.0, 2.0**-20, 57344.0, 6.0e4, 2.0**-51, 2.0**-52, 2.0**-44,
+                 3.0e7, 2.0**25, 2.0**32, float("inf")):
         a = torch.tensor(amax).to(TORCH[dt]).float()
         vals = allv[allv.abs() <= a]
         n = (vals.numel() + 126) // 127
         pad = torch.zeros(n * 127 - vals.numel())
         body = torch.cat([vals, pad]).reshape(n, 127)
         groups.append(torch.cat([a.expand(n, 1), body], dim=1))
+    special = torch.zeros(128)
+    special[:8] = torch.tensor([float("nan"), -float("inf"), float("inf"), -0.0, 5.0, -5.0, 1.0e-30, -1.0e-30])
+    groups.append(special[None])
     g = torch.cat(groups)
     g = torch.cat([g, torch.zeros((-g.shape[0]) % 4, 128)])  # whole rows of 4 groups
     x = g.reshape(-1, 512).to(TORCH[dt])
@@ -150,3 +157,47 @@ def test_every_input_under_fixed_group_amax(cuda_device, dt, fmt):
     okv, _ = ma.kv_paged_fp8_rows_to_mla_linear(cache, slots.cuda(), out_dtype=TORCH[dt], fp8_format=fmt)
     rk, _ = O.mla_fp8_rows_load(want, slots.numpy(), kv_dim=512, pe_dim=64, out_dtype=dt, fp8_format=fmt)
     eq(okv, rk[0], "decode")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", ("bfloat16", "float16"))
+def test_division_free_quotient_selfcheck(cuda_device, dt, fmt):
+    """The store divides by a group scale through one reciprocal per group and a
+    Markstein correction per value; on the device it must agree with the IEEE fp32
+    division for every 16-bit input and every scale significand, at the ends of the
+    fast range and in between."""
+    from musa_aiter import _native
+
+    lib = _native.load()
+    counts = torch.zeros(2, dtype=torch.int64, device="cuda")
+    code = _native.dtype_code(TORCH[dt])
+    f = _native.MAK_FP8_E4M3 if fmt == "e4m3" else _native.MAK_FP8_E5M2
+    for e in (-60, -41, -9, -1, 0, 8, 16):
+        rc = lib.mak_fp8_quotient_selfcheck(code, f, e, counts.data_ptr(), _native.stream_ptr(counts.device))
+        _native.check(rc, "mak_fp8_quotient_selfcheck")
+    assert counts.tolist() == [0, 0], f"differing codes / quotients: {counts.tolist()}"
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", ("bfloat16", "float16"))
+def test_load_every_code_byte(cuda_device, dt, fmt):
+    """Rows holding all 256 code bytes in every lane position (also the codes the encoder
+    never writes: exponent field 0 with a mantissa, the top codes) under finite scales of
+    several magnitudes decode as the reference decoder does."""
+    row = ma.mla_fp8_row_bytes()
+    t = 512
+    g = torch.Generator().manual_seed(11)
+    codes = torch.stack([torch.roll(torch.arange(256, dtype=torch.int32), s)[torch.arange(512) % 256]
+                         for s in range(t)]).to(torch.uint8)
+    scale_pool = torch.tensor([1.0, 0.5, 3.0e-3, 1.7e5, 2.0**-60, 2.0**20, 0.0, 1.0e-40], dtype=torch.float32)
+    scales = scale_pool[torch.randint(0, scale_pool.numel(), (t, 4), generator=g)]
+    pe = torch.randn((t, 64), generator=g).to(TORCH[dt])
+    rows = torch.cat([codes, scales.view(torch.uint8).reshape(t, 16), pe.view(torch.uint8).reshape(t, 128)], dim=1)
+    cache = rows.reshape(8, 64, row).contiguous()
+    slots = torch.randperm(t, generator=g)
+    slots[5] = -1
+    okv, ope = ma.kv_paged_fp8_rows_to_mla_linear(cache.cuda(), slots.cuda(), out_dtype=TORCH[dt], fp8_format=fmt)
+    rk, rp = O.mla_fp8_rows_load(cache.numpy().reshape(1, t, row), slots.numpy(), kv_dim=512, pe_dim=64,
+                                 out_dtype=dt, fp8_format=fmt)
+    eq(okv, rk[0], "decoded latent")
+    eq(ope, rp[0], "rope")

@@ -149,11 +149,18 @@ def _scatter(op: str, linear: list[torch.Tensor], paged: list[torch.Tensor], slo
     if p.row_bytes != q.row_bytes:
         raise ValueError(f"{op}: cache row and buffer row sizes differ ({p.row_bytes} vs {q.row_bytes} bytes)")
     ks, code = kernel_slots(slots)
-    ws, nbytes = _native.workspace(ks.numel(), paged[0].device)
+    n = ks.numel()
+    dev = paged[0].device
+    sp = _native.stream_ptr(dev)
     pd, pa = p.desc()
     ld, la = q.desc()
-    rc = lib.mak_rows_scatter(ctypes.byref(ld), ctypes.byref(pd), None, p.row_bytes, _native.ptr(ks), code, ks.numel(),
-                              int(skip_prefix), _native.ptr(ws), nbytes, _native.stream_ptr(paged[0].device))
+    skip = int(skip_prefix)
+    rc = _native.owned_scatter(dev, sp, int(p.num_rows), n, lambda own, rows, epoch: lib.mak_rows_scatterv_owned(
+        ctypes.byref(ld), ctypes.byref(pd), 1, None, p.row_bytes, ks.data_ptr(), code, n, skip, own, rows, epoch, sp))
+    if rc is None:
+        ws, nbytes = _native.workspace(n, dev)
+        rc = lib.mak_rows_scatter(ctypes.byref(ld), ctypes.byref(pd), None, p.row_bytes, ks.data_ptr(), code, n, skip,
+                                  ws.data_ptr(), nbytes, sp)
     _native.check(rc, op)
 
 

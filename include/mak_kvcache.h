@@ -448,12 +448,13 @@ MAK_API int mak_mla_fp8_rows_store_owned(const mak_mla_linear_desc* lin, const m
 
 /*
  * Self-check of the store's division-free quotient (a reciprocal per group and
- * Markstein's correction step per value) against the IEEE fp32 division on this
- * device: for the 2^23 scales 2^scale_exp * [1, 2) and every 16-bit input of
- * elem_dtype (MAK_DT_BF16 / MAK_DT_F16) that a group with that scale can hold,
- * adds to counts[0] the FP8 codes that differ and to counts[1] the quotients
- * >= 2^-14 in magnitude that differ in any bit (device memory, 2 x uint64,
- * zeroed by the caller).  Scales outside the fast range ([2^-60, 2^16]) take
+ * Markstein's correction step per value, then the range-bounded encoder) against
+ * the IEEE fp32 division and the full encoder on this device: for the 2^23
+ * scales 2^scale_exp * [1, 2) and every 16-bit input of elem_dtype
+ * (MAK_DT_BF16 / MAK_DT_F16) that a group with that scale can hold (|x / s| up
+ * to fp8_max, inf and nan), adds to counts[0] the FP8 codes that differ and to
+ * counts[1] the finite quotients >= 2^-14 in magnitude that differ in any bit
+ * (device memory, 2 x uint64, zeroed by the caller).  Scales outside the fast range ([2^-60, 2^16]) take
  * the IEEE division in the store and are not counted.  No reference
  * counterpart: a test entry point.
  */

@@ -122,6 +122,23 @@ __device__ __forceinline__ uint32_t fp8_encode2(float w0, float w1) {
   return fp8_encode2s<F>(w0, w0, w1, w1);
 }
 
+// fp8_encode2s for callers whose finite values never exceed the format's
+// standard maximum by more than rounding (|w| <= 448.001 for E4M3, 57344.01
+// for E5M2: a value divided by its own group's amax / fp8_max).  The extended
+// top codes are then unreachable and cvt.rn.satfinite rounds every in-range
+// magnitude exactly as the reference rule does; what remains is the flush
+// below the smallest normal, non-finite values (both to magnitude 0, decided
+// by one range test on |w|) and the sign from g < 0.
+template <int F>
+__device__ __forceinline__ uint32_t fp8_encode2s_bounded(float g0, float w0, float g1, float w1) {
+  constexpr float kMin = (F == MAK_FP8_E4M3) ? 0.015625f : 6.103515625e-05f;
+  const float a0 = fabsf(w0), a1 = fabsf(w1);
+  const float v0 = (a0 >= kMin && a0 <= 3.40282346638528859812e+38f) ? a0 : 0.f;
+  const float v1 = (a1 >= kMin && a1 <= 3.40282346638528859812e+38f) ? a1 : 0.f;
+  const uint32_t c = (F == MAK_FP8_E4M3) ? cvt_e4m3x2(v1, v0) : cvt_e5m2x2(v1, v0);
+  return c | ((g0 < 0.f) ? 0x80u : 0u) | ((g1 < 0.f) ? 0x8000u : 0u);
+}
+
 // x / s rounded to nearest in fp32 without a division per value, by
 // Markstein's correction step (P. Markstein, "IA-64 and Elementary Functions",
 // 2000): with y = RN(1/s) and q0 = RN(x * y), q0 is within one ulp of x / s,

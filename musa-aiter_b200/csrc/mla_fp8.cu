@@ -115,6 +115,41 @@ __device__ __forceinline__ Bytes<E> load_bytes(const unsigned char* src) {
   return b;
 }
 
+// 16-bit pattern of +infinity: |raw| at or above it is inf or nan.
+template <typename T>
+constexpr uint32_t kInfBits = 0x7F80u;  // bfloat16
+template <>
+constexpr uint32_t kInfBits<__half> = 0x7C00u;
+
+// Per-token inputs of the store, fetched one token ahead so the next token's
+// loads are in flight while this one is encoded.
+template <int E>
+struct StoreIn {
+  uint4 v[E / 8];   // this lane's latent values (raw 16-bit elements)
+  uint2 pe[2];      // this lane's rope bytes (b = 8 * lane and 8 * lane + 256)
+  int64_t dr;       // destination row
+  unsigned long long own;  // owner-table entry of dr (owner mode)
+};
+
+template <int E>
+__device__ __forceinline__ void store_fetch(const MlaLaunch& p, const unsigned char* kv_layer,
+                                            const unsigned char* pe_layer, int64_t t, int lane, StoreIn<E>& s) {
+  const uint4* src = reinterpret_cast<const uint4*>(kv_layer + t * p.kv_st + lane * E * 2);
+#pragma unroll
+  for (int k = 0; k < E / 8; ++k) s.v[k] = src[k];
+  const unsigned char* pe_src = pe_layer + t * p.pe_st;
+  const int b0 = lane * 8;
+  s.pe[0] = b0 < p.pe_bytes ? *reinterpret_cast<const uint2*>(pe_src + b0) : make_uint2(0u, 0u);
+  s.pe[1] = b0 + 256 < p.pe_bytes ? *reinterpret_cast<const uint2*>(pe_src + b0 + 256) : make_uint2(0u, 0u);
+  s.dr = load_index(p.idx, p.idx64, t);
+  s.own = 0;
+}
+
+template <int E>
+__device__ __forceinline__ void store_fetch_owner(const MlaLaunch& p, StoreIn<E>& s) {
+  if (p.owner != nullptr && s.dr >= 0 && s.dr < p.num_rows) s.own = __ldcg(p.owner + s.dr);
+}
+
 template <typename T, int F, int E>
 __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid_constant__ MlaLaunch p) {
   constexpr int kLanesPerGroup = 128 / E;
@@ -124,29 +159,47 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
   unsigned char* plane = reinterpret_cast<unsigned char*>(p.cache[layer]);
   const unsigned char* kv_layer = p.kv + layer * p.kv_sl;
   const unsigned char* pe_layer = p.pe + layer * p.pe_sl;
-  for (int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < p.num_tokens; t += step) {
-    const int64_t dr = load_index(p.idx, p.idx64, t);
-    if (dr < 0 || dr >= p.num_rows) continue;
-    if (p.owner != nullptr && __ldcg(p.owner + dr) != (p.tag_hi | static_cast<uint64_t>(t))) continue;
-    unsigned char* row = plane + mla_row_offset(p, dr);
-    // latent values of this lane
-    const uint4* src = reinterpret_cast<const uint4*>(kv_layer + t * p.kv_st + lane * E * 2);
+  int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (t >= p.num_tokens) return;
+  StoreIn<E> cur;
+  store_fetch<E>(p, kv_layer, pe_layer, t, lane, cur);
+  store_fetch_owner<E>(p, cur);
+  while (true) {
+    const int64_t tn = t + step;
+    const bool more = tn < p.num_tokens;  // warp-uniform: a warp works on one token
+    StoreIn<E> nxt;
+    if (more) store_fetch<E>(p, kv_layer, pe_layer, tn, lane, nxt);
     float x[E];
 #pragma unroll
     for (int k = 0; k < E / 8; ++k) {
-      const uint4 v = src[k];
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      const uint32_t w[4] = {cur.v[k].x, cur.v[k].y, cur.v[k].z, cur.v[k].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         x[8 * k + 2 * j] = bits_to_f32<T>(w[j] & 0xFFFFu);
         x[8 * k + 2 * j + 1] = bits_to_f32<T>(w[j] >> 16);
       }
     }
-    float amax = 0.f;  // over the finite values only: every stored scale is finite
+    // amax over the finite values only (every stored scale is finite): the
+    // magnitudes' 16-bit patterns order like the values, so a packed unsigned
+    // max of |raw| finds the lane's largest; a non-finite one (pattern at or
+    // above the format's infinity, rare) sends the lane to the exact loop.
+    uint32_t m2 = 0;
 #pragma unroll
-    for (int j = 0; j < E; ++j) {
-      const float a = fabsf(x[j]);
-      if (a <= 3.40282346638528859812e+38f) amax = fmaxf(amax, a);
+    for (int k = 0; k < E / 8; ++k) {
+      m2 = __vmaxu2(m2, cur.v[k].x & 0x7FFF7FFFu);
+      m2 = __vmaxu2(m2, cur.v[k].y & 0x7FFF7FFFu);
+      m2 = __vmaxu2(m2, cur.v[k].z & 0x7FFF7FFFu);
+      m2 = __vmaxu2(m2, cur.v[k].w & 0x7FFF7FFFu);
+    }
+    const uint32_t mraw = max(m2 & 0xFFFFu, m2 >> 16);
+    float amax = bits_to_f32<T>(mraw);
+    if (mraw >= kInfBits<T>) {
+      amax = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        const float a = fabsf(x[j]);
+        if (a <= 3.40282346638528859812e+38f) amax = fmaxf(amax, a);
+      }
     }
 #pragma unroll
     for (int o = 1; o < kLanesPerGroup; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -159,7 +212,8 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
       for (int j = 0; j < E / 4; ++j) {
         const FastQuot a = fast_quot(x[4 * j], scale, y), b = fast_quot(x[4 * j + 1], scale, y);
         const FastQuot c = fast_quot(x[4 * j + 2], scale, y), d = fast_quot(x[4 * j + 3], scale, y);
-        codes.w[j] = fp8_encode2s<F>(a.q0, a.q1, b.q0, b.q1) | (fp8_encode2s<F>(c.q0, c.q1, d.q0, d.q1) << 16);
+        codes.w[j] = fp8_encode2s_bounded<F>(a.q0, a.q1, b.q0, b.q1) |
+                     (fp8_encode2s_bounded<F>(c.q0, c.q1, d.q0, d.q1) << 16);
       }
     } else {
 #pragma unroll
@@ -169,57 +223,98 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
         codes.w[j] = lo | (hi << 16);
       }
     }
-    store_bytes<E>(row + lane * E, codes);
-    if ((lane % kLanesPerGroup) == 0) reinterpret_cast<float*>(row + p.kv_dim)[lane / kLanesPerGroup] = scale;
-    // rope part, 8 bytes per lane
-    unsigned char* rope = row + p.kv_dim + (p.kv_dim / 128) * 4;
-    const unsigned char* pe_src = pe_layer + t * p.pe_st;
-    for (int b = lane * 8; b < p.pe_bytes; b += 256)
-      *reinterpret_cast<uint2*>(rope + b) = *reinterpret_cast<const uint2*>(pe_src + b);
+    const bool write = cur.dr >= 0 && cur.dr < p.num_rows &&
+                       (p.owner == nullptr || cur.own == (p.tag_hi | static_cast<uint64_t>(t)));
+    if (write) {
+      unsigned char* row = plane + mla_row_offset(p, cur.dr);
+      store_bytes<E>(row + lane * E, codes);
+      if ((lane % kLanesPerGroup) == 0) reinterpret_cast<float*>(row + p.kv_dim)[lane / kLanesPerGroup] = scale;
+      unsigned char* rope = row + p.kv_dim + (p.kv_dim / 128) * 4;
+      const int b0 = lane * 8;
+      if (b0 < p.pe_bytes) *reinterpret_cast<uint2*>(rope + b0) = cur.pe[0];
+      if (b0 + 256 < p.pe_bytes) *reinterpret_cast<uint2*>(rope + b0 + 256) = cur.pe[1];
+    }
+    if (!more) break;
+    store_fetch_owner<E>(p, nxt);
+    cur = nxt;
+    t = tn;
   }
+}
+
+// Per-token inputs of the load: the cache row's codes, group scale and rope
+// bytes, fetched one token ahead (and the row index two tokens ahead).
+template <int E>
+struct LoadIn {
+  Bytes<E> codes;
+  float scale;
+  uint2 pe[2];
+  bool have;
+};
+
+template <int E>
+__device__ __forceinline__ void load_fetch(const MlaLaunch& p, const unsigned char* plane, int64_t sr, int lane,
+                                           LoadIn<E>& r) {
+  constexpr int kLanesPerGroup = 128 / E;
+  r.have = sr >= 0 && sr < p.num_rows;
+  if (!r.have) return;
+  const unsigned char* row = plane + mla_row_offset(p, sr);
+  r.codes = load_bytes<E>(row + lane * E);
+  r.scale = reinterpret_cast<const float*>(row + p.kv_dim)[lane / kLanesPerGroup];
+  const unsigned char* rope = row + p.kv_dim + (p.kv_dim / 128) * 4;
+  const int b0 = lane * 8;
+  r.pe[0] = b0 < p.pe_bytes ? *reinterpret_cast<const uint2*>(rope + b0) : make_uint2(0u, 0u);
+  r.pe[1] = b0 + 256 < p.pe_bytes ? *reinterpret_cast<const uint2*>(rope + b0 + 256) : make_uint2(0u, 0u);
 }
 
 template <typename T, int F, int E>
 __global__ void __launch_bounds__(kMlaThreads) mla_fp8_load_kernel(const __grid_constant__ MlaLaunch p,
                                                                    unsigned char* kv_out, unsigned char* pe_out) {
-  constexpr int kLanesPerGroup = 128 / E;
   const int lane = threadIdx.x & 31;
   const int layer = blockIdx.y;
   const int64_t step = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const unsigned char* plane = reinterpret_cast<const unsigned char*>(p.cache[layer]);
   unsigned char* kv_layer = kv_out + layer * p.kv_sl;
   unsigned char* pe_layer = pe_out + layer * p.pe_sl;
-  for (int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < p.num_tokens; t += step) {
-    const int64_t sr = load_index(p.idx, p.idx64, t);
-    const bool have = sr >= 0 && sr < p.num_rows;
+  int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (t >= p.num_tokens) return;
+  LoadIn<E> cur;
+  load_fetch<E>(p, plane, load_index(p.idx, p.idx64, t), lane, cur);
+  int64_t sr_next = t + step < p.num_tokens ? load_index(p.idx, p.idx64, t + step) : -1;
+  while (true) {
+    const int64_t tn = t + step;
+    const bool more = tn < p.num_tokens;
+    LoadIn<E> nxt;
+    if (more) load_fetch<E>(p, plane, sr_next, lane, nxt);
+    if (tn + step < p.num_tokens) sr_next = load_index(p.idx, p.idx64, tn + step);
     uint4* dst = reinterpret_cast<uint4*>(kv_layer + t * p.kv_st + lane * E * 2);
     unsigned char* pe_dst = pe_layer + t * p.pe_st;
-    if (!have) {
+    const int b0 = lane * 8;
+    if (cur.have) {
+#pragma unroll
+      for (int k = 0; k < E / 8; ++k) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          // codes 2j, 2j+1 of word 2k + j/2, each moved to the top byte
+          const uint32_t cw = cur.codes.w[2 * k + (j >> 1)];
+          const int b = 2 * (j & 1);
+          const uint32_t x0 = __byte_perm(cw, 0u, 0x0444u | (b << 12));
+          const uint32_t x1 = __byte_perm(cw, 0u, 0x0444u | ((b + 1) << 12));
+          w[j] = pack2<T>(__fmul_rn(fp8_decode_top<F>(x0), cur.scale), __fmul_rn(fp8_decode_top<F>(x1), cur.scale));
+        }
+        dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      if (b0 < p.pe_bytes) *reinterpret_cast<uint2*>(pe_dst + b0) = cur.pe[0];
+      if (b0 + 256 < p.pe_bytes) *reinterpret_cast<uint2*>(pe_dst + b0 + 256) = cur.pe[1];
+    } else {
 #pragma unroll
       for (int k = 0; k < E / 8; ++k) dst[k] = make_uint4(0u, 0u, 0u, 0u);
-      for (int b = lane * 8; b < p.pe_bytes; b += 256) *reinterpret_cast<uint2*>(pe_dst + b) = make_uint2(0u, 0u);
-      continue;
+      if (b0 < p.pe_bytes) *reinterpret_cast<uint2*>(pe_dst + b0) = make_uint2(0u, 0u);
+      if (b0 + 256 < p.pe_bytes) *reinterpret_cast<uint2*>(pe_dst + b0 + 256) = make_uint2(0u, 0u);
     }
-    const unsigned char* row = plane + mla_row_offset(p, sr);
-    const Bytes<E> codes = load_bytes<E>(row + lane * E);
-    const float scale = reinterpret_cast<const float*>(row + p.kv_dim)[lane / kLanesPerGroup];
-#pragma unroll
-    for (int k = 0; k < E / 8; ++k) {
-      uint32_t w[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        // codes 2j, 2j+1 of word 2k + j/2, each moved to the top byte
-        const uint32_t cw = codes.w[2 * k + (j >> 1)];
-        const int b = 2 * (j & 1);
-        const uint32_t x0 = __byte_perm(cw, 0u, 0x0444u | (b << 12));
-        const uint32_t x1 = __byte_perm(cw, 0u, 0x0444u | ((b + 1) << 12));
-        w[j] = pack2<T>(__fmul_rn(fp8_decode_top<F>(x0), scale), __fmul_rn(fp8_decode_top<F>(x1), scale));
-      }
-      dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    const unsigned char* rope = row + p.kv_dim + (p.kv_dim / 128) * 4;
-    for (int b = lane * 8; b < p.pe_bytes; b += 256)
-      *reinterpret_cast<uint2*>(pe_dst + b) = *reinterpret_cast<const uint2*>(rope + b);
+    if (!more) break;
+    cur = nxt;
+    t = tn;
   }
 }
 
@@ -332,10 +427,11 @@ static int dispatch(MlaLaunch& L, const mak_mla_linear_desc* lin, const mak_rows
                              : dispatch_e<STORE, __half, MAK_FP8_E5M2>(L, lin, cache, st);
 }
 
-// Self-check of the division-free quotient (fast_quot) against the IEEE fp32
-// division: thread k takes the scale s = 2^scale_exp * (1 + k / 2^23) and every
-// 16-bit input x of type T with |x| <= 2 * fp8_max * s (the inputs a group with
-// that scale can hold), and counts (a) FP8 codes that differ from
+// Self-check of the store's fast path (fast_quot + fp8_encode2s_bounded)
+// against the IEEE fp32 division and the full encoder: thread k takes the scale
+// s = 2^scale_exp * (1 + k / 2^23) and every 16-bit input x of type T that a
+// group with that scale can hold (|x / s| <= fp8_max up to rounding, and the
+// non-finite inputs), and counts (a) FP8 codes that differ from
 // fp8_encode(x / s) and (b) quotients with |x / s| >= 2^-14 that differ in any
 // bit.  Only scales the store kernel sends down the fast path are tested.
 template <typename T, int F>
@@ -346,16 +442,17 @@ __global__ void fp8_quotient_check_kernel(int scale_exp, unsigned long long* cou
   unsigned long long bad_code = 0, bad_quot = 0;
   if (fast_quot_ok(s)) {
     const float y = __frcp_rn(s);
-    const float lim = 2.f * fp8_max_of<F>() * s;
+    const float lim = fp8_max_of<F>() * (1.f + 0x1p-20f);
     for (uint32_t u = 0; u < 65536u; u += 2) {
       const float x0 = bits_to_f32<T>(u), x1 = bits_to_f32<T>(u + 1);
       const FastQuot a = fast_quot(x0, s, y), b = fast_quot(x1, s, y);
       const float w0 = __fdiv_rn(x0, s), w1 = __fdiv_rn(x1, s);
-      const uint32_t got = fp8_encode2s<F>(a.q0, a.q1, b.q0, b.q1);
-      const bool in0 = !(fabsf(x0) > lim), in1 = !(fabsf(x1) > lim);  // nan inputs stay in
+      const uint32_t got = fp8_encode2s_bounded<F>(a.q0, a.q1, b.q0, b.q1);
+      // the inputs a group with scale s holds: |x / s| <= fp8_max up to rounding; inf / nan stay in
+      const bool in0 = !(fabsf(w0) > lim) || !isfinite(x0), in1 = !(fabsf(w1) > lim) || !isfinite(x1);
       bad_code += (in0 && (got & 0xFFu) != fp8_encode<F>(w0)) + (in1 && (got >> 8) != fp8_encode<F>(w1));
-      bad_quot += (in0 && fabsf(w0) >= 0x1p-14f && __float_as_uint(w0) != __float_as_uint(a.q1)) +
-                  (in1 && fabsf(w1) >= 0x1p-14f && __float_as_uint(w1) != __float_as_uint(b.q1));
+      bad_quot += (in0 && isfinite(x0) && fabsf(w0) >= 0x1p-14f && __float_as_uint(w0) != __float_as_uint(a.q1)) +
+                  (in1 && isfinite(x1) && fabsf(w1) >= 0x1p-14f && __float_as_uint(w1) != __float_as_uint(b.q1));
     }
   }
 #pragma unroll

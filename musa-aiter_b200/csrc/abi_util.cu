@@ -166,6 +166,8 @@ __global__ void hash_resolve_kernel(const void* slots, int is64, int64_t n, cons
 
 __global__ void owner_mark_kernel(const void* slots, int is64, int64_t n, unsigned long long* owner, int64_t rows,
                                   unsigned long long tag_hi) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t s = load_index(slots, is64, i);
     if (s >= 0 && s < rows) atomicMax(owner + s, tag_hi | static_cast<unsigned long long>(i));
@@ -181,10 +183,9 @@ int mark_owners(const void* slots, int32_t slot_dtype, int64_t n, uint64_t* owne
   if (n == 0) return MAK_OK;
   const int threads = 256;
   const int grid = grid_for(reinterpret_cast<const void*>(owner_mark_kernel), threads, 0, (n + threads - 1) / threads);
-  owner_mark_kernel<<<grid, threads, 0, st>>>(slots, slot_dtype == MAK_DT_I64, n,
-                                              reinterpret_cast<unsigned long long*>(owner), owner_rows,
-                                              static_cast<unsigned long long>(epoch) << 32);
-  return launch_status("owner_mark_kernel");
+  return launch_pdl("owner_mark_kernel", owner_mark_kernel, dim3(grid), dim3(threads), 0, st, slots,
+                    static_cast<int>(slot_dtype == MAK_DT_I64), n, reinterpret_cast<unsigned long long*>(owner),
+                    owner_rows, static_cast<unsigned long long>(epoch) << 32);
 }
 
 int64_t hash_capacity(int64_t n) {

@@ -51,6 +51,43 @@ int resolve_last_writer(const void* slots, int32_t slot_dtype, int64_t n, const 
 int mark_owners(const void* slots, int32_t slot_dtype, int64_t n, uint64_t* owner, int64_t owner_rows, uint32_t epoch,
                 cudaStream_t st, const char* name);
 
+// ---- programmatic dependent launch -------------------------------------------
+// Kernels of this library that are launched with launch_pdl() may start while
+// the previous kernel of the stream is still draining: their CTAs become
+// resident early and block in pdl_wait() (griddepcontrol.wait) until every
+// prerequisite grid has completed and its memory is visible.  pdl_wait() must
+// therefore come before the kernel's first global-memory access (read or
+// write); pdl_trigger() (griddepcontrol.launch_dependents) then lets the next
+// launch of the stream be scheduled in the same way.  Both are no-ops for a
+// grid launched without the attribute, and the wait is a hardware dependency,
+// not a spin on memory.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with cudaLaunchAttributeProgrammaticStreamSerialization (the kernel
+// must call pdl_wait() before touching global memory).  Counts the launch and
+// returns MAK_OK or the CUDA error as a status.
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return cuda_fail(e, what);
+  }
+  return launch_status(what);
+}
+
 // ---- device helpers -----------------------------------------------------------
 __device__ __forceinline__ int64_t load_index(const void* p, int is64, int64_t i) {
   return is64 ? __ldg(reinterpret_cast<const long long*>(p) + i)

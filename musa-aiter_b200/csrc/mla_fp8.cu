@@ -159,6 +159,8 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
   unsigned char* plane = reinterpret_cast<unsigned char*>(p.cache[layer]);
   const unsigned char* kv_layer = p.kv + layer * p.kv_sl;
   const unsigned char* pe_layer = p.pe + layer * p.pe_sl;
+  pdl_wait();
+  pdl_trigger();
   int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (t >= p.num_tokens) return;
   StoreIn<E> cur;
@@ -275,6 +277,8 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_load_kernel(const __grid_
   const unsigned char* plane = reinterpret_cast<const unsigned char*>(p.cache[layer]);
   unsigned char* kv_layer = kv_out + layer * p.kv_sl;
   unsigned char* pe_layer = pe_out + layer * p.pe_sl;
+  pdl_wait();
+  pdl_trigger();
   int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (t >= p.num_tokens) return;
   LoadIn<E> cur;
@@ -394,12 +398,10 @@ static int launch_mla(MlaLaunch& L, int64_t layers, unsigned char* kv_out, unsig
     MlaLaunch P = L;
     P.kv = L.kv + l0 * L.kv_sl;
     P.pe = L.pe + l0 * L.pe_sl;
-    if (STORE) {
-      mla_fp8_store_kernel<T, F, E><<<grid, kMlaThreads, 0, st>>>(P);
-    } else {
-      mla_fp8_load_kernel<T, F, E><<<grid, kMlaThreads, 0, st>>>(P, kv_out + l0 * L.kv_sl, pe_out + l0 * L.pe_sl);
-    }
-    const int rc = launch_status(STORE ? "mla_fp8_store_kernel" : "mla_fp8_load_kernel");
+    const int rc = STORE ? launch_pdl("mla_fp8_store_kernel", mla_fp8_store_kernel<T, F, E>, grid, dim3(kMlaThreads), 0,
+                                      st, P)
+                         : launch_pdl("mla_fp8_load_kernel", mla_fp8_load_kernel<T, F, E>, grid, dim3(kMlaThreads), 0,
+                                      st, P, kv_out + l0 * L.kv_sl, pe_out + l0 * L.pe_sl);
     if (rc) return rc;
   }
   return MAK_OK;

@@ -120,6 +120,8 @@ __global__ void __launch_bounds__(kRowThreads) rows_kernel(const __grid_constant
   constexpr int U = (VEC >= 8) ? 4 : 8;  // independent vectors in flight per lane
   __shared__ int64_t s_src[kRowWarps][kRowChunk];  // source byte offset, -1 = zero row
   __shared__ int64_t s_dst[kRowWarps][kRowChunk];  // destination byte offset, -1 = skip
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   const int plane = blockIdx.y;
@@ -277,8 +279,7 @@ static int launch_rows_vec(const RowLaunch& p, cudaStream_t st) {
   const int64_t want = (max_chunks + kRowWarps - 1) / kRowWarps;
   const int64_t cap = std::max<int64_t>(1, (4 * resident_blocks + p.num_planes - 1) / p.num_planes);
   const dim3 grid(static_cast<unsigned>(std::min(want, cap)), static_cast<unsigned>(p.num_planes));
-  rows_kernel<VEC><<<grid, kRowThreads, 0, st>>>(p);
-  return launch_status("rows_kernel");
+  return launch_pdl("rows_kernel", rows_kernel<VEC>, grid, dim3(kRowThreads), 0, st, p);
 }
 
 struct RowCall {
@@ -360,7 +361,8 @@ static int run_rows(const RowCall& c, cudaStream_t st, const char* name) {
   }
   const int vec = vec_width(bits);
   // Chunk length per group: target ~1/8 of a resident warp's share of the call's
-  // bytes (clamped to [1 KB, 64 KB]), as whole rows of the group's widest plane.
+  // bytes (clamped to [2 KB, 64 KB]: at least one full batch of U 16-byte
+  // vectors per lane), as whole rows of the group's widest plane.
   int64_t max_rb[kRowGroups] = {1, 1, 1, 1};
   int64_t bytes = 0;
   for (const PlaneRef& r : all) {
@@ -370,7 +372,7 @@ static int run_rows(const RowCall& c, cudaStream_t st, const char* name) {
   const int64_t resident_warps =
       static_cast<int64_t>(blocks_per_sm(reinterpret_cast<const void*>(rows_kernel<16>), kRowThreads, 0)) * sm_count() *
       kRowWarps;
-  const int64_t target = std::min<int64_t>(64 * 1024, std::max<int64_t>(1024, bytes / (8 * resident_warps)));
+  const int64_t target = std::min<int64_t>(64 * 1024, std::max<int64_t>(2048, bytes / (8 * resident_warps)));
   int glg[kRowGroups];
   for (int g = 0; g < kRowGroups; ++g) {
     int lgc = 5;

@@ -278,6 +278,8 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
   const uint32_t wmask = W >= 32 ? 0xffffffffu : ((1u << W) - 1u);
   const int64_t windows = (p.n_tokens + W - 1) / W;
   const int64_t wstride = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  pdl_wait();
+  pdl_trigger();
 
   for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < windows; w += wstride) {
     const int64_t t0 = w * W;
@@ -500,8 +502,7 @@ static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
   int64_t gx = std::max<int64_t>(1, target / planes);
   gx = std::min<int64_t>(gx, (windows + (threads / 32) - 1) / (threads / 32));
   const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(planes));
-  kern<<<grid, threads, 0, st>>>(p);
-  return launch_status("tile_seg_kernel");
+  return launch_pdl("tile_seg_kernel", kern, grid, dim3(threads), 0, st, p);
 }
 
 template <typename CT, typename LT, int CODEC, bool SCATTER>

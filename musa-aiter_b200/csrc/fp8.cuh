@@ -139,6 +139,18 @@ __device__ __forceinline__ uint32_t fp8_encode2s_bounded(float g0, float w0, flo
   return c | ((g0 < 0.f) ? 0x80u : 0u) | ((g1 < 0.f) ? 0x8000u : 0u);
 }
 
+// fp8_encode2s_bounded for a pair of finite values (w0, w1: the correctly
+// rounded quotients x / s, e.g. fast_quot's q1).  The reference's flush of
+// |w| < 2^-6 (E4M3) / 2^-14 (E5M2) to a signed zero is one flush-to-zero
+// multiply by 2^-K (K = 120 / 112 puts the threshold on fp32's smallest
+// normal, so the product is exact above it and flushed below it), undone by a
+// multiply by 2^K; the signed result then goes straight through
+// cvt.rn.satfinite.  Its sign equals the reference's (w < 0) rule for every
+// finite x: x = -0 gives q1 = +0 (the remainder step adds +0 to -0), and a
+// flushed negative value keeps its sign.  Four multiplies, no compares.
+template <int F>
+__device__ __forceinline__ uint32_t fp8_encode2_finite(float w0, float w1);
+
 // x / s rounded to nearest in fp32 without a division per value, by
 // Markstein's correction step (P. Markstein, "IA-64 and Elementary Functions",
 // 2000): with y = RN(1/s) and q0 = RN(x * y), q0 is within one ulp of x / s,
@@ -188,6 +200,46 @@ __device__ __forceinline__ float fp8_decode_top(uint32_t x) {
   const uint32_t sign = x & 0x80000000u;
   const uint32_t bits = (((x >> (1 + mb)) & kMag) + (static_cast<uint32_t>(127 - bias) << 23)) | sign;
   return __uint_as_float((x & kExp) ? bits : sign);
+}
+
+// Flush-to-zero decode (fast path of the MLA row loader).  The code's seven
+// magnitude bits go straight into the fp32 exponent and mantissa fields with
+// no bias added, so the code's exponent field e becomes the fp32 exponent
+// field: e >= 1 gives 2^(e - 127) * (1 + m / 2^mb), a normal number, and e = 0
+// gives an fp32 subnormal or zero.  One flush-to-zero multiply by
+// s' = s * 2^(127 - bias) then yields RN(decode(code) * s) exactly: the power
+// of two moves no rounding point, a subnormal input (e = 0) becomes the
+// signed zero that the reference decoder gives, and no product is subnormal
+// or overflows differently while s lies in [2^(bias - 127), 2^(bias + 1))
+// (fp8_ftz_scale_ok).  The code sits in the top byte of x; the arithmetic
+// shift copies its sign over the bits that the mask then clears.
+template <int F>
+__device__ __forceinline__ float fp8_raw_top(uint32_t x) {
+  constexpr int sh = (F == MAK_FP8_E4M3) ? 4 : 3;
+  constexpr uint32_t mask = (F == MAK_FP8_E4M3) ? 0x87F00000u : 0x8FE00000u;
+  return __uint_as_float(static_cast<uint32_t>(static_cast<int32_t>(x) >> sh) & mask);
+}
+template <int F>
+__device__ __forceinline__ float fp8_ftz_bias() {
+  return F == MAK_FP8_E4M3 ? 0x1p120f : 0x1p112f;
+}
+template <int F>
+__device__ __forceinline__ bool fp8_ftz_scale_ok(float s) {
+  return F == MAK_FP8_E4M3 ? (s >= 0x1p-120f && s < 0x1p8f) : (s >= 0x1p-112f && s < 0x1p16f);
+}
+__device__ __forceinline__ float fmul_ftz(float a, float b) {
+  float r;
+  asm("mul.rn.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+template <int F>
+__device__ __forceinline__ uint32_t fp8_encode2_finite(float w0, float w1) {
+  constexpr float kDown = (F == MAK_FP8_E4M3) ? 0x1p-120f : 0x1p-112f;
+  constexpr float kUp = (F == MAK_FP8_E4M3) ? 0x1p120f : 0x1p112f;
+  const float v0 = __fmul_rn(fmul_ftz(w0, kDown), kUp);
+  const float v1 = __fmul_rn(fmul_ftz(w1, kDown), kUp);
+  return (F == MAK_FP8_E4M3) ? cvt_e4m3x2(v1, v0) : cvt_e5m2x2(v1, v0);
 }
 
 }  // namespace mak

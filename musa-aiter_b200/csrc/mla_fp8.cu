@@ -195,7 +195,8 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
     }
     const uint32_t mraw = max(m2 & 0xFFFFu, m2 >> 16);
     float amax = bits_to_f32<T>(mraw);
-    if (mraw >= kInfBits<T>) {
+    const bool all_finite = mraw < kInfBits<T>;
+    if (!all_finite) {
       amax = 0.f;
 #pragma unroll
       for (int j = 0; j < E; ++j) {
@@ -207,8 +208,17 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
     for (int o = 1; o < kLanesPerGroup; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float scale = __fdiv_rn(amax, fp8_max_of<F>());
     Bytes<E> codes;
-    if (fast_quot_ok(scale)) {
-      // one reciprocal per group, three fp32 operations per value (fp8.cuh)
+    if (fast_quot_ok(scale) && all_finite) {
+      // one reciprocal per group; per value three fp32 operations for the
+      // quotient and two multiplies for the flush (fp8.cuh), no compares
+      const float y = __frcp_rn(scale);
+#pragma unroll
+      for (int j = 0; j < E / 4; ++j) {
+        const float a = fast_quot(x[4 * j], scale, y).q1, b = fast_quot(x[4 * j + 1], scale, y).q1;
+        const float c = fast_quot(x[4 * j + 2], scale, y).q1, d = fast_quot(x[4 * j + 3], scale, y).q1;
+        codes.w[j] = fp8_encode2_finite<F>(a, b) | (fp8_encode2_finite<F>(c, d) << 16);
+      }
+    } else if (fast_quot_ok(scale)) {
       const float y = __frcp_rn(scale);
 #pragma unroll
       for (int j = 0; j < E / 4; ++j) {
@@ -293,7 +303,25 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_load_kernel(const __grid_
     uint4* dst = reinterpret_cast<uint4*>(kv_layer + t * p.kv_st + lane * E * 2);
     unsigned char* pe_dst = pe_layer + t * p.pe_st;
     const int b0 = lane * 8;
-    if (cur.have) {
+    if (cur.have && fp8_ftz_scale_ok<F>(cur.scale)) {
+      // flush-to-zero decode (fp8.cuh): three integer operations and one multiply per code
+      const float sf = __fmul_rn(cur.scale, fp8_ftz_bias<F>());  // exact: a power of two
+#pragma unroll
+      for (int k = 0; k < E / 8; ++k) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          // codes 2j, 2j+1 of word 2k + j/2 (bytes b, b + 1), each shifted to the top byte
+          const uint32_t cw = cur.codes.w[2 * k + (j >> 1)];
+          const uint32_t x0 = (j & 1) ? (cw << 8) : (cw << 24);
+          const uint32_t x1 = (j & 1) ? cw : (cw << 16);
+          w[j] = pack2<T>(fmul_ftz(fp8_raw_top<F>(x0), sf), fmul_ftz(fp8_raw_top<F>(x1), sf));
+        }
+        dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      if (b0 < p.pe_bytes) *reinterpret_cast<uint2*>(pe_dst + b0) = cur.pe[0];
+      if (b0 + 256 < p.pe_bytes) *reinterpret_cast<uint2*>(pe_dst + b0 + 256) = cur.pe[1];
+    } else if (cur.have) {
 #pragma unroll
       for (int k = 0; k < E / 8; ++k) {
         uint32_t w[4];
@@ -429,8 +457,9 @@ static int dispatch(MlaLaunch& L, const mak_mla_linear_desc* lin, const mak_rows
                              : dispatch_e<STORE, __half, MAK_FP8_E5M2>(L, lin, cache, st);
 }
 
-// Self-check of the store's fast path (fast_quot + fp8_encode2s_bounded)
-// against the IEEE fp32 division and the full encoder: thread k takes the scale
+// Self-check of the store's fast path (fast_quot, then fp8_encode2_finite for
+// finite values and fp8_encode2s_bounded next to non-finite ones) against the
+// IEEE fp32 division and the full encoder: thread k takes the scale
 // s = 2^scale_exp * (1 + k / 2^23) and every 16-bit input x of type T that a
 // group with that scale can hold (|x / s| <= fp8_max up to rounding, and the
 // non-finite inputs), and counts (a) FP8 codes that differ from
@@ -449,7 +478,10 @@ __global__ void fp8_quotient_check_kernel(int scale_exp, unsigned long long* cou
       const float x0 = bits_to_f32<T>(u), x1 = bits_to_f32<T>(u + 1);
       const FastQuot a = fast_quot(x0, s, y), b = fast_quot(x1, s, y);
       const float w0 = __fdiv_rn(x0, s), w1 = __fdiv_rn(x1, s);
-      const uint32_t got = fp8_encode2s_bounded<F>(a.q0, a.q1, b.q0, b.q1);
+      // the store's choice: finite values through fp8_encode2_finite, a non-finite one
+      // sends its lane to fp8_encode2s_bounded
+      const uint32_t got = (isfinite(x0) && isfinite(x1)) ? fp8_encode2_finite<F>(a.q1, b.q1)
+                                                          : fp8_encode2s_bounded<F>(a.q0, a.q1, b.q0, b.q1);
       // the inputs a group with scale s holds: |x / s| <= fp8_max up to rounding; inf / nan stay in
       const bool in0 = !(fabsf(w0) > lim) || !isfinite(x0), in1 = !(fabsf(w1) > lim) || !isfinite(x1);
       bad_code += (in0 && (got & 0xFFu) != fp8_encode<F>(w0)) + (in1 && (got >> 8) != fp8_encode<F>(w1));

@@ -172,7 +172,9 @@ def test_division_free_quotient_selfcheck(cuda_device, dt, fmt):
     counts = torch.zeros(2, dtype=torch.int64, device="cuda")
     code = _native.dtype_code(TORCH[dt])
     f = _native.MAK_FP8_E4M3 if fmt == "e4m3" else _native.MAK_FP8_E5M2
-    for e in (-60, -41, -9, -1, 0, 8, 16):
+    # the ends of the flush-to-zero encoder's threshold placement and of the fast range, and
+    # exponents where 16-bit inputs near the flush threshold are subnormal, normal or absent
+    for e in (-60, -41, -20, -12, -9, -1, 0, 5, 6, 8, 13, 14, 16):
         rc = lib.mak_fp8_quotient_selfcheck(code, f, e, counts.data_ptr(), _native.stream_ptr(counts.device))
         _native.check(rc, "mak_fp8_quotient_selfcheck")
     assert counts.tolist() == [0, 0], f"differing codes / quotients: {counts.tolist()}"
@@ -189,7 +191,11 @@ def test_load_every_code_byte(cuda_device, dt, fmt):
     g = torch.Generator().manual_seed(11)
     codes = torch.stack([torch.roll(torch.arange(256, dtype=torch.int32), s)[torch.arange(512) % 256]
                          for s in range(t)]).to(torch.uint8)
-    scale_pool = torch.tensor([1.0, 0.5, 3.0e-3, 1.7e5, 2.0**-60, 2.0**20, 0.0, 1.0e-40], dtype=torch.float32)
+    # includes both ends of the flush-to-zero decoder's scale range (E4M3 [2^-120, 2^8),
+    # E5M2 [2^-112, 2^16)), values just outside them, negative and subnormal scales
+    scale_pool = torch.tensor([1.0, 0.5, 3.0e-3, 1.7e5, 2.0**-60, 2.0**20, 0.0, 1.0e-40, 2.0**-120, 2.0**-121,
+                               2.0**-112, 2.0**-113, 255.99998, 256.0, 65535.996, 65536.0, -1.0, -3.0e-3,
+                               2.0**-126, 2.0**-149], dtype=torch.float32)
     scales = scale_pool[torch.randint(0, scale_pool.numel(), (t, 4), generator=g)]
     pe = torch.randn((t, 64), generator=g).to(TORCH[dt])
     rows = torch.cat([codes, scales.view(torch.uint8).reshape(t, 16), pe.view(torch.uint8).reshape(t, 128)], dim=1)

@@ -233,6 +233,56 @@ __device__ __forceinline__ float fmul_ftz(float a, float b) {
   return r;
 }
 
+// Packed fp32 pairs (sm_100 .f32x2 arithmetic): each element is rounded
+// exactly as the scalar operation would round it, two values per instruction.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul_ftz(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// Per-group constants of the packed store path: the scale s, -s and y = RN(1/s)
+// (fast_quot_ok(s) must hold), each in both halves.
+struct QuotPair {
+  uint64_t y, neg_s;
+};
+__device__ __forceinline__ QuotPair quot_pair(float s, float y) { return {f2_pack(y, y), f2_pack(-s, -s)}; }
+
+// fast_quot + fp8_encode2_finite on a pair (x0, x1) of finite values in five
+// packed operations: q0 = x * y, r = x - q0 * s (exact), q1 = q0 + r * y, then
+// the flush-to-zero multiply pair.  Returns code(x0) | code(x1) << 8.
+template <int F>
+__device__ __forceinline__ uint32_t fp8_encode2_quot_finite(float x0, float x1, const QuotPair& c) {
+  constexpr float kDown = (F == MAK_FP8_E4M3) ? 0x1p-120f : 0x1p-112f;
+  constexpr float kUp = (F == MAK_FP8_E4M3) ? 0x1p120f : 0x1p112f;
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t q0 = f2_mul(x, c.y);
+  const uint64_t r = f2_fma(q0, c.neg_s, x);
+  const uint64_t q1 = f2_fma(r, c.y, q0);
+  const uint64_t v = f2_mul(f2_mul_ftz(q1, f2_pack(kDown, kDown)), f2_pack(kUp, kUp));
+  float v0, v1;
+  f2_unpack(v, v0, v1);
+  return (F == MAK_FP8_E4M3) ? cvt_e4m3x2(v1, v0) : cvt_e5m2x2(v1, v0);
+}
+
 template <int F>
 __device__ __forceinline__ uint32_t fp8_encode2_finite(float w0, float w1) {
   constexpr float kDown = (F == MAK_FP8_E4M3) ? 0x1p-120f : 0x1p-112f;

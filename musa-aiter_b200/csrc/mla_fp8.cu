@@ -211,13 +211,11 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
     if (fast_quot_ok(scale) && all_finite) {
       // one reciprocal per group; per value three fp32 operations for the
       // quotient and two multiplies for the flush (fp8.cuh), no compares
-      const float y = __frcp_rn(scale);
+      const QuotPair qc = quot_pair(scale, __frcp_rn(scale));
 #pragma unroll
-      for (int j = 0; j < E / 4; ++j) {
-        const float a = fast_quot(x[4 * j], scale, y).q1, b = fast_quot(x[4 * j + 1], scale, y).q1;
-        const float c = fast_quot(x[4 * j + 2], scale, y).q1, d = fast_quot(x[4 * j + 3], scale, y).q1;
-        codes.w[j] = fp8_encode2_finite<F>(a, b) | (fp8_encode2_finite<F>(c, d) << 16);
-      }
+      for (int j = 0; j < E / 4; ++j)
+        codes.w[j] = fp8_encode2_quot_finite<F>(x[4 * j], x[4 * j + 1], qc) |
+                     (fp8_encode2_quot_finite<F>(x[4 * j + 2], x[4 * j + 3], qc) << 16);
     } else if (fast_quot_ok(scale)) {
       const float y = __frcp_rn(scale);
 #pragma unroll
@@ -306,6 +304,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_load_kernel(const __grid_
     if (cur.have && fp8_ftz_scale_ok<F>(cur.scale)) {
       // flush-to-zero decode (fp8.cuh): three integer operations and one multiply per code
       const float sf = __fmul_rn(cur.scale, fp8_ftz_bias<F>());  // exact: a power of two
+      const uint64_t sf2 = f2_pack(sf, sf);
 #pragma unroll
       for (int k = 0; k < E / 8; ++k) {
         uint32_t w[4];
@@ -315,7 +314,9 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_load_kernel(const __grid_
           const uint32_t cw = cur.codes.w[2 * k + (j >> 1)];
           const uint32_t x0 = (j & 1) ? (cw << 8) : (cw << 24);
           const uint32_t x1 = (j & 1) ? cw : (cw << 16);
-          w[j] = pack2<T>(fmul_ftz(fp8_raw_top<F>(x0), sf), fmul_ftz(fp8_raw_top<F>(x1), sf));
+          float v0, v1;
+          f2_unpack(f2_mul_ftz(f2_pack(fp8_raw_top<F>(x0), fp8_raw_top<F>(x1)), sf2), v0, v1);
+          w[j] = pack2<T>(v0, v1);
         }
         dst[k] = make_uint4(w[0], w[1], w[2], w[3]);
       }
@@ -457,8 +458,8 @@ static int dispatch(MlaLaunch& L, const mak_mla_linear_desc* lin, const mak_rows
                              : dispatch_e<STORE, __half, MAK_FP8_E5M2>(L, lin, cache, st);
 }
 
-// Self-check of the store's fast path (fast_quot, then fp8_encode2_finite for
-// finite values and fp8_encode2s_bounded next to non-finite ones) against the
+// Self-check of the store's fast path (fp8_encode2_quot_finite for finite
+// values, fast_quot + fp8_encode2s_bounded next to non-finite ones) against the
 // IEEE fp32 division and the full encoder: thread k takes the scale
 // s = 2^scale_exp * (1 + k / 2^23) and every 16-bit input x of type T that a
 // group with that scale can hold (|x / s| <= fp8_max up to rounding, and the
@@ -473,6 +474,7 @@ __global__ void fp8_quotient_check_kernel(int scale_exp, unsigned long long* cou
   unsigned long long bad_code = 0, bad_quot = 0;
   if (fast_quot_ok(s)) {
     const float y = __frcp_rn(s);
+    const QuotPair qc = quot_pair(s, y);
     const float lim = fp8_max_of<F>() * (1.f + 0x1p-20f);
     for (uint32_t u = 0; u < 65536u; u += 2) {
       const float x0 = bits_to_f32<T>(u), x1 = bits_to_f32<T>(u + 1);
@@ -480,7 +482,7 @@ __global__ void fp8_quotient_check_kernel(int scale_exp, unsigned long long* cou
       const float w0 = __fdiv_rn(x0, s), w1 = __fdiv_rn(x1, s);
       // the store's choice: finite values through fp8_encode2_finite, a non-finite one
       // sends its lane to fp8_encode2s_bounded
-      const uint32_t got = (isfinite(x0) && isfinite(x1)) ? fp8_encode2_finite<F>(a.q1, b.q1)
+      const uint32_t got = (isfinite(x0) && isfinite(x1)) ? fp8_encode2_quot_finite<F>(x0, x1, qc)
                                                           : fp8_encode2s_bounded<F>(a.q0, a.q1, b.q0, b.q1);
       // the inputs a group with scale s holds: |x / s| <= fp8_max up to rounding; inf / nan stay in
       const bool in0 = !(fabsf(w0) > lim) || !isfinite(x0), in1 = !(fabsf(w1) > lim) || !isfinite(x1);

@@ -150,9 +150,88 @@ __device__ __forceinline__ void store_fetch_owner(const MlaLaunch& p, StoreIn<E>
   if (p.owner != nullptr && s.dr >= 0 && s.dr < p.num_rows) s.own = __ldcg(p.owner + s.dr);
 }
 
+// Quantise and write one token of the store (inputs fetched by store_fetch).
+template <typename T, int F, int E>
+__device__ __forceinline__ void store_token(const MlaLaunch& p, unsigned char* plane, const StoreIn<E>& cur, int64_t t,
+                                            int lane) {
+  constexpr int kLanesPerGroup = 128 / E;
+  float x[E];
+#pragma unroll
+  for (int k = 0; k < E / 8; ++k) {
+    const uint32_t w[4] = {cur.v[k].x, cur.v[k].y, cur.v[k].z, cur.v[k].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      x[8 * k + 2 * j] = bits_to_f32<T>(w[j] & 0xFFFFu);
+      x[8 * k + 2 * j + 1] = bits_to_f32<T>(w[j] >> 16);
+    }
+  }
+  // amax over the finite values only (every stored scale is finite): the
+  // magnitudes' 16-bit patterns order like the values, so a packed unsigned
+  // max of |raw| finds the lane's largest; a non-finite one (pattern at or
+  // above the format's infinity, rare) sends the lane to the exact loop.
+  uint32_t m2 = 0;
+#pragma unroll
+  for (int k = 0; k < E / 8; ++k) {
+    m2 = __vmaxu2(m2, cur.v[k].x & 0x7FFF7FFFu);
+    m2 = __vmaxu2(m2, cur.v[k].y & 0x7FFF7FFFu);
+    m2 = __vmaxu2(m2, cur.v[k].z & 0x7FFF7FFFu);
+    m2 = __vmaxu2(m2, cur.v[k].w & 0x7FFF7FFFu);
+  }
+  const uint32_t mraw = max(m2 & 0xFFFFu, m2 >> 16);
+  float amax = bits_to_f32<T>(mraw);
+  const bool all_finite = mraw < kInfBits<T>;
+  if (!all_finite) {
+    amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      const float a = fabsf(x[j]);
+      if (a <= 3.40282346638528859812e+38f) amax = fmaxf(amax, a);
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < kLanesPerGroup; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float scale = __fdiv_rn(amax, fp8_max_of<F>());
+  Bytes<E> codes;
+  if (fast_quot_ok(scale) && all_finite) {
+    // one reciprocal per group; per value three fp32 operations for the
+    // quotient and two multiplies for the flush (fp8.cuh), no compares
+    const QuotPair qc = quot_pair(scale, __frcp_rn(scale));
+#pragma unroll
+    for (int j = 0; j < E / 4; ++j)
+      codes.w[j] = fp8_encode2_quot_finite<F>(x[4 * j], x[4 * j + 1], qc) |
+                   (fp8_encode2_quot_finite<F>(x[4 * j + 2], x[4 * j + 3], qc) << 16);
+  } else if (fast_quot_ok(scale)) {
+    const float y = __frcp_rn(scale);
+#pragma unroll
+    for (int j = 0; j < E / 4; ++j) {
+      const FastQuot a = fast_quot(x[4 * j], scale, y), b = fast_quot(x[4 * j + 1], scale, y);
+      const FastQuot c = fast_quot(x[4 * j + 2], scale, y), d = fast_quot(x[4 * j + 3], scale, y);
+      codes.w[j] = fp8_encode2s_bounded<F>(a.q0, a.q1, b.q0, b.q1) |
+                   (fp8_encode2s_bounded<F>(c.q0, c.q1, d.q0, d.q1) << 16);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < E / 4; ++j) {
+      const uint32_t lo = fp8_encode2<F>(__fdiv_rn(x[4 * j], scale), __fdiv_rn(x[4 * j + 1], scale));
+      const uint32_t hi = fp8_encode2<F>(__fdiv_rn(x[4 * j + 2], scale), __fdiv_rn(x[4 * j + 3], scale));
+      codes.w[j] = lo | (hi << 16);
+    }
+  }
+  const bool write = cur.dr >= 0 && cur.dr < p.num_rows &&
+                     (p.owner == nullptr || cur.own == (p.tag_hi | static_cast<uint64_t>(t)));
+  if (write) {
+    unsigned char* row = plane + mla_row_offset(p, cur.dr);
+    store_bytes<E>(row + lane * E, codes);
+    if ((lane % kLanesPerGroup) == 0) reinterpret_cast<float*>(row + p.kv_dim)[lane / kLanesPerGroup] = scale;
+    unsigned char* rope = row + p.kv_dim + (p.kv_dim / 128) * 4;
+    const int b0 = lane * 8;
+    if (b0 < p.pe_bytes) *reinterpret_cast<uint2*>(rope + b0) = cur.pe[0];
+    if (b0 + 256 < p.pe_bytes) *reinterpret_cast<uint2*>(rope + b0 + 256) = cur.pe[1];
+  }
+}
+
 template <typename T, int F, int E>
 __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid_constant__ MlaLaunch p) {
-  constexpr int kLanesPerGroup = 128 / E;
   const int lane = threadIdx.x & 31;
   const int layer = blockIdx.y;
   const int64_t step = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -163,90 +242,25 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_store_kernel(const __grid
   pdl_trigger();
   int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (t >= p.num_tokens) return;
-  StoreIn<E> cur;
-  store_fetch<E>(p, kv_layer, pe_layer, t, lane, cur);
-  store_fetch_owner<E>(p, cur);
+  // Two input buffers used in turn (no register copies between tokens): the
+  // next token's loads are in flight while this one is encoded.
+  StoreIn<E> a, b;
+  store_fetch<E>(p, kv_layer, pe_layer, t, lane, a);
+  store_fetch_owner<E>(p, a);
   while (true) {
-    const int64_t tn = t + step;
-    const bool more = tn < p.num_tokens;  // warp-uniform: a warp works on one token
-    StoreIn<E> nxt;
-    if (more) store_fetch<E>(p, kv_layer, pe_layer, tn, lane, nxt);
-    float x[E];
-#pragma unroll
-    for (int k = 0; k < E / 8; ++k) {
-      const uint32_t w[4] = {cur.v[k].x, cur.v[k].y, cur.v[k].z, cur.v[k].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        x[8 * k + 2 * j] = bits_to_f32<T>(w[j] & 0xFFFFu);
-        x[8 * k + 2 * j + 1] = bits_to_f32<T>(w[j] >> 16);
-      }
-    }
-    // amax over the finite values only (every stored scale is finite): the
-    // magnitudes' 16-bit patterns order like the values, so a packed unsigned
-    // max of |raw| finds the lane's largest; a non-finite one (pattern at or
-    // above the format's infinity, rare) sends the lane to the exact loop.
-    uint32_t m2 = 0;
-#pragma unroll
-    for (int k = 0; k < E / 8; ++k) {
-      m2 = __vmaxu2(m2, cur.v[k].x & 0x7FFF7FFFu);
-      m2 = __vmaxu2(m2, cur.v[k].y & 0x7FFF7FFFu);
-      m2 = __vmaxu2(m2, cur.v[k].z & 0x7FFF7FFFu);
-      m2 = __vmaxu2(m2, cur.v[k].w & 0x7FFF7FFFu);
-    }
-    const uint32_t mraw = max(m2 & 0xFFFFu, m2 >> 16);
-    float amax = bits_to_f32<T>(mraw);
-    const bool all_finite = mraw < kInfBits<T>;
-    if (!all_finite) {
-      amax = 0.f;
-#pragma unroll
-      for (int j = 0; j < E; ++j) {
-        const float a = fabsf(x[j]);
-        if (a <= 3.40282346638528859812e+38f) amax = fmaxf(amax, a);
-      }
-    }
-#pragma unroll
-    for (int o = 1; o < kLanesPerGroup; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float scale = __fdiv_rn(amax, fp8_max_of<F>());
-    Bytes<E> codes;
-    if (fast_quot_ok(scale) && all_finite) {
-      // one reciprocal per group; per value three fp32 operations for the
-      // quotient and two multiplies for the flush (fp8.cuh), no compares
-      const QuotPair qc = quot_pair(scale, __frcp_rn(scale));
-#pragma unroll
-      for (int j = 0; j < E / 4; ++j)
-        codes.w[j] = fp8_encode2_quot_finite<F>(x[4 * j], x[4 * j + 1], qc) |
-                     (fp8_encode2_quot_finite<F>(x[4 * j + 2], x[4 * j + 3], qc) << 16);
-    } else if (fast_quot_ok(scale)) {
-      const float y = __frcp_rn(scale);
-#pragma unroll
-      for (int j = 0; j < E / 4; ++j) {
-        const FastQuot a = fast_quot(x[4 * j], scale, y), b = fast_quot(x[4 * j + 1], scale, y);
-        const FastQuot c = fast_quot(x[4 * j + 2], scale, y), d = fast_quot(x[4 * j + 3], scale, y);
-        codes.w[j] = fp8_encode2s_bounded<F>(a.q0, a.q1, b.q0, b.q1) |
-                     (fp8_encode2s_bounded<F>(c.q0, c.q1, d.q0, d.q1) << 16);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < E / 4; ++j) {
-        const uint32_t lo = fp8_encode2<F>(__fdiv_rn(x[4 * j], scale), __fdiv_rn(x[4 * j + 1], scale));
-        const uint32_t hi = fp8_encode2<F>(__fdiv_rn(x[4 * j + 2], scale), __fdiv_rn(x[4 * j + 3], scale));
-        codes.w[j] = lo | (hi << 16);
-      }
-    }
-    const bool write = cur.dr >= 0 && cur.dr < p.num_rows &&
-                       (p.owner == nullptr || cur.own == (p.tag_hi | static_cast<uint64_t>(t)));
-    if (write) {
-      unsigned char* row = plane + mla_row_offset(p, cur.dr);
-      store_bytes<E>(row + lane * E, codes);
-      if ((lane % kLanesPerGroup) == 0) reinterpret_cast<float*>(row + p.kv_dim)[lane / kLanesPerGroup] = scale;
-      unsigned char* rope = row + p.kv_dim + (p.kv_dim / 128) * 4;
-      const int b0 = lane * 8;
-      if (b0 < p.pe_bytes) *reinterpret_cast<uint2*>(rope + b0) = cur.pe[0];
-      if (b0 + 256 < p.pe_bytes) *reinterpret_cast<uint2*>(rope + b0 + 256) = cur.pe[1];
-    }
+    int64_t tn = t + step;
+    bool more = tn < p.num_tokens;  // warp-uniform: a warp works on one token
+    if (more) store_fetch<E>(p, kv_layer, pe_layer, tn, lane, b);
+    store_token<T, F, E>(p, plane, a, t, lane);
     if (!more) break;
-    store_fetch_owner<E>(p, nxt);
-    cur = nxt;
+    store_fetch_owner<E>(p, b);
+    t = tn;
+    tn = t + step;
+    more = tn < p.num_tokens;
+    if (more) store_fetch<E>(p, kv_layer, pe_layer, tn, lane, a);
+    store_token<T, F, E>(p, plane, b, t, lane);
+    if (!more) break;
+    store_fetch_owner<E>(p, a);
     t = tn;
   }
 }

@@ -38,7 +38,8 @@ struct TileLaunch {
   int64_t l_sl, l_st, l_sh;        // linear strides (elements); head_dim stride is 1
   int64_t num_layers, num_heads, head_dim, block_size, num_slots, n_tokens, n_chunks;
   int32_t slots64, n_kv, fill_zero, cache_vec, lin_vec, scale_mode, heads_per_step;
-  int32_t window;  // tokens per warp window of the segment kernel (8, 16 or 32)
+  int32_t window;       // tokens per warp window of the segment kernel (8, 16 or 32)
+  int32_t plane_group;  // (kv, layer) planes a segment-kernel block walks per window
 };
 
 template <typename CT, typename LT, int CODEC>
@@ -257,7 +258,7 @@ __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileL
 // ---------------------------------------------------------------------------
 // MODE 1 handles segments of at least G tokens (plus zero rows), MODE 2 the shorter ones;
 // the two are launched back to back so each keeps the register budget its path needs.
-template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE>
+template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE, bool GROUPED>
 __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg_kernel(const __grid_constant__ TileLaunch p) {
   constexpr int G = 16 / sizeof(CT);
   constexpr int R = 16 / sizeof(LT);
@@ -267,9 +268,12 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
   const int NH = static_cast<int>(p.num_heads);
   const int units = NH * upr;
   const int64_t cap = p.block_size < 32 ? p.block_size : 32;
-  const int plane = blockIdx.y;
-  const int64_t l = plane % p.num_layers;
-  const int kv = plane / static_cast<int>(p.num_layers);
+  const int planes = static_cast<int>(p.num_layers) * p.n_kv;
+  const int plane_lo = GROUPED ? static_cast<int>(blockIdx.y) * p.plane_group : static_cast<int>(blockIdx.y);
+  const int plane_hi = GROUPED ? min(plane_lo + p.plane_group, planes) : plane_lo + 1;
+  // plane variables (set here for the first plane; a grouped block resets them per plane)
+  int64_t l = plane_lo % p.num_layers;
+  int kv = plane_lo / static_cast<int>(p.num_layers);
   const CT* cache_r = reinterpret_cast<const CT*>(p.cache[kv]) + l * p.c_sl;
   CT* cache_w = reinterpret_cast<CT*>(p.cache[kv]) + l * p.c_sl;
   LT* lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl;
@@ -312,6 +316,27 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
                            (static_cast<uint64_t>(__ballot_sync(0xffffffffu, startB)) << 32) |
                            ~(static_cast<uint64_t>(__ballot_sync(0xffffffffu, sA >= 0)) |
                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, sB >= 0)) << 32));
+    // The window's segments are the same for every plane: skip the planes when
+    // none is this launch's kind (and, in MODE 1, no zero rows are due).
+    if (GROUPED) {
+      bool work = MODE == 1 && !SCATTER && p.fill_zero && (~__ballot_sync(0xffffffffu, sA >= 0) & wmask) != 0;
+      for (uint32_t m = mStartA & wmask; m && !work; m &= m - 1) {
+        const int q = __ffs(m) - 1;
+        const uint64_t rest = bound >> (q + 1);
+        const int len = rest ? (__ffsll(static_cast<long long>(rest))) : (64 - q);
+        work = (MODE == 1) == (len >= G);
+      }
+      if (!work) continue;
+    }
+    for (int plane = plane_lo; plane < plane_hi; ++plane) {
+    if (GROUPED) {
+      l = plane % p.num_layers;
+      kv = plane / static_cast<int>(p.num_layers);
+      cache_r = reinterpret_cast<const CT*>(p.cache[kv]) + l * p.c_sl;
+      cache_w = reinterpret_cast<CT*>(p.cache[kv]) + l * p.c_sl;
+      lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl;
+      scl = CODEC ? p.scale[kv] : nullptr;
+    }
     // zero rows for skipped tokens of this window (gather, fill mode)
     if (MODE == 1 && !SCATTER && p.fill_zero) {
       uint32_t mZero = ~__ballot_sync(0xffffffffu, sA >= 0) & wmask;
@@ -477,6 +502,7 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
         }
       }
     }
+    }  // planes of the group
   }
 }
 
@@ -489,7 +515,7 @@ template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE>
 static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
   const int threads = 256;
   const int64_t planes = p.num_layers * p.n_kv;
-  auto kern = tile_seg_kernel<CT, LT, CODEC, SCATTER, MODE>;
+  auto kern = tile_seg_kernel<CT, LT, CODEC, SCATTER, MODE, false>;
   const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kern), threads, 0);
   // Narrower windows when 32-token windows would not give every resident warp a few windows
   // (short batches; runs of random slots are one token each, so parallelism comes from windows).
@@ -497,11 +523,21 @@ static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
   p.window = 32;
   while (p.window > 8 && (p.n_tokens + p.window - 1) / p.window * planes < 4 * resident_warps) p.window /= 2;
   const int64_t windows = (p.n_tokens + p.window - 1) / p.window;
-  // About 4 device-fulls of CTAs, spread over the planes; each CTA walks windows grid-stride.
+  // Planes per block: a window's slot scan serves all planes of its group, so
+  // group as many planes (up to 8) as still leave every resident warp a few
+  // (window, group) items.
+  p.plane_group = 8;
+  while (p.plane_group > 1 && windows * ((planes + p.plane_group - 1) / p.plane_group) < 4 * resident_warps)
+    p.plane_group /= 2;
+  const int64_t groups = (planes + p.plane_group - 1) / p.plane_group;
+  // About 4 device-fulls of CTAs, spread over the groups; each CTA walks windows grid-stride.
   const int64_t target = static_cast<int64_t>(per_sm) * sm_count() * 4;
-  int64_t gx = std::max<int64_t>(1, target / planes);
+  int64_t gx = std::max<int64_t>(1, target / groups);
   gx = std::min<int64_t>(gx, (windows + (threads / 32) - 1) / (threads / 32));
-  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(planes));
+  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(groups));
+  if (p.plane_group > 1)
+    return launch_pdl("tile_seg_kernel", tile_seg_kernel<CT, LT, CODEC, SCATTER, MODE, true>, grid, dim3(threads), 0, st,
+                      p);
   return launch_pdl("tile_seg_kernel", kern, grid, dim3(threads), 0, st, p);
 }
 

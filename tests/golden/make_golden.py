@@ -36,7 +36,9 @@ from pathlib import Path
 import numpy as np
 
 sys.dont_write_bytecode = True
-REF = os.environ.get("MUSA_AITER_REF", "/root/reference")
+REF = os.environ.get("MUSA_AITER_REF")
+if not REF:
+    raise SystemExit("set MUSA_AITER_REF to the reference musa-aiter source tree")
 if REF not in sys.path:
     sys.path.insert(0, REF)
 

@@ -59,8 +59,9 @@ def parse_args():
     ap.add_argument("--cpu-requests", type=int, default=8, help="requests in the bounded CPU sample")
     ap.add_argument("--workload", default="cfg2",
                     choices=("cfg2", "cfg1", "cfg1-tile", "cfg2-tile", "cfg3-e4m3", "cfg3-e5m2", "cfg4", "cfg5",
-                             "cfg5-fp8", "cfg5m"),
-                    help="cfg2 (default) is the headline; the others measure the remaining configs")
+                             "cfg5-fp8", "cfg5m", "ops"),
+                    help="cfg2 (default) is the headline; the others measure the remaining configs, "
+                         "'ops' times each remaining kvcache op once")
     ap.add_argument("--tokens", type=int, default=8192, help="cfg3 batch tokens (256 decode / 8192 prefill)")
     return ap.parse_args()
 
@@ -749,6 +750,195 @@ def run_workload(args) -> None:
         dist.destroy_process_group()
 
 
+def run_ops_sweep(args) -> None:
+    """One timing per remaining kvcache op (the rows not carried by configs 1-5): block-table
+    shapes of the Llama-3-8B cache (32 layers, 8 kv heads, head_dim 128, block_size 16), inputs on
+    the device, CUDA events around `--steps` calls after `--warmup` calls.  Algorithmic bytes =
+    payload read + written (index vectors excluded); host<->device ops report PCIe GB/s."""
+    import musa_aiter as ma
+    from musa_aiter import _native
+
+    os.environ.setdefault("MUSA_AITER_SKIP_VALIDATION", "1")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    peak, kind = load_peak()
+    L, NB, NH, HD, BS = 32, 4096, 8, 128, 16
+    T = 16384
+    res = {}
+
+    def timed(name, bytes_, fn, pcie=False, note=""):
+        for _ in range(max(1, args.warmup)):
+            fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = _native.launch_count()
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b) / args.steps
+        gbs = bytes_ / (ms * 1e-3) / 1e9
+        ent = {"gb_s": round(gbs, 1), "ms": round(ms, 4), "bytes": int(bytes_),
+               "launches_per_call": round((_native.launch_count() - l0) / args.steps, 2)}
+        if not pcie:
+            ent["frac_of_hbm"] = round(gbs / peak, 3)
+        if note:
+            ent["shape"] = note
+        res[name] = ent
+        print(f"# {name}: {ent}", file=sys.stderr, flush=True)
+
+    # block-table slots: T tokens in T/BS whole blocks drawn from a permutation
+    blocks = torch.randperm(NB, generator=torch.Generator().manual_seed(1))[: T // BS]
+    slots = (blocks[:, None] * BS + torch.arange(BS)[None, :]).flatten().to(dev)
+    tile = f"[{L},{NB},{NH},{HD},{BS}] tile caches, {T} block-table tokens"
+
+    # a5/a6 merged K/V rows <-> tile caches, all layers one launch
+    kc = torch.empty((L, NB, NH, HD, BS), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    vc = torch.empty_like(kc).normal_(generator=g)
+    merged = torch.empty((L, T, 2, NH, HD), dtype=torch.bfloat16, device=dev)
+    nbytes = 2 * L * T * 2 * NH * HD * 2
+    timed("kv_paged_to_merged_linear_multi_layer", nbytes,
+          lambda: ma.kv_paged_to_merged_linear_multi_layer(kc, vc, slots, out=merged), note=tile)
+    timed("kv_merged_linear_to_paged_multi_layer", nbytes,
+          lambda: ma.kv_merged_linear_to_paged_multi_layer(merged, kc, vc, slots), note=tile)
+
+    # a13 block copies: 1024 (src, dst) pairs, all layers, K and V
+    pairs = torch.stack([torch.randperm(NB, generator=torch.Generator().manual_seed(2))[:1024],
+                         torch.randperm(NB, generator=torch.Generator().manual_seed(3))[:1024]], 1).to(dev)
+    dk, dv = torch.empty_like(kc), torch.empty_like(vc)
+    timed("kv_copy_paged_blocks", 2 * 2 * 1024 * L * NH * HD * BS * 2,
+          lambda: ma.kv_copy_paged_blocks(kc, vc, dk, dv, pairs), note=f"1024 block pairs of {tile.split(' tile')[0]}")
+    del dk, dv
+
+    # a14 Flash dense load / cache-back, one layer, 64 sequences of up to 2048 tokens
+    B, S = 64, 2048
+    lens = torch.randint(S // 2, S + 1, (B,), generator=torch.Generator().manual_seed(4))
+    bt = torch.stack([torch.randperm(NB, generator=torch.Generator().manual_seed(10 + i))[: S // BS] for i in range(B)]).to(torch.int32)
+    tok = int(lens.sum())
+    lens_d, bt_d = lens.to(dev), bt.to(dev)
+    ok = torch.empty((B, S, NH, HD), dtype=torch.bfloat16, device=dev)
+    ov = torch.empty_like(ok)
+    timed("kv_load_and_reshape_flash", 2 * (tok * NH * HD * 2) + 2 * B * S * NH * HD * 2,
+          lambda: ma.kv_load_and_reshape_flash(kc[0], vc[0], bt_d, lens_d, max_seq_len=S, out_k=ok, out_v=ov),
+          note=f"[{NB},{NH},{HD},{BS}] caches -> [{B},{S},{NH},{HD}] x2, {tok} valid tokens (zero padding written)")
+    timed("kv_reshape_and_cache_back_flash", 2 * 2 * tok * NH * HD * 2,
+          lambda: ma.kv_reshape_and_cache_back_flash(ok, ov, kc[0], vc[0], bt_d, lens_d), note=f"{tok} tokens x2")
+
+    # a11 FP8 merged store / load (per-layer-head scales) and a12 FP8 Flash dequant-load
+    k8 = torch.zeros((L, NB, NH, HD, BS), dtype=torch.uint8, device=dev)
+    v8 = torch.zeros_like(k8)
+    ks = torch.full((L, NH), 0.01, device=dev)
+    vs = torch.full((L, NH), 0.02, device=dev)
+    nb8 = 2 * L * T * NH * HD * 3
+    timed("kv_merged_linear_to_paged_fp8_multi_layer", nb8,
+          lambda: ma.kv_merged_linear_to_paged_fp8_multi_layer(merged, k8, v8, slots, ks, vs), note=tile + ", e4m3")
+    timed("kv_paged_fp8_to_merged_linear_multi_layer", nb8,
+          lambda: ma.kv_paged_fp8_to_merged_linear_multi_layer(k8, v8, slots, ks, vs, out=merged), note=tile + ", e4m3 -> bf16")
+    timed("kv_load_and_dequantize_fp8_flash", 2 * tok * NH * HD * 1 + 2 * B * S * NH * HD * 2,
+          lambda: ma.kv_load_and_dequantize_fp8_flash(k8[0], v8[0], bt_d, lens_d, 0.01, 0.02, max_seq_len=S),
+          note=f"[{NB},{NH},{HD},{BS}] uint8 -> [{B},{S},{NH},{HD}] bf16 x2")
+    del k8, v8, kc, vc, merged, ok, ov
+
+    # a18 LMCache MLA buffer <-> [NL, NB, BS, 576] (all layers one launch)
+    NLm, NBm, BSm, W = 8, 4096, 64, 576
+    Tm = 65536
+    bm = torch.randperm(NBm, generator=torch.Generator().manual_seed(5))[: Tm // BSm]
+    sm = (bm[:, None] * BSm + torch.arange(BSm)[None, :]).flatten().to(dev)
+    pm = torch.empty((NLm, NBm, BSm, W), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    bufm = torch.empty((NLm, Tm, W), dtype=torch.bfloat16, device=dev)
+    mb = 2 * NLm * Tm * W * 2
+    timed("lmcache_paged_to_kv_buffer_mla", mb, lambda: ma.lmcache_paged_to_kv_buffer_mla(pm, bufm, sm),
+          note=f"[{NLm},{NBm},{BSm},{W}] -> [{NLm},{Tm},{W}]")
+    timed("lmcache_kv_buffer_to_paged_mla", mb, lambda: ma.lmcache_kv_buffer_to_paged_mla(bufm, pm, sm),
+          note=f"[{NLm},{Tm},{W}] -> [{NLm},{NBm},{BSm},{W}]")
+    del pm, bufm
+
+    # a19 DSV4 strided block transfer: staging [NL, T, 656] <-> padded pages, mode 1 (values then scales)
+    row, vb, sb = 656, 640, 16
+    NLs, NBs, BSs = 8, 2048, 64
+    stride = BSs * row + 256
+    pages = [torch.zeros(NBs * stride, dtype=torch.uint8, device=dev) for _ in range(NLs)]
+    ptrs = [t.data_ptr() for t in pages]
+    nblk = 1024
+    bids = torch.randperm(NBs, generator=torch.Generator().manual_seed(6))[:nblk].to(dev)
+    Ts = nblk * BSs
+    staging = torch.randint(0, 256, (NLs, Ts, row), dtype=torch.uint8, device=dev, generator=g)
+    sbytes = 2 * NLs * Ts * row
+    timed("lmcache_kv_strided_block_transfer (staging->paged)", sbytes,
+          lambda: ma.lmcache_kv_strided_block_transfer(staging, ptrs, bids, 0, NLs, 0, nblk, 0, Ts, BSs, row, stride, 1, vb, sb),
+          note=f"{NLs} layers x {nblk} blocks x {BSs} rows of {row} B, mode 1")
+    timed("lmcache_kv_strided_block_transfer (paged->staging)", sbytes,
+          lambda: ma.lmcache_kv_strided_block_transfer(staging, ptrs, bids, 1, NLs, 0, nblk, 0, Ts, BSs, row, stride, 1, vb, sb),
+          note=f"{NLs} layers x {nblk} blocks x {BSs} rows of {row} B, mode 1")
+    del pages, staging
+
+    # a20 DSV4 opaque byte rows by index (single pool and layer table)
+    item = 1728
+    npg = 262144
+    src = torch.randint(0, 256, (npg, item), dtype=torch.uint8, device=dev, generator=g)
+    dst = torch.zeros_like(src)
+    nrow = 131072
+    si = torch.randperm(npg, generator=torch.Generator().manual_seed(7))[:nrow].to(dev)
+    di = torch.randperm(npg, generator=torch.Generator().manual_seed(8))[:nrow].to(dev)
+    timed("kv_copy_paged_rows", 2 * nrow * item, lambda: ma.kv_copy_paged_rows(src, dst, si, di),
+          note=f"{nrow} of [{npg},{item}] uint8 rows")
+    del src, dst
+
+    # a21 HiCache: layer-first device pool -> page-first device pool, and device <-> pinned host
+    Lh, P, IB = 32, 65536, 2048
+    lf_k = torch.empty((Lh, P, IB // 2), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    lf_v = torch.empty_like(lf_k).normal_(generator=g)
+    pf_k = torch.empty((P, Lh, IB // 2), dtype=torch.bfloat16, device=dev)
+    pf_v = torch.empty_like(pf_k)
+    npages = 16384
+    hs = torch.randperm(P, generator=torch.Generator().manual_seed(9))[:npages].to(dev)
+    hd_ = torch.randperm(P, generator=torch.Generator().manual_seed(10))[:npages].to(dev)
+    hb = 2 * 2 * Lh * npages * IB
+    timed("hicache_transfer_kv_all_layer_lf_pf", hb,
+          lambda: ma.hicache_transfer_kv_all_layer_lf_pf(lf_k, pf_k, lf_v, pf_v, hs, hd_),
+          note=f"{npages} pages x {Lh} layers x {IB} B, K and V")
+    del pf_k, pf_v
+    hp = 4096
+    host_k = torch.empty((Lh, hp, IB // 2), dtype=torch.bfloat16, pin_memory=True)
+    host_v = torch.empty_like(host_k, pin_memory=True)
+    hsi = hs[:hp]
+    hdi = torch.arange(hp, device=dev)
+    timed("hicache_transfer_kv_all_layer (device->pinned host)", 2 * Lh * hp * IB,
+          lambda: ma.hicache_transfer_kv_all_layer(lf_k, host_k, lf_v, host_v, hsi, hdi), pcie=True,
+          note=f"{hp} pages x {Lh} layers x {IB} B, K and V, zero-copy kernel stores over PCIe")
+    del lf_k, lf_v, host_k, host_v
+
+    # a15 CacheGen codec on a [T, 4096] bf16 slab
+    x = (torch.empty((16384, 4096), dtype=torch.bfloat16, device=dev).normal_(generator=g) * 5.0)
+    timed("kv_cachegen_encode", x.numel() * (2 + 2 + 1), lambda: ma.kv_cachegen_encode(x, num_bins=256),
+          note="[16384,4096] bf16, 256 bins (min/max pass + encode pass)")
+    enc, cb, _ = ma.kv_cachegen_encode(x, num_bins=256)
+    timed("kv_cachegen_decode", x.numel() * (1 + 2), lambda: ma.kv_cachegen_decode(enc, cb, dtype=torch.bfloat16),
+          note="[16384,4096] uint8 -> bf16")
+    del x, enc
+
+    # a22 host<->device byte-copy batch (copy engines for large entries)
+    host = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    devb = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    n_ent = 256
+    size = (1 << 30) // n_ent
+    offs = [i * size for i in range(n_ent)]
+    timed("lmcache_musa_memcpy_batch_async (H2D)", n_ent * size,
+          lambda: ma.lmcache_musa_memcpy_batch_async([devb] * n_ent, [host] * n_ent, [size] * n_ent,
+                                                     destination_offsets=offs, source_offsets=offs), pcie=True,
+          note=f"{n_ent} entries of {size >> 20} MiB")
+    timed("lmcache_musa_memcpy_batch_async (D2H)", n_ent * size,
+          lambda: ma.lmcache_musa_memcpy_batch_async([host] * n_ent, [devb] * n_ent, [size] * n_ent,
+                                                     destination_offsets=offs, source_offsets=offs), pcie=True,
+          note=f"{n_ent} entries of {size >> 20} MiB")
+    print(json.dumps({"metric": METRIC, "workload": "ops: one timing per remaining kvcache op", "unit": "GB/s",
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "peak": peak, "peak_source": f"{kind} hbm_gbs",
+                      "data": "synthetic", "validation": "off in the timed loop (MUSA_AITER_SKIP_VALIDATION=1)",
+                      "ops": res}), flush=True)
+
+
 def main():
     args = parse_args()
     if args.requests is None:
@@ -757,6 +947,8 @@ def main():
         args.blocks = 32768
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "ops":
+        run_ops_sweep(args)
     elif args.workload != "cfg2":
         run_workload(args)
     else:

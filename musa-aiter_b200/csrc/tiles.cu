@@ -42,6 +42,16 @@ struct TileLaunch {
   int32_t plane_group;  // (kv, layer) planes a segment-kernel block walks per window
 };
 
+// Four consecutive linear elements as one aligned vector.
+template <typename LT>
+struct Vec4Of {
+  using T = uint2;
+};
+template <>
+struct Vec4Of<float> {
+  using T = uint4;
+};
+
 template <typename CT, typename LT, int CODEC>
 struct Codec {
   // raw copy: CT and LT are same-width integer carriers
@@ -368,6 +378,61 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
         // sectors per instruction) and a contiguous piece of the token row; four items
         // per lane in flight.
         const int hd = static_cast<int>(p.head_dim);
+        if (CODEC && (hd & 127) == 0) {
+          // FP8 caches, head_dim a multiple of 128: a lane takes dims lane + 32e (e < 4) of a
+          // 128-dim group, so each of its four cache loads (stores) is one warp access to 32
+          // consecutive cache rows and each token-row access 64 contiguous bytes; items
+          // (token, head, group) are walked with carried counters, two in flight per lane.
+          const int gpr = hd >> 7;
+          const int items = len * NH * gpr;
+          const int64_t sd = p.c_sd;
+          int j = 0, h = 0, g = 0;
+          for (int i0 = 0; i0 < items; i0 += 2) {
+            CT code[2][4];
+            LT vals[2][4];
+            int pk[2];  // (token << 16) | (head << 8) | group of each item in flight, -1 = none
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              pk[k] = -1;
+              if (i0 + k < items) {
+                pk[k] = (j << 16) | (h << 8) | g;
+                const int d0 = (g << 7) + lane;
+                if (!SCATTER) {
+                  const CT* c = cache_r + cbase + h * p.c_sh + static_cast<int64_t>(d0) * sd + o_s + j;
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) code[k][e] = c[32 * e * sd];
+                } else {
+                  const LT* x = lin_l + (ts + j) * p.l_st + h * p.l_sh + d0;
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) vals[k][e] = x[32 * e];
+                }
+                if (++g == gpr) {
+                  g = 0;
+                  if (++h == NH) {
+                    h = 0;
+                    ++j;
+                  }
+                }
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              if (pk[k] < 0) continue;
+              const int jj = pk[k] >> 16, hh = (pk[k] >> 8) & 0xFF, d0 = ((pk[k] & 0xFF) << 7) + lane;
+              const float sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? hh : l * NH + hh)];
+              if (!SCATTER) {
+                LT* o = lin_l + (ts + jj) * p.l_st + hh * p.l_sh + d0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[32 * e] = C::load(code[k][e], sc);
+              } else {
+                CT* c = cache_w + cbase + hh * p.c_sh + static_cast<int64_t>(d0) * sd + o_s + jj;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) c[32 * e * sd] = C::store(vals[k][e], sc);
+              }
+            }
+          }
+          continue;
+        }
         if ((hd & 31) == 0) {
           // head_dim a multiple of 32: lane = dim within a 32-dim group; every lane walks the
           // same (token, head, group) sequence with carried counters (no divisions), eight

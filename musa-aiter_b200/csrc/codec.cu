@@ -8,6 +8,9 @@
 //   3. CDF: sequential float32 prefix sum of the counts divided by numel (the
 //      reference's host bincount + cumsum).
 // Decode: out = codebook[code] converted to the output dtype.
+// All three passes read 16-byte vectors of the input (scalar tails), the
+// histogram is kept per warp in shared memory and the decode codebook sits in
+// shared memory as output-type bit patterns.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -40,12 +43,52 @@ __device__ __forceinline__ float key2f(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-__global__ void minmax_kernel(const void* x, int dt, int64_t n, uint32_t* keys) {
+// Element types as 16-byte vectors: VE elements per vector, each widened to fp32.
+template <int DT>
+struct Elem;
+template <>
+struct Elem<MAK_DT_F16> {
+  static constexpr int VE = 8;
+  __device__ static float at(const uint4& v, int i) {
+    const uint32_t w = reinterpret_cast<const uint32_t*>(&v)[i >> 1];
+    return __half2float(__ushort_as_half(static_cast<unsigned short>((i & 1) ? (w >> 16) : (w & 0xFFFFu))));
+  }
+};
+template <>
+struct Elem<MAK_DT_BF16> {
+  static constexpr int VE = 8;
+  __device__ static float at(const uint4& v, int i) {
+    const uint32_t w = reinterpret_cast<const uint32_t*>(&v)[i >> 1];
+    return __uint_as_float((i & 1) ? (w & 0xFFFF0000u) : (w << 16));
+  }
+};
+template <>
+struct Elem<MAK_DT_F32> {
+  static constexpr int VE = 4;
+  __device__ static float at(const uint4& v, int i) { return reinterpret_cast<const float*>(&v)[i]; }
+};
+
+// Grid-stride over 16-byte vectors (when x is 16-byte aligned) with a scalar tail.
+template <int DT>
+__global__ void minmax_kernel(const void* x, int64_t n, int vec_ok, uint32_t* keys) {
+  constexpr int VE = Elem<DT>::VE;
   float lo = 3.402823466e38f, hi = -3.402823466e38f;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const float v = load_f32(x, dt, i);
-    lo = fminf(lo, v);
-    hi = fmaxf(hi, v);
+  const int64_t nv = vec_ok ? n / VE : 0;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  for (int64_t i = tid; i < nv; i += nt) {
+    const uint4 v = __ldg(xv + i);
+#pragma unroll
+    for (int e = 0; e < VE; ++e) {
+      const float f = Elem<DT>::at(v, e);
+      lo = fminf(lo, f);
+      hi = fmaxf(hi, f);
+    }
+  }
+  for (int64_t i = nv * VE + tid; i < n; i += nt) {
+    const float f = load_f32(x, DT, i);
+    lo = fminf(lo, f);
+    hi = fmaxf(hi, f);
   }
   for (int o = 16; o > 0; o >>= 1) {
     lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
@@ -64,25 +107,58 @@ __global__ void minmax_finish_kernel(uint32_t* keys) {
   out[1] = hi;
 }
 
-__global__ void cachegen_encode_kernel(const void* x, int dt, int64_t n, const float* minmax, int bins, uint8_t* codes,
-                                       unsigned long long* counts) {
-  __shared__ unsigned int hist[256];
-  for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+__device__ __forceinline__ uint32_t cachegen_code(float v, float lo, float scale, float top) {
+  float q = rintf(__fmul_rn(__fsub_rn(v, lo), scale));
+  q = fminf(fmaxf(q, 0.f), top);  // fmaxf drops a NaN (max == min case) to 0
+  return static_cast<uint32_t>(q);
+}
+
+// Codes of VE elements per 16-byte vector (one VE-byte store), counted in a
+// per-warp shared-memory histogram that is folded into `counts` at the end.
+template <int DT>
+__global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int64_t n, int vec_ok, const float* minmax,
+                                                              int bins, uint8_t* codes, unsigned long long* counts) {
+  constexpr int VE = Elem<DT>::VE;
+  __shared__ unsigned int hist[8][256];
+  const int wib = threadIdx.x >> 5;
+  for (int b = threadIdx.x; b < 8 * 256; b += blockDim.x) (&hist[0][0])[b] = 0;
   __syncthreads();
   const float lo = minmax[0], hi = minmax[1];
   const float scale = __fmul_rn(__frcp_rn(__fsub_rn(hi, lo)), static_cast<float>(bins - 1));
   const float top = static_cast<float>(bins - 1);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const float v = load_f32(x, dt, i);
-    float q = rintf(__fmul_rn(__fsub_rn(v, lo), scale));
-    q = fminf(fmaxf(q, 0.f), top);  // fmaxf drops a NaN (max == min case) to 0
-    const uint32_t c = static_cast<uint32_t>(q);
+  const int64_t nv = vec_ok ? n / VE : 0;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  unsigned int* h = hist[wib];
+  for (int64_t i = tid; i < nv; i += nt) {
+    const uint4 v = __ldg(xv + i);
+    uint32_t packed[VE / 4];
+#pragma unroll
+    for (int w = 0; w < VE / 4; ++w) packed[w] = 0;
+#pragma unroll
+    for (int e = 0; e < VE; ++e) {
+      const uint32_t c = cachegen_code(Elem<DT>::at(v, e), lo, scale, top);
+      packed[e >> 2] |= c << (8 * (e & 3));
+      atomicAdd(h + c, 1u);
+    }
+    if (VE == 8) {
+      reinterpret_cast<uint2*>(codes)[i] = make_uint2(packed[0], packed[VE / 4 - 1]);
+    } else {
+      reinterpret_cast<uint32_t*>(codes)[i] = packed[0];
+    }
+  }
+  for (int64_t i = nv * VE + tid; i < n; i += nt) {
+    const uint32_t c = cachegen_code(load_f32(x, DT, i), lo, scale, top);
     codes[i] = static_cast<uint8_t>(c);
-    atomicAdd(&hist[c], 1u);
+    atomicAdd(h + c, 1u);
   }
   __syncthreads();
-  for (int b = threadIdx.x; b < bins; b += blockDim.x)
-    if (hist[b]) atomicAdd(counts + b, static_cast<unsigned long long>(hist[b]));
+  for (int b = threadIdx.x; b < bins; b += blockDim.x) {
+    unsigned int t = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += hist[w][b];
+    if (t) atomicAdd(counts + b, static_cast<unsigned long long>(t));
+  }
 }
 
 __global__ void cachegen_cdf_kernel(const unsigned long long* counts, int bins, int64_t n, float* cdf) {
@@ -96,14 +172,51 @@ __global__ void cachegen_cdf_kernel(const unsigned long long* counts, int bins, 
   }
 }
 
-__global__ void cachegen_decode_kernel(const uint8_t* codes, int64_t n, const void* codebook, int cb_dt, int bins,
-                                       void* out, int out_dt) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = codes[i];
+// 16 codes per 16-byte load, the codebook (as the output type's bits) in shared
+// memory, 16 outputs per thread iteration; a scalar tail for the rest.
+template <int OUT>
+__global__ void __launch_bounds__(256) cachegen_decode_kernel(const uint8_t* codes, int64_t n, int vec_ok,
+                                                              const void* codebook, int cb_dt, int bins, void* out) {
+  __shared__ uint32_t book[256];  // output-type bit pattern of each code (0 beyond the codebook)
+  for (int c = threadIdx.x; c < 256; c += blockDim.x) {
     const float v = c < bins ? load_f32(codebook, cb_dt, c) : 0.f;
-    store_from_f32(out, out_dt, i, v);
+    uint32_t b;
+    if (OUT == MAK_DT_F16) b = __half_as_ushort(__float2half_rn(v));
+    else if (OUT == MAK_DT_BF16) b = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    else b = __float_as_uint(v);
+    book[c] = b;
+  }
+  __syncthreads();
+  const int64_t nv = vec_ok ? n / 16 : 0;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = tid; i < nv; i += nt) {
+    const uint4 cv = __ldg(reinterpret_cast<const uint4*>(codes) + i);
+    const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w};
+    if (OUT == MAK_DT_F32) {
+      uint4* o = reinterpret_cast<uint4*>(out) + 4 * i;
+#pragma unroll
+      for (int w = 0; w < 4; ++w)
+        o[w] = make_uint4(book[cw[w] & 0xFF], book[(cw[w] >> 8) & 0xFF], book[(cw[w] >> 16) & 0xFF], book[cw[w] >> 24]);
+    } else {
+      uint4* o = reinterpret_cast<uint4*>(out) + 2 * i;
+      uint32_t r[8];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        r[2 * w] = book[cw[w] & 0xFF] | (book[(cw[w] >> 8) & 0xFF] << 16);
+        r[2 * w + 1] = book[(cw[w] >> 16) & 0xFF] | (book[cw[w] >> 24] << 16);
+      }
+      o[0] = make_uint4(r[0], r[1], r[2], r[3]);
+      o[1] = make_uint4(r[4], r[5], r[6], r[7]);
+    }
+  }
+  for (int64_t i = nv * 16 + tid; i < n; i += nt) {
+    const uint32_t b = book[codes[i]];
+    if (OUT == MAK_DT_F32) reinterpret_cast<uint32_t*>(out)[i] = b;
+    else reinterpret_cast<unsigned short*>(out)[i] = static_cast<unsigned short>(b);
   }
 }
+
+static bool aligned16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 static bool float_dtype(int32_t dt) { return dt == MAK_DT_F16 || dt == MAK_DT_BF16 || dt == MAK_DT_F32; }
 
@@ -122,8 +235,14 @@ int mak_minmax(const void* x, int32_t dtype, int64_t n, float* out_minmax, void*
   if (e == cudaSuccess) e = cudaMemsetAsync(keys + 1, 0x00, sizeof(uint32_t), st);
   if (e != cudaSuccess) return cuda_fail(e, "mak_minmax: init");
   const int threads = 256;
-  const int grid = grid_for(reinterpret_cast<const void*>(minmax_kernel), threads, 0, (n + threads - 1) / threads);
-  minmax_kernel<<<grid, threads, 0, st>>>(x, dtype, n, keys);
+  const int vec_ok = aligned16p(x);
+  const void* kern = dtype == MAK_DT_F16 ? reinterpret_cast<const void*>(minmax_kernel<MAK_DT_F16>)
+                     : dtype == MAK_DT_BF16 ? reinterpret_cast<const void*>(minmax_kernel<MAK_DT_BF16>)
+                                            : reinterpret_cast<const void*>(minmax_kernel<MAK_DT_F32>);
+  const int grid = grid_for(kern, threads, 0, (n / 4 + threads - 1) / threads + 1);
+  if (dtype == MAK_DT_F16) minmax_kernel<MAK_DT_F16><<<grid, threads, 0, st>>>(x, n, vec_ok, keys);
+  else if (dtype == MAK_DT_BF16) minmax_kernel<MAK_DT_BF16><<<grid, threads, 0, st>>>(x, n, vec_ok, keys);
+  else minmax_kernel<MAK_DT_F32><<<grid, threads, 0, st>>>(x, n, vec_ok, keys);
   int rc = launch_status("minmax_kernel");
   if (rc) return rc;
   minmax_finish_kernel<<<1, 1, 0, st>>>(keys);
@@ -140,9 +259,17 @@ int mak_cachegen_encode(const void* x, int32_t dtype, int64_t n, const float* mi
   cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(uint64_t) * num_bins, st);
   if (e != cudaSuccess) return cuda_fail(e, "mak_cachegen_encode: clear counts");
   const int threads = 256;
-  const int grid = grid_for(reinterpret_cast<const void*>(cachegen_encode_kernel), threads, 0, (n + threads - 1) / threads);
-  cachegen_encode_kernel<<<grid, threads, 0, st>>>(x, dtype, n, minmax, num_bins, codes,
-                                                   reinterpret_cast<unsigned long long*>(counts));
+  // vector path: 16-byte input vectors and VE-byte code stores (codes aligned to VE bytes)
+  const int ve = dtype == MAK_DT_F32 ? 4 : 8;
+  const int vec_ok = aligned16p(x) && (reinterpret_cast<uintptr_t>(codes) % ve) == 0;
+  auto* cnt = reinterpret_cast<unsigned long long*>(counts);
+  const void* kern = dtype == MAK_DT_F16 ? reinterpret_cast<const void*>(cachegen_encode_kernel<MAK_DT_F16>)
+                     : dtype == MAK_DT_BF16 ? reinterpret_cast<const void*>(cachegen_encode_kernel<MAK_DT_BF16>)
+                                            : reinterpret_cast<const void*>(cachegen_encode_kernel<MAK_DT_F32>);
+  const int grid = grid_for(kern, threads, 0, (n / ve + threads - 1) / threads + 1);
+  if (dtype == MAK_DT_F16) cachegen_encode_kernel<MAK_DT_F16><<<grid, threads, 0, st>>>(x, n, vec_ok, minmax, num_bins, codes, cnt);
+  else if (dtype == MAK_DT_BF16) cachegen_encode_kernel<MAK_DT_BF16><<<grid, threads, 0, st>>>(x, n, vec_ok, minmax, num_bins, codes, cnt);
+  else cachegen_encode_kernel<MAK_DT_F32><<<grid, threads, 0, st>>>(x, n, vec_ok, minmax, num_bins, codes, cnt);
   int rc = launch_status("cachegen_encode_kernel");
   if (rc) return rc;
   cachegen_cdf_kernel<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned long long*>(counts), num_bins, n, cdf);
@@ -157,9 +284,18 @@ int mak_cachegen_decode(const uint8_t* codes, int64_t n, const void* codebook, i
   if (n <= 0) return MAK_OK;
   if (!codes || !codebook || !out) return fail(MAK_E_INVALID, "mak_cachegen_decode: NULL pointer");
   const int threads = 256;
-  const int grid = grid_for(reinterpret_cast<const void*>(cachegen_decode_kernel), threads, 0, (n + threads - 1) / threads);
-  cachegen_decode_kernel<<<grid, threads, 0, as_stream(stream)>>>(codes, n, codebook, codebook_dtype, num_bins, out,
-                                                                  out_dtype);
+  const int vec_ok = aligned16p(codes) && aligned16p(out);
+  cudaStream_t st = as_stream(stream);
+  const void* kern = out_dtype == MAK_DT_F16 ? reinterpret_cast<const void*>(cachegen_decode_kernel<MAK_DT_F16>)
+                     : out_dtype == MAK_DT_BF16 ? reinterpret_cast<const void*>(cachegen_decode_kernel<MAK_DT_BF16>)
+                                                : reinterpret_cast<const void*>(cachegen_decode_kernel<MAK_DT_F32>);
+  const int grid = grid_for(kern, threads, 0, (n / 16 + threads - 1) / threads + 1);
+  if (out_dtype == MAK_DT_F16)
+    cachegen_decode_kernel<MAK_DT_F16><<<grid, threads, 0, st>>>(codes, n, vec_ok, codebook, codebook_dtype, num_bins, out);
+  else if (out_dtype == MAK_DT_BF16)
+    cachegen_decode_kernel<MAK_DT_BF16><<<grid, threads, 0, st>>>(codes, n, vec_ok, codebook, codebook_dtype, num_bins, out);
+  else
+    cachegen_decode_kernel<MAK_DT_F32><<<grid, threads, 0, st>>>(codes, n, vec_ok, codebook, codebook_dtype, num_bins, out);
   return launch_status("cachegen_decode_kernel");
 }
 

@@ -10,8 +10,8 @@
 //           all values first (block*stride + t*value_bytes) then all scales
 //           (block*stride + BS*value_bytes + t*scale_bytes).
 // direction 0 writes the paged pages, 1 reads them into staging.  One warp moves
-// one token row with the widest vector every address allows; all layers go in
-// one launch.  Negative block ids are skipped.
+// one (layer, block) with the widest vector every address allows, four vectors
+// per lane in flight; all layers go in one launch.  Negative block ids are skipped.
 #include <algorithm>
 
 #include "common.cuh"
@@ -38,51 +38,61 @@ struct VecOf<8> { using T = uint2; };
 template <>
 struct VecOf<4> { using T = uint32_t; };
 
+// Copy `n` vectors of a 2-D span: vector i lies at row i / per_row, column
+// i % per_row, rows `src_pitch` / `dst_pitch` bytes apart (a contiguous span is
+// one row).  Each lane keeps four vectors in flight.
 template <int VEC>
-__device__ __forceinline__ void copy_span(uint8_t* dst, const uint8_t* src, int64_t bytes, int lane) {
+__device__ __forceinline__ void copy_rows(uint8_t* dst, int64_t dst_pitch, const uint8_t* src, int64_t src_pitch,
+                                          uint32_t per_row, uint32_t n, int lane) {
   using V = typename VecOf<VEC>::T;
-  const int64_t nv = bytes / VEC;
-  V* d = reinterpret_cast<V*>(dst);
-  const V* s = reinterpret_cast<const V*>(src);
-  for (int64_t v0 = lane; v0 < nv; v0 += 32 * 4) {
+  for (uint32_t i0 = lane; i0 < n; i0 += 32 * 4) {
     V r[4];
+    int64_t so[4], dof[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t i = i0 + 32 * u;
+      const uint32_t row = i / per_row, col = i - row * per_row;
+      so[u] = row * src_pitch + static_cast<int64_t>(col) * VEC;
+      dof[u] = row * dst_pitch + static_cast<int64_t>(col) * VEC;
+      if (i < n) r[u] = *reinterpret_cast<const V*>(src + so[u]);
+    }
 #pragma unroll
     for (int u = 0; u < 4; ++u)
-      if (v0 + 32 * u < nv) r[u] = s[v0 + 32 * u];
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (v0 + 32 * u < nv) d[v0 + 32 * u] = r[u];
+      if (i0 + 32 * u < n) *reinterpret_cast<V*>(dst + dof[u]) = r[u];
   }
 }
 
+// One warp per (layer, block) of the batch: mode 0 moves the block's BS rows as
+// one contiguous span; mode 1 moves the values (BS rows of value_bytes, staging
+// pitch row_bytes, page pitch value_bytes) and then the scales as two 2-D spans.
 template <int VEC>
 __global__ void __launch_bounds__(256) strided_block_kernel(const __grid_constant__ StridedLaunch p) {
   const int lane = threadIdx.x & 31;
-  const int64_t rows = static_cast<int64_t>(p.num_layers) * p.n_valid * p.block_size;
+  const int64_t units = static_cast<int64_t>(p.num_layers) * p.n_valid;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < rows; w += nwarps) {
-    const int64_t t = w % p.block_size;
-    const int64_t rest = w / p.block_size;
-    const int64_t blk_i = rest % p.n_valid;
-    const int layer = static_cast<int>(rest / p.n_valid);
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < units; w += nwarps) {
+    const int layer = static_cast<int>(w / p.n_valid);
+    const int64_t blk_i = w - static_cast<int64_t>(layer) * p.n_valid;
     const int64_t blk = p.block_ids[p.idx_start + blk_i];
     if (blk < 0) continue;
     uint8_t* staged = p.staging + ((static_cast<int64_t>(p.layer_base + layer) * p.staging_tokens) + p.offset_in_object +
-                                   blk_i * p.block_size + t) * p.row_bytes;
+                                   blk_i * p.block_size) * p.row_bytes;
     uint8_t* page = reinterpret_cast<uint8_t*>(p.layers[layer]) + blk * p.block_stride;
+    const uint32_t bs = static_cast<uint32_t>(p.block_size);
     if (p.mode == 0) {
-      uint8_t* paged = page + t * p.row_bytes;
-      if (p.direction == 0) copy_span<VEC>(paged, staged, p.row_bytes, lane);
-      else copy_span<VEC>(staged, paged, p.row_bytes, lane);
+      const uint32_t n = static_cast<uint32_t>(p.block_size * p.row_bytes / VEC);
+      if (p.direction == 0) copy_rows<VEC>(page, 0, staged, 0, n, n, lane);
+      else copy_rows<VEC>(staged, 0, page, 0, n, n, lane);
     } else {
-      uint8_t* pv = page + t * p.value_bytes;
-      uint8_t* ps = page + p.block_size * p.value_bytes + t * p.scale_bytes;
+      const uint32_t vv = static_cast<uint32_t>(p.value_bytes / VEC), sv = static_cast<uint32_t>(p.scale_bytes / VEC);
+      uint8_t* pv = page;
+      uint8_t* ps = page + p.block_size * p.value_bytes;
       if (p.direction == 0) {
-        copy_span<VEC>(pv, staged, p.value_bytes, lane);
-        copy_span<VEC>(ps, staged + p.value_bytes, p.scale_bytes, lane);
+        if (vv) copy_rows<VEC>(pv, p.value_bytes, staged, p.row_bytes, vv, vv * bs, lane);
+        if (sv) copy_rows<VEC>(ps, p.scale_bytes, staged + p.value_bytes, p.row_bytes, sv, sv * bs, lane);
       } else {
-        copy_span<VEC>(staged, pv, p.value_bytes, lane);
-        copy_span<VEC>(staged + p.value_bytes, ps, p.scale_bytes, lane);
+        if (vv) copy_rows<VEC>(staged, p.row_bytes, pv, p.value_bytes, vv, vv * bs, lane);
+        if (sv) copy_rows<VEC>(staged + p.value_bytes, p.row_bytes, ps, p.scale_bytes, sv, sv * bs, lane);
       }
     }
   }
@@ -91,8 +101,8 @@ __global__ void __launch_bounds__(256) strided_block_kernel(const __grid_constan
 template <int VEC>
 static int launch_strided(const StridedLaunch& p, cudaStream_t st) {
   const int threads = 256;
-  const int64_t rows = static_cast<int64_t>(p.num_layers) * p.n_valid * p.block_size;
-  const int grid = grid_for(reinterpret_cast<const void*>(strided_block_kernel<VEC>), threads, 0, (rows + 7) / 8);
+  const int64_t units = static_cast<int64_t>(p.num_layers) * p.n_valid;  // one warp each
+  const int grid = grid_for(reinterpret_cast<const void*>(strided_block_kernel<VEC>), threads, 0, (units + 7) / 8);
   if (grid <= 0) return MAK_OK;
   strided_block_kernel<VEC><<<grid, threads, 0, st>>>(p);
   return launch_status("strided_block_kernel");
@@ -177,6 +187,9 @@ int mak_lmcache_strided_block_transfer(void* staging, const uint64_t* paged_ptrs
     return fail(MAK_E_INVALID, "%s: mode 1 needs value_bytes + scale_bytes == row_bytes, both multiples of 4", name);
   if (offset_in_object < 0 || offset_in_object + n_valid * block_size > staging_tokens)
     return fail(MAK_E_INVALID, "%s: block range exceeds the staging object", name);
+  if (block_size * row_bytes >= (int64_t{1} << 31))
+    return fail(MAK_E_UNSUPPORTED, "%s: a block of %lld rows of %lld bytes exceeds 2 GiB", name, (long long)block_size,
+                (long long)row_bytes);
   uint64_t bits = reinterpret_cast<uint64_t>(staging) | static_cast<uint64_t>(row_bytes) |
                   static_cast<uint64_t>(paged_block_stride);
   if (mode == 1) bits |= static_cast<uint64_t>(value_bytes) | static_cast<uint64_t>(scale_bytes);

@@ -1201,6 +1201,30 @@ def _flash_block_check(bt_cpu: torch.Tensor, lens_cpu: torch.Tensor, nb: int, bs
         raise ValueError(f"{name}: invalid block id {int(bt_cpu.flatten()[idx])}")
 
 
+def _flash_cache_back_check(seq_lens: torch.Tensor, block_tables: torch.Tensor, nb: int, bs: int, dense_len: int,
+                            name: str) -> None:
+    """kv_transfer.py:1625-1726 checks, sequence by sequence in batch order: the first sequence with a
+    length outside [0, dense_len], too few block-table columns, or an invalid block id among the blocks
+    it needs raises that error (the checks vectorised over the batch, one host copy of each table)."""
+    lens_cpu = seq_lens.to(device="cpu", dtype=torch.long)
+    bt_cpu = block_tables.to(device="cpu", dtype=torch.long)
+    need = (lens_cpu.clamp(min=0) + bs - 1) // bs
+    e_len = (lens_cpu < 0) | (lens_cpu > dense_len)
+    e_cols = need > int(bt_cpu.shape[1])
+    used = torch.arange(bt_cpu.shape[1]).unsqueeze(0) < need.unsqueeze(1)
+    bad = used & ((bt_cpu < 0) | (bt_cpu >= nb))
+    err = e_len | e_cols | bad.any(dim=1)
+    if not bool(err.any()):
+        return
+    b = int(torch.nonzero(err)[0])
+    if bool(e_len[b]):
+        raise ValueError(f"{name}: seq_lens exceeds dense sequence length")
+    if bool(e_cols[b]):
+        raise ValueError(f"{name}: block_tables does not contain enough columns")
+    j = int(torch.nonzero(bad[b])[0])
+    raise ValueError(f"{name}: invalid block id {int(bt_cpu[b, j])}")
+
+
 def _dense_slots(block_tables: torch.Tensor, seq_lens: torch.Tensor, bs: int, dense_len: int) -> torch.Tensor:
     from .kv_transfer_plan import build_slot_mapping
 
@@ -1235,10 +1259,13 @@ def kv_load_and_reshape_flash(
     if not _index_tensor_ok(seq_lens):
         raise ValueError(f"{name}: seq_lens must use an integer dtype")
     batch = int(block_tables.shape[0])
-    lens_cpu = seq_lens.to(device="cpu", dtype=torch.long)
-    if lens_cpu.numel() > 0 and int(lens_cpu.min()) < 0:
+    # the host copy of seq_lens serves the length checks and, without max_seq_len, the dense length;
+    # with max_seq_len given and validation off it is skipped (the device slot builder clamps)
+    check = seq_lens.device.type != "cuda" or validation_enabled()
+    lens_cpu = seq_lens.to(device="cpu", dtype=torch.long) if (check or max_seq_len is None) else None
+    if lens_cpu is not None and lens_cpu.numel() > 0 and int(lens_cpu.min()) < 0:
         raise ValueError(f"{name}: seq_lens must be non-negative")
-    inferred = int(lens_cpu.max()) if lens_cpu.numel() > 0 else 0
+    inferred = int(lens_cpu.max()) if lens_cpu is not None and lens_cpu.numel() > 0 else 0
     dense_len = inferred if max_seq_len is None else int(max_seq_len)
     if dense_len < inferred:
         raise ValueError(f"{name}: max_seq_len is smaller than seq_lens max")
@@ -1248,7 +1275,8 @@ def kv_load_and_reshape_flash(
     for o, c, w in ((out_k, key_cache, "out_k"), (out_v, value_cache, "out_v")):
         if o is not None and (tuple(o.shape) != shape or o.dtype != c.dtype or o.device != c.device):
             raise ValueError(f"{name}: {w} must match [B, S, kv_heads, head_dim] dtype/device")
-    _flash_block_check(block_tables.to(device="cpu", dtype=torch.long), lens_cpu, nb, bs, name)
+    if check:
+        _flash_block_check(block_tables.to(device="cpu", dtype=torch.long), lens_cpu, nb, bs, name)
     require_cuda(name, key_cache, value_cache, block_tables, seq_lens, out_k, out_v)
     ok = out_k if out_k is not None else torch.empty(shape, dtype=key_cache.dtype, device=key_cache.device)
     ov = out_v if out_v is not None else torch.empty(shape, dtype=value_cache.dtype, device=value_cache.device)
@@ -1296,20 +1324,9 @@ def kv_reshape_and_cache_back_flash(
         raise ValueError(f"{name}: block_tables must use an integer dtype")
     if not _index_tensor_ok(seq_lens):
         raise ValueError(f"{name}: seq_lens must use an integer dtype")
-    lens_cpu = seq_lens.to(device="cpu", dtype=torch.long)
-    bt_cpu = block_tables.to(device="cpu", dtype=torch.long)
     batch, dense_len = int(dense_k.shape[0]), int(dense_k.shape[1])
-    for b in range(batch):
-        n = int(lens_cpu[b])
-        if n < 0 or n > dense_len:
-            raise ValueError(f"{name}: seq_lens exceeds dense sequence length")
-        need = (n + bs - 1) // bs
-        if need > int(block_tables.shape[1]):
-            raise ValueError(f"{name}: block_tables does not contain enough columns")
-        row = bt_cpu[b, :need]
-        bad = (row < 0) | (row >= nb)
-        if bool(bad.any()):
-            raise ValueError(f"{name}: invalid block id {int(row[torch.nonzero(bad)[0]])}")
+    if batch and (seq_lens.device.type != "cuda" or validation_enabled()):
+        _flash_cache_back_check(seq_lens, block_tables, nb, bs, dense_len, name)
     require_cuda(name, dense_k, dense_v, key_cache, value_cache, block_tables, seq_lens)
     if batch * dense_len:
         slots = _dense_slots(block_tables, seq_lens, bs, dense_len)
@@ -1346,10 +1363,13 @@ def kv_load_and_dequantize_fp8_flash(
     if not _index_tensor_ok(block_tables) or not _index_tensor_ok(seq_lens):
         raise ValueError(f"{name}: block_tables and seq_lens must be integer tensors")
     batch = int(block_tables.shape[0])
-    lens_cpu = seq_lens.to(device="cpu", dtype=torch.long)
-    if lens_cpu.numel() > 0 and int(lens_cpu.min()) < 0:
+    # the host copy of seq_lens serves the length checks and, without max_seq_len, the dense length;
+    # with max_seq_len given and validation off it is skipped (the device slot builder clamps)
+    check = seq_lens.device.type != "cuda" or validation_enabled()
+    lens_cpu = seq_lens.to(device="cpu", dtype=torch.long) if (check or max_seq_len is None) else None
+    if lens_cpu is not None and lens_cpu.numel() > 0 and int(lens_cpu.min()) < 0:
         raise ValueError(f"{name}: seq_lens must be non-negative")
-    inferred = int(lens_cpu.max()) if lens_cpu.numel() > 0 else 0
+    inferred = int(lens_cpu.max()) if lens_cpu is not None and lens_cpu.numel() > 0 else 0
     dense_len = inferred if max_seq_len is None else int(max_seq_len)
     if dense_len < inferred:
         raise ValueError(f"{name}: max_seq_len is smaller than seq_lens max")
@@ -1359,7 +1379,8 @@ def kv_load_and_dequantize_fp8_flash(
     for o, w in ((out_k, "out_k"), (out_v, "out_v")):
         if o is not None and (tuple(o.shape) != shape or o.dtype is not out_dtype or o.device != key_cache_fp8.device):
             raise ValueError(f"{name}: {w} must match [B, S, kv_heads, head_dim] dtype/device")
-    _flash_block_check(block_tables.to(device="cpu", dtype=torch.long), lens_cpu, nb, bs, name)
+    if check:
+        _flash_block_check(block_tables.to(device="cpu", dtype=torch.long), lens_cpu, nb, bs, name)
     _validate_fp8_cache_tensor(key_cache_fp8, name=f"{name} key_cache_fp8")
     _validate_fp8_cache_tensor(value_cache_fp8, name=f"{name} value_cache_fp8")
     require_cuda(name, key_cache_fp8, value_cache_fp8, block_tables, seq_lens, out_k, out_v)
@@ -1871,7 +1892,8 @@ def kv_cachegen_decode(encoded: torch.Tensor, codebook: torch.Tensor, *, dtype: 
         raise ValueError(f"{name}: encoded and codebook must be on same device")
     if not codebook.is_floating_point():
         raise ValueError(f"{name}: codebook must use a floating dtype")
-    if encoded.numel() > 0 and int(encoded.max().item()) >= int(codebook.numel()):
+    if encoded.numel() > 0 and (encoded.device.type != "cuda" or validation_enabled()) and \
+            int(encoded.max().item()) >= int(codebook.numel()):
         raise ValueError(f"{name}: encoded bin exceeds codebook size")
     require_cuda(name, encoded, codebook)
     out_dtype = codebook.dtype if dtype is None else dtype

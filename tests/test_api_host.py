@@ -71,3 +71,29 @@ def test_dispatch_trace_line(monkeypatch, capsys):
     dispatch.emit_native("kv_paged_to_linear", torch.zeros(1), "unit test")
     err = capsys.readouterr().err
     assert "[MUSA_AITER DISPATCH] op=kv_paged_to_linear backend=cuda-sm100a" in err
+
+
+def test_flash_cache_back_checks_in_sequence_order():
+    """kv_reshape_and_cache_back_flash raises the reference's error of the first offending
+    sequence: length outside [0, S], too few block-table columns, or an invalid block id."""
+    kc = torch.zeros((8, 2, 4, 4))
+    vc = torch.zeros_like(kc)
+    dk = torch.zeros((3, 10, 2, 4))
+    dv = torch.zeros_like(dk)
+    bt = torch.tensor([[0, 1, 2], [3, 4, 5], [6, 7, 0]])
+    name = "kv_reshape_and_cache_back_flash"
+    cases = [
+        (torch.tensor([4, 11, 4]), bt, "seq_lens exceeds dense sequence length"),
+        (torch.tensor([4, -1, 4]), bt, "seq_lens exceeds dense sequence length"),
+        (torch.tensor([4, 4, 10]), bt[:, :2], "block_tables does not contain enough columns"),
+        (torch.tensor([4, 9, 11]), torch.tensor([[0, 1, 2], [3, 9, 5], [6, 7, 0]]), "invalid block id 9"),
+        (torch.tensor([4, 3, 9]), torch.tensor([[0, 1, 2], [3, -2, 5], [6, 7, 8]]), "invalid block id 8"),
+    ]
+    for lens, table, msg in cases:
+        with pytest.raises(ValueError, match=f"{name}: {msg}"):
+            ma.kv_reshape_and_cache_back_flash(dk, dv, kc, vc, table, lens)
+    # the block -2 of sequence 1 lies past that sequence's blocks, so it is not checked: only the
+    # device requirement remains
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        ma.kv_reshape_and_cache_back_flash(dk, dv, kc, vc, torch.tensor([[0, 1, 2], [3, -2, 5], [6, 7, 0]]),
+                                           torch.tensor([4, 3, 9]))

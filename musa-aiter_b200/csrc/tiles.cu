@@ -21,6 +21,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "fp8.cuh"
@@ -76,6 +77,52 @@ struct Codec<uint8_t, LT, MAK_FP8_E5M2> {
     return fp8_encode<MAK_FP8_E5M2>(__fdiv_rn(to_f32<LT>(x), sc));
   }
 };
+
+// FP8 store of one full (R dims x G tokens) chunk from 16-bit token vectors when
+// every value is finite and |x| / scale stays below the FP8 maximum (the usual
+// case: scales from an amax): one reciprocal per chunk and, per value pair, the
+// packed division-free quotient + flush-to-zero encoder of the MLA FP8 rows
+// (fp8_encode2_quot_finite), which mak_fp8_quotient_selfcheck checks against the
+// IEEE division for every 16-bit input in that range.  Returns false (nothing
+// written) when the chunk needs the per-element reference encoder.
+template <typename CT, typename LT, int CODEC, int G, int R>
+__device__ __forceinline__ bool encode_chunk_bounded(const uint4 (&toks)[G], float sc, CT* dst, int64_t row_pitch) {
+  if constexpr (CODEC == 0 || sizeof(LT) != 2 || sizeof(CT) != 1 || G != 16 || R != 8) {
+    return false;
+  } else {
+    constexpr uint32_t kInf = std::is_same<LT, __half>::value ? 0x7C00u : 0x7F80u;
+    constexpr float kBound = CODEC == MAK_FP8_E4M3 ? 447.99f : 57343.f;
+    if (!fast_quot_ok(sc)) return false;
+    uint32_t m2 = 0;
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+      m2 = __vmaxu2(m2, toks[i].x & 0x7FFF7FFFu);
+      m2 = __vmaxu2(m2, toks[i].y & 0x7FFF7FFFu);
+      m2 = __vmaxu2(m2, toks[i].z & 0x7FFF7FFFu);
+      m2 = __vmaxu2(m2, toks[i].w & 0x7FFF7FFFu);
+    }
+    const uint32_t mraw = max(m2 & 0xFFFFu, m2 >> 16);
+    if (mraw >= kInf) return false;
+    const float y = __frcp_rn(sc);
+    const unsigned short mbits = static_cast<unsigned short>(mraw);
+    if (!(__fmul_rn(to_f32<LT>(*reinterpret_cast<const LT*>(&mbits)), y) <= kBound)) return false;
+    const QuotPair qc = quot_pair(sc, y);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float a = to_f32<LT>(reinterpret_cast<const LT*>(&toks[4 * q])[r]);
+        const float b = to_f32<LT>(reinterpret_cast<const LT*>(&toks[4 * q + 1])[r]);
+        const float c = to_f32<LT>(reinterpret_cast<const LT*>(&toks[4 * q + 2])[r]);
+        const float d = to_f32<LT>(reinterpret_cast<const LT*>(&toks[4 * q + 3])[r]);
+        w[q] = fp8_encode2_quot_finite<CODEC>(a, b, qc) | (fp8_encode2_quot_finite<CODEC>(c, d, qc) << 16);
+      }
+      *reinterpret_cast<uint4*>(dst + r * row_pitch) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    return true;
+  }
+}
 
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileLaunch p) {
@@ -537,13 +584,15 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
             uint4 toks[G];
 #pragma unroll
             for (int i = 0; i < G; ++i) toks[i] = __ldg(reinterpret_cast<const uint4*>(lrow + (col0 + i - o_s) * p.l_st));
+            if (!encode_chunk_bounded<CT, LT, CODEC, G, R>(toks, sc, cache_w + row0 + col0, p.c_sd)) {
 #pragma unroll
-            for (int r = 0; r < R; ++r) {
-              uint4 v;
-              CT* e = reinterpret_cast<CT*>(&v);
+              for (int r = 0; r < R; ++r) {
+                uint4 v;
+                CT* e = reinterpret_cast<CT*>(&v);
 #pragma unroll
-              for (int i = 0; i < G; ++i) e[i] = C::store(reinterpret_cast<const LT*>(&toks[i])[r], sc);
-              *reinterpret_cast<uint4*>(cache_w + row0 + r * p.c_sd + col0) = v;
+                for (int i = 0; i < G; ++i) e[i] = C::store(reinterpret_cast<const LT*>(&toks[i])[r], sc);
+                *reinterpret_cast<uint4*>(cache_w + row0 + r * p.c_sd + col0) = v;
+              }
             }
           }
         } else {

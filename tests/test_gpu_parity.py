@@ -381,3 +381,37 @@ def test_empty_and_out_of_range(cuda_device):
     all_neg = torch.full((5,), -1, device="cuda")
     ok, _ = ma.kv_paged_to_linear(kc, vc, all_neg)
     assert torch.count_nonzero(ok) == 0
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", ("bfloat16", "float16"))
+def test_fp8_block_table_store_bounded_and_fallback_chunks(cuda_device, dt, fmt):
+    """Full 16-token chunks whose values stay below fp8_max * scale take the division-free
+    encoder, the others the per-element one; both must equal the reference rule: amax-derived
+    per-head scales, plus chunks holding -0, values at and below the flush threshold, values
+    beyond the scaled range, inf and nan."""
+    g = torch.Generator().manual_seed(17)
+    nb, nh, hd, bs = 64, 2, 128, 16
+    slots = block_table_slots([160, 96, 33], nb, bs, g)
+    t = slots.numel()
+    fmax = 448.0 if fmt == "e4m3" else 57344.0
+    flush = 2.0**-6 if fmt == "e4m3" else 2.0**-14
+    kl = torch.randn((t, nh, hd), generator=g) * 3.0
+    ks = kl.abs().amax(dim=(0, 2)) / fmax  # [NH]
+    kl[5, 0, :8] = torch.tensor([-0.0, 0.0, flush * ks[0] * 0.999, -flush * ks[0] * 0.999, flush * ks[0],
+                                 -flush * ks[0] * 1.001, ks[0] * fmax * 0.9999, -ks[0] * fmax])
+    kl[40, 1, 16:20] = torch.tensor([ks[1] * fmax * 4.0, -ks[1] * fmax * 1.2, 1.0e-30, -1.0e-30])
+    kl[70, 0, 64] = float("inf")
+    kl[71, 1, 100] = float("nan")
+    kl[100, 0, 3] = -float("inf")
+    kl = kl.to(TORCH_OF[dt])
+    vl = (torch.randn((t, nh, hd), generator=g) * 0.5).to(TORCH_OF[dt])
+    vs = torch.tensor(0.5 / fmax)
+    kc = torch.zeros((nb, nh, hd, bs), dtype=torch.uint8, device="cuda")
+    vc = torch.zeros_like(kc)
+    ma.kv_linear_to_paged_fp8(kl.cuda(), vl.cuda(), kc, vc, slots.cuda(), ks.cuda(), float(vs), fp8_format=fmt)
+    rkc, rvc = np.zeros(kc.shape, np.uint8), np.zeros(vc.shape, np.uint8)
+    O.kv_linear_to_paged_fp8(to_np(kl), to_np(vl), rkc, rvc, slots.numpy(), ks.numpy(), np.float32(vs), lin_dtype=dt,
+                             fp8_format=fmt)
+    eq(kc, rkc, "fp8 block-table store k")
+    eq(vc, rvc, "fp8 block-table store v")

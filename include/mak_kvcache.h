@@ -326,6 +326,14 @@ MAK_API int mak_rows_scatter_static(const mak_rows_desc* linear, const mak_rows_
 MAK_API int mak_rows_copy(const mak_rows_desc* src, const mak_rows_desc* dst, const int64_t* row_bytes, int64_t row_bytes0,
                   const void* src_idx, int32_t src_idx_dtype, const void* dst_idx, int32_t dst_idx_dtype, int64_t n,
                   void* workspace, size_t workspace_bytes, void* stream);
+/* mak_rows_copy with an indexed destination whose duplicate destinations are
+ * resolved through a caller-kept owner table instead of a workspace (same table
+ * and epoch rules as mak_rows_scatterv_owned; owner_rows >= dst->num_rows):
+ * one marking launch, then the copy.  Same replaced launchers as mak_rows_copy. */
+MAK_API int mak_rows_copy_owned(const mak_rows_desc* src, const mak_rows_desc* dst, const int64_t* row_bytes,
+                                int64_t row_bytes0, const void* src_idx, int32_t src_idx_dtype, const void* dst_idx,
+                                int32_t dst_idx_dtype, int64_t n, uint64_t* owner, int64_t owner_rows, uint32_t epoch,
+                                void* stream);
 
 
 /*

@@ -532,6 +532,40 @@ int mak_rows_scatterv_owned(const mak_rows_desc* linear, const mak_rows_desc* pa
   return run_rows(c, st, name);
 }
 
+int mak_rows_copy_owned(const mak_rows_desc* src, const mak_rows_desc* dst, const int64_t* row_bytes,
+                        int64_t row_bytes0, const void* src_idx, int32_t src_idx_dtype, const void* dst_idx,
+                        int32_t dst_idx_dtype, int64_t n, uint64_t* owner, int64_t owner_rows, uint32_t epoch,
+                        void* stream) {
+  const char* name = "mak_rows_copy_owned";
+  if (n < 0) return fail(MAK_E_INVALID, "%s: negative item count", name);
+  if (n == 0) return MAK_OK;
+  if (dst == nullptr) return fail(MAK_E_INVALID, "%s: row descriptor is NULL", name);
+  if (dst_idx == nullptr || !valid_index_dtype(dst_idx_dtype))
+    return fail(MAK_E_INVALID, "%s: needs an int32 or int64 destination index", name);
+  if (dst->num_rows > owner_rows)
+    return fail(MAK_E_INVALID, "%s: owner table has %lld rows, the destination %lld", name, (long long)owner_rows,
+                (long long)dst->num_rows);
+  cudaStream_t st = as_stream(stream);
+  int rc = mark_owners(dst_idx, dst_idx_dtype, n, owner, owner_rows, epoch, st, name);
+  if (rc) return rc;
+  RowCall c{};
+  c.src = src;
+  c.dst = dst;
+  c.n_groups = 1;
+  c.row_bytes = row_bytes;
+  c.row_bytes0 = row_bytes0;
+  c.src_idx = src_idx;
+  c.src_idx_dtype = src_idx_dtype;
+  c.dst_idx = dst_idx;
+  c.dst_idx_dtype = dst_idx_dtype;
+  c.n_items = n;
+  c.n_total = n;
+  c.owner = reinterpret_cast<const unsigned long long*>(owner);
+  c.owner_rows = owner_rows;
+  c.tag_hi = static_cast<uint64_t>(epoch) << 32;
+  return run_rows(c, st, name);
+}
+
 int mak_rows_copy(const mak_rows_desc* src, const mak_rows_desc* dst, const int64_t* row_bytes, int64_t row_bytes0,
                   const void* src_idx, int32_t src_idx_dtype, const void* dst_idx, int32_t dst_idx_dtype, int64_t n,
                   void* workspace, size_t workspace_bytes, void* stream) {

@@ -219,6 +219,11 @@ _PROTOTYPES = {
         [POINTER(MlaLinearDesc), c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, ctypes.c_uint32, c_void_p],
     ),
     "mak_fp8_quotient_selfcheck": (c_int32, [c_int32, c_int32, c_int32, c_void_p, c_void_p]),
+    "mak_rows_copy_owned": (
+        c_int32,
+        [c_void_p, c_void_p, POINTER(c_int64), c_int64, c_void_p, c_int32, c_void_p, c_int32, c_int64, c_void_p, c_int64,
+         ctypes.c_uint32, c_void_p],
+    ),
     "mak_rows_copy": (
         c_int32,
         [
@@ -352,6 +357,20 @@ def owned_scatter(device: torch.device, stream: int, rows: int, n: int, launch):
             epoch = 1
         ent[3] = epoch + 1
         return launch(ent[2], ent[1], epoch)
+
+
+def rows_copy(src_desc, dst_desc, row_bytes0: int, si: int, sdt: int, di: int, ddt: int, n: int, dst_rows: int,
+              device: torch.device, stream: int) -> int:
+    """``mak_rows_copy`` with an indexed destination: duplicate destinations resolved through this
+    stream's owner table (``mak_rows_copy_owned``), or through a workspace from torch's caching
+    allocator where owner tables do not apply (stream capture, very large destinations)."""
+    lib = load()
+    rc = owned_scatter(device, stream, dst_rows, n, lambda own, orows, epoch: lib.mak_rows_copy_owned(
+        src_desc, dst_desc, None, row_bytes0, si, sdt, di, ddt, n, own, orows, epoch, stream))
+    if rc is None:
+        ws, nbytes = workspace(n, device)
+        rc = lib.mak_rows_copy(src_desc, dst_desc, None, row_bytes0, si, sdt, di, ddt, n, ws.data_ptr(), nbytes, stream)
+    return rc
 
 
 def plane_array(ptrs: list[int]):

@@ -143,12 +143,10 @@ def _transfer(src_k, dst_k, src_v, dst_v, src_indices, dst_indices, *, src_layou
         dst_planes += [dst_v.data_ptr() + l * dg[4] for l in layers]
     si, sc = kernel_slots(src_indices.to(dev))
     di, dc = kernel_slots(dst_indices.to(dev))
-    lib = _native.load()
-    ws, nbytes = _native.workspace(n, dev)
     sd, sa = _native.rows_desc(src_planes, 1, sg[3], 0, sg[1])
     dd, da = _native.rows_desc(dst_planes, 1, dg[3], 0, dg[1])
-    rc = lib.mak_rows_copy(ctypes.byref(sd), ctypes.byref(dd), None, item_bytes, _native.ptr(si), sc, _native.ptr(di), dc,
-                           n, _native.ptr(ws), nbytes, _native.stream_ptr(dev))
+    rc = _native.rows_copy(ctypes.byref(sd), ctypes.byref(dd), item_bytes, _native.ptr(si), sc, _native.ptr(di), dc, n,
+                           int(dg[1]), dev, _native.stream_ptr(dev))
     _native.check(rc, "hicache_transfer")
     emit_native("hicache_transfer", src_k, f"sm100a row engine {src_layout}->{dst_layout}, {len(src_planes)} planes, one launch")
     return True
@@ -230,15 +228,13 @@ def _page_rows(values: torch.Tensor, page_size: int) -> torch.Tensor:
 
 
 def _direct_copy(src_planes, dst_planes, s_geo, d_geo, src_rows, dst_rows, item_bytes, dev, name):
-    lib = _native.load()
     n = int(src_rows.numel())
     si = src_rows.to(dev)
     di = dst_rows.to(dev)
-    ws, nbytes = _native.workspace(n, dev)
     sd, sa = _native.rows_desc(src_planes, *s_geo)
     dd, da = _native.rows_desc(dst_planes, *d_geo)
-    rc = lib.mak_rows_copy(ctypes.byref(sd), ctypes.byref(dd), None, item_bytes, _native.ptr(si), _native.MAK_DT_I64,
-                           _native.ptr(di), _native.MAK_DT_I64, n, _native.ptr(ws), nbytes, _native.stream_ptr(dev))
+    rc = _native.rows_copy(ctypes.byref(sd), ctypes.byref(dd), item_bytes, _native.ptr(si), _native.MAK_DT_I64,
+                           _native.ptr(di), _native.MAK_DT_I64, n, int(d_geo[3]), dev, _native.stream_ptr(dev))
     _native.check(rc, name)
 
 

@@ -1524,7 +1524,6 @@ def _block_tail_contiguous(t: torch.Tensor, multi_layer: bool) -> bool:
 
 
 def _copy_blocks(src_k, src_v, dst_k, dst_v, pairs_dev: torch.Tensor, multi_layer: bool, name: str) -> None:
-    lib = _native.load()
     for t in (src_k, src_v, dst_k, dst_v):
         if not _block_tail_contiguous(t, multi_layer) or (multi_layer and t.stride(0) % 1):
             raise ValueError(f"{name}: each cache block must be contiguous")
@@ -1537,11 +1536,10 @@ def _copy_blocks(src_k, src_v, dst_k, dst_v, pairs_dev: torch.Tensor, multi_laye
     src_idx = pairs_dev[:, 0].contiguous()
     dst_idx = torch.where(src_idx >= 0, pairs_dev[:, 1], torch.full_like(src_idx, -1)).contiguous()
     n = int(src_idx.numel())
-    ws, nbytes = _native.workspace(n, dst_k.device)
     sd, sa = _native.rows_desc(sp, 1, s_bstride, 0, s_nb)
     dd, da = _native.rows_desc(dp, 1, d_bstride, 0, d_nb)
-    rc = lib.mak_rows_copy(ctypes.byref(sd), ctypes.byref(dd), None, row, _native.ptr(src_idx), _native.MAK_DT_I64,
-                           _native.ptr(dst_idx), _native.MAK_DT_I64, n, _native.ptr(ws), nbytes,
+    rc = _native.rows_copy(ctypes.byref(sd), ctypes.byref(dd), row, _native.ptr(src_idx), _native.MAK_DT_I64,
+                           _native.ptr(dst_idx), _native.MAK_DT_I64, n, d_nb, dst_k.device,
                            _native.stream_ptr(dst_k.device))
     _native.check(rc, name)
 
@@ -1711,7 +1709,7 @@ def _addressable(t: torch.Tensor) -> bool:
 
 def _rows_copy_planes(srcs: list[torch.Tensor], dsts: list[torch.Tensor], src_indices, dst_indices, name: str) -> None:
     """dst[l][dst_idx[i]] = src[l][src_idx[i]] for every plane pair, one launch."""
-    lib = _native.load()
+    _native.load()
     s0, d0 = srcs[0], dsts[0]
     dev = s0.device if s0.device.type == "cuda" else d0.device
     if dev.type != "cuda":
@@ -1727,11 +1725,10 @@ def _rows_copy_planes(srcs: list[torch.Tensor], dsts: list[torch.Tensor], src_in
     n = int(si.numel())
     if n == 0:
         return
-    ws, nbytes = _native.workspace(n, dev)
     sd, sa = _native.rows_desc([t.data_ptr() for t in srcs], 1, s0.stride(0), 0, int(s0.shape[0]))
     dd, da = _native.rows_desc([t.data_ptr() for t in dsts], 1, d0.stride(0), 0, int(d0.shape[0]))
-    rc = lib.mak_rows_copy(ctypes.byref(sd), ctypes.byref(dd), None, int(s0.shape[1]), _native.ptr(si), sc,
-                           _native.ptr(di), dc, n, _native.ptr(ws), nbytes, _native.stream_ptr(dev))
+    rc = _native.rows_copy(ctypes.byref(sd), ctypes.byref(dd), int(s0.shape[1]), _native.ptr(si), sc, _native.ptr(di), dc,
+                           n, int(d0.shape[0]), dev, _native.stream_ptr(dev))
     _native.check(rc, name)
 
 

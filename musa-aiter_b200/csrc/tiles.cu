@@ -124,6 +124,34 @@ __device__ __forceinline__ bool encode_chunk_bounded(const uint4 (&toks)[G], flo
   }
 }
 
+// FP8 load of one full (R dims x G tokens) chunk through the flush-to-zero
+// decode of the MLA FP8 rows (fp8_raw_top + one flush-to-zero multiply by
+// scale * 2^(127 - bias), exact for scales in fp8_ftz_scale_ok's range): three
+// integer operations and one multiply per code instead of the field-by-field
+// decoder.  Returns false (nothing written) for other scales.
+template <typename CT, typename LT, int CODEC, int G, int R>
+__device__ __forceinline__ bool decode_chunk_ftz(const uint4 (&rows)[R], float sc, LT* out, int64_t token_pitch) {
+  if constexpr (CODEC == 0 || sizeof(CT) != 1) {
+    return false;
+  } else {
+    if (!fp8_ftz_scale_ok<CODEC>(sc)) return false;
+    const float sf = __fmul_rn(sc, fp8_ftz_bias<CODEC>());  // exact: a power of two
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+      uint4 outv;
+      LT* o = reinterpret_cast<LT*>(&outv);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const uint32_t w = reinterpret_cast<const uint32_t*>(&rows[r])[i >> 2];
+        const uint32_t x = w << (8 * (3 - (i & 3)));  // code i in the top byte
+        o[r] = from_f32<LT>(fmul_ftz(fp8_raw_top<CODEC>(x), sf));
+      }
+      *reinterpret_cast<uint4*>(out + i * token_pitch) = outv;
+    }
+    return true;
+  }
+}
+
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileLaunch p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -572,13 +600,15 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
             uint4 rows[R];
 #pragma unroll
             for (int r = 0; r < R; ++r) rows[r] = __ldg(reinterpret_cast<const uint4*>(cache_r + row0 + r * p.c_sd + col0));
+            if (!decode_chunk_ftz<CT, LT, CODEC, G, R>(rows, sc, lrow + (col0 - o_s) * p.l_st, p.l_st)) {
 #pragma unroll
-            for (int i = 0; i < G; ++i) {
-              uint4 outv;
-              LT* o = reinterpret_cast<LT*>(&outv);
+              for (int i = 0; i < G; ++i) {
+                uint4 outv;
+                LT* o = reinterpret_cast<LT*>(&outv);
 #pragma unroll
-              for (int r = 0; r < R; ++r) o[r] = C::load(reinterpret_cast<const CT*>(&rows[r])[i], sc);
-              *reinterpret_cast<uint4*>(lrow + (col0 + i - o_s) * p.l_st) = outv;
+                for (int r = 0; r < R; ++r) o[r] = C::load(reinterpret_cast<const CT*>(&rows[r])[i], sc);
+                *reinterpret_cast<uint4*>(lrow + (col0 + i - o_s) * p.l_st) = outv;
+              }
             }
           } else {
             uint4 toks[G];

@@ -415,3 +415,26 @@ def test_fp8_block_table_store_bounded_and_fallback_chunks(cuda_device, dt, fmt)
                              fp8_format=fmt)
     eq(kc, rkc, "fp8 block-table store k")
     eq(vc, rvc, "fp8 block-table store v")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", ("bfloat16", "float16", "float32"))
+def test_fp8_block_table_load_scales_inside_and_outside_fast_range(cuda_device, dt, fmt):
+    """Full-chunk FP8 loads decode through a flush-to-zero multiply when the scale lies in
+    [2^(bias-127), 2^(bias+1)) and field by field otherwise; every code byte under per-head scales
+    at, inside and outside both ends of that range must decode as the reference does."""
+    g = torch.Generator().manual_seed(23)
+    nb, nh, hd, bs = 32, 8, 64, 16
+    slots = block_table_slots([160, 96], nb, bs, g)
+    kc = torch.randint(0, 256, (nb, nh, hd, bs), generator=g, dtype=torch.int32).to(torch.uint8)
+    vc = torch.randint(0, 256, (nb, nh, hd, bs), generator=g, dtype=torch.int32).to(torch.uint8)
+    hi = 2.0**8 if fmt == "e4m3" else 2.0**16
+    lo = 2.0**-120 if fmt == "e4m3" else 2.0**-112
+    ks = torch.tensor([1.0, hi, hi * 0.999999, lo, lo * 0.5, 3.0e-3, 2.0**-126, 1.0e-30], dtype=torch.float32)
+    vs = torch.tensor(0.0371, dtype=torch.float32)
+    ok, ov = ma.kv_paged_fp8_to_linear(kc.cuda(), vc.cuda(), slots.cuda(), ks.cuda(), float(vs), out_dtype=TORCH_OF[dt],
+                                       fp8_format=fmt)
+    rk, rv = O.kv_paged_fp8_to_linear(kc.numpy(), vc.numpy(), slots.numpy(), ks.numpy(), np.float32(vs), out_dtype=dt,
+                                      fp8_format=fmt)
+    eq(ok, rk, "fp8 block-table load k")
+    eq(ov, rv, "fp8 block-table load v")

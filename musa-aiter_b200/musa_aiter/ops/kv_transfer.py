@@ -17,6 +17,7 @@ wins, as in the reference's sequential loop.
 from __future__ import annotations
 
 import ctypes
+import math
 from typing import Literal
 
 import torch
@@ -524,7 +525,16 @@ def _validate_fp8_cache_tensor(tensor: torch.Tensor, *, name: str) -> None:
 
 
 def _ensure_fp8_scale(scale, *, device: torch.device, name: str, num_heads: int, num_layers: int | None = None) -> torch.Tensor:
-    """musa_aiter/ops/kv_transfer.py:2110-2121: positive finite scalar, [NH] or [L, NH]."""
+    """musa_aiter/ops/kv_transfer.py:2110-2121: positive finite scalar, [NH] or [L, NH].
+
+    A Python number is checked on the host and placed with a fill launch: copying it from host
+    memory would synchronise the stream on every call.
+    """
+    if isinstance(scale, (int, float)) and not isinstance(scale, bool):
+        value = float(scale)
+        if not math.isfinite(value) or value <= 0.0:
+            raise ValueError(f"{name}: FP8 scale must be positive and finite")
+        return torch.full((), value, dtype=torch.float32, device=device)
     scale_tensor = torch.as_tensor(scale, dtype=torch.float32, device=device)
     if scale_tensor.device.type != "cuda" or validation_enabled():
         if not bool(torch.isfinite(scale_tensor).all()) or float(scale_tensor.min().item()) <= 0.0:

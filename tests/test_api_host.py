@@ -39,6 +39,11 @@ def test_shape_and_dtype_messages():
     with pytest.raises(ValueError, match="positive and finite"):
         ma.kv_linear_to_paged_fp8(torch.zeros(1, 2, 4), torch.zeros(1, 2, 4), torch.zeros(2, 2, 4, 4, dtype=torch.uint8),
                                   torch.zeros(2, 2, 4, 4, dtype=torch.uint8), torch.tensor([0]), 0.0, 1.0)
+    # Python numbers are checked on the host, tensors through their values
+    for bad in (float("nan"), float("inf"), -1.0, -2, torch.tensor(0.0), torch.tensor([1.0, float("nan")])):
+        with pytest.raises(ValueError, match="positive and finite"):
+            ma.kv_linear_to_paged_fp8(torch.zeros(1, 2, 4), torch.zeros(1, 2, 4), torch.zeros(2, 2, 4, 4, dtype=torch.uint8),
+                                      torch.zeros(2, 2, 4, 4, dtype=torch.uint8), torch.tensor([0]), 1.0, bad)
     with pytest.raises(ValueError, match="FP8 cache storage"):
         ma.kv_linear_to_paged_fp8(torch.zeros(1, 2, 4), torch.zeros(1, 2, 4), torch.zeros(2, 2, 4, 4),
                                   torch.zeros(2, 2, 4, 4), torch.tensor([0]), 1.0, 1.0)

@@ -230,6 +230,34 @@ MAK_API int mak_kv_linear_to_paged_fp8(const mak_linear_desc* in, const mak_page
                                int32_t slot_dtype, const float* k_scale, const float* v_scale, int32_t scale_mode,
                                int32_t fp8_format, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * The four calls above with a segment map: a device vector of uint32 that the
+ * pass over runs of 2+ consecutive slots fills with (epoch << 1) | (a
+ * single-slot run starts here), one entry per window of 8-32 tokens
+ * (ceil(T / 8) entries always suffice; a smaller map is ignored), so that the
+ * single-slot pass skips the windows without such runs instead of scanning
+ * them.  epoch in [1, 2^31) must differ from the one
+ * of any call still in flight on the same map; entries of other epochs are
+ * never trusted, so a map may start with any contents.  Results are identical
+ * to the unmapped calls.  Host-side additions, no reference counterpart.
+ */
+MAK_API int mak_kv_paged_to_linear_mapped(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
+                                          int32_t slot_dtype, int32_t fill_zero, uint32_t* seg_map,
+                                          int64_t seg_map_entries, uint32_t epoch, void* stream);
+MAK_API int mak_kv_linear_to_paged_mapped(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                                          int32_t slot_dtype, void* workspace, size_t workspace_bytes,
+                                          uint32_t* seg_map, int64_t seg_map_entries, uint32_t epoch, void* stream);
+MAK_API int mak_kv_paged_fp8_to_linear_mapped(const mak_paged_desc* cache, const mak_linear_desc* out,
+                                              const void* slots, int32_t slot_dtype, const float* k_scale,
+                                              const float* v_scale, int32_t scale_mode, int32_t fp8_format,
+                                              uint32_t* seg_map, int64_t seg_map_entries, uint32_t epoch,
+                                              void* stream);
+MAK_API int mak_kv_linear_to_paged_fp8_mapped(const mak_linear_desc* in, const mak_paged_desc* cache,
+                                              const void* slots, int32_t slot_dtype, const float* k_scale,
+                                              const float* v_scale, int32_t scale_mode, int32_t fp8_format,
+                                              void* workspace, size_t workspace_bytes, uint32_t* seg_map,
+                                              int64_t seg_map_entries, uint32_t epoch, void* stream);
+
 /* ---- row family (token-major caches) ------------------------------------ */
 
 /*

@@ -6,10 +6,11 @@
 // layer) plane, splits the window's slot mapping into segments (runs of
 // consecutive slots inside one block) with ballots, and moves each segment
 // through 16-byte chunks of the cache rows ([d][o0 .. o0 + G)), transposing
-// in registers.  Long segments (>= G tokens: block-table traffic) and short
-// ones (random slots, run ends) are handled by two instantiations launched
-// back to back, so the short, latency-bound path runs at high occupancy while
-// the long path keeps the registers its transposes need.
+// in registers.  Runs of two or more tokens (block-table traffic and its
+// ragged ends) and single tokens (random slots) are handled by two
+// instantiations launched back to back, so the single-token, latency-bound
+// path runs at high occupancy while the run path keeps the registers its
+// transposes need.
 //
 // Fallback (tile_kernel): any head_dim / block_size / alignment, through a
 // shared-memory transpose of 32-token chunks.
@@ -41,6 +42,14 @@ struct TileLaunch {
   int32_t slots64, n_kv, fill_zero, cache_vec, lin_vec, scale_mode, heads_per_step;
   int32_t window;       // tokens per warp window of the segment kernel (8, 16 or 32)
   int32_t plane_group;  // (kv, layer) planes a segment-kernel block walks per window
+  // Segment map (optional): the run launch (MODE 1) stores, per window of map_window tokens,
+  // (epoch << 1) | (a single-token run starts in it); the single-token launch (MODE 2) skips
+  // the windows whose entries read (epoch << 1).  Entries of another epoch are never trusted.
+  uint32_t* seg_map;
+  uint32_t seg_epoch;
+  int32_t map_window;       // tokens per map entry (the run launch's window: 8, 16 or 32)
+  int32_t map_shift;        // log2(map_window)
+  int64_t seg_map_entries;  // host side: capacity of seg_map
 };
 
 // Four consecutive linear elements as one aligned vector.
@@ -341,12 +350,17 @@ __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileL
 //            write, so concurrent segments of one block never race).
 // No shared memory, no block barriers; FP8 codecs run in registers.
 // ---------------------------------------------------------------------------
-// MODE 1 handles segments of at least G tokens (plus zero rows), MODE 2 the shorter ones;
+// MODE 1 handles segments of at least kRunMin tokens (plus zero rows), MODE 2 the single tokens;
 // the two are launched back to back so each keeps the register budget its path needs.
 template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE, bool GROUPED>
 __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg_kernel(const __grid_constant__ TileLaunch p) {
   constexpr int G = 16 / sizeof(CT);
   constexpr int R = 16 / sizeof(LT);
+  // Runs of this many tokens or more take the 16-byte chunk path (MODE 1).  A gather reads
+  // whole chunks, so even a ragged end of 2..G-1 tokens costs one round trip per item, where
+  // the element path would walk its tokens one after another; a scatter must not write the
+  // chunk's other slots, so its runs shorter than a chunk stay on the element path.
+  constexpr int kRunMin = SCATTER ? G : 2;
   using C = Codec<CT, LT, CODEC>;
   const int lane = threadIdx.x & 31;
   const int upr = static_cast<int>(p.head_dim) / R;
@@ -372,6 +386,16 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
 
   for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < windows; w += wstride) {
     const int64_t t0 = w * W;
+    if (MODE == 2 && p.seg_map != nullptr) {
+      // Skip the window when the run launch of this call found no single-token run starting in
+      // any of its map windows that cover [t0, t0 + W) (at most 32 / 8 = 4 of them).
+      const int64_t m0 = t0 >> p.map_shift;
+      const int64_t m1 = (min(t0 + W, p.n_tokens) - 1) >> p.map_shift;
+      const uint32_t clean = p.seg_epoch << 1;
+      uint32_t v = clean;
+      if (lane <= m1 - m0) v = p.seg_map[m0 + lane];
+      if (__all_sync(0xffffffffu, v == clean)) continue;
+    }
     // Slots of tokens t0 + lane (A) and t0 + 32 + lane (B), as (block element offset, in-block offset).
     int64_t offA = -1, offB = -1, sA = -1, sB = -1, oA = 0, oB = 0;
     {
@@ -401,6 +425,19 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
                            (static_cast<uint64_t>(__ballot_sync(0xffffffffu, startB)) << 32) |
                            ~(static_cast<uint64_t>(__ballot_sync(0xffffffffu, sA >= 0)) |
                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, sB >= 0)) << 32));
+    if (MODE == 1 && p.seg_map != nullptr && blockIdx.y == 0) {
+      // Does a single-token run start in this window?  A run's length is bounded by the
+      // next boundary in the 64 loaded slots; 64 - lane > 32, so a run that reaches past
+      // them is long whatever follows, and the single-token launch classifies alike.
+      bool single = false;
+      if (lane < W && ((mStartA >> lane) & 1u)) {
+        const uint64_t rest = bound >> (lane + 1);
+        const int len = rest ? __ffsll(static_cast<long long>(rest)) : (64 - lane);
+        single = len < kRunMin;
+      }
+      const uint32_t anySingle = __ballot_sync(0xffffffffu, single) != 0u ? 1u : 0u;
+      if (lane == 0) p.seg_map[w] = (p.seg_epoch << 1) | anySingle;
+    }
     // The window's segments are the same for every plane: skip the planes when
     // none is this launch's kind (and, in MODE 1, no zero rows are due).
     if (GROUPED) {
@@ -409,7 +446,7 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
         const int q = __ffs(m) - 1;
         const uint64_t rest = bound >> (q + 1);
         const int len = rest ? (__ffsll(static_cast<long long>(rest))) : (64 - q);
-        work = (MODE == 1) == (len >= G);
+        work = (MODE == 1) == (len >= kRunMin);
       }
       if (!work) continue;
     }
@@ -446,9 +483,9 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
       const int o_s = static_cast<int>(__shfl_sync(0xffffffffu, oA, q));
       const int64_t ts = t0 + q;
       const int64_t cbase = soff - o_s;  // block start (element offset)
-      if ((MODE == 1) != (len >= G)) continue;
-      if (len < G) {
-        // Short segment (random slots, run ends): one element per item, head_dim fastest
+      if ((MODE == 1) != (len >= kRunMin)) continue;
+      if (len < kRunMin) {
+        // Single-token segment (random slots): one element per item, head_dim fastest
         // across lanes, so a warp instruction touches consecutive cache rows (whole
         // sectors per instruction) and a contiguous piece of the token row; four items
         // per lane in flight.
@@ -625,23 +662,30 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
               }
             }
           }
+        } else if (!SCATTER) {
+          // partially covered chunk, gather: the whole 16-byte chunk of each cache row is read
+          // (its other slots lie in the same block row), only the covered tokens are written
+          uint4 rows[R];
+#pragma unroll
+          for (int r = 0; r < R; ++r) rows[r] = __ldg(reinterpret_cast<const uint4*>(cache_r + row0 + r * p.c_sd + col0));
+#pragma unroll
+          for (int i = 0; i < G; ++i) {
+            if (col0 + i < lo || col0 + i >= hi) continue;
+            uint4 outv;
+            LT* o = reinterpret_cast<LT*>(&outv);
+#pragma unroll
+            for (int r = 0; r < R; ++r) o[r] = C::load(reinterpret_cast<const CT*>(&rows[r])[i], sc);
+            *reinterpret_cast<uint4*>(lrow + (col0 + i - o_s) * p.l_st) = outv;
+          }
         } else {
-          // partially covered chunk: element accesses on the cache side, 16-byte token rows
+          // partially covered chunk, scatter: element stores on the cache side (the chunk's
+          // other slots belong to other tokens), 16-byte token rows
 #pragma unroll 1
           for (int col = lo; col < hi; ++col) {
-            LT* trow = lrow + (col - o_s) * p.l_st;
-            if (!SCATTER) {
-              uint4 outv;
-              LT* o = reinterpret_cast<LT*>(&outv);
+            const uint4 tv = __ldg(reinterpret_cast<const uint4*>(lrow + (col - o_s) * p.l_st));
+            const LT* x = reinterpret_cast<const LT*>(&tv);
 #pragma unroll
-              for (int r = 0; r < R; ++r) o[r] = C::load(cache_r[row0 + r * p.c_sd + col], sc);
-              *reinterpret_cast<uint4*>(trow) = outv;
-            } else {
-              const uint4 tv = __ldg(reinterpret_cast<const uint4*>(trow));
-              const LT* x = reinterpret_cast<const LT*>(&tv);
-#pragma unroll
-              for (int r = 0; r < R; ++r) cache_w[row0 + r * p.c_sd + col] = C::store(x[r], sc);
-            }
+            for (int r = 0; r < R; ++r) cache_w[row0 + r * p.c_sd + col] = C::store(x[r], sc);
           }
         }
       }
@@ -667,6 +711,13 @@ static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
   p.window = 32;
   while (p.window > 8 && (p.n_tokens + p.window - 1) / p.window * planes < 4 * resident_warps) p.window /= 2;
   const int64_t windows = (p.n_tokens + p.window - 1) / p.window;
+  if (MODE == 1 && p.seg_map != nullptr) {
+    if (windows > p.seg_map_entries) p.seg_map = nullptr;  // too small: the single-token launch scans every window
+    else {
+      p.map_window = p.window;
+      p.map_shift = p.window == 32 ? 5 : (p.window == 16 ? 4 : 3);
+    }
+  }
   // Planes per block: a window's slot scan serves all planes of its group, so
   // group as many planes (up to 8) as still leave every resident warp a few
   // (window, group) items.
@@ -728,6 +779,9 @@ struct TileCall {
   int32_t scale_mode;
   int32_t fp8_format;  // 0 = plain copy
   bool scatter;
+  uint32_t* seg_map;  // optional segment map (see TileLaunch)
+  int64_t seg_map_entries;
+  uint32_t seg_epoch;
 };
 
 static int run_tile(const TileCall& c, cudaStream_t st, const char* name) {
@@ -782,6 +836,14 @@ static int run_tile(const TileCall& c, cudaStream_t st, const char* name) {
   p.n_kv = n_kv;
   p.fill_zero = c.fill_zero ? 1 : 0;
   p.scale_mode = c.scale_mode;
+  if (c.seg_map != nullptr) {
+    if (c.seg_epoch == 0 || c.seg_epoch >= (1u << 31) || c.seg_map_entries < 0)
+      return fail(MAK_E_INVALID, "%s: segment map epoch must be in [1, 2^31) and its size non-negative", name);
+    if ((reinterpret_cast<uintptr_t>(c.seg_map) & 3u) != 0) return fail(MAK_E_INVALID, "%s: misaligned segment map", name);
+    p.seg_map = c.seg_map;
+    p.seg_map_entries = c.seg_map_entries;
+    p.seg_epoch = c.seg_epoch;
+  }
   // 16-byte cache vectors need every cache address of a packed group aligned.
   const int G = 16 / ce;
   const uint64_t cbits = static_cast<uint64_t>(p.c_sl | p.c_sb | p.c_sh | p.c_sd) * ce;
@@ -834,28 +896,54 @@ extern "C" {
 
 int mak_kv_paged_to_linear(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
                            int32_t slot_dtype, int32_t fill_zero, void* stream) {
+  return mak_kv_paged_to_linear_mapped(cache, out, slots, slot_dtype, fill_zero, nullptr, 0, 0, stream);
+}
+
+int mak_kv_paged_to_linear_mapped(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
+                                  int32_t slot_dtype, int32_t fill_zero, uint32_t* seg_map, int64_t seg_map_entries,
+                                  uint32_t epoch, void* stream) {
   TileCall c{};
   c.cache = cache;
   c.lin = out;
   c.slots = slots;
   c.slot_dtype = slot_dtype;
   c.fill_zero = fill_zero;
+  c.seg_map = seg_map;
+  c.seg_map_entries = seg_map_entries;
+  c.seg_epoch = epoch;
   return run_tile(c, as_stream(stream), "mak_kv_paged_to_linear");
 }
 
 int mak_kv_linear_to_paged(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
                            int32_t slot_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  return mak_kv_linear_to_paged_mapped(in, cache, slots, slot_dtype, workspace, workspace_bytes, nullptr, 0, 0, stream);
+}
+
+int mak_kv_linear_to_paged_mapped(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                                  int32_t slot_dtype, void* workspace, size_t workspace_bytes, uint32_t* seg_map,
+                                  int64_t seg_map_entries, uint32_t epoch, void* stream) {
   TileCall c{};
   c.cache = cache;
   c.lin = in;
   c.slots = slots;
   c.slot_dtype = slot_dtype;
+  c.seg_map = seg_map;
+  c.seg_map_entries = seg_map_entries;
+  c.seg_epoch = epoch;
   return tile_scatter(c, workspace, workspace_bytes, as_stream(stream), "mak_kv_linear_to_paged");
 }
 
 int mak_kv_paged_fp8_to_linear(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
                                int32_t slot_dtype, const float* k_scale, const float* v_scale, int32_t scale_mode,
                                int32_t fp8_format, void* stream) {
+  return mak_kv_paged_fp8_to_linear_mapped(cache, out, slots, slot_dtype, k_scale, v_scale, scale_mode, fp8_format,
+                                           nullptr, 0, 0, stream);
+}
+
+int mak_kv_paged_fp8_to_linear_mapped(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
+                                      int32_t slot_dtype, const float* k_scale, const float* v_scale,
+                                      int32_t scale_mode, int32_t fp8_format, uint32_t* seg_map,
+                                      int64_t seg_map_entries, uint32_t epoch, void* stream) {
   if (fp8_format != MAK_FP8_E4M3 && fp8_format != MAK_FP8_E5M2)
     return fail(MAK_E_INVALID, "mak_kv_paged_fp8_to_linear: unknown FP8 format %d", fp8_format);
   TileCall c{};
@@ -868,12 +956,24 @@ int mak_kv_paged_fp8_to_linear(const mak_paged_desc* cache, const mak_linear_des
   c.v_scale = v_scale;
   c.scale_mode = scale_mode;
   c.fp8_format = fp8_format;
+  c.seg_map = seg_map;
+  c.seg_map_entries = seg_map_entries;
+  c.seg_epoch = epoch;
   return run_tile(c, as_stream(stream), "mak_kv_paged_fp8_to_linear");
 }
 
 int mak_kv_linear_to_paged_fp8(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
                                int32_t slot_dtype, const float* k_scale, const float* v_scale, int32_t scale_mode,
                                int32_t fp8_format, void* workspace, size_t workspace_bytes, void* stream) {
+  return mak_kv_linear_to_paged_fp8_mapped(in, cache, slots, slot_dtype, k_scale, v_scale, scale_mode, fp8_format,
+                                           workspace, workspace_bytes, nullptr, 0, 0, stream);
+}
+
+int mak_kv_linear_to_paged_fp8_mapped(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                                      int32_t slot_dtype, const float* k_scale, const float* v_scale,
+                                      int32_t scale_mode, int32_t fp8_format, void* workspace,
+                                      size_t workspace_bytes, uint32_t* seg_map, int64_t seg_map_entries,
+                                      uint32_t epoch, void* stream) {
   if (fp8_format != MAK_FP8_E4M3 && fp8_format != MAK_FP8_E5M2)
     return fail(MAK_E_INVALID, "mak_kv_linear_to_paged_fp8: unknown FP8 format %d", fp8_format);
   TileCall c{};
@@ -885,6 +985,9 @@ int mak_kv_linear_to_paged_fp8(const mak_linear_desc* in, const mak_paged_desc* 
   c.v_scale = v_scale;
   c.scale_mode = scale_mode;
   c.fp8_format = fp8_format;
+  c.seg_map = seg_map;
+  c.seg_map_entries = seg_map_entries;
+  c.seg_epoch = epoch;
   return tile_scatter(c, workspace, workspace_bytes, as_stream(stream), "mak_kv_linear_to_paged_fp8");
 }
 

@@ -150,6 +150,26 @@ _PROTOTYPES = {
             c_void_p,
         ],
     ),
+    "mak_kv_paged_to_linear_mapped": (
+        c_int32,
+        [POINTER(PagedDesc), POINTER(LinearDesc), c_void_p, c_int32, c_int32, c_void_p, c_int64, ctypes.c_uint32,
+         c_void_p],
+    ),
+    "mak_kv_linear_to_paged_mapped": (
+        c_int32,
+        [POINTER(LinearDesc), POINTER(PagedDesc), c_void_p, c_int32, c_void_p, c_size_t, c_void_p, c_int64,
+         ctypes.c_uint32, c_void_p],
+    ),
+    "mak_kv_paged_fp8_to_linear_mapped": (
+        c_int32,
+        [POINTER(PagedDesc), POINTER(LinearDesc), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p,
+         c_int64, ctypes.c_uint32, c_void_p],
+    ),
+    "mak_kv_linear_to_paged_fp8_mapped": (
+        c_int32,
+        [POINTER(LinearDesc), POINTER(PagedDesc), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p,
+         c_size_t, c_void_p, c_int64, ctypes.c_uint32, c_void_p],
+    ),
     "mak_rows_gather": (
         c_int32,
         [c_void_p, c_void_p, POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int32, c_void_p],
@@ -357,6 +377,38 @@ def owned_scatter(device: torch.device, stream: int, rows: int, n: int, launch):
             epoch = 1
         ent[3] = epoch + 1
         return launch(ent[2], ent[1], epoch)
+
+
+# Segment maps for the tile engine's long-run / short-run launch pair
+# (mak_kv_*_mapped): one uint32 vector per (device, stream), one entry per 8
+# tokens of the largest call seen, and the next epoch.  Every entry the short-run
+# launch reads was written by the long-run launch of the same call, so the
+# contents never need clearing, and a wrapped epoch may start again at 1.
+_SEGMAPS: dict = {}
+_SEG_EPOCH_MAX = (1 << 31) - 1
+_SEGMAP_MAX_ENTRIES = 1 << 28
+
+
+def seg_map(device: torch.device, stream: int, n_tokens: int) -> tuple[int | None, int, int]:
+    """(map address, entries, epoch) for one tile call of ``n_tokens`` tokens on this stream, or
+    (None, 0, 0) where the short-run launch scans every window instead (stream capture: replays
+    of a captured epoch could meet on one map; very large calls)."""
+    need = (int(n_tokens) + 7) // 8
+    if need <= 0 or need > _SEGMAP_MAX_ENTRIES or torch.cuda.is_current_stream_capturing():
+        return None, 0, 0
+    key = (device.index, stream)
+    with _OWNER_LOCK:
+        ent = _SEGMAPS.get(key)
+        if ent is None or ent[1] < need:
+            cap = max(need, 2 * ent[1]) if ent is not None else max(need, 1 << 12)
+            cap = min(cap, _SEGMAP_MAX_ENTRIES)
+            t = torch.zeros(cap, dtype=torch.int32, device=device)
+            ent = _SEGMAPS[key] = [t, cap, t.data_ptr(), 1]
+        epoch = ent[3]
+        if epoch > _SEG_EPOCH_MAX:
+            epoch = 1
+        ent[3] = epoch + 1
+        return ent[2], ent[1], epoch
 
 
 def rows_copy(src_desc, dst_desc, row_bytes0: int, si: int, sdt: int, di: int, ddt: int, n: int, dst_rows: int,

@@ -166,14 +166,17 @@ def _tile_gather(kc, vc, slots, ok, ov, *, layered: bool, fill_zero: bool, op: s
     for c0, c1, l0, l1, which in groups:
         pd = paged_desc(c0, c1, layered=layered)
         ld = linear_desc(l0, l1, layered=layered)
+        smap, sents, sepoch = _native.seg_map(dev, stream, ks.numel())
         if fp8 is None:
-            rc = lib.mak_kv_paged_to_linear(ctypes.byref(pd), ctypes.byref(ld), _native.ptr(ks), code, int(fill_zero), stream)
+            rc = lib.mak_kv_paged_to_linear_mapped(ctypes.byref(pd), ctypes.byref(ld), _native.ptr(ks), code,
+                                                   int(fill_zero), smap, sents, sepoch, stream)
         else:
             k_s, v_s, mode, fmt = fp8
             s0 = k_s if which == 0 else v_s
             s1 = v_s if c1 is not None else None
-            rc = lib.mak_kv_paged_fp8_to_linear(
-                ctypes.byref(pd), ctypes.byref(ld), _native.ptr(ks), code, _native.ptr(s0), _native.ptr(s1), mode, fmt, stream
+            rc = lib.mak_kv_paged_fp8_to_linear_mapped(
+                ctypes.byref(pd), ctypes.byref(ld), _native.ptr(ks), code, _native.ptr(s0), _native.ptr(s1), mode, fmt,
+                smap, sents, sepoch, stream,
             )
         _native.check(rc, op)
     if ok_tmp:
@@ -200,17 +203,19 @@ def _tile_scatter(kl, vl, kc, vc, slots, *, layered: bool, op: str, fp8: tuple |
     for l0, l1, c0, c1, which in groups:
         pd = paged_desc(c0, c1, layered=layered)
         ld = linear_desc(l0, l1, layered=layered)
+        smap, sents, sepoch = _native.seg_map(dev, stream, ks.numel())
         if fp8 is None:
-            rc = lib.mak_kv_linear_to_paged(
-                ctypes.byref(ld), ctypes.byref(pd), _native.ptr(ks), code, _native.ptr(ws), nbytes, stream
+            rc = lib.mak_kv_linear_to_paged_mapped(
+                ctypes.byref(ld), ctypes.byref(pd), _native.ptr(ks), code, _native.ptr(ws), nbytes, smap, sents, sepoch,
+                stream,
             )
         else:
             k_s, v_s, mode, fmt = fp8
             s0 = k_s if which == 0 else v_s
             s1 = v_s if c1 is not None else None
-            rc = lib.mak_kv_linear_to_paged_fp8(
+            rc = lib.mak_kv_linear_to_paged_fp8_mapped(
                 ctypes.byref(ld), ctypes.byref(pd), _native.ptr(ks), code, _native.ptr(s0), _native.ptr(s1), mode, fmt,
-                _native.ptr(ws), nbytes, stream,
+                _native.ptr(ws), nbytes, smap, sents, sepoch, stream,
             )
         _native.check(rc, op)
     if kc_tmp:

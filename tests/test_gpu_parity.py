@@ -438,3 +438,91 @@ def test_fp8_block_table_load_scales_inside_and_outside_fast_range(cuda_device, 
                                       fp8_format=fmt)
     eq(ok, rk, "fp8 block-table load k")
     eq(ov, rv, "fp8 block-table load v")
+
+
+def _mixed_run_slots(n_target, nb, bs, gen) -> torch.Tensor:
+    """Unique slots in runs of every kind the two tile launches split between them: whole
+    blocks, runs of 1-15 slots from a random in-block offset, lone random slots and negatives."""
+    perm = torch.randperm(nb, generator=gen).tolist()
+    kinds = torch.randint(0, 4, (n_target,), generator=gen).tolist()
+    lens = torch.randint(1, bs, (n_target,), generator=gen).tolist()
+    offs = torch.randint(0, bs, (n_target,), generator=gen).tolist()
+    out, n, i = [], 0, 0
+    while n < n_target:
+        k, b = kinds[i], perm[i]
+        if k == 0:
+            piece = [b * bs + o for o in range(bs)]
+        elif k == 1:
+            o0 = min(offs[i], bs - lens[i])
+            piece = [b * bs + o0 + o for o in range(lens[i])]
+        elif k == 2:
+            piece = [b * bs + offs[i]]
+        else:
+            piece = [-1] * (1 + offs[i] % 3)
+        out.extend(piece)
+        n += len(piece)
+        i += 1
+    return torch.tensor(out[:n_target], dtype=torch.int64)
+
+
+@pytest.mark.parametrize("fp8", (False, True))
+def test_tile_segment_map_skips_only_clean_windows(cuda_device, monkeypatch, fp8):
+    """The short-run launch skips the windows that the long-run launch of the same call marked
+    free of short runs: results equal the unmapped launches' and the oracle's for calls whose
+    window sizes differ between the two launches (8 to 32 tokens), also when the map already
+    holds this call's epoch marked clean everywhere (the long-run launch rewrites every entry)."""
+    from musa_aiter import _native
+
+    g = torch.Generator().manual_seed(11)
+    nb, nh, hd, bs = 32768, 1, 16, 16
+    ks, vs = torch.tensor(0.013), torch.tensor(0.021)
+    for t in (600, 40000, 170000):
+        slots = _mixed_run_slots(t, nb, bs, g)
+        if fp8:
+            kc = torch.randint(0, 256, (nb, nh, hd, bs), generator=g, dtype=torch.uint8)
+            vc = torch.randint(0, 256, (nb, nh, hd, bs), generator=g, dtype=torch.uint8)
+            kc[(kc & 0x7F) == 0x7F] = 0  # e4m3 nan codes decode to nan: keep the comparison bitwise
+            vc[(vc & 0x7F) == 0x7F] = 0
+            load = lambda: ma.kv_paged_fp8_to_linear(kc.cuda(), vc.cuda(), slots.cuda(), ks.cuda(), vs.cuda())  # noqa: E731
+            rk, rv = O.kv_paged_fp8_to_linear(kc.numpy(), vc.numpy(), slots.numpy(), ks.numpy(), vs.numpy())
+        else:
+            kc = torch.randn((nb, nh, hd, bs), generator=g).to(torch.bfloat16)
+            vc = torch.randn((nb, nh, hd, bs), generator=g).to(torch.bfloat16)
+            load = lambda: ma.kv_paged_to_linear(kc.cuda(), vc.cuda(), slots.cuda())  # noqa: E731
+            rk, rv = O.kv_paged_to_linear(to_np(kc), to_np(vc), slots.numpy())
+        kl = (torch.randn((t, nh, hd), generator=g) * 3.0).to(torch.bfloat16)
+        vl = (torch.randn((t, nh, hd), generator=g) * 3.0).to(torch.bfloat16)
+
+        def store():
+            kd = torch.zeros((nb, nh, hd, bs), dtype=torch.uint8 if fp8 else torch.bfloat16, device="cuda")
+            vd = torch.zeros_like(kd)
+            if fp8:
+                ma.kv_linear_to_paged_fp8(kl.cuda(), vl.cuda(), kd, vd, slots.cuda(), ks.cuda(), vs.cuda())
+            else:
+                ma.kv_linear_to_paged(kl.cuda(), vl.cuda(), kd, vd, slots.cuda())
+            return kd, vd
+
+        # this stream's map, pre-set to "clean" for the epoch the next call takes
+        dev = torch.device("cuda", torch.cuda.current_device())
+        _native.seg_map(dev, _native.stream_ptr(dev), t)
+        ent = _native._SEGMAPS[(dev.index, _native.stream_ptr(dev))]
+        ent[0].fill_(ent[3] << 1)
+        mk, mv = load()
+        ent[0].fill_(ent[3] << 1)
+        sk, sv = store()
+        eq(mk, rk, f"mapped load k t={t}")
+        eq(mv, rv, f"mapped load v t={t}")
+        with monkeypatch.context() as m:
+            m.setattr(_native, "seg_map", lambda *a: (None, 0, 0))
+            uk, uv = load()
+            usk, usv = store()
+        assert torch.equal(mk.view(torch.int16), uk.view(torch.int16)) and torch.equal(mv.view(torch.int16), uv.view(torch.int16))
+        assert torch.equal(sk.view(torch.uint8), usk.view(torch.uint8)) and torch.equal(sv.view(torch.uint8), usv.view(torch.uint8))
+        if fp8:
+            rkc, rvc = np.zeros(sk.shape, np.uint8), np.zeros(sv.shape, np.uint8)
+            O.kv_linear_to_paged_fp8(to_np(kl), to_np(vl), rkc, rvc, slots.numpy(), ks.numpy(), vs.numpy())
+        else:
+            rkc, rvc = np.zeros(sk.shape, to_np(kl).dtype), np.zeros(sv.shape, to_np(vl).dtype)
+            O.kv_linear_to_paged(to_np(kl), to_np(vl), rkc, rvc, slots.numpy())
+        eq(sk, rkc, f"mapped store k t={t}")
+        eq(sv, rvc, f"mapped store v t={t}")

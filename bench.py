@@ -63,6 +63,8 @@ def parse_args():
                     help="cfg2 (default) is the headline; the others measure the remaining configs, "
                          "'ops' times each remaining kvcache op once")
     ap.add_argument("--tokens", type=int, default=8192, help="cfg3 batch tokens (256 decode / 8192 prefill)")
+    ap.add_argument("--ops", default=None,
+                    help="--workload ops: comma-separated name fragments; only the matching ops run (profiling one op)")
     return ap.parse_args()
 
 
@@ -763,11 +765,15 @@ def run_ops_sweep(args) -> None:
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(0)
     peak, kind = load_peak()
-    L, NB, NH, HD, BS = 32, 4096, 8, 128, 16
+    L, NB, NH, HD, BS = args.layers, 4096, 8, 128, 16  # --layers (default 32) shrinks the caches for profiling
     T = 16384
     res = {}
 
+    only = [f for f in (args.ops or "").split(",") if f]
+
     def timed(name, bytes_, fn, pcie=False, note=""):
+        if only and not any(f in name for f in only):
+            return
         for _ in range(max(1, args.warmup)):
             fn()
         torch.cuda.synchronize(dev)

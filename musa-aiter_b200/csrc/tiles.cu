@@ -50,6 +50,7 @@ struct TileLaunch {
   int32_t map_window;       // tokens per map entry (the run launch's window: 8, 16 or 32)
   int32_t map_shift;        // log2(map_window)
   int64_t seg_map_entries;  // host side: capacity of seg_map
+  int64_t windows;          // ceil(n_tokens / window), set per launch
 };
 
 // Four consecutive linear elements as one aligned vector.
@@ -370,16 +371,18 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
   const int planes = static_cast<int>(p.num_layers) * p.n_kv;
   const int plane_lo = GROUPED ? static_cast<int>(blockIdx.y) * p.plane_group : static_cast<int>(blockIdx.y);
   const int plane_hi = GROUPED ? min(plane_lo + p.plane_group, planes) : plane_lo + 1;
-  // plane variables (set here for the first plane; a grouped block resets them per plane)
-  int64_t l = plane_lo % p.num_layers;
-  int kv = plane_lo / static_cast<int>(p.num_layers);
+  // plane variables (set here for the first plane; a grouped block resets them per plane);
+  // planes <= 65535, so 32-bit division
+  const int nl = static_cast<int>(p.num_layers);
+  int64_t l = plane_lo % nl;
+  int kv = plane_lo / nl;
   const CT* cache_r = reinterpret_cast<const CT*>(p.cache[kv]) + l * p.c_sl;
   CT* cache_w = reinterpret_cast<CT*>(p.cache[kv]) + l * p.c_sl;
   LT* lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl;
   const float* scl = CODEC ? p.scale[kv] : nullptr;
   const int W = p.window;
   const uint32_t wmask = W >= 32 ? 0xffffffffu : ((1u << W) - 1u);
-  const int64_t windows = (p.n_tokens + W - 1) / W;
+  const int64_t windows = p.windows;
   const int64_t wstride = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   pdl_wait();
   pdl_trigger();
@@ -452,8 +455,8 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
     }
     for (int plane = plane_lo; plane < plane_hi; ++plane) {
     if (GROUPED) {
-      l = plane % p.num_layers;
-      kv = plane / static_cast<int>(p.num_layers);
+      l = plane % nl;
+      kv = plane / nl;
       cache_r = reinterpret_cast<const CT*>(p.cache[kv]) + l * p.c_sl;
       cache_w = reinterpret_cast<CT*>(p.cache[kv]) + l * p.c_sl;
       lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl;
@@ -711,6 +714,7 @@ static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
   p.window = 32;
   while (p.window > 8 && (p.n_tokens + p.window - 1) / p.window * planes < 4 * resident_warps) p.window /= 2;
   const int64_t windows = (p.n_tokens + p.window - 1) / p.window;
+  p.windows = windows;
   if (MODE == 1 && p.seg_map != nullptr) {
     if (windows > p.seg_map_entries) p.seg_map = nullptr;  // too small: the single-token launch scans every window
     else {

@@ -258,6 +258,24 @@ MAK_API int mak_kv_linear_to_paged_fp8_mapped(const mak_linear_desc* in, const m
                                               void* workspace, size_t workspace_bytes, uint32_t* seg_map,
                                               int64_t seg_map_entries, uint32_t epoch, void* stream);
 
+/*
+ * The two tile scatters with the owner-table last-writer resolution of
+ * mak_rows_scatterv_owned (owner_rows >= num_blocks * block_size; same table,
+ * epoch and zeroing rules) instead of a workspace, plus the optional segment
+ * map of the *_mapped calls (seg_map may be NULL).  Results are identical to
+ * mak_kv_linear_to_paged / mak_kv_linear_to_paged_fp8.  Host-side additions,
+ * no reference counterpart.
+ */
+MAK_API int mak_kv_linear_to_paged_owned(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                                         int32_t slot_dtype, uint64_t* owner, int64_t owner_rows, uint32_t epoch,
+                                         uint32_t* seg_map, int64_t seg_map_entries, uint32_t seg_epoch,
+                                         void* stream);
+MAK_API int mak_kv_linear_to_paged_fp8_owned(const mak_linear_desc* in, const mak_paged_desc* cache,
+                                             const void* slots, int32_t slot_dtype, const float* k_scale,
+                                             const float* v_scale, int32_t scale_mode, int32_t fp8_format,
+                                             uint64_t* owner, int64_t owner_rows, uint32_t epoch, uint32_t* seg_map,
+                                             int64_t seg_map_entries, uint32_t seg_epoch, void* stream);
+
 /* ---- row family (token-major caches) ------------------------------------ */
 
 /*

@@ -51,7 +51,23 @@ struct TileLaunch {
   int32_t map_shift;        // log2(map_window)
   int64_t seg_map_entries;  // host side: capacity of seg_map
   int64_t windows;          // ceil(n_tokens / window), set per launch
+  // Owned scatter (optional): owner[slot] holds (epoch << 32) | last token writing the slot,
+  // marked by owner_mark_kernel just before; a token whose entry names another token is skipped.
+  const unsigned long long* owner;
+  unsigned long long tag_hi;
 };
+
+// Slot of token t; -1 when it lies past the cache or, in an owned scatter, when a later token
+// writes the same slot (negative slots are returned as they are: skipped by the callers).
+template <bool SCATTER>
+__device__ __forceinline__ int64_t token_slot(const TileLaunch& p, int64_t t) {
+  const int64_t s = load_index(p.slots, p.slots64, t);
+  if (s >= p.num_slots) return -1;
+  if (SCATTER && s >= 0 && p.owner != nullptr &&
+      __ldcg(p.owner + s) != (p.tag_hi | static_cast<unsigned long long>(t)))
+    return -1;
+  return s;
+}
 
 // Four consecutive linear elements as one aligned vector.
 template <typename LT>
@@ -191,8 +207,8 @@ __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileL
     if (tid < kTT) {
       int64_t off = -1;
       if (tid < cnt) {
-        const int64_t s = load_index(p.slots, p.slots64, t0 + tid);
-        if (s >= 0 && s < p.num_slots) {
+        const int64_t s = token_slot<SCATTER>(p, t0 + tid);
+        if (s >= 0) {
           int64_t b, o;
           split_slot(s, p.block_size, &b, &o);
           off = b * p.c_sb + o;
@@ -403,18 +419,15 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
     int64_t offA = -1, offB = -1, sA = -1, sB = -1, oA = 0, oB = 0;
     {
       const int64_t ta = t0 + lane, tb = t0 + 32 + lane;
-      if (ta < p.n_tokens) sA = load_index(p.slots, p.slots64, ta);
-      if (tb < p.n_tokens) sB = load_index(p.slots, p.slots64, tb);
-      if (sA >= p.num_slots) sA = -1;
-      if (sB >= p.num_slots) sB = -1;
+      if (ta < p.n_tokens) sA = token_slot<SCATTER>(p, ta);
+      if (tb < p.n_tokens) sB = token_slot<SCATTER>(p, tb);
       int64_t b;
       if (sA >= 0) { split_slot(sA, p.block_size, &b, &oA); offA = b * p.c_sb + oA; }
       if (sB >= 0) { split_slot(sB, p.block_size, &b, &oB); offB = b * p.c_sb + oB; }
     }
     int64_t sPrev = -1;  // slot of token t0 - 1 (for lane 0)
     if (lane == 0 && t0 > 0) {
-      sPrev = load_index(p.slots, p.slots64, t0 - 1);
-      if (sPrev >= p.num_slots) sPrev = -1;
+      sPrev = token_slot<SCATTER>(p, t0 - 1);
     }
     const int64_t upA = __shfl_up_sync(0xffffffffu, sA, 1);
     const int64_t lastA = __shfl_sync(0xffffffffu, sA, 31);
@@ -786,6 +799,8 @@ struct TileCall {
   uint32_t* seg_map;  // optional segment map (see TileLaunch)
   int64_t seg_map_entries;
   uint32_t seg_epoch;
+  const uint64_t* owner;  // owned scatter: marked owner table (see TileLaunch)
+  uint32_t owner_epoch;
 };
 
 static int run_tile(const TileCall& c, cudaStream_t st, const char* name) {
@@ -848,6 +863,10 @@ static int run_tile(const TileCall& c, cudaStream_t st, const char* name) {
     p.seg_map_entries = c.seg_map_entries;
     p.seg_epoch = c.seg_epoch;
   }
+  if (c.owner != nullptr) {
+    p.owner = reinterpret_cast<const unsigned long long*>(c.owner);
+    p.tag_hi = static_cast<unsigned long long>(c.owner_epoch) << 32;
+  }
   // 16-byte cache vectors need every cache address of a packed group aligned.
   const int G = 16 / ce;
   const uint64_t cbits = static_cast<uint64_t>(p.c_sl | p.c_sb | p.c_sh | p.c_sd) * ce;
@@ -888,6 +907,25 @@ static int tile_scatter(TileCall c, void* workspace, size_t ws_bytes, cudaStream
   if (rc) return rc;
   c.slots = ws.eff;
   c.slot_dtype = MAK_DT_I64;
+  c.scatter = true;
+  return run_tile(c, st, name);
+}
+
+// Owned scatter: one marking launch (atomicMax of (epoch << 32) | token per slot) replaces the
+// workspace's clear / insert / resolve launches; the tile kernels skip tokens that lost.
+static int tile_scatter_owned(TileCall c, uint64_t* owner, int64_t owner_rows, uint32_t epoch, cudaStream_t st,
+                              const char* name) {
+  if (!c.lin || c.lin->num_tokens <= 0) return MAK_OK;
+  if (!c.cache) return fail(MAK_E_INVALID, "%s: NULL descriptor", name);
+  if (!c.slots || !valid_index_dtype(c.slot_dtype)) return fail(MAK_E_INVALID, "%s: slots must be int32/int64", name);
+  if (c.cache->num_blocks <= 0 || c.cache->block_size <= 0) return fail(MAK_E_INVALID, "%s: all cache extents must be positive", name);
+  if (owner_rows < c.cache->num_blocks * c.cache->block_size)
+    return fail(MAK_E_INVALID, "%s: owner table has %lld rows, the cache %lld slots", name, (long long)owner_rows,
+                (long long)(c.cache->num_blocks * c.cache->block_size));
+  int rc = mark_owners(c.slots, c.slot_dtype, c.lin->num_tokens, owner, owner_rows, epoch, st, name);
+  if (rc) return rc;
+  c.owner = owner;
+  c.owner_epoch = epoch;
   c.scatter = true;
   return run_tile(c, st, name);
 }
@@ -935,6 +973,20 @@ int mak_kv_linear_to_paged_mapped(const mak_linear_desc* in, const mak_paged_des
   c.seg_map_entries = seg_map_entries;
   c.seg_epoch = epoch;
   return tile_scatter(c, workspace, workspace_bytes, as_stream(stream), "mak_kv_linear_to_paged");
+}
+
+int mak_kv_linear_to_paged_owned(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                                 int32_t slot_dtype, uint64_t* owner, int64_t owner_rows, uint32_t epoch,
+                                 uint32_t* seg_map, int64_t seg_map_entries, uint32_t seg_epoch, void* stream) {
+  TileCall c{};
+  c.cache = cache;
+  c.lin = in;
+  c.slots = slots;
+  c.slot_dtype = slot_dtype;
+  c.seg_map = seg_map;
+  c.seg_map_entries = seg_map_entries;
+  c.seg_epoch = seg_epoch;
+  return tile_scatter_owned(c, owner, owner_rows, epoch, as_stream(stream), "mak_kv_linear_to_paged_owned");
 }
 
 int mak_kv_paged_fp8_to_linear(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
@@ -993,6 +1045,28 @@ int mak_kv_linear_to_paged_fp8_mapped(const mak_linear_desc* in, const mak_paged
   c.seg_map_entries = seg_map_entries;
   c.seg_epoch = epoch;
   return tile_scatter(c, workspace, workspace_bytes, as_stream(stream), "mak_kv_linear_to_paged_fp8");
+}
+
+int mak_kv_linear_to_paged_fp8_owned(const mak_linear_desc* in, const mak_paged_desc* cache, const void* slots,
+                                     int32_t slot_dtype, const float* k_scale, const float* v_scale,
+                                     int32_t scale_mode, int32_t fp8_format, uint64_t* owner, int64_t owner_rows,
+                                     uint32_t epoch, uint32_t* seg_map, int64_t seg_map_entries, uint32_t seg_epoch,
+                                     void* stream) {
+  if (fp8_format != MAK_FP8_E4M3 && fp8_format != MAK_FP8_E5M2)
+    return fail(MAK_E_INVALID, "mak_kv_linear_to_paged_fp8_owned: unknown FP8 format %d", fp8_format);
+  TileCall c{};
+  c.cache = cache;
+  c.lin = in;
+  c.slots = slots;
+  c.slot_dtype = slot_dtype;
+  c.k_scale = k_scale;
+  c.v_scale = v_scale;
+  c.scale_mode = scale_mode;
+  c.fp8_format = fp8_format;
+  c.seg_map = seg_map;
+  c.seg_map_entries = seg_map_entries;
+  c.seg_epoch = seg_epoch;
+  return tile_scatter_owned(c, owner, owner_rows, epoch, as_stream(stream), "mak_kv_linear_to_paged_fp8_owned");
 }
 
 }  // extern "C"

@@ -170,6 +170,16 @@ _PROTOTYPES = {
         [POINTER(LinearDesc), POINTER(PagedDesc), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p,
          c_size_t, c_void_p, c_int64, ctypes.c_uint32, c_void_p],
     ),
+    "mak_kv_linear_to_paged_owned": (
+        c_int32,
+        [POINTER(LinearDesc), POINTER(PagedDesc), c_void_p, c_int32, c_void_p, c_int64, ctypes.c_uint32, c_void_p,
+         c_int64, ctypes.c_uint32, c_void_p],
+    ),
+    "mak_kv_linear_to_paged_fp8_owned": (
+        c_int32,
+        [POINTER(LinearDesc), POINTER(PagedDesc), c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p,
+         c_int64, ctypes.c_uint32, c_void_p, c_int64, ctypes.c_uint32, c_void_p],
+    ),
     "mak_rows_gather": (
         c_int32,
         [c_void_p, c_void_p, POINTER(c_int64), c_int64, c_void_p, c_int32, c_int64, c_int32, c_void_p],

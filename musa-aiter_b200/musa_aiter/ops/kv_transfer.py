@@ -186,7 +186,9 @@ def _tile_gather(kc, vc, slots, ok, ov, *, layered: bool, fill_zero: bool, op: s
 
 
 def _tile_scatter(kl, vl, kc, vc, slots, *, layered: bool, op: str, fp8: tuple | None = None) -> None:
-    """linear (kl, vl) -> cache (kc, vc), last writer wins."""
+    """linear (kl, vl) -> cache (kc, vc), last writer wins: through this stream's owner table
+    (``mak_kv_linear_to_paged[_fp8]_owned``), or a workspace from torch's caching allocator where
+    owner tables do not apply (stream capture, very large caches)."""
     lib = _native.load()
     dev = kc.device
     ks, code = kernel_slots(slots)
@@ -195,7 +197,7 @@ def _tile_scatter(kl, vl, kc, vc, slots, *, layered: bool, op: str, fp8: tuple |
     kc_w, kc_tmp = _as_unit_inner(kc)
     vc_w, vc_tmp = _as_unit_inner(vc)
     stream = _native.stream_ptr(dev)
-    ws, nbytes = _native.workspace(ks.numel(), dev)
+    ws = None
     if same_geometry(kc_w, vc_w) and same_geometry(kl, vl):
         groups = [(kl, vl, kc_w, vc_w, 0)]
     else:
@@ -203,20 +205,32 @@ def _tile_scatter(kl, vl, kc, vc, slots, *, layered: bool, op: str, fp8: tuple |
     for l0, l1, c0, c1, which in groups:
         pd = paged_desc(c0, c1, layered=layered)
         ld = linear_desc(l0, l1, layered=layered)
+        n_slots = int(pd.num_blocks) * int(pd.block_size)
         smap, sents, sepoch = _native.seg_map(dev, stream, ks.numel())
         if fp8 is None:
-            rc = lib.mak_kv_linear_to_paged_mapped(
-                ctypes.byref(ld), ctypes.byref(pd), _native.ptr(ks), code, _native.ptr(ws), nbytes, smap, sents, sepoch,
-                stream,
-            )
+            owned = lambda own, orows, epoch: lib.mak_kv_linear_to_paged_owned(  # noqa: E731
+                ctypes.byref(ld), ctypes.byref(pd), _native.ptr(ks), code, own, orows, epoch, smap, sents, sepoch, stream)
         else:
             k_s, v_s, mode, fmt = fp8
             s0 = k_s if which == 0 else v_s
             s1 = v_s if c1 is not None else None
-            rc = lib.mak_kv_linear_to_paged_fp8_mapped(
+            owned = lambda own, orows, epoch: lib.mak_kv_linear_to_paged_fp8_owned(  # noqa: E731
                 ctypes.byref(ld), ctypes.byref(pd), _native.ptr(ks), code, _native.ptr(s0), _native.ptr(s1), mode, fmt,
-                _native.ptr(ws), nbytes, smap, sents, sepoch, stream,
-            )
+                own, orows, epoch, smap, sents, sepoch, stream)
+        rc = _native.owned_scatter(dev, stream, n_slots, ks.numel(), owned)
+        if rc is None:
+            if ws is None:
+                ws, nbytes = _native.workspace(ks.numel(), dev)
+            if fp8 is None:
+                rc = lib.mak_kv_linear_to_paged_mapped(
+                    ctypes.byref(ld), ctypes.byref(pd), _native.ptr(ks), code, _native.ptr(ws), nbytes, smap, sents,
+                    sepoch, stream,
+                )
+            else:
+                rc = lib.mak_kv_linear_to_paged_fp8_mapped(
+                    ctypes.byref(ld), ctypes.byref(pd), _native.ptr(ks), code, _native.ptr(s0), _native.ptr(s1), mode,
+                    fmt, _native.ptr(ws), nbytes, smap, sents, sepoch, stream,
+                )
         _native.check(rc, op)
     if kc_tmp:
         kc.copy_(kc_w)

@@ -526,3 +526,51 @@ def test_tile_segment_map_skips_only_clean_windows(cuda_device, monkeypatch, fp8
             O.kv_linear_to_paged(to_np(kl), to_np(vl), rkc, rvc, slots.numpy())
         eq(sk, rkc, f"mapped store k t={t}")
         eq(sv, rvc, f"mapped store v t={t}")
+
+
+@pytest.mark.parametrize("fp8", (False, True))
+def test_tile_owned_scatter_duplicates_vs_workspace_and_oracle(cuda_device, monkeypatch, fp8):
+    """Tile scatters resolve duplicate slots through the stream's owner table: block tables that
+    share blocks (runs written several times, later tokens win), lone duplicates and negatives give
+    the oracle's cache and the workspace path's, also after a row scatter used the same table."""
+    from musa_aiter import _native
+
+    g = torch.Generator().manual_seed(21)
+    nl, nb, nh, hd, bs = 2, 96, 4, 64, 16
+    tables = [torch.randperm(nb, generator=g)[:6] for _ in range(5)]  # sequences share blocks
+    slots = torch.cat([(bt[:, None] * bs + torch.arange(bs)[None, :]).flatten()[: 70 + 3 * i] for i, bt in enumerate(tables)])
+    extra = torch.randint(-3, nb * bs, (200,), generator=g)
+    slots = torch.cat([slots, extra, slots[:40]])  # lone duplicates, negatives, a repeated run
+    t = slots.numel()
+    kl = (torch.randn((nl, t, nh, hd), generator=g) * 2.0).to(torch.bfloat16)
+    vl = (torch.randn((nl, t, nh, hd), generator=g) * 2.0).to(torch.bfloat16)
+    ks, vs = torch.rand(nh, generator=g) * 0.01 + 0.003, torch.tensor(0.02)
+    dt = torch.uint8 if fp8 else torch.bfloat16
+
+    def store():
+        kc = torch.zeros((nl, nb, nh, hd, bs), dtype=dt, device="cuda")
+        vc = torch.zeros_like(kc)
+        if fp8:
+            ma.kv_linear_to_paged_fp8_multi_layer(kl.cuda(), vl.cuda(), kc, vc, slots.cuda(), ks.cuda(), vs.cuda())
+        else:
+            ma.kv_linear_to_paged_multi_layer(kl.cuda(), vl.cuda(), kc, vc, slots.cuda())
+        return kc, vc
+
+    # a row scatter on the same stream first leaves its own marks in the owner table
+    rows_dst = torch.zeros((4 * nb * bs, 8), dtype=torch.uint8, device="cuda")
+    ma.kv_copy_paged_rows(torch.randint(0, 256, (64, 8), generator=g, dtype=torch.uint8).cuda(), rows_dst,
+                          torch.arange(64, device="cuda"), torch.arange(64, device="cuda") * 3)
+    ok_k, ok_v = store()
+    with monkeypatch.context() as m:
+        m.setattr(_native, "owned_scatter", lambda *a: None)
+        ws_k, ws_v = store()
+    assert torch.equal(ok_k.view(torch.uint8), ws_k.view(torch.uint8))
+    assert torch.equal(ok_v.view(torch.uint8), ws_v.view(torch.uint8))
+    if fp8:
+        rk, rv = np.zeros(ok_k.shape, np.uint8), np.zeros(ok_v.shape, np.uint8)
+        O.kv_linear_to_paged_fp8_multi_layer(to_np(kl), to_np(vl), rk, rv, slots.numpy(), ks.numpy(), vs.numpy())
+    else:
+        rk, rv = np.zeros(ok_k.shape, to_np(kl).dtype), np.zeros(ok_v.shape, to_np(vl).dtype)
+        O.kv_linear_to_paged_multi_layer(to_np(kl), to_np(vl), rk, rv, slots.numpy())
+    eq(ok_k, rk, "owned scatter k")
+    eq(ok_v, rv, "owned scatter v")

@@ -23,7 +23,7 @@ import torch
 
 from .. import _native
 from ..dispatch import emit_native
-from ._common import kernel_slots, linear_desc, paged_desc, require_cuda, validation_enabled
+from ._common import kernel_slots, require_cuda, validation_enabled
 
 __all__ = ["apply_rope", "apply_rope_to_key_cache", "copy_to_kv_cache"]
 
@@ -267,20 +267,9 @@ def copy_to_kv_cache(
     if vl.stride() != kl.stride():
         vl = vl.contiguous()
         kl = kl.contiguous()
-    pdesc = paged_desc(kc, vc, layered=False)
-    ldesc = linear_desc(kl, vl, layered=False)
-    same = vc.stride() == kc.stride()
-    lib = _native.load()
-    ws, nbytes = _native.workspace(ks.numel(), k.device)
-    stream = _native.stream_ptr(k.device)
-    if same:
-        _native.check(lib.mak_kv_linear_to_paged(ctypes.byref(ldesc), ctypes.byref(pdesc), ks.data_ptr(), code,
-                                                 ws.data_ptr(), nbytes, stream), name)
-    else:
-        for lin, cache in ((kl, kc), (vl, vc)):
-            pd = paged_desc(cache, None, layered=False)
-            ld = linear_desc(lin, None, layered=False)
-            _native.check(lib.mak_kv_linear_to_paged(ctypes.byref(ld), ctypes.byref(pd), ks.data_ptr(), code,
-                                                     ws.data_ptr(), nbytes, stream), name)
+    from .kv_transfer import _tile_scatter  # noqa: PLC0415 (kv_transfer does not import this module)
+
+    # owner-table last-writer resolution and segment map, as the other tile scatters
+    _tile_scatter(kl, vl, kc, vc, ks, layered=False, op=name)
     emit_native(name, k, "sm100a tile scatter (copy_to_kv_cache)")
     return None

@@ -113,15 +113,20 @@ __device__ __forceinline__ uint32_t cachegen_code(float v, float lo, float scale
   return static_cast<uint32_t>(q);
 }
 
-// Codes of VE elements per 16-byte vector (one VE-byte store), counted in a
-// per-warp shared-memory histogram that is folded into `counts` at the end.
+// Codes of VE elements per 16-byte vector (one VE-byte store), counted in
+// shared-memory histograms that are folded into `counts` at the end.  Each warp
+// keeps kHistCopies copies (lane % kHistCopies picks one), padded to 257 words so
+// that one bin of different copies falls in different banks: lanes whose codes
+// collide (the middle bins of a bell-shaped slab) serialise kHistCopies times less.
 template <int DT>
 __global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int64_t n, int vec_ok, const float* minmax,
                                                               int bins, uint8_t* codes, unsigned long long* counts) {
   constexpr int VE = Elem<DT>::VE;
-  __shared__ unsigned int hist[8][256];
+  constexpr int kHistCopies = 4;
+  constexpr int kHistPitch = 257;
+  __shared__ unsigned int hist[8 * kHistCopies][kHistPitch];
   const int wib = threadIdx.x >> 5;
-  for (int b = threadIdx.x; b < 8 * 256; b += blockDim.x) (&hist[0][0])[b] = 0;
+  for (int b = threadIdx.x; b < 8 * kHistCopies * kHistPitch; b += blockDim.x) (&hist[0][0])[b] = 0;
   __syncthreads();
   const float lo = minmax[0], hi = minmax[1];
   const float scale = __fmul_rn(__frcp_rn(__fsub_rn(hi, lo)), static_cast<float>(bins - 1));
@@ -129,7 +134,7 @@ __global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int
   const int64_t nv = vec_ok ? n / VE : 0;
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
-  unsigned int* h = hist[wib];
+  unsigned int* h = hist[wib * kHistCopies + (threadIdx.x & (kHistCopies - 1))];
   for (int64_t i = tid; i < nv; i += nt) {
     const uint4 v = __ldg(xv + i);
     uint32_t packed[VE / 4];
@@ -156,20 +161,30 @@ __global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int
   for (int b = threadIdx.x; b < bins; b += blockDim.x) {
     unsigned int t = 0;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) t += hist[w][b];
+    for (int w = 0; w < 8 * kHistCopies; ++w) t += hist[w][b];
     if (t) atomicAdd(counts + b, static_cast<unsigned long long>(t));
   }
 }
 
+// CDF = [0, cumsum(counts) / n], summed in order in fp32.  The warp stages the counts in
+// shared memory first: the single-thread sum over counts read from global memory waited on
+// one load per bin (27 us for 256 bins).
 __global__ void cachegen_cdf_kernel(const unsigned long long* counts, int bins, int64_t n, float* cdf) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  float run = 0.f;
-  const float denom = static_cast<float>(n);
-  cdf[0] = 0.f;
-  for (int b = 0; b < bins; ++b) {
-    run = __fadd_rn(run, static_cast<float>(counts[b]));
-    cdf[b + 1] = __fdiv_rn(run, denom);
+  __shared__ float c[257];
+  const int lane = threadIdx.x;
+  for (int b = lane; b < bins; b += 32) c[b + 1] = static_cast<float>(counts[b]);
+  __syncwarp();
+  if (lane == 0) {
+    float run = 0.f;
+    const float denom = static_cast<float>(n);
+    c[0] = 0.f;
+    for (int b = 1; b <= bins; ++b) {
+      run = __fadd_rn(run, c[b]);
+      c[b] = __fdiv_rn(run, denom);
+    }
   }
+  __syncwarp();
+  for (int b = lane; b <= bins; b += 32) cdf[b] = c[b];
 }
 
 // 16 codes per 16-byte load, the codebook (as the output type's bits) in shared

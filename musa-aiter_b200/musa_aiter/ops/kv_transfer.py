@@ -1892,17 +1892,25 @@ def kv_cachegen_encode(tensor: torch.Tensor, *, num_bins: int = 256) -> tuple[to
     code = _native.dtype_code(x.dtype)
     mm = torch.empty(2, dtype=torch.float32, device=dev)
     _native.check(lib.mak_minmax(_native.ptr(x), code, x.numel(), _native.ptr(mm), stream), name)
-    lo, hi = mm.tolist()
-    if lo == hi:
-        cdf = torch.zeros(num_bins + 1, dtype=torch.float32, device=dev)
-        cdf[1:] = 1.0
-        return (torch.zeros_like(tensor, dtype=torch.uint8), torch.full((num_bins,), lo, dtype=torch.float32, device=dev), cdf)
+    # min/max go to the host behind an event while the encode launches are queued: the device
+    # runs min/max, encode and CDF back to back, and the host waits only for the codebook bounds.
+    # A slab with max == min takes the same launches: every code is 0 (the NaN of 0 * inf is
+    # clamped to 0), so counts = [n, 0, ...] and the CDF is [0, 1, ..., 1].
+    mm_host = torch.empty(2, dtype=torch.float32, pin_memory=True)
+    mm_host.copy_(mm, non_blocking=True)
+    ready = torch.cuda.Event()
+    ready.record(torch.cuda.current_stream(dev))
     codes = torch.empty(x.shape, dtype=torch.uint8, device=dev)
     counts = torch.empty(num_bins, dtype=torch.int64, device=dev)
     cdf = torch.empty(num_bins + 1, dtype=torch.float32, device=dev)
     _native.check(lib.mak_cachegen_encode(_native.ptr(x), code, x.numel(), _native.ptr(mm), num_bins, _native.ptr(codes),
                                           _native.ptr(counts), _native.ptr(cdf), stream), name)
-    codebook = torch.linspace(lo, hi, num_bins, dtype=torch.float32, device=dev)
+    ready.synchronize()
+    lo, hi = mm_host.tolist()
+    if lo == hi:
+        codebook = torch.full((num_bins,), lo, dtype=torch.float32, device=dev)
+    else:
+        codebook = torch.linspace(lo, hi, num_bins, dtype=torch.float32, device=dev)
     emit_native(name, tensor, "sm100a min/max + encode/histogram + CDF kernels")
     return codes, codebook, cdf
 

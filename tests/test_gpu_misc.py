@@ -161,6 +161,21 @@ def test_cachegen_large_vs_oracle(cuda_device):
     eq(cb, rcb, "codebook")
 
 
+@pytest.mark.parametrize("bins", (2, 17, 256))
+@pytest.mark.parametrize("dt", ("bfloat16", "float32"))
+def test_cachegen_constant_and_two_valued_slabs_vs_oracle(cuda_device, dt, bins):
+    """max == min (every code 0, CDF [0, 1, ..., 1], codebook filled with the value) and a slab
+    of two values (codes 0 and bins - 1 only), through the same device launches as any slab."""
+    const = torch.full((5, 333), -2.75).to(TORCH_OF[dt])
+    two = torch.where(torch.rand((7, 129), generator=torch.Generator().manual_seed(3)) < 0.3, 1.5, -0.5).to(TORCH_OF[dt])
+    for x in (const, two):
+        enc, cb, cdf = ma.kv_cachegen_encode(x.cuda(), num_bins=bins)
+        renc, rcb, rcdf = O.kv_cachegen_encode(O.to_f32(to_np(x), dt), bins)
+        eq(enc, renc, "codes")
+        eq(cdf, rcdf, "cdf")
+        eq(cb, rcb, "codebook")
+
+
 @pytest.mark.parametrize("mode", (0, 1))
 def test_strided_block_transfer_vs_oracle(cuda_device, mode):
     """DSV4 staging <-> padded pages, both directions, vs the restated kernel semantics."""

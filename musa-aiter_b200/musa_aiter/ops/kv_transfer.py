@@ -1534,6 +1534,38 @@ def _ensure_block_mapping_pairs(block_mapping: torch.Tensor, *, src_blocks: int,
     return pairs
 
 
+def _count_and_copy_blocks(block_mapping: torch.Tensor, dst: torch.Tensor, *, src_blocks: int, dst_blocks: int,
+                           name: str, launch) -> int:
+    """Valid-pair count of ``block_mapping`` and ``launch(device int64 pairs)`` for the copy.
+
+    With validation off and the mapping already on the caches' device, the host neither copies
+    the mapping back for bounds checks (the row kernel skips out-of-range blocks) nor waits for
+    the stream before launching: the count goes to pinned memory behind an event, the copy is
+    queued, and the host waits for the count only, so the next call's host work overlaps this
+    copy.  Otherwise the reference's host checks run first (ValueError on out-of-range blocks).
+    """
+    if block_mapping.device == dst.device and not validation_enabled():
+        if block_mapping.dim() != 2 or block_mapping.shape[1] != 2:
+            raise ValueError(f"{name}: block_mapping must be [num_pairs, 2] with source and destination block ids")
+        if not _index_tensor_ok(block_mapping):
+            raise ValueError(f"{name}: block_mapping must use an integer dtype")
+        if block_mapping.numel() == 0:
+            return 0
+        pairs = block_mapping.to(dtype=torch.int64)
+        host = torch.empty((), dtype=torch.int64, pin_memory=True)
+        host.copy_(((pairs[:, 0] >= 0) & (pairs[:, 1] >= 0)).sum(), non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(dst.device))
+        launch(pairs)
+        ready.synchronize()
+        return int(host)
+    pairs = _ensure_block_mapping_pairs(block_mapping, src_blocks=src_blocks, dst_blocks=dst_blocks, name=name)
+    count = int(((pairs[:, 0] >= 0) & (pairs[:, 1] >= 0)).sum()) if pairs.numel() else 0
+    if count:
+        launch(block_mapping.to(device=dst.device, dtype=torch.int64))
+    return count
+
+
 def _block_planes(k: torch.Tensor, v: torch.Tensor, multi_layer: bool):
     """One plane per (kv, layer); a row is one whole block (its [NH, HD, BS] tail must be contiguous)."""
     e = k.element_size()
@@ -1588,12 +1620,10 @@ def kv_copy_paged_blocks(
     name = "kv_copy_paged_blocks"
     src_blocks, dst_blocks, multi = _validate_block_copy_shapes(src_key_cache, src_value_cache, dst_key_cache,
                                                                 dst_value_cache, name=name)
-    pairs = _ensure_block_mapping_pairs(block_mapping, src_blocks=src_blocks, dst_blocks=dst_blocks, name=name)
     require_cuda(name, src_key_cache, src_value_cache, dst_key_cache, dst_value_cache)
-    count = int(((pairs[:, 0] >= 0) & (pairs[:, 1] >= 0)).sum()) if pairs.numel() else 0
-    if count:
-        dev_pairs = block_mapping.to(device=dst_key_cache.device, dtype=torch.int64)
-        _copy_blocks(src_key_cache, src_value_cache, dst_key_cache, dst_value_cache, dev_pairs, multi, name)
+    count = _count_and_copy_blocks(
+        block_mapping, dst_key_cache, src_blocks=src_blocks, dst_blocks=dst_blocks, name=name,
+        launch=lambda dp: _copy_blocks(src_key_cache, src_value_cache, dst_key_cache, dst_value_cache, dp, multi, name))
     emit_native(name, dst_key_cache, "sm100a row engine, one block per row")
     return count
 
@@ -1611,13 +1641,11 @@ def kv_copy_paged_blocks_fp8(
                                                                 dst_value_cache_fp8, name=name)
     for t in (src_key_cache_fp8, src_value_cache_fp8, dst_key_cache_fp8, dst_value_cache_fp8):
         _validate_fp8_cache_tensor(t, name=name)
-    pairs = _ensure_block_mapping_pairs(block_mapping, src_blocks=src_blocks, dst_blocks=dst_blocks, name=name)
     require_cuda(name, src_key_cache_fp8, src_value_cache_fp8, dst_key_cache_fp8, dst_value_cache_fp8)
-    count = int(((pairs[:, 0] >= 0) & (pairs[:, 1] >= 0)).sum()) if pairs.numel() else 0
-    if count:
-        dev_pairs = block_mapping.to(device=dst_key_cache_fp8.device, dtype=torch.int64)
-        _copy_blocks(_u8_view(src_key_cache_fp8), _u8_view(src_value_cache_fp8), _u8_view(dst_key_cache_fp8),
-                     _u8_view(dst_value_cache_fp8), dev_pairs, multi, name)
+    count = _count_and_copy_blocks(
+        block_mapping, dst_key_cache_fp8, src_blocks=src_blocks, dst_blocks=dst_blocks, name=name,
+        launch=lambda dp: _copy_blocks(_u8_view(src_key_cache_fp8), _u8_view(src_value_cache_fp8),
+                                       _u8_view(dst_key_cache_fp8), _u8_view(dst_value_cache_fp8), dp, multi, name))
     emit_native(name, dst_key_cache_fp8, "sm100a row engine, one FP8 block per row")
     return count
 

@@ -69,6 +69,29 @@ def test_golden_flash_triton_blocks(cuda_device, misc, dt):
     eq(dv1, misc[f"{r}/dst1_v"], "blocks v")
 
 
+@pytest.mark.parametrize("fp8", (False, True))
+def test_block_copy_device_mapping_without_validation(cuda_device, misc, monkeypatch, fp8):
+    """Validation off and a device mapping: the count comes back behind an event after the copy
+    is queued; copies and count equal the golden ones (negative pairs included)."""
+    monkeypatch.setenv("MUSA_AITER_SKIP_VALIDATION", "1")
+    r = "blocks/bfloat16"
+    sk, sv = T(misc[f"{r}/src_k"], "bfloat16"), T(misc[f"{r}/src_v"], "bfloat16")
+    dk = torch.zeros(misc[f"{r}/dst_k"].shape, dtype=torch.bfloat16, device="cuda")
+    dv = torch.zeros_like(dk)
+    if fp8:  # the same bytes as raw FP8 blocks
+        sk, sv, dk, dv = (t.view(torch.uint8) for t in (sk, sv, dk, dv))
+    copy = ma.kv_copy_paged_blocks_fp8 if fp8 else ma.kv_copy_paged_blocks
+    for _ in range(2):  # a repeated call waits on its own count only
+        n = copy(sk, sv, dk, dv, T(misc["blocks/pairs"]))
+        assert n == int(misc[f"{r}/count"])
+    want_k, want_v = misc[f"{r}/dst_k"], misc[f"{r}/dst_v"]
+    if fp8:
+        want_k, want_v = want_k.view(np.uint8), want_v.view(np.uint8)
+    eq(dk, want_k, "blocks k (no validation)")
+    eq(dv, want_v, "blocks v (no validation)")
+    assert copy(sk, sv, dk, dv, torch.empty((0, 2), dtype=torch.int64, device="cuda")) == 0
+
+
 @pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
 def test_golden_fp8_flash(cuda_device, misc, fmt):
     ok, ov = ma.kv_load_and_dequantize_fp8_flash(T(misc["fp8flash/k8"]), T(misc["fp8flash/v8"]), T(misc["fp8flash/bt"]),

@@ -232,11 +232,12 @@ MAK_API int mak_kv_linear_to_paged_fp8(const mak_linear_desc* in, const mak_page
 
 /*
  * The four calls above with a segment map: a device vector of uint32 that the
- * pass over runs of 2+ consecutive slots fills with (epoch << 1) | (a
- * single-slot run starts here), one entry per window of 8-32 tokens
- * (ceil(T / 8) entries always suffice; a smaller map is ignored), so that the
- * single-slot pass skips the windows without such runs instead of scanning
- * them.  epoch in [1, 2^31) must differ from the one
+ * pass over runs of consecutive slots fills with (epoch << 2) | (a single-slot
+ * run starts here) | (a scatter run of 2 to 15 slots, shorter than a 16-byte
+ * chunk, starts here) << 1, one entry per window of 8-32 tokens (ceil(T / 8)
+ * entries always suffice; a smaller map is ignored), so that the passes for
+ * those runs skip the windows without them instead of scanning them.  epoch
+ * in [1, 2^30) must differ from the one
  * of any call still in flight on the same map; entries of other epochs are
  * never trusted, so a map may start with any contents.  Results are identical
  * to the unmapped calls.  Host-side additions, no reference counterpart.

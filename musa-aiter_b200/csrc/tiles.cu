@@ -7,10 +7,11 @@
 // consecutive slots inside one block) with ballots, and moves each segment
 // through 16-byte chunks of the cache rows ([d][o0 .. o0 + G)), transposing
 // in registers.  Runs of two or more tokens (block-table traffic and its
-// ragged ends) and single tokens (random slots) are handled by two
+// ragged ends) and single tokens (random slots) are handled by separate
 // instantiations launched back to back, so the single-token, latency-bound
 // path runs at high occupancy while the run path keeps the registers its
-// transposes need.
+// transposes need; scatters give the run ends shorter than a 16-byte chunk a
+// third instantiation, whose batched token loads would spill the run path.
 //
 // Fallback (tile_kernel): any head_dim / block_size / alignment, through a
 // shared-memory transpose of 32-token chunks.
@@ -43,8 +44,10 @@ struct TileLaunch {
   int32_t window;       // tokens per warp window of the segment kernel (8, 16 or 32)
   int32_t plane_group;  // (kv, layer) planes a segment-kernel block walks per window
   // Segment map (optional): the run launch (MODE 1) stores, per window of map_window tokens,
-  // (epoch << 1) | (a single-token run starts in it); the single-token launch (MODE 2) skips
-  // the windows whose entries read (epoch << 1).  Entries of another epoch are never trusted.
+  // (epoch << 2) | (a single-token run starts in it) | (a scatter run end of 2..G-1 tokens
+  // starts in it) << 1; the single-token launch (MODE 2) and the run-end launch (MODE 3) skip
+  // the windows whose entry has this epoch and their bit clear.  Entries of another epoch are
+  // never trusted.
   uint32_t* seg_map;
   uint32_t seg_epoch;
   int32_t map_window;       // tokens per map entry (the run launch's window: 8, 16 or 32)
@@ -367,7 +370,8 @@ __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileL
 //            write, so concurrent segments of one block never race).
 // No shared memory, no block barriers; FP8 codecs run in registers.
 // ---------------------------------------------------------------------------
-// MODE 1 handles segments of at least kRunMin tokens (plus zero rows), MODE 2 the single tokens;
+// MODE 1 handles segments of at least kRunMin tokens (plus zero rows), MODE 2 the single tokens,
+// MODE 3 (scatters only) the runs of 2..kRunMin-1 tokens;
 // the two are launched back to back so each keeps the register budget its path needs.
 template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE, bool GROUPED>
 __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg_kernel(const __grid_constant__ TileLaunch p) {
@@ -378,6 +382,8 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
   // the element path would walk its tokens one after another; a scatter must not write the
   // chunk's other slots, so its runs shorter than a chunk stay on the element path.
   constexpr int kRunMin = SCATTER ? G : 2;
+  // launch that owns a segment of len tokens
+  auto seg_mode = [](int len) { return len >= kRunMin ? 1 : (len >= 2 ? 3 : 2); };
   using C = Codec<CT, LT, CODEC>;
   const int lane = threadIdx.x & 31;
   const int upr = static_cast<int>(p.head_dim) / R;
@@ -405,15 +411,15 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
 
   for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < windows; w += wstride) {
     const int64_t t0 = w * W;
-    if (MODE == 2 && p.seg_map != nullptr) {
+    if (MODE != 1 && p.seg_map != nullptr) {
       // Skip the window when the run launch of this call found no single-token run starting in
       // any of its map windows that cover [t0, t0 + W) (at most 32 / 8 = 4 of them).
       const int64_t m0 = t0 >> p.map_shift;
       const int64_t m1 = (min(t0 + W, p.n_tokens) - 1) >> p.map_shift;
-      const uint32_t clean = p.seg_epoch << 1;
-      uint32_t v = clean;
+      const uint32_t tag = p.seg_epoch << 2, bit = MODE == 2 ? 1u : 2u;
+      uint32_t v = tag;
       if (lane <= m1 - m0) v = p.seg_map[m0 + lane];
-      if (__all_sync(0xffffffffu, v == clean)) continue;
+      if (__all_sync(0xffffffffu, (v & ~3u) == tag && (v & bit) == 0u)) continue;
     }
     // Slots of tokens t0 + lane (A) and t0 + 32 + lane (B), as (block element offset, in-block offset).
     int64_t offA = -1, offB = -1, sA = -1, sB = -1, oA = 0, oB = 0;
@@ -445,14 +451,15 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
       // Does a single-token run start in this window?  A run's length is bounded by the
       // next boundary in the 64 loaded slots; 64 - lane > 32, so a run that reaches past
       // them is long whatever follows, and the single-token launch classifies alike.
-      bool single = false;
+      int mode = 1;
       if (lane < W && ((mStartA >> lane) & 1u)) {
         const uint64_t rest = bound >> (lane + 1);
         const int len = rest ? __ffsll(static_cast<long long>(rest)) : (64 - lane);
-        single = len < kRunMin;
+        mode = seg_mode(len);
       }
-      const uint32_t anySingle = __ballot_sync(0xffffffffu, single) != 0u ? 1u : 0u;
-      if (lane == 0) p.seg_map[w] = (p.seg_epoch << 1) | anySingle;
+      const uint32_t bits = (__ballot_sync(0xffffffffu, mode == 2) != 0u ? 1u : 0u) |
+                            (__ballot_sync(0xffffffffu, mode == 3) != 0u ? 2u : 0u);
+      if (lane == 0) p.seg_map[w] = (p.seg_epoch << 2) | bits;
     }
     // The window's segments are the same for every plane: skip the planes when
     // none is this launch's kind (and, in MODE 1, no zero rows are due).
@@ -462,7 +469,7 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
         const int q = __ffs(m) - 1;
         const uint64_t rest = bound >> (q + 1);
         const int len = rest ? (__ffsll(static_cast<long long>(rest))) : (64 - q);
-        work = (MODE == 1) == (len >= kRunMin);
+        work = seg_mode(len) == MODE;
       }
       if (!work) continue;
     }
@@ -499,8 +506,8 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
       const int o_s = static_cast<int>(__shfl_sync(0xffffffffu, oA, q));
       const int64_t ts = t0 + q;
       const int64_t cbase = soff - o_s;  // block start (element offset)
-      if ((MODE == 1) != (len >= kRunMin)) continue;
-      if (len < kRunMin) {
+      if (seg_mode(len) != MODE) continue;
+      if (MODE == 2) {
         // Single-token segment (random slots): one element per item, head_dim fastest
         // across lanes, so a warp instruction touches consecutive cache rows (whole
         // sectors per instruction) and a contiguous piece of the token row; four items
@@ -695,13 +702,23 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
           }
         } else {
           // partially covered chunk, scatter: element stores on the cache side (the chunk's
-          // other slots belong to other tokens), 16-byte token rows
+          // other slots belong to other tokens), 16-byte token rows; the run-end launch loads
+          // up to eight covered rows at a time, the run launch one (its registers go to the
+          // full-chunk transposes)
+          constexpr int kTok = MODE == 3 ? (G < 8 ? G : 8) : 1;
 #pragma unroll 1
-          for (int col = lo; col < hi; ++col) {
-            const uint4 tv = __ldg(reinterpret_cast<const uint4*>(lrow + (col - o_s) * p.l_st));
-            const LT* x = reinterpret_cast<const LT*>(&tv);
+          for (int c0 = lo; c0 < hi; c0 += kTok) {
+            uint4 tv[kTok];
 #pragma unroll
-            for (int r = 0; r < R; ++r) cache_w[row0 + r * p.c_sd + col] = C::store(x[r], sc);
+            for (int i = 0; i < kTok; ++i)
+              if (c0 + i < hi) tv[i] = __ldg(reinterpret_cast<const uint4*>(lrow + (c0 + i - o_s) * p.l_st));
+#pragma unroll
+            for (int i = 0; i < kTok; ++i) {
+              if (c0 + i >= hi) continue;
+              const LT* x = reinterpret_cast<const LT*>(&tv[i]);
+#pragma unroll
+              for (int r = 0; r < R; ++r) cache_w[row0 + r * p.c_sd + c0 + i] = C::store(x[r], sc);
+            }
           }
         }
       }
@@ -743,7 +760,8 @@ static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
     p.plane_group /= 2;
   const int64_t groups = (planes + p.plane_group - 1) / p.plane_group;
   // About 4 device-fulls of CTAs, spread over the groups; each CTA walks windows grid-stride.
-  const int64_t target = static_cast<int64_t>(per_sm) * sm_count() * 4;
+  // The run-end launch has work in few windows (sequence ends): one device-full.
+  const int64_t target = static_cast<int64_t>(per_sm) * sm_count() * (MODE == 3 ? 1 : 4);
   int64_t gx = std::max<int64_t>(1, target / groups);
   gx = std::min<int64_t>(gx, (windows + (threads / 32) - 1) / (threads / 32));
   const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(groups));
@@ -757,6 +775,10 @@ template <typename CT, typename LT, int CODEC, bool SCATTER>
 static int launch_tile_segments(TileLaunch& p, cudaStream_t st) {
   int rc = launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 1>(p, st);
   if (rc) return rc;
+  if constexpr (SCATTER) {
+    rc = launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 3>(p, st);
+    if (rc) return rc;
+  }
   return launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 2>(p, st);
 }
 
@@ -856,8 +878,8 @@ static int run_tile(const TileCall& c, cudaStream_t st, const char* name) {
   p.fill_zero = c.fill_zero ? 1 : 0;
   p.scale_mode = c.scale_mode;
   if (c.seg_map != nullptr) {
-    if (c.seg_epoch == 0 || c.seg_epoch >= (1u << 31) || c.seg_map_entries < 0)
-      return fail(MAK_E_INVALID, "%s: segment map epoch must be in [1, 2^31) and its size non-negative", name);
+    if (c.seg_epoch == 0 || c.seg_epoch >= (1u << 30) || c.seg_map_entries < 0)
+      return fail(MAK_E_INVALID, "%s: segment map epoch must be in [1, 2^30) and its size non-negative", name);
     if ((reinterpret_cast<uintptr_t>(c.seg_map) & 3u) != 0) return fail(MAK_E_INVALID, "%s: misaligned segment map", name);
     p.seg_map = c.seg_map;
     p.seg_map_entries = c.seg_map_entries;

@@ -395,7 +395,7 @@ def owned_scatter(device: torch.device, stream: int, rows: int, n: int, launch):
 # launch reads was written by the long-run launch of the same call, so the
 # contents never need clearing, and a wrapped epoch may start again at 1.
 _SEGMAPS: dict = {}
-_SEG_EPOCH_MAX = (1 << 31) - 1
+_SEG_EPOCH_MAX = (1 << 30) - 1
 _SEGMAP_MAX_ENTRIES = 1 << 28
 
 

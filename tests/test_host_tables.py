@@ -28,7 +28,7 @@ def test_seg_map_epochs_growth_and_wrap(monkeypatch):
     assert _native.seg_map(CPU, stream, 100)[1:] == (cap2, 2)
     ent = _native._SEGMAPS[(CPU.index, stream)]
     assert ent[0].numel() == cap2 and ent[0].dtype == torch.int32
-    ent[3] = _native._SEG_EPOCH_MAX + 1  # epochs stay below 2^31: the next one starts again at 1
+    ent[3] = _native._SEG_EPOCH_MAX + 1  # epochs stay below 2^30: the next one starts again at 1
     assert _native.seg_map(CPU, stream, 100)[2] == 1
     _native._SEGMAPS.pop((CPU.index, stream), None)
 

@@ -351,8 +351,10 @@ MAK_API int mak_rows_scatterv_owned(const mak_rows_desc* linear, const mak_rows_
  * loads the library, held until exit), so no workspace is passed.
  * - At most MAK_STATIC_SCATTER_MAX_SLOTS slots per call; larger calls return
  *   MAK_E_UNSUPPORTED without launching anything.
- * - The first call on a device looks up the array's device address for that
- *   device; make that first call before any stream capture.
+ * - The first call on a device (per CUDA context: the primary context, or a
+ *   driver-API context the caller made current) looks up the array's device
+ *   address there; make that first call before any stream capture.  A device
+ *   reset (cudaDeviceReset) after the first call is not supported.
  * - Every call shares the one array: calls that may overlap on the GPU (other
  *   streams, other host threads) race and must be serialised by the caller.
  * - Allocates nothing: no cudaMalloc, cudaFree or allocating library routine.

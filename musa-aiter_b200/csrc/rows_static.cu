@@ -11,7 +11,13 @@
 // outputs.
 //
 // The array has a fixed size (enough for MAK_STATIC_SCATTER_MAX_SLOTS slots)
-// and lives on every GPU that loads the library until the process exits.
+// and lives on every GPU that loads the library until the process exits.  Its
+// device address is looked up on the first call in each (device, CUDA context)
+// pair and cached; a context destroyed and re-created at the same handle (a
+// cudaDeviceReset after the first call) is not detected, so callers that reset
+// a device must not use this entry point on it afterwards.
+#include <cuda.h>  // CUcontext / CUresult types only: cuCtxGetCurrent is fetched through the runtime
+
 #include <mutex>
 
 #include "common.cuh"
@@ -28,27 +34,68 @@ constexpr size_t kStaticScratchBytes = (static_cast<size_t>(kStaticCapacity) * 8
 static __device__ __align__(256) unsigned char g_static_scatter_scratch[kStaticScratchBytes];
 
 namespace {
-constexpr int kMaxScratchDevices = 64;
-void* g_scratch_addr[kMaxScratchDevices] = {nullptr};
+// One cached address per (device, CUDA context): the array has its own copy, at its own
+// address, in every context that loads the library's module -- the runtime's primary context
+// and any context a caller created with the driver API and made current.
+constexpr int kMaxScratchEntries = 64;
+struct ScratchEntry {
+  int device;
+  CUcontext ctx;
+  void* addr;
+};
+ScratchEntry g_scratch[kMaxScratchEntries];
+int g_scratch_used = 0;
 std::mutex g_scratch_mu;
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
 }  // namespace
 
-// Device address of the scratch array on the current device.  The name
+// Device address of the scratch array in the current context.  The name
 // g_static_scatter_scratch in host code is only a host-side stand-in, so the
-// address is looked up once per device (with that device current) and cached.
+// address is looked up once per (device, context), with that device current, and cached.
 static int static_scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "mak_rows_scatter_static: cudaGetDevice");
-  if (dev < 0 || dev >= kMaxScratchDevices) return fail(MAK_E_UNSUPPORTED, "mak_rows_scatter_static: device %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_static_scatter_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "mak_rows_scatter_static: cudaGetSymbolAddress");
-    g_scratch_addr[dev] = p;
+  if (g_ctx_get_current == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return fail(MAK_E_CUDA, "mak_rows_scatter_static: cuCtxGetCurrent entry point unavailable");
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
   }
-  *out = g_scratch_addr[dev];
+  CUcontext ctx = nullptr;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS)
+    return fail(MAK_E_CUDA, "mak_rows_scatter_static: cuCtxGetCurrent failed");
+  for (int i = 0; i < g_scratch_used; ++i) {
+    if (g_scratch[i].device == dev && g_scratch[i].ctx == ctx) {
+      *out = g_scratch[i].addr;
+      return MAK_OK;
+    }
+  }
+  // Miss (or no context current on this thread yet: the lookup binds the device's primary
+  // context, and the entry is stored under the context that is current afterwards).
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_static_scatter_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "mak_rows_scatter_static: cudaGetSymbolAddress");
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+    return fail(MAK_E_CUDA, "mak_rows_scatter_static: no CUDA context current after the symbol lookup");
+  for (int i = 0; i < g_scratch_used; ++i) {
+    if (g_scratch[i].device == dev && g_scratch[i].ctx == ctx) {
+      g_scratch[i].addr = p;
+      *out = p;
+      return MAK_OK;
+    }
+  }
+  // A full table drops its oldest entry (a context beyond the 64th seen is looked up again later).
+  if (g_scratch_used == kMaxScratchEntries) {
+    for (int i = 1; i < kMaxScratchEntries; ++i) g_scratch[i - 1] = g_scratch[i];
+    --g_scratch_used;
+  }
+  g_scratch[g_scratch_used++] = ScratchEntry{dev, ctx, p};
+  *out = p;
   return MAK_OK;
 }
 

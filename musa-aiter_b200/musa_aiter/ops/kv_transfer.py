@@ -1873,6 +1873,21 @@ def kv_copy_paged_rows_multi_pool(pools: list[PoolSpec], indices: torch.Tensor, 
                 f"sm100a row engine ({len(pools)} pools, direction={direction})")
 
 
+_bounce_lock = _threading.Lock()
+_bounce_in_flight: list = []  # (event, pinned bounce buffer) pairs still read by a queued kernel
+
+
+def _hold_bounce(bounce: torch.Tensor, dev: torch.device) -> None:
+    """Keep a pinned bounce buffer alive until the kernel queued on the current stream that
+    reads it has run: torch's pinned-memory cache would otherwise hand the block to the next
+    ``pin_memory`` allocation as soon as the tensor is released, while the copy is still queued."""
+    ev = torch.cuda.Event()
+    ev.record(torch.cuda.current_stream(dev))
+    with _bounce_lock:
+        _bounce_in_flight[:] = [(e, b) for e, b in _bounce_in_flight if not e.query()]
+        _bounce_in_flight.append((ev, bounce))
+
+
 def _staged_rows_copy(src: torch.Tensor, dst: torch.Tensor, indices: torch.Tensor, name: str) -> None:
     """Copy rows where one side is pageable host memory, through a pinned bounce buffer."""
     rows = indices.to(torch.long)
@@ -1884,6 +1899,8 @@ def _staged_rows_copy(src: torch.Tensor, dst: torch.Tensor, indices: torch.Tenso
         torch.index_select(src, 0, rows.cpu(), out=bounce)
         ident = torch.arange(n, device=dst.device if dst.device.type == "cuda" else "cpu")
         _rows_copy_planes([bounce], [dst], ident, rows.to(ident.device), name)
+        if dst.device.type == "cuda":
+            _hold_bounce(bounce, dst.device)
     else:
         bounce = torch.empty((n, dst.shape[1]), dtype=torch.uint8, pin_memory=True)
         dev = src.device

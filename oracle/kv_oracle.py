@@ -322,6 +322,35 @@ def kv_paged_fp8_to_linear_multi_layer(k_cache8, v_cache8, slots, k_scale, v_sca
     return out_k, out_v
 
 
+def kv_merged_linear_to_paged_fp8(merged, k_cache8, v_cache8, slots, k_scale, v_scale, *, fp8_format="e4m3",
+                                  lin_dtype="bfloat16"):
+    """kv_transfer.py:3489-3505: the K half ``merged[:, 0]`` and V half ``merged[:, 1]`` of a
+    ``[T, 2, NH, HD]`` buffer go through the single-layer FP8 store."""
+    kv_linear_to_paged_fp8(merged[:, 0], merged[:, 1], k_cache8, v_cache8, slots, k_scale, v_scale,
+                           fp8_format=fp8_format, lin_dtype=lin_dtype)
+
+
+def kv_paged_fp8_to_merged_linear(k_cache8, v_cache8, slots, k_scale, v_scale, *, out_dtype="bfloat16", fp8_format="e4m3"):
+    """kv_transfer.py:3460-3486: FP8 gather + dequantize into ``[T, 2, NH, HD]`` (K at 0, V at 1)."""
+    ok, ov = kv_paged_fp8_to_linear(k_cache8, v_cache8, slots, k_scale, v_scale, out_dtype=out_dtype, fp8_format=fp8_format)
+    return np.stack([ok, ov], axis=1)
+
+
+def kv_merged_linear_to_paged_fp8_multi_layer(merged, k_cache8, v_cache8, slots, k_scale, v_scale, *, fp8_format="e4m3",
+                                              lin_dtype="bfloat16"):
+    """kv_transfer.py:3537-3553: ``[L, T, 2, NH, HD]`` halves through the multi-layer FP8 store."""
+    kv_linear_to_paged_fp8_multi_layer(merged[:, :, 0], merged[:, :, 1], k_cache8, v_cache8, slots, k_scale, v_scale,
+                                       fp8_format=fp8_format, lin_dtype=lin_dtype)
+
+
+def kv_paged_fp8_to_merged_linear_multi_layer(k_cache8, v_cache8, slots, k_scale, v_scale, *, out_dtype="bfloat16",
+                                              fp8_format="e4m3"):
+    """kv_transfer.py:3508-3534: multi-layer FP8 gather + dequantize into ``[L, T, 2, NH, HD]``."""
+    ok, ov = kv_paged_fp8_to_linear_multi_layer(k_cache8, v_cache8, slots, k_scale, v_scale, out_dtype=out_dtype,
+                                                fp8_format=fp8_format)
+    return np.stack([ok, ov], axis=2)
+
+
 # ---------------------------------------------------------------------------
 # row caches (LMCache / SGLang MP / MLA flat): musa_aiter/ops/lmcache_kv_transfer.py
 # ---------------------------------------------------------------------------
@@ -709,6 +738,15 @@ def kv_copy_paged_rows(src: np.ndarray, dst: np.ndarray, src_idx, dst_idx) -> No
     di = np.asarray(dst_idx, dtype=np.int64)
     keep = last_writer_mask(di)
     dst[di[keep]] = src[si[keep]]
+
+
+def kv_copy_paged_rows_multi_pool(pools, indices) -> None:
+    """kv_transfer.py:4619-4660: every (src, dst) layer pair of every pool copies the rows named
+    by the one shared index vector (same index on both sides), in pool and layer order.
+    ``pools`` is a list of (src layers, dst layers)."""
+    for srcs, dsts in pools:
+        for s, d in zip(srcs, dsts):
+            kv_copy_paged_rows(s, d, indices, indices)
 
 
 def hicache_transfer(src_k, dst_k, src_v, dst_v, src_idx, dst_idx, src_layout, dst_layout, start_layer, num_layers):

@@ -23,6 +23,9 @@ Families:
 
 - cache.npz   apply_rope (dtype pairs, interleaved, broadcast shapes), apply_rope_to_key_cache
               (1-D and 2-D tables, repeated slots), copy_to_kv_cache
+- merged_fp8.npz  FP8 merged store / load, single and multi-layer, e4m3 / e5m2, scalar /
+              [NH] / [L, NH] scales, block_size 16 and 4, negative and duplicate slots
+- pools.npz   DSV4 multi-pool page-row copy, both directions, four pools of different widths
 
 ``python tests/golden/make_golden.py mla_fp8`` regenerates one family only.
 """
@@ -590,9 +593,90 @@ def make_cache() -> None:
     st.save("cache.npz")
 
 
+def make_merged_fp8() -> None:
+    """FP8 merged wrappers (reference ops/kv_transfer.py:3460-3553): a merged ``[T, 2, NH, HD]`` /
+    ``[L, T, 2, NH, HD]`` buffer quantised into two uint8 tile caches and dequantised back, for
+    both formats, scalar / ``[NH]`` / ``[L, NH]`` scales, negative and duplicate slots."""
+    st = Store()
+    nb, nh, hd = 6, 2, 16
+    sl = torch.tensor([5, 6, 7, -1, 5, 40, 63, 0, 1, 2, 3, 4, 8, 9, 10, 11, 12, 13, 14, 15, 95, 16, 17, -7, 63],
+                      dtype=torch.int64)
+    gsl = torch.tensor([63, 5, -1, 6, 7, 40, 0, 1, 2, 3, 4, 8, 9, 10, 11, 12, 13, 14, 15, 95, 94, -3, 16], dtype=torch.int64)
+    nl = 3
+    for bs in (16, 4):
+        t = int(sl.numel())
+        ss = torch.where(sl < 0, sl, sl % (nb * bs))  # duplicates survive the fold (5, 63 twice)
+        gs = torch.where(gsl < 0, gsl, gsl % (nb * bs))
+        st.put(f"bs{bs}/slots", ss)
+        st.put(f"bs{bs}/gslots", gs)
+        for fmt in ("e4m3", "e5m2"):
+            for lname, ldt in (("bfloat16", torch.bfloat16), ("float16", torch.float16)):
+                g = gen(60 + bs)
+                merged = (randn((t, 2, nh, hd), torch.float32, g) * 2.0).to(ldt)
+                merged_ml = (randn((nl, t, 2, nh, hd), torch.float32, g) * 2.0).to(ldt)
+                scale_forms = {
+                    "scalar": (0.0123, 0.0177),
+                    "head": (torch.rand((nh,), generator=g) * 0.02 + 0.001, torch.rand((nh,), generator=g) * 0.02 + 0.001),
+                }
+                for sname, (ks, vs) in scale_forms.items():
+                    p = f"bs{bs}/{fmt}/{lname}/{sname}"
+                    kc = torch.zeros((nb, nh, hd, bs), dtype=torch.uint8)
+                    vc = torch.zeros((nb, nh, hd, bs), dtype=torch.uint8)
+                    ref.kv_merged_linear_to_paged_fp8(merged, kc, vc, ss, ks, vs, fp8_format=fmt)
+                    st.put(f"{p}/merged", merged)
+                    st.put(f"{p}/k_scale", torch.as_tensor(ks, dtype=torch.float32))
+                    st.put(f"{p}/v_scale", torch.as_tensor(vs, dtype=torch.float32))
+                    st.put(f"{p}/k_cache", kc)
+                    st.put(f"{p}/v_cache", vc)
+                    out = ref.kv_paged_fp8_to_merged_linear(kc, vc, gs, ks, vs, out_dtype=ldt, fp8_format=fmt)
+                    st.put(f"{p}/gather", out)
+                ml_forms = dict(scale_forms)
+                ml_forms["layer_head"] = (torch.rand((nl, nh), generator=g) * 0.02 + 0.001, 0.0149)
+                for sname, (ks, vs) in ml_forms.items():
+                    p = f"bs{bs}/{fmt}/{lname}/ml_{sname}"
+                    kc = torch.zeros((nl, nb, nh, hd, bs), dtype=torch.uint8)
+                    vc = torch.zeros((nl, nb, nh, hd, bs), dtype=torch.uint8)
+                    ref.kv_merged_linear_to_paged_fp8_multi_layer(merged_ml, kc, vc, ss, ks, vs, fp8_format=fmt)
+                    st.put(f"{p}/merged", merged_ml)
+                    st.put(f"{p}/k_scale", torch.as_tensor(ks, dtype=torch.float32))
+                    st.put(f"{p}/v_scale", torch.as_tensor(vs, dtype=torch.float32))
+                    st.put(f"{p}/k_cache", kc)
+                    st.put(f"{p}/v_cache", vc)
+                    out = ref.kv_paged_fp8_to_merged_linear_multi_layer(kc, vc, gs, ks, vs, out_dtype=ldt, fp8_format=fmt)
+                    st.put(f"{p}/gather", out)
+    st.save("merged_fp8.npz")
+
+
+def make_pools() -> None:
+    """DSV4 multi-pool page-row copy (reference ops/kv_transfer.py:4619-4660): pools of different
+    row widths and layer counts sharing one index vector, run on CPU tensors in both directions
+    (the reference's copy is the same index_select / index_copy_ whatever the devices)."""
+    from musa_aiter.ops.kv_transfer import PoolSpec as RefPoolSpec
+
+    st = Store()
+    g = gen(70)
+    pages = 24
+    idx = torch.tensor([3, 17, 0, 23, 8, 17, 22, 5], dtype=torch.int64)
+    st.put("indices", idx)
+    specs = [(2, 656), (1, 24), (3, 129), (1, 1)]  # (layers, item_bytes)
+    for direction in ("H2D", "D2H"):
+        pools = []
+        for p, (nl, item) in enumerate(specs):
+            srcs = [torch.randint(0, 256, (pages, item), generator=g, dtype=torch.int32).to(torch.uint8) for _ in range(nl)]
+            dsts = [torch.randint(0, 256, (pages, item), generator=g, dtype=torch.int32).to(torch.uint8) for _ in range(nl)]
+            st.put(f"{direction}/{p}/src", torch.stack(srcs))
+            st.put(f"{direction}/{p}/dst_in", torch.stack(dsts))
+            pools.append((srcs, dsts, item))
+        ref.ops.kv_transfer.kv_copy_paged_rows_multi_pool(
+            [RefPoolSpec(src_ptrs=s, dst_ptrs=d, item_bytes=i) for s, d, i in pools], idx, direction=direction)
+        for p, (_, dsts, _) in enumerate(pools):
+            st.put(f"{direction}/{p}/dst_out", torch.stack(dsts))
+    st.save("pools.npz")
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     families = {"tile": make_tile, "fp8": make_fp8, "rows": make_rows, "misc": make_misc, "mla_fp8": make_mla_fp8,
-                "cache": make_cache}
+                "cache": make_cache, "merged_fp8": make_merged_fp8, "pools": make_pools}
     for name in (sys.argv[1:] or list(families)):
         families[name]()

@@ -465,12 +465,16 @@ def _mixed_run_slots(n_target, nb, bs, gen) -> torch.Tensor:
     return torch.tensor(out[:n_target], dtype=torch.int64)
 
 
+@pytest.mark.parametrize("stale_bits", (0, 1))
 @pytest.mark.parametrize("fp8", (False, True))
-def test_tile_segment_map_skips_only_clean_windows(cuda_device, monkeypatch, fp8):
-    """The short-run launch skips the windows that the long-run launch of the same call marked
-    free of short runs: results equal the unmapped launches' and the oracle's for calls whose
-    window sizes differ between the two launches (8 to 32 tokens), also when the map already
-    holds this call's epoch marked clean everywhere (the long-run launch rewrites every entry)."""
+def test_tile_segment_map_skips_only_clean_windows(cuda_device, monkeypatch, fp8, stale_bits):
+    """The single-token and run-end launches skip the windows that the run launch of the same
+    call marked free of their kind: results equal the unmapped launches' and the oracle's for
+    calls whose window sizes differ between the launches (8 to 32 tokens), also when the map
+    already holds this call's epoch (entry = epoch << 2 | bits) marked clean everywhere
+    (stale_bits 0), or marked with only the single-token bit (stale_bits 1: a run-end launch
+    that trusted it would drop the scatter runs of 2..G-1 tokens) -- the run launch rewrites
+    every entry before the other launches read it."""
     from musa_aiter import _native
 
     g = torch.Generator().manual_seed(11)
@@ -506,9 +510,9 @@ def test_tile_segment_map_skips_only_clean_windows(cuda_device, monkeypatch, fp8
         dev = torch.device("cuda", torch.cuda.current_device())
         _native.seg_map(dev, _native.stream_ptr(dev), t)
         ent = _native._SEGMAPS[(dev.index, _native.stream_ptr(dev))]
-        ent[0].fill_(ent[3] << 1)
+        ent[0].fill_((ent[3] << 2) | stale_bits)
         mk, mv = load()
-        ent[0].fill_(ent[3] << 1)
+        ent[0].fill_((ent[3] << 2) | stale_bits)
         sk, sv = store()
         eq(mk, rk, f"mapped load k t={t}")
         eq(mv, rv, f"mapped load v t={t}")

@@ -359,3 +359,44 @@ def test_rope_key_cache_and_copy(cache_g, cn):
     vcc = np.zeros_like(cache_g[f"{q}/vc"])
     O.copy_to_kv_cache(cache_g[f"{q}/k"], cache_g[f"{q}/v"], kcc, vcc, cache_g[f"{q}/slots"])
     assert kcc.tobytes() == cache_g[f"{q}/kc"].tobytes() and vcc.tobytes() == cache_g[f"{q}/vc"].tobytes()
+
+
+@pytest.fixture(scope="module")
+def merged_fp8():
+    return np.load(GOLDEN / "merged_fp8.npz")
+
+
+def _merged_fp8_keys(g):
+    """(block size, format, input dtype, scale form) of every case in merged_fp8.npz."""
+    return sorted({tuple(k.split("/")[:4]) for k in g.files if k.count("/") == 4})
+
+
+def test_merged_fp8_store_and_load(merged_fp8):
+    g = merged_fp8
+    cases = _merged_fp8_keys(g)
+    assert len(cases) == 2 * 2 * 2 * 5, cases  # bs x format x dtype x (2 single + 3 multi-layer scale forms)
+    for bs, fmt, dt, form in cases:
+        p = f"{bs}/{fmt}/{dt}/{form}"
+        slots, gslots = g[f"{bs}/slots"], g[f"{bs}/gslots"]
+        kc = np.zeros_like(g[f"{p}/k_cache"])
+        vc = np.zeros_like(g[f"{p}/v_cache"])
+        ks, vs = g[f"{p}/k_scale"], g[f"{p}/v_scale"]
+        if form.startswith("ml_"):
+            O.kv_merged_linear_to_paged_fp8_multi_layer(g[f"{p}/merged"], kc, vc, slots, ks, vs, fp8_format=fmt, lin_dtype=dt)
+            out = O.kv_paged_fp8_to_merged_linear_multi_layer(kc, vc, gslots, ks, vs, out_dtype=dt, fp8_format=fmt)
+        else:
+            O.kv_merged_linear_to_paged_fp8(g[f"{p}/merged"], kc, vc, slots, ks, vs, fp8_format=fmt, lin_dtype=dt)
+            out = O.kv_paged_fp8_to_merged_linear(kc, vc, gslots, ks, vs, out_dtype=dt, fp8_format=fmt)
+        assert same_bits(kc, g[f"{p}/k_cache"]) and same_bits(vc, g[f"{p}/v_cache"]), p
+        assert same_bits(out, g[f"{p}/gather"]), p
+
+
+def test_multi_pool_rows():
+    g = np.load(GOLDEN / "pools.npz")
+    idx = g["indices"]
+    for direction in ("H2D", "D2H"):
+        n = len({k.split("/")[1] for k in g.files if k.startswith(direction)})
+        pools = [(list(g[f"{direction}/{p}/src"]), [d.copy() for d in g[f"{direction}/{p}/dst_in"]]) for p in range(n)]
+        O.kv_copy_paged_rows_multi_pool(pools, idx)
+        for p, (_, dsts) in enumerate(pools):
+            assert same_bits(np.stack(dsts), g[f"{direction}/{p}/dst_out"]), (direction, p)

@@ -6,8 +6,10 @@ engine that reserved its HBM up front and scatters inside its step loop, or a
 foreign-language caller holding only raw pointers from another framework's
 allocator); its duplicate-slot scratch is a static device array inside the
 library.  Two calls in a row must both match the regular entry point bit for
-bit (the second call must not see the first call's scratch contents), and a
-call above the slot limit must be refused without touching anything.
+bit (the second call must not see the first call's scratch contents), also at
+exactly the slot limit; a warmed-up call must leave the device's free memory
+unchanged; and a call above the slot limit must be refused without touching
+anything.
 
 This file is named so pytest collects it last.
 """
@@ -99,3 +101,43 @@ def test_static_scratch_scatter_rejects_oversized_calls(cuda_device):
     assert b"static scratch limit" in lib.mak_last_error()
     torch.cuda.synchronize()
     assert torch.count_nonzero(paged[0]) == 0
+
+
+def test_static_scratch_scatter_at_the_slot_limit_allocates_nothing(cuda_device):
+    """A call of exactly MAK_STATIC_SCATTER_MAX_SLOTS slots (the size at which the hash keys,
+    hash values and resolved-slot vector fill the fixed array) matches the workspace scatter,
+    twice; and once warmed up, a static call leaves the device's free memory unchanged."""
+    from musa_aiter import _native
+
+    lib = _native.load()
+    g = torch.Generator(device="cuda").manual_seed(12)
+    planes, nb, bs, hidden = 2, 8192, 16, 256
+    base = [torch.randn((nb, bs, hidden), device="cuda", generator=g).to(torch.bfloat16) for _ in range(planes)]
+    paged_a = [b.clone() for b in base]
+    paged_b = [b.clone() for b in base]
+    for call in range(2):
+        linear = [torch.randn((MAX_SLOTS, hidden), device="cuda", generator=g).to(torch.bfloat16) for _ in range(planes)]
+        slots = torch.randint(-1, nb * bs // (2 + call), (MAX_SLOTS,), device="cuda", generator=g)
+        slots[-4096:] = slots[:4096]  # duplicates across the whole call: the late copies win
+        _scatter_both(lib, linear, paged_a, paged_b, slots, 0)
+        for a, b in zip(paged_a, paged_b):
+            assert torch.equal(a.view(torch.int16), b.view(torch.int16)), f"call {call}"
+
+    # free device memory across a warmed-up static call (no workspace, no allocator)
+    ld, la = _planes(linear, 1)
+    pa, pa_arr = _planes(paged_a, bs)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    row_bytes = hidden * 2
+
+    def static_call():
+        rc = lib.mak_rows_scatter_static(ctypes.byref(ld), ctypes.byref(pa), None, row_bytes,
+                                         ctypes.c_void_p(slots.data_ptr()), _native.MAK_DT_I64, slots.numel(), 0, stream)
+        assert rc == 0, lib.mak_last_error()
+
+    static_call()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        static_call()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0

@@ -656,8 +656,9 @@ def run_e2e(args, d: Dist, caches, mem, slots_cpu, P, P_all):
     per_rank_ms = [r[0] for r in d.gather([ms_rank])]
     ms = max(per_rank_ms)
     del host_mem
-    # Ceiling: per rank, the slower direction of its concurrent PCIe copy moves its P bytes.
-    ceil_ms = max(P / (min(h, dd) * 1e9) * 1e3 for h, dd in pcie)
+    # Ceiling: per rank, its 2P bytes (P each way) at the summed rate of its two directions
+    # running at once; the slowest rank bounds the step.
+    ceil_ms = max(2 * P / ((h + dd) * 1e9) * 1e3 for h, dd in pcie)
     value = 4 * P_all / (ms * 1e-3) / 1e9
     ceiling = 4 * P_all / (ceil_ms * 1e-3) / 1e9
     return {
@@ -670,8 +671,9 @@ def run_e2e(args, d: Dist, caches, mem, slots_cpu, P, P_all):
         "per_rank_ms": [round(x, 2) for x in per_rank_ms],
         "pcie_gbs_per_rank": [{"h2d": round(h, 1), "d2h": round(dd, 1)} for h, dd in pcie],
         "ceiling": {"value": round(ceiling, 3), "unit": "GB/s", "frac": round(value / ceiling, 4),
-                    "how": "every rank copies its whole buffer D2H and H2D at once, all ranks together; per rank the "
-                           "slower direction sets the time its P bytes need; the slowest rank bounds the step"},
+                    "how": "every rank copies its whole buffer D2H and H2D at once, all ranks together; per rank "
+                           "its 2P bytes move at the sum of the two directions' rates; the slowest rank bounds the "
+                           "step (device work hidden)"},
         "numa": numa,
         "path": "pinned host slots -> device; lmcache_kv_paged_to_buffer (this rank's layers); buffer D2H to pinned "
                 "host and H2D back per (kv, layer) slice on two copy streams (both PCIe directions at once); "

@@ -80,6 +80,8 @@ def parse_args():
                     help="cfg2 (default) is the headline run; the others time one config alone (profiling), "
                          "'ops' times each remaining kvcache op once")
     ap.add_argument("--tokens", type=int, default=8192, help="cfg3 batch tokens (256 decode / 8192 prefill)")
+    ap.add_argument("--mla-layers", type=int, default=8,
+                    help="layers of --workload cfg5 / cfg5-fp8 run alone (the configs block uses the 61-layer model)")
     ap.add_argument("--ops", default=None,
                     help="--workload ops: comma-separated name fragments; only the matching ops run (profiling one op)")
     return ap.parse_args()
@@ -812,7 +814,7 @@ def setup_workload(args, w: str, dev, rank: int, world: int):
                "scaling": "weak (10 layers per rank: the 80-layer model's shard at N=8)"}
         return cfg, 4 * 2 * nl * tot * nh * hs * 2, step, "rows_kernel (2 x NL planes per launch)"
     if w == "cfg5":
-        lay = rank_layers(61, world, rank) if args.workload == "cfg2" else range(8)
+        lay = rank_layers(61, world, rank) if args.workload == "cfg2" else range(args.mla_layers)
         nl, nb, bs, kvd, ped = len(lay), args.blocks if args.workload != "cfg2" and args.blocks else 16384, 64, 512, 64
         g2 = torch.Generator().manual_seed(2)
         nreq = args.requests if args.workload == "cfg5" else 256
@@ -831,7 +833,7 @@ def setup_workload(args, w: str, dev, rank: int, world: int):
                "scaling": "strong (61 layers split over the ranks)" if args.workload == "cfg2" else "single GPU"}
         return cfg, 4 * nl * tot * (kvd + ped) * 2, step, "rows_kernel (MLA latent + rope rows)"
     if w == "cfg5-fp8":
-        lay = rank_layers(61, world, rank) if args.workload == "cfg2" else range(8)
+        lay = rank_layers(61, world, rank) if args.workload == "cfg2" else range(args.mla_layers)
         nl, nb, bs, kvd, ped = len(lay), args.blocks if args.workload != "cfg2" and args.blocks else 16384, 64, 512, 64
         g2 = torch.Generator().manual_seed(2)
         nreq = args.requests if args.workload == "cfg5-fp8" else 256

@@ -512,8 +512,11 @@ MAK_API int mak_mla_fp8_rows_store_owned(const mak_mla_linear_desc* lin, const m
  * to fp8_max, inf and nan), adds to counts[0] the FP8 codes that differ and to
  * counts[1] the finite quotients >= 2^-14 in magnitude that differ in any bit
  * (device memory, 2 x uint64, zeroed by the caller).  Scales outside the fast range ([2^-60, 2^16]) take
- * the IEEE division in the store and are not counted.  No reference
- * counterpart: a test entry point.
+ * the IEEE division in the store and are not counted.  Every call also checks
+ * the group scale of the two-token store (amax / fp8_max by one multiply and a
+ * correction step) against the IEEE division for every finite non-negative
+ * 16-bit amax, adding differences to counts[1].  No reference counterpart: a
+ * test entry point.
  */
 MAK_API int mak_fp8_quotient_selfcheck(int32_t elem_dtype, int32_t fp8_format, int32_t scale_exp, uint64_t* counts,
                                        void* stream);

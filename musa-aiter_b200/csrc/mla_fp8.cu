@@ -4,10 +4,20 @@
 // next to its scales and the unquantised rope part, one row per token and
 // layer:  [kv_dim codes][kv_dim/128 fp32 scales][pe_dim rope elements].
 //
-// One warp per (token, layer): lane l owns E = kv_dim / 32 consecutive values
-// (16-byte loads), the group amax is a shuffle reduction over the 128 / E lanes
-// of a group, the codes leave as one E-byte store per lane.  The element codec
-// is the musa-aiter reference rule (fp8.cuh).  grid = (token warps, layers).
+// kv_dim 512 (the DeepSeek shape) with rope rows of at most 128 bytes takes the
+// pair kernels: a warp moves two tokens at once, a half-warp per token and 32
+// values per lane, so the per-token work that does not depend on the values
+// (slot and owner lookups, address arithmetic, the group scale, the loop) is
+// shared by two tokens; slots and offsets are 32-bit after one range check.
+// The store keeps the next pair's inputs in registers; the load streams rows
+// through a per-warp ring of shared-memory stages filled by cp.async, with the
+// slots of 16 pairs fetched by one warp load.
+//
+// Other shapes: one warp per (token, layer): lane l owns E = kv_dim / 32
+// consecutive values (16-byte loads), the group amax is a shuffle reduction
+// over the 128 / E lanes of a group, the codes leave as one E-byte store per
+// lane.  The element codec is the musa-aiter reference rule (fp8.cuh).
+// grid = (token warps or pairs, layers).
 #include <algorithm>
 
 #include "common.cuh"
@@ -365,6 +375,341 @@ __global__ void __launch_bounds__(kMlaThreads) mla_fp8_load_kernel(const __grid_
   }
 }
 
+// ---- pair kernels (kv_dim 512, rope rows of at most 128 bytes) --------------
+
+// max(|a|, |b|) per 16-bit half with NaN propagation (the result's sign bits
+// are not meaningful); a non-finite input leaves a magnitude at or above the
+// format's infinity pattern.
+template <typename T>
+__device__ __forceinline__ uint32_t amax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+template <>
+__device__ __forceinline__ uint32_t amax2<__half>(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// amax / fp8_max rounded to nearest in fp32 without a division: Markstein's
+// correction step with the constant reciprocal (see fast_quot in fp8.cuh),
+// exact for every finite 16-bit amax >= 2^-100 (mak_fp8_quotient_selfcheck
+// compares it with the IEEE division for all of them); smaller ones divide.
+template <int F>
+__device__ __forceinline__ float group_scale(float amax) {
+  constexpr float M = F == MAK_FP8_E4M3 ? 448.f : 57344.f;
+  constexpr float Y = F == MAK_FP8_E4M3 ? (1.f / 448.f) : (1.f / 57344.f);
+  if (amax >= 0x1p-100f) {
+    const float q0 = __fmul_rn(amax, Y);
+    return __fmaf_rn(__fmaf_rn(-q0, M, amax), Y, q0);
+  }
+  return __fdiv_rn(amax, M);
+}
+
+// Slot i as a row index below num_rows, or -1 (negative or out of range).
+template <bool I64>
+__device__ __forceinline__ int slot_row(const MlaLaunch& p, int64_t i) {
+  const int64_t v = I64 ? static_cast<int64_t>(__ldg(reinterpret_cast<const long long*>(p.idx) + i))
+                        : static_cast<int64_t>(__ldg(reinterpret_cast<const int*>(p.idx) + i));
+  return (v >= 0 && v < p.num_rows) ? static_cast<int>(v) : -1;
+}
+
+// Row address from a row index (rows_per_block a power of two; block and row
+// strides below 2^32 and rows below 2^31, checked on the host).
+__device__ __forceinline__ unsigned char* row_at(const MlaLaunch& p, unsigned char* plane, int r) {
+  const uint32_t b = static_cast<uint32_t>(r) >> p.lg_rows;
+  const uint32_t o = static_cast<uint32_t>(r) & ((1u << p.lg_rows) - 1u);
+  return plane + (static_cast<uint64_t>(b) * static_cast<uint32_t>(p.block_stride) +
+                  static_cast<uint64_t>(o) * static_cast<uint32_t>(p.row_stride));
+}
+
+// Inputs of one token of a store pair, per lane: 32 values, 8 rope bytes.
+struct PairIn {
+  uint4 v[4];
+  uint2 pe;
+};
+
+// Quantise one token (the calling half-warp's) and write its row.  Lane j of
+// the half owns values [32j, 32j + 32): a 128-value group is 4 lanes.
+template <typename T, int F, bool OWN>
+__device__ __forceinline__ void pair_store_token(const MlaLaunch& p, unsigned char* plane, const PairIn& in, int row,
+                                                 unsigned long long own, uint32_t epoch, int tt, int j) {
+  const uint32_t wd[16] = {in.v[0].x, in.v[0].y, in.v[0].z, in.v[0].w, in.v[1].x, in.v[1].y, in.v[1].z, in.v[1].w,
+                           in.v[2].x, in.v[2].y, in.v[2].z, in.v[2].w, in.v[3].x, in.v[3].y, in.v[3].z, in.v[3].w};
+  uint32_t m8[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m8[i] = amax2<T>(wd[2 * i], wd[2 * i + 1]);
+  uint32_t m = amax2<T>(amax2<T>(amax2<T>(m8[0], m8[1]), amax2<T>(m8[2], m8[3])),
+                        amax2<T>(amax2<T>(m8[4], m8[5]), amax2<T>(m8[6], m8[7])));
+  m &= 0x7FFF7FFFu;
+  const uint32_t mraw = max(m & 0xFFFFu, m >> 16);
+  const bool all_finite = mraw < kInfBits<T>;
+  float amax = bits_to_f32<T>(mraw);
+  if (!all_finite) {  // rare: the amax over this lane's finite values only
+    amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float a = fabsf(bits_to_f32<T>(wd[i] & 0xFFFFu)), b = fabsf(bits_to_f32<T>(wd[i] >> 16));
+      if (a <= 3.40282346638528859812e+38f) amax = fmaxf(amax, a);
+      if (b <= 3.40282346638528859812e+38f) amax = fmaxf(amax, b);
+    }
+  }
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const float scale = group_scale<F>(amax);
+  uint32_t codes[8];
+  if (fast_quot_ok(scale) && all_finite) {
+    const QuotPair qc = quot_pair(scale, __frcp_rn(scale));
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      codes[i] = fp8_encode2_quot_finite<F>(bits_to_f32<T>(wd[2 * i] & 0xFFFFu), bits_to_f32<T>(wd[2 * i] >> 16), qc) |
+                 (fp8_encode2_quot_finite<F>(bits_to_f32<T>(wd[2 * i + 1] & 0xFFFFu), bits_to_f32<T>(wd[2 * i + 1] >> 16),
+                                             qc) << 16);
+  } else if (fast_quot_ok(scale)) {
+    const float y = __frcp_rn(scale);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const FastQuot a = fast_quot(bits_to_f32<T>(wd[2 * i] & 0xFFFFu), scale, y);
+      const FastQuot b = fast_quot(bits_to_f32<T>(wd[2 * i] >> 16), scale, y);
+      const FastQuot c = fast_quot(bits_to_f32<T>(wd[2 * i + 1] & 0xFFFFu), scale, y);
+      const FastQuot d = fast_quot(bits_to_f32<T>(wd[2 * i + 1] >> 16), scale, y);
+      codes[i] = fp8_encode2s_bounded<F>(a.q0, a.q1, b.q0, b.q1) | (fp8_encode2s_bounded<F>(c.q0, c.q1, d.q0, d.q1) << 16);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t lo = fp8_encode2<F>(__fdiv_rn(bits_to_f32<T>(wd[2 * i] & 0xFFFFu), scale),
+                                         __fdiv_rn(bits_to_f32<T>(wd[2 * i] >> 16), scale));
+      const uint32_t hi = fp8_encode2<F>(__fdiv_rn(bits_to_f32<T>(wd[2 * i + 1] & 0xFFFFu), scale),
+                                         __fdiv_rn(bits_to_f32<T>(wd[2 * i + 1] >> 16), scale));
+      codes[i] = lo | (hi << 16);
+    }
+  }
+  const bool write = row >= 0 && (!OWN || (static_cast<uint32_t>(own >> 32) == epoch &&
+                                            static_cast<uint32_t>(own) == static_cast<uint32_t>(tt)));
+  if (write) {
+    unsigned char* dst = row_at(p, plane, row);
+    reinterpret_cast<uint4*>(dst + j * 32)[0] = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+    reinterpret_cast<uint4*>(dst + j * 32)[1] = make_uint4(codes[4], codes[5], codes[6], codes[7]);
+    if ((j & 3) == 0) reinterpret_cast<float*>(dst + 512)[j >> 2] = scale;
+    if (j * 8 < p.pe_bytes) *reinterpret_cast<uint2*>(dst + 528 + j * 8) = in.pe;
+  }
+}
+
+// Store, two tokens per warp: tokens 2q and 2q + 1 of pair q (q = warp, warp +
+// warps, ...); the next pair's inputs and slots load while this pair is
+// encoded, its owner entries one pair ahead, slots two pairs ahead.
+template <typename T, int F, bool OWN, bool I64>
+__global__ void __launch_bounds__(256, 3) mla_fp8_store2_kernel(const __grid_constant__ MlaLaunch p) {
+  const int lane = threadIdx.x & 31, hl = lane >> 4, j = lane & 15;
+  const int layer = blockIdx.y;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int n = static_cast<int>(p.num_tokens);
+  const int npairs = (n + 1) >> 1;
+  unsigned char* plane = reinterpret_cast<unsigned char*>(p.cache[layer]);
+  pdl_wait();
+  pdl_trigger();
+  if (w >= npairs) return;
+  const int tstep = 2 * nw;
+  int t = 2 * w + hl;  // this half's token
+  const unsigned char* kvp = p.kv + layer * p.kv_sl + j * 64 + static_cast<int64_t>(t) * p.kv_st;
+  const unsigned char* pep = p.pe + layer * p.pe_sl + j * 8 + static_cast<int64_t>(t) * p.pe_st;
+  const int64_t kv_inc = static_cast<int64_t>(tstep) * p.kv_st, pe_inc = static_cast<int64_t>(tstep) * p.pe_st;
+  const bool pe_lane = j * 8 < p.pe_bytes;
+  const uint32_t epoch = static_cast<uint32_t>(p.tag_hi >> 32);
+  int64_t st = t;  // token whose slot loads next
+  auto fetch = [&](int tt, PairIn& in) {
+    if (tt < n) {
+      const uint4* src = reinterpret_cast<const uint4*>(kvp);
+      in.v[0] = src[0];
+      in.v[1] = src[1];
+      in.v[2] = src[2];
+      in.v[3] = src[3];
+      in.pe = pe_lane ? *reinterpret_cast<const uint2*>(pep) : make_uint2(0u, 0u);
+    }
+    kvp += kv_inc;
+    pep += pe_inc;
+  };
+  auto next_slot = [&]() -> int {
+    const int r = st < n ? slot_row<I64>(p, st) : -1;
+    st += tstep;
+    return r;
+  };
+  auto owner_of = [&](int r) -> unsigned long long { return (OWN && r >= 0) ? __ldcg(p.owner + r) : 0ull; };
+  PairIn a, b;
+  fetch(t, a);
+  int r0 = next_slot(), r1 = next_slot();
+  unsigned long long o0 = owner_of(r0);
+  // Two input buffers used in turn (no register copies between pairs).
+  while (true) {
+    int tn = t + tstep;
+    bool more = tn - hl < n;  // the next pair exists (warp-uniform)
+    if (more) fetch(tn, b);
+    unsigned long long o1 = owner_of(r1);
+    int r2 = next_slot();
+    pair_store_token<T, F, OWN>(p, plane, a, r0, o0, epoch, t, j);
+    if (!more) break;
+    t = tn;
+    r0 = r1;
+    r1 = r2;
+    o0 = o1;
+    tn = t + tstep;
+    more = tn - hl < n;
+    if (more) fetch(tn, a);
+    o1 = owner_of(r1);
+    r2 = next_slot();
+    pair_store_token<T, F, OWN>(p, plane, b, r0, o0, epoch, t, j);
+    if (!more) break;
+    t = tn;
+    r0 = r1;
+    r1 = r2;
+    o0 = o1;
+  }
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// 16 codes (one 16-byte chunk) of one group -> 16 elements (32 bytes) at dst.
+template <typename T, int F>
+__device__ __forceinline__ void decode_chunk16(uint4 c, float sc, bool have, uint4* dst) {
+  const uint32_t cw4[4] = {c.x, c.y, c.z, c.w};
+  if (have && fp8_ftz_scale_ok<F>(sc)) {
+    const float sf = __fmul_rn(sc, fp8_ftz_bias<F>());  // exact: a power of two
+    const uint64_t sf2 = f2_pack(sf, sf);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t cw = cw4[2 * h + (i >> 1)];
+        const uint32_t x0 = (i & 1) ? (cw << 8) : (cw << 24);
+        const uint32_t x1 = (i & 1) ? cw : (cw << 16);
+        float v0, v1;
+        f2_unpack(f2_mul_ftz(f2_pack(fp8_raw_top<F>(x0), fp8_raw_top<F>(x1)), sf2), v0, v1);
+        o[i] = pack2<T>(v0, v1);
+      }
+      dst[h] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else if (have) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t cw = cw4[2 * h + (i >> 1)];
+        const int b = 2 * (i & 1);
+        const uint32_t x0 = __byte_perm(cw, 0u, 0x0444u | (b << 12));
+        const uint32_t x1 = __byte_perm(cw, 0u, 0x0444u | ((b + 1) << 12));
+        o[i] = pack2<T>(__fmul_rn(fp8_decode_top<F>(x0), sc), __fmul_rn(fp8_decode_top<F>(x1), sc));
+      }
+      dst[h] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else {
+    dst[0] = make_uint4(0u, 0u, 0u, 0u);
+    dst[1] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+constexpr int kMlaLoadStages = 4;  // ring stages per warp (a power of two)
+
+// Load, two tokens per warp: each warp streams its pairs' cache rows through a
+// ring of kMlaLoadStages shared-memory stages (cp.async, three stages in flight
+// while one is decoded); a half-warp takes one row: lane j decodes codes
+// [16j, 16j + 16) and [256 + 16j, 256 + 16j + 16) (conflict-free 16-byte shared
+// reads), the group scales come from one broadcast read.  Slots of 16 pairs
+// are loaded by one warp instruction, lane l holding pair l / 2, half l % 2.
+// Dynamic shared memory: warps x stages x 2 x row_bytes.
+template <typename T, int F, bool I64>
+__global__ void __launch_bounds__(256) mla_fp8_load2_kernel(const __grid_constant__ MlaLaunch p, unsigned char* kv_out,
+                                                            unsigned char* pe_out) {
+  constexpr int D = kMlaLoadStages;
+  extern __shared__ __align__(16) unsigned char mla_ring[];
+  const int lane = threadIdx.x & 31, hl = lane >> 4, j = lane & 15, wid = threadIdx.x >> 5;
+  const int rb = 528 + p.pe_bytes;  // row bytes, a multiple of 16
+  const int stage = 2 * rb;
+  unsigned char* my = mla_ring + wid * (D * stage) + hl * rb;
+  const int layer = blockIdx.y;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  const int w = blockIdx.x * (blockDim.x >> 5) + wid;
+  const int n = static_cast<int>(p.num_tokens);
+  const int npairs = (n + 1) >> 1;
+  unsigned char* plane = reinterpret_cast<unsigned char*>(p.cache[layer]);
+  pdl_wait();
+  pdl_trigger();
+  if (w >= npairs) return;
+  const int n_my = (npairs - 1 - w) / nw + 1;  // pairs of this warp
+  const int tail_chunks = rb / 16 - 32;         // chunks of a row beyond the first 512 bytes
+  auto slot_batch = [&](int kb) -> int {
+    const int k = kb + (lane >> 1);
+    const int tt = 2 * (w + k * nw) + (lane & 1);
+    return (k < n_my && tt < n) ? slot_row<I64>(p, tt) : -1;
+  };
+  int cur = slot_batch(0), nxt = slot_batch(16);
+  uint32_t have = 0;  // bit i: the row of pair k + i (this half) was fetched
+  auto issue = [&](int ki, int bit) {
+    const int r = __shfl_sync(0xffffffffu, cur, 2 * (ki & 15) + hl);
+    if (ki < n_my && r >= 0) {
+      const unsigned char* src = row_at(p, plane, r) + j * 16;
+      unsigned char* dst = my + (ki & (D - 1)) * stage + j * 16;
+      cp_async16(dst, src);
+      cp_async16(dst + 256, src + 256);
+      if (j < tail_chunks) cp_async16(dst + 512, src + 512);
+      have |= 1u << bit;
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int i = 0; i < D - 1; ++i) issue(i, i);
+  int t = 2 * w + hl;
+  unsigned char* kvo = kv_out + layer * p.kv_sl + j * 32 + static_cast<int64_t>(t) * p.kv_st;
+  unsigned char* peo = pe_out + layer * p.pe_sl + j * 8 + static_cast<int64_t>(t) * p.pe_st;
+  const int64_t kvo_inc = static_cast<int64_t>(2 * nw) * p.kv_st, peo_inc = static_cast<int64_t>(2 * nw) * p.pe_st;
+  const bool pe_lane = j * 8 < p.pe_bytes;
+  for (int k = 0; k < n_my; ++k) {
+    const int ki = k + D - 1;
+    if ((ki & 15) == 0) {
+      cur = nxt;
+      nxt = slot_batch(ki + 16);
+    }
+    issue(ki, D - 1);
+    cp_async_wait<D - 1>();
+    __syncwarp();
+    const unsigned char* rs = my + (k & (D - 1)) * stage;
+    const bool ok = have & 1u;
+    have >>= 1;
+    uint4 c0 = make_uint4(0u, 0u, 0u, 0u), c1 = c0;
+    float4 sc = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint2 pev = make_uint2(0u, 0u);
+    if (ok) {
+      c0 = *reinterpret_cast<const uint4*>(rs + j * 16);
+      c1 = *reinterpret_cast<const uint4*>(rs + 256 + j * 16);
+      sc = *reinterpret_cast<const float4*>(rs + 512);
+      if (pe_lane) pev = *reinterpret_cast<const uint2*>(rs + 528 + j * 8);
+    }
+    __syncwarp();  // the stage is refilled by the next iteration's issue
+    if (t < n) {
+      const bool g1 = j >= 8;  // chunk j lies in group j / 8, chunk j + 16 in group 2 + j / 8
+      decode_chunk16<T, F>(c0, g1 ? sc.y : sc.x, ok, reinterpret_cast<uint4*>(kvo));
+      decode_chunk16<T, F>(c1, g1 ? sc.w : sc.z, ok, reinterpret_cast<uint4*>(kvo + 512));
+      if (pe_lane) *reinterpret_cast<uint2*>(peo) = pev;
+    }
+    t += 2 * nw;
+    kvo += kvo_inc;
+    peo += peo_inc;
+  }
+}
+
 static int64_t mla_row_bytes(int64_t kv_dim, int64_t pe_dim, int elem_bytes) {
   return kv_dim + (kv_dim / 128) * 4 + pe_dim * elem_bytes;
 }
@@ -426,9 +771,58 @@ static int mla_prepare(const mak_mla_linear_desc* lin, const mak_rows_desc* cach
   return MAK_OK;
 }
 
+// Can this call take the pair kernels?  kv_dim 512, rope rows of at most 128
+// bytes (the load: a multiple of 16, so rows stay 16-byte aligned for
+// cp.async), rows_per_block a power of two, 32-bit row indices and strides,
+// fewer than 2^30 tokens.
+static bool mla_pair_ok(const MlaLaunch& L, bool store) {
+  return L.kv_dim == 512 && L.pe_bytes <= 128 && (store || L.pe_bytes % 16 == 0) && L.lg_rows >= 0 &&
+         L.num_rows < (int64_t{1} << 31) && L.block_stride < (int64_t{1} << 32) && L.row_stride < (int64_t{1} << 32) &&
+         L.num_tokens < (int64_t{1} << 30);
+}
+
+template <bool STORE, typename T, int F, bool OWN, bool I64>
+static int launch_mla_pairs(MlaLaunch& L, int64_t layers, unsigned char* kv_out, unsigned char* pe_out, cudaStream_t st,
+                            const mak_rows_desc* cache) {
+  const void* kern = STORE ? reinterpret_cast<const void*>(mla_fp8_store2_kernel<T, F, OWN, I64>)
+                           : reinterpret_cast<const void*>(mla_fp8_load2_kernel<T, F, I64>);
+  const size_t smem = STORE ? 0 : static_cast<size_t>(kMlaThreads / 32) * kMlaLoadStages * 2 * (528 + L.pe_bytes);
+  const int64_t resident = static_cast<int64_t>(blocks_per_sm(kern, kMlaThreads, smem)) * sm_count();
+  const int64_t pairs = (L.num_tokens + 1) / 2;
+  for (int64_t l0 = 0; l0 < layers; l0 += kMlaPlanes) {
+    const int64_t nl = std::min<int64_t>(kMlaPlanes, layers - l0);
+    for (int64_t q = 0; q < nl; ++q) L.cache[q] = cache->plane_ptrs[l0 + q];
+    const int64_t want = (pairs + (kMlaThreads / 32) - 1) / (kMlaThreads / 32);
+    const int64_t cap = std::max<int64_t>(1, (4 * resident + nl - 1) / nl);
+    const dim3 grid(static_cast<unsigned>(std::min(want, cap)), static_cast<unsigned>(nl));
+    MlaLaunch P = L;
+    P.kv = L.kv + l0 * L.kv_sl;
+    P.pe = L.pe + l0 * L.pe_sl;
+    const int rc = STORE ? launch_pdl("mla_fp8_store2_kernel", mla_fp8_store2_kernel<T, F, OWN, I64>, grid,
+                                      dim3(kMlaThreads), 0, st, P)
+                         : launch_pdl("mla_fp8_load2_kernel", mla_fp8_load2_kernel<T, F, I64>, grid, dim3(kMlaThreads),
+                                      smem, st, P, kv_out + l0 * L.kv_sl, pe_out + l0 * L.pe_sl);
+    if (rc) return rc;
+  }
+  return MAK_OK;
+}
+
+template <bool STORE, typename T, int F>
+static int launch_mla_pairs(MlaLaunch& L, int64_t layers, unsigned char* kv_out, unsigned char* pe_out, cudaStream_t st,
+                            const mak_rows_desc* cache) {
+  const bool own = STORE && L.owner != nullptr;
+  if (L.idx64) {
+    return own ? launch_mla_pairs<STORE, T, F, true, true>(L, layers, kv_out, pe_out, st, cache)
+               : launch_mla_pairs<STORE, T, F, false, true>(L, layers, kv_out, pe_out, st, cache);
+  }
+  return own ? launch_mla_pairs<STORE, T, F, true, false>(L, layers, kv_out, pe_out, st, cache)
+             : launch_mla_pairs<STORE, T, F, false, false>(L, layers, kv_out, pe_out, st, cache);
+}
+
 template <bool STORE, typename T, int F, int E>
 static int launch_mla(MlaLaunch& L, int64_t layers, unsigned char* kv_out, unsigned char* pe_out, cudaStream_t st,
                       const mak_rows_desc* cache) {
+  if (E == 16 && mla_pair_ok(L, STORE)) return launch_mla_pairs<STORE, T, F>(L, layers, kv_out, pe_out, st, cache);
   const void* kern = STORE ? reinterpret_cast<const void*>(mla_fp8_store_kernel<T, F, E>)
                            : reinterpret_cast<const void*>(mla_fp8_load_kernel<T, F, E>);
   const int64_t resident = static_cast<int64_t>(blocks_per_sm(kern, kMlaThreads, 0)) * sm_count();
@@ -480,10 +874,19 @@ static int dispatch(MlaLaunch& L, const mak_mla_linear_desc* lin, const mak_rows
 // non-finite inputs), and counts (a) FP8 codes that differ from
 // fp8_encode(x / s) and (b) quotients with |x / s| >= 2^-14 that differ in any
 // bit.  Only scales the store kernel sends down the fast path are tested.
+// Threads k < 2^15 also check group_scale(amax) for the 16-bit amax of bits k.
 template <typename T, int F>
 __global__ void fp8_quotient_check_kernel(int scale_exp, unsigned long long* counts) {
   const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
   if (k >= (1u << 23)) return;
+  if (k < 0x8000u) {
+    // the pair store's group scale: group_scale(amax) against the IEEE division for every
+    // finite non-negative 16-bit amax (counted as a differing quotient)
+    const float amax = bits_to_f32<T>(k);
+    if (amax <= 3.40282346638528859812e+38f &&
+        __float_as_uint(group_scale<F>(amax)) != __float_as_uint(__fdiv_rn(amax, fp8_max_of<F>())))
+      atomicAdd(counts + 1, 1ull);
+  }
   const float s = __uint_as_float((static_cast<uint32_t>(scale_exp + 127) << 23) | k);
   unsigned long long bad_code = 0, bad_quot = 0;
   if (fast_quot_ok(s)) {

@@ -43,6 +43,10 @@ struct TileLaunch {
   int32_t slots64, n_kv, fill_zero, cache_vec, lin_vec, scale_mode, heads_per_step;
   int32_t window;       // tokens per warp window of the segment kernel (8, 16 or 32)
   int32_t plane_group;  // (kv, layer) planes a segment-kernel block walks per window
+  // Single-token launch (MODE 2): a window's heads are split into 2^head_split_shift groups,
+  // each a separate warp item, when the call has too few windows to fill the device (decode
+  // batches); 0 elsewhere.
+  int32_t head_split_shift;
   // Segment map (optional): the run launch (MODE 1) stores, per window of map_window tokens,
   // (epoch << 2) | (a single-token run starts in it) | (a scatter run end of 2..G-1 tokens
   // starts in it) << 1; the single-token launch (MODE 2) and the run-end launch (MODE 3) skip
@@ -406,10 +410,17 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
   const uint32_t wmask = W >= 32 ? 0xffffffffu : ((1u << W) - 1u);
   const int64_t windows = p.windows;
   const int64_t wstride = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  // head groups of a MODE 2 item: heads [h_lo, h_lo + NHp)
+  const int hs_shift = MODE == 2 ? p.head_split_shift : 0;
+  const int NHp = NH >> hs_shift;
   pdl_wait();
   pdl_trigger();
 
-  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < windows; w += wstride) {
+  for (int64_t wi = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); wi < (windows << hs_shift);
+       wi += wstride) {
+    const int64_t w = wi >> hs_shift;
+    const int h_lo = static_cast<int>(wi & ((1 << hs_shift) - 1)) * NHp;
+    const int h_hi = h_lo + NHp;
     const int64_t t0 = w * W;
     if (MODE != 1 && p.seg_map != nullptr) {
       // Skip the window when the run launch of this call found no single-token run starting in
@@ -519,9 +530,9 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
           // consecutive cache rows and each token-row access 64 contiguous bytes; items
           // (token, head, group) are walked with carried counters, two in flight per lane.
           const int gpr = hd >> 7;
-          const int items = len * NH * gpr;
+          const int items = len * NHp * gpr;
           const int64_t sd = p.c_sd;
-          int j = 0, h = 0, g = 0;
+          int j = 0, h = h_lo, g = 0;
           for (int i0 = 0; i0 < items; i0 += 2) {
             CT code[2][4];
             LT vals[2][4];
@@ -543,8 +554,8 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
                 }
                 if (++g == gpr) {
                   g = 0;
-                  if (++h == NH) {
-                    h = 0;
+                  if (++h == h_hi) {
+                    h = h_lo;
                     ++j;
                   }
                 }
@@ -573,8 +584,8 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
           // same (token, head, group) sequence with carried counters (no divisions), eight
           // elements in flight per lane.
           const int mpr = hd >> 5;
-          const int steps = len * NH * mpr;
-          int j = 0, h = 0, m = 0;
+          const int steps = len * NHp * mpr;
+          int j = 0, h = h_lo, m = 0;
           for (int s0 = 0; s0 < steps; s0 += 8) {
             CT cv[8];
             LT lv[8];
@@ -589,8 +600,8 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
                 else lv[k] = lin_l[(ts + j) * p.l_st + h * p.l_sh + d];
                 if (++m == mpr) {
                   m = 0;
-                  if (++h == NH) {
-                    h = 0;
+                  if (++h == h_hi) {
+                    h = h_lo;
                     ++j;
                   }
                 }
@@ -759,11 +770,20 @@ static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
   while (p.plane_group > 1 && windows * ((planes + p.plane_group - 1) / p.plane_group) < 4 * resident_warps)
     p.plane_group /= 2;
   const int64_t groups = (planes + p.plane_group - 1) / p.plane_group;
+  // Single tokens with few windows (decode batches): split each window's heads over up to
+  // num_heads warp items (head_dim a multiple of 32, power-of-two splits dividing num_heads).
+  p.head_split_shift = 0;
+  if (MODE == 2 && p.head_dim % 32 == 0) {
+    while ((windows << p.head_split_shift) * groups < 4 * resident_warps &&
+           p.num_heads % (int64_t{2} << p.head_split_shift) == 0)
+      ++p.head_split_shift;
+  }
+  const int64_t items = windows << p.head_split_shift;
   // About 4 device-fulls of CTAs, spread over the groups; each CTA walks windows grid-stride.
   // The run-end launch has work in few windows (sequence ends): one device-full.
   const int64_t target = static_cast<int64_t>(per_sm) * sm_count() * (MODE == 3 ? 1 : 4);
   int64_t gx = std::max<int64_t>(1, target / groups);
-  gx = std::min<int64_t>(gx, (windows + (threads / 32) - 1) / (threads / 32));
+  gx = std::min<int64_t>(gx, (items + (threads / 32) - 1) / (threads / 32));
   const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(groups));
   if (p.plane_group > 1)
     return launch_pdl("tile_seg_kernel", tile_seg_kernel<CT, LT, CODEC, SCATTER, MODE, true>, grid, dim3(threads), 0, st,
@@ -785,8 +805,9 @@ static int launch_tile_segments(TileLaunch& p, cudaStream_t st) {
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 static int launch_tile(TileLaunch& p, cudaStream_t st) {
   constexpr int VL = 16 / sizeof(LT);
-  // Segment path: 16-byte chunks on both sides; needs aligned chunks and whole linear vectors.
-  if (p.lin_vec && p.cache_vec && p.head_dim % VL == 0 && p.num_layers * p.n_kv <= 65535)
+  // Segment path: 16-byte chunks on both sides; needs aligned chunks and whole linear vectors
+  // (and fewer than 256 heads: the single-token walk packs a head index into 8 bits).
+  if (p.lin_vec && p.cache_vec && p.head_dim % VL == 0 && p.num_layers * p.n_kv <= 65535 && p.num_heads < 256)
     return launch_tile_segments<CT, LT, CODEC, SCATTER>(p, st);
   const int threads = 256;
   const size_t per_head = static_cast<size_t>(kTT) * (p.head_dim + VL) * sizeof(LT);

@@ -56,7 +56,7 @@ def _oracle_cache(cache: torch.Tensor) -> np.ndarray:
     return c.reshape(c.shape[0], -1, c.shape[-1]).copy()
 
 
-@pytest.mark.parametrize("kvd,ped", ((512, 64), (256, 32), (1024, 128), (512, 0)))
+@pytest.mark.parametrize("kvd,ped", ((512, 64), (256, 32), (1024, 128), (512, 0), (512, 8), (512, 24), (512, 72)))
 @pytest.mark.parametrize("dt", ("bfloat16", "float16"))
 def test_random_multi_layer_vs_oracle(cuda_device, kvd, ped, dt):
     g = torch.Generator().manual_seed(kvd + ped)
@@ -81,6 +81,55 @@ def test_random_multi_layer_vs_oracle(cuda_device, kvd, ped, dt):
     rk, rp = O.mla_fp8_rows_load(want, lslots.numpy(), kv_dim=kvd, pe_dim=ped, out_dtype=dt)
     eq(okv, rk, "load latent")
     eq(ope, rp, "load rope")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+@pytest.mark.parametrize("dt", ("bfloat16", "float16"))
+def test_pair_kernels_odd_counts_int32_and_workspace_path(cuda_device, dt, fmt, monkeypatch):
+    """kv_dim 512 moves two tokens per warp: odd token counts (the last pair has one token),
+    single tokens, int32 and int64 slots with negatives and duplicates, rope rows of 0 to 144
+    bytes, and the workspace last-writer path that CUDA graph capture takes next to the owner
+    table path of eager calls."""
+    g = torch.Generator().manual_seed(91)
+    for ped, t in ((64, 91), (8, 1), (24, 33), (72, 77), (0, 5), (64, 2)):
+        nl, nb, bs = 2, 7, 64
+        x = (torch.randn((nl, t, 512), generator=g) * 3).to(TORCH[dt])
+        pe = torch.randn((nl, t, ped), generator=g).to(TORCH[dt])
+        slots = torch.randint(-3, nb * bs, (t,), generator=g, dtype=torch.int64)
+        if t > 4:
+            slots[t - 1] = slots[1]  # duplicate: the last token wins
+        row = ma.mla_fp8_row_bytes(512, ped)
+        cache0 = torch.randint(0, 256, (nl, nb, bs, row), generator=g, dtype=torch.uint8)
+        want = _oracle_cache(cache0)
+        O.mla_fp8_rows_store(to_np(x), to_np(pe), want, slots.numpy(), in_dtype=dt, fp8_format=fmt)
+        xs, pes, ss = x.cuda(), pe.cuda(), slots.cuda()
+        cache = cache0.cuda()
+        assert ma.kv_mla_linear_to_paged_fp8_rows(xs, pes, cache, ss.to(torch.int32), fp8_format=fmt) is True
+        eq(cache.view(nl, nb * bs, row), want, f"store, owner table, int32 slots {ped, t}")
+        # the workspace path: a captured call replayed onto the original cache
+        cache2 = cache0.cuda()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # warm-up outside capture
+            ma.kv_mla_linear_to_paged_fp8_rows(xs, pes, cache2, ss, fp8_format=fmt)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with monkeypatch.context() as m:
+            m.setenv("MUSA_AITER_SKIP_VALIDATION", "1")  # the bounds check reads back: not capturable
+            with torch.cuda.graph(graph):
+                ma.kv_mla_linear_to_paged_fp8_rows(xs, pes, cache2, ss, fp8_format=fmt)
+        cache2.copy_(cache0.cuda())
+        graph.replay()
+        torch.cuda.synchronize()
+        del graph
+        eq(cache2.view(nl, nb * bs, row), want, f"store, workspace path (graph replay) {ped, t}")
+        for idx_dt in (torch.int64, torch.int32):
+            lslots = torch.cat([slots.flip(0), torch.tensor([-1])]).to(idx_dt)
+            okv, ope = ma.kv_paged_fp8_rows_to_mla_linear(cache, lslots.cuda(), kv_dim=512, pe_dim=ped,
+                                                          out_dtype=TORCH[dt], fp8_format=fmt)
+            rk, rp = O.mla_fp8_rows_load(want, lslots.numpy(), kv_dim=512, pe_dim=ped, out_dtype=dt, fp8_format=fmt)
+            eq(okv, rk, f"load latent {ped, t, idx_dt}")
+            eq(ope, rp, f"load rope {ped, t, idx_dt}")
 
 
 def test_flat_cache_strided_inputs_and_e5m2(cuda_device):

@@ -279,6 +279,55 @@ def test_random_slots_tile_multi_layer_vs_oracle(cuda_device, dt):
         eq(vd, rvc, "scatter v")
 
 
+@pytest.mark.parametrize("fmt", (None, "e4m3", "e5m2"))
+def test_decode_batch_head_split_vs_oracle(cuda_device, fmt):
+    """Decode-sized batches of random slots: the single-token launch splits each window's heads
+    over several warp items (num_heads 1..16, head_dim 64..256, splits of 1, 2 and up to 16 warps
+    per window), with negative and duplicate slots; gathers, scatters, FP8 stores and loads."""
+    g = torch.Generator().manual_seed(11)
+    for (nl, nb, nh, hd, bs, t) in [(2, 256, 8, 128, 16, 40), (1, 64, 6, 96, 16, 17), (3, 128, 16, 64, 16, 9),
+                                    (1, 64, 1, 256, 16, 33), (2, 96, 2, 128, 8, 64), (1, 300, 4, 128, 16, 200)]:
+        slots = torch.randperm(nb * bs, generator=g)[:t]
+        slots[::7] = -1
+        slots[5::11] = slots[3]
+        if fmt is None:
+            kc = torch.randn((nl, nb, nh, hd, bs), generator=g).to(torch.bfloat16)
+            vc = torch.randn((nl, nb, nh, hd, bs), generator=g).to(torch.bfloat16)
+            ok, ov = ma.kv_paged_to_linear_multi_layer(kc.cuda(), vc.cuda(), slots.cuda())
+            rk, rv = O.kv_paged_to_linear_multi_layer(to_np(kc), to_np(vc), slots.numpy())
+            eq(ok, rk, f"gather {nl, nb, nh, hd, bs, t}")
+            eq(ov, rv, f"gather {nl, nb, nh, hd, bs, t}")
+            kl = torch.randn((nl, t, nh, hd), generator=g).to(torch.bfloat16)
+            vl = torch.randn((nl, t, nh, hd), generator=g).to(torch.bfloat16)
+            kd, vd = kc.clone().cuda(), vc.clone().cuda()
+            ma.kv_linear_to_paged_multi_layer(kl.cuda(), vl.cuda(), kd, vd, slots.cuda())
+            rkc, rvc = to_np(kc), to_np(vc)
+            O.kv_linear_to_paged_multi_layer(to_np(kl), to_np(vl), rkc, rvc, slots.numpy())
+            eq(kd, rkc, f"scatter k {nl, nb, nh, hd, bs, t}")
+            eq(vd, rvc, f"scatter v {nl, nb, nh, hd, bs, t}")
+            continue
+        kl = (torch.randn((nl, t, nh, hd), generator=g) * 2.0).to(torch.bfloat16)
+        vl = (torch.randn((nl, t, nh, hd), generator=g) * 2.0).to(torch.bfloat16)
+        fmax = 448.0 if fmt == "e4m3" else 57344.0
+        ks = kl.float().abs().amax(dim=(1, 3)) / fmax
+        vs = vl.float().abs().amax() / fmax
+        kc = torch.randint(0, 256, (nl, nb, nh, hd, bs), generator=g, dtype=torch.uint8)
+        vc = torch.randint(0, 256, (nl, nb, nh, hd, bs), generator=g, dtype=torch.uint8)
+        kd, vd = kc.cuda(), vc.cuda()
+        ma.kv_linear_to_paged_fp8_multi_layer(kl.cuda(), vl.cuda(), kd, vd, slots.cuda(), ks.cuda(), vs.cuda(), fp8_format=fmt)
+        rkc, rvc = kc.numpy().copy(), vc.numpy().copy()
+        O.kv_linear_to_paged_fp8_multi_layer(to_np(kl), to_np(vl), rkc, rvc, slots.numpy(), ks.numpy(), vs.numpy(),
+                                             fp8_format=fmt)
+        eq(kd, rkc, f"fp8 store k {nl, nb, nh, hd, bs, t}")
+        eq(vd, rvc, f"fp8 store v {nl, nb, nh, hd, bs, t}")
+        ok, ov = ma.kv_paged_fp8_to_linear_multi_layer(kd, vd, slots.cuda(), ks.cuda(), vs.cuda(), out_dtype=torch.bfloat16,
+                                                       fp8_format=fmt)
+        rk, rv = O.kv_paged_fp8_to_linear_multi_layer(rkc, rvc, slots.numpy(), ks.numpy(), vs.numpy(), out_dtype="bfloat16",
+                                                      fp8_format=fmt)
+        eq(ok, rk, f"fp8 load k {nl, nb, nh, hd, bs, t}")
+        eq(ov, rv, f"fp8 load v {nl, nb, nh, hd, bs, t}")
+
+
 @pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
 def test_config3_fp8_random_slots_vs_oracle(cuda_device, fmt):
     """Config 3 style: randn*2 bf16, random unique slots, per-layer-head (E4M3) / scalar (E5M2) scales."""

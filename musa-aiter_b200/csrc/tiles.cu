@@ -157,6 +157,32 @@ __device__ __forceinline__ bool encode_chunk_bounded(const uint4 (&toks)[G], flo
   }
 }
 
+// Four 16-bit values -> four FP8 codes (byte i = code of x[i]) through the packed
+// division-free encoder when they are finite and |x| / scale stays below the FP8
+// maximum, as encode_chunk_bounded; false (nothing computed) otherwise or for
+// fp32 inputs.
+template <typename LT, int CODEC>
+__device__ __forceinline__ bool encode4_bounded(const LT (&x)[4], float sc, uint32_t* out) {
+  if constexpr (CODEC == 0 || sizeof(LT) != 2) {
+    return false;
+  } else {
+    constexpr uint32_t kInf = std::is_same<LT, __half>::value ? 0x7C00u : 0x7F80u;
+    constexpr float kBound = CODEC == MAK_FP8_E4M3 ? 447.99f : 57343.f;
+    if (!fast_quot_ok(sc)) return false;
+    uint32_t mraw = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mraw = max(mraw, static_cast<uint32_t>(*reinterpret_cast<const unsigned short*>(&x[i])) & 0x7FFFu);
+    if (mraw >= kInf) return false;
+    const float y = __frcp_rn(sc);
+    const unsigned short mbits = static_cast<unsigned short>(mraw);
+    if (!(__fmul_rn(to_f32<LT>(*reinterpret_cast<const LT*>(&mbits)), y) <= kBound)) return false;
+    const QuotPair qc = quot_pair(sc, y);
+    *out = fp8_encode2_quot_finite<CODEC>(to_f32<LT>(x[0]), to_f32<LT>(x[1]), qc) |
+           (fp8_encode2_quot_finite<CODEC>(to_f32<LT>(x[2]), to_f32<LT>(x[3]), qc) << 16);
+    return true;
+  }
+}
+
 // FP8 load of one full (R dims x G tokens) chunk through the flush-to-zero
 // decode of the MLA FP8 rows (fp8_raw_top + one flush-to-zero multiply by
 // scale * 2^(127 - bias), exact for scales in fp8_ftz_scale_ok's range): three
@@ -739,6 +765,158 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
 }
 
 // ---------------------------------------------------------------------------
+// FP8 single tokens (head_dim a multiple of 128): the single-token launch of
+// FP8 calls, in two phases per block.
+//   1. The block's warps find the single-token segments among its token range
+//      (one slot per lane plus the neighbours by shuffles: a token is a segment
+//      of its own when it starts one and the next token does not continue it,
+//      the same rule the window scans apply) and append (token, slot offset)
+//      to a shared-memory list.
+//   2. All warps walk list entry x plane x head x 128-dim group items: a lane
+//      takes dims lane + 32e (e < 4) of a group, so every cache access is one
+//      warp access to 32 consecutive cache rows; four items per warp in flight.
+// Nothing of phase 1 stays live in phase 2, so the kernel runs with few
+// registers and a full SM of warps: the single tokens are bound by DRAM sector
+// traffic (a token touches every sector of its head tile), and the number of
+// sector requests in flight decides the rate.
+// grid = (token ranges of tpc tokens, planes, head groups of hpc heads).
+// ---------------------------------------------------------------------------
+constexpr int kSingleMaxTok = 256;  // tokens per block, at most (8 scanning warps)
+constexpr int kSingleInFlight = 4;  // items per warp in flight
+
+template <typename LT, int CODEC, bool SCATTER>
+__global__ void __launch_bounds__(256, 4) tile_single_fp8_kernel(const __grid_constant__ TileLaunch p, int tpc, int hpc) {
+  using C = Codec<uint8_t, LT, CODEC>;
+  __shared__ int64_t s_off[kSingleMaxTok];  // slot's element offset in the plane: block * c_sb + in-block offset
+  __shared__ int s_tok[kSingleMaxTok];
+  __shared__ int s_cnt;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t n = p.n_tokens;
+  if (threadIdx.x == 0) s_cnt = 0;
+  pdl_wait();
+  pdl_trigger();
+  __syncthreads();
+  const int64_t cap = p.block_size < 32 ? p.block_size : 32;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * tpc + warp * 32;
+  if (warp * 32 < tpc && t0 < n) {
+    bool scan = true;
+    if (p.seg_map != nullptr) {
+      // the run launch of this call marked, per map window, whether a single-token run starts there
+      const int64_t m0 = t0 >> p.map_shift, m1 = (min(t0 + 32, n) - 1) >> p.map_shift;
+      const uint32_t tag = p.seg_epoch << 2;
+      uint32_t v = tag;
+      if (lane <= m1 - m0) v = p.seg_map[m0 + lane];
+      scan = !__all_sync(0xffffffffu, (v & ~3u) == tag && (v & 1u) == 0u);
+    }
+    if (scan) {
+      const int64_t t = t0 + lane;
+      const int64_t s = t < n ? token_slot<SCATTER>(p, t) : -1;
+      int64_t sp = __shfl_up_sync(0xffffffffu, s, 1);
+      int64_t sn = __shfl_down_sync(0xffffffffu, s, 1);
+      if (lane == 0) sp = t0 > 0 ? token_slot<SCATTER>(p, t0 - 1) : -1;
+      if (lane == 31) sn = t0 + 32 < n ? token_slot<SCATTER>(p, t0 + 32) : -1;
+      int64_t b = 0, o = 0;
+      if (s >= 0) split_slot(s, p.block_size, &b, &o);
+      const bool start = s >= 0 && (sp < 0 || s != sp + 1 || (o % cap) == 0);
+      const bool cont = sn >= 0 && sn == s + 1 && ((o + 1) % cap) != 0;
+      const bool single = start && !cont;
+      const uint32_t m = __ballot_sync(0xffffffffu, single);
+      int base = 0;
+      if (lane == 0 && m) base = atomicAdd(&s_cnt, __popc(m));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      if (single) {
+        const int k = base + __popc(m & ((1u << lane) - 1u));
+        s_tok[k] = static_cast<int>(t);
+        s_off[k] = b * p.c_sb + o;
+      }
+    }
+  }
+  __syncthreads();
+  const int cnt = s_cnt;
+  if (cnt == 0) return;
+  const int plane = blockIdx.y;
+  const int nl = static_cast<int>(p.num_layers);
+  const int64_t l = plane % nl;
+  const int kv = plane / nl;
+  const uint8_t* cache_r = reinterpret_cast<const uint8_t*>(p.cache[kv]) + l * p.c_sl;
+  uint8_t* cache_w = reinterpret_cast<uint8_t*>(p.cache[kv]) + l * p.c_sl;
+  LT* lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl;
+  const float* scl = p.scale[kv];
+  const int NH = static_cast<int>(p.num_heads);
+  const int h_lo = blockIdx.z * hpc;
+  const int gpr = static_cast<int>(p.head_dim) >> 7;
+  const int per_entry = hpc * gpr;
+  const int64_t sd = p.c_sd;
+  // this warp's contiguous share of the cnt x per_entry items, walked with carried counters
+  const int total = cnt * per_entry;
+  const int share = (total + 7) >> 3;
+  int q = warp * share;
+  const int q_end = min(q + share, total);
+  if (q >= q_end) return;
+  int e = q / per_entry;
+  int j = q - e * per_entry;
+  int hh = j / gpr;
+  int g = j - hh * gpr;
+  for (; q < q_end; q += kSingleInFlight) {
+    uint8_t code[kSingleInFlight][4];
+    LT vals[kSingleInFlight][4];
+    int it_e[kSingleInFlight], it_h[kSingleInFlight], it_d[kSingleInFlight];
+#pragma unroll
+    for (int k = 0; k < kSingleInFlight; ++k) {
+      it_e[k] = -1;
+      if (q + k < q_end) {
+        it_e[k] = e;
+        it_h[k] = h_lo + hh;
+        it_d[k] = (g << 7) + lane;
+        if (!SCATTER) {
+          const uint8_t* c = cache_r + s_off[e] + it_h[k] * p.c_sh + static_cast<int64_t>(it_d[k]) * sd;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) code[k][i] = c[32 * i * sd];
+        } else {
+          const LT* x = lin_l + static_cast<int64_t>(s_tok[e]) * p.l_st + it_h[k] * p.l_sh + it_d[k];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) vals[k][i] = x[32 * i];
+        }
+        if (++g == gpr) {
+          g = 0;
+          if (++hh == hpc) {
+            hh = 0;
+            ++e;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kSingleInFlight; ++k) {
+      if (it_e[k] < 0) continue;
+      const int h = it_h[k];
+      const float sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? h : l * NH + h)];
+      if (!SCATTER) {
+        LT* o = lin_l + static_cast<int64_t>(s_tok[it_e[k]]) * p.l_st + h * p.l_sh + it_d[k];
+        if (fp8_ftz_scale_ok<CODEC>(sc)) {
+          const float sf = __fmul_rn(sc, fp8_ftz_bias<CODEC>());  // exact: a power of two
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[32 * i] = from_f32<LT>(fmul_ftz(fp8_raw_top<CODEC>(static_cast<uint32_t>(code[k][i]) << 24), sf));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) o[32 * i] = C::load(code[k][i], sc);
+        }
+      } else {
+        uint8_t* c = cache_w + s_off[it_e[k]] + h * p.c_sh + static_cast<int64_t>(it_d[k]) * sd;
+        uint32_t w = 0;
+        if (!encode4_bounded<LT, CODEC>(vals[k], sc, &w)) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) w |= static_cast<uint32_t>(C::store(vals[k][i], sc)) << (8 * i);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c[32 * i * sd] = static_cast<uint8_t>(w >> (8 * i));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
@@ -791,6 +969,24 @@ static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
   return launch_pdl("tile_seg_kernel", kern, grid, dim3(threads), 0, st, p);
 }
 
+// The single-token launch of FP8 calls with head_dim a multiple of 128 (cfg3's random slots,
+// ragged ends of block-table calls): tile_single_fp8_kernel.  Token ranges of up to 256 tokens
+// per block, narrowed (and the heads split) until there are about four blocks per resident one.
+template <typename LT, int CODEC, bool SCATTER>
+static int launch_tile_single_fp8(TileLaunch& p, cudaStream_t st) {
+  const int threads = 256;
+  auto kern = tile_single_fp8_kernel<LT, CODEC, SCATTER>;
+  const int64_t resident = static_cast<int64_t>(blocks_per_sm(reinterpret_cast<const void*>(kern), threads, 0)) * sm_count();
+  const int64_t planes = p.num_layers * p.n_kv;
+  int tpc = kSingleMaxTok, hpc = static_cast<int>(p.num_heads);
+  auto blocks = [&]() { return (p.n_tokens + tpc - 1) / tpc * planes * (p.num_heads / hpc); };
+  while (blocks() < 4 * resident && tpc > 32) tpc >>= 1;
+  while (blocks() < 4 * resident && hpc % 2 == 0) hpc >>= 1;
+  const dim3 grid(static_cast<unsigned>((p.n_tokens + tpc - 1) / tpc), static_cast<unsigned>(planes),
+                  static_cast<unsigned>(p.num_heads / hpc));
+  return launch_pdl("tile_single_fp8_kernel", kern, grid, dim3(threads), 0, st, p, tpc, hpc);
+}
+
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 static int launch_tile_segments(TileLaunch& p, cudaStream_t st) {
   int rc = launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 1>(p, st);
@@ -798,6 +994,10 @@ static int launch_tile_segments(TileLaunch& p, cudaStream_t st) {
   if constexpr (SCATTER) {
     rc = launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 3>(p, st);
     if (rc) return rc;
+  }
+  if constexpr (CODEC != 0 && sizeof(CT) == 1) {
+    if (p.head_dim % 128 == 0 && p.n_tokens < (int64_t{1} << 31) && p.num_heads <= 65535)
+      return launch_tile_single_fp8<LT, CODEC, SCATTER>(p, st);
   }
   return launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 2>(p, st);
 }

@@ -382,43 +382,140 @@ __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileL
   }
 }
 
+// Runs of this many tokens or more take the 16-byte chunk path of tile_run_kernel.  A gather
+// reads whole chunks, so even a ragged end of 2..G-1 tokens costs one round trip per item, where
+// the element path would walk its tokens one after another; a scatter must not write a chunk's
+// other slots, so its runs shorter than a chunk go to the run-end launch (MODE 3).
+template <typename CT, bool SCATTER>
+__host__ __device__ constexpr int run_min_tokens() {
+  return SCATTER ? static_cast<int>(16 / sizeof(CT)) : 2;
+}
+
 // ---------------------------------------------------------------------------
-// Segment tile kernel (the main path).
+// One segment (a run of consecutive slots inside one cache block, at most 32
+// tokens, chunk-aligned in slot space) of one (kv, layer) plane through the
+// 16-byte cache chunks it touches.  The lanes split the (head, head_dim-group)
+// units x chunks; neighbouring lanes take neighbouring chunks of one unit, so
+// one warp instruction covers whole 32-byte sectors of a cache row.  A unit
+// moves R head_dim rows (R = 16 / sizeof(linear element)) of G token columns
+// (G = 16 / sizeof(cache element)):
+//   gather : R chunk loads, then one 16-byte token row per covered column (a
+//            partly covered chunk is read whole, only its tokens are written);
+//   scatter: a fully covered chunk takes G token-row loads then R chunk
+//            stores; a partly covered one element stores on the cache side (the
+//            chunk's other slots belong to other tokens: no read-modify-write,
+//            so concurrent segments of one block never race), its token rows
+//            loaded KTOK at a time.
+// cbase = element offset of the block in the plane, o_s = first in-block
+// offset, ts = first token.
+// ---------------------------------------------------------------------------
+template <typename CT, typename LT, int CODEC, bool SCATTER, int KTOK>
+__device__ __forceinline__ void move_run(const TileLaunch& p, const CT* cache_r, CT* cache_w, LT* lin_l, const float* scl,
+                                         int64_t l, int64_t cbase, int o_s, int len, int64_t ts, int lane) {
+  constexpr int G = 16 / sizeof(CT);
+  constexpr int R = 16 / sizeof(LT);
+  using C = Codec<CT, LT, CODEC>;
+  const int upr = static_cast<int>(p.head_dim) / R;
+  const int NH = static_cast<int>(p.num_heads);
+  const int units = NH * upr;
+  const int c_first = o_s / G, nch = (o_s + len - 1) / G - c_first + 1;
+  for (int it = lane; it < units * nch; it += 32) {
+    const int u = it / nch;
+    const int c = c_first + (it - u * nch);
+    const int h = u / upr, dg = u - h * upr;
+    float sc = 1.f;
+    if (CODEC) sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? h : l * NH + h)];
+    const int64_t row0 = cbase + h * p.c_sh + static_cast<int64_t>(dg) * R * p.c_sd;
+    LT* lrow = lin_l + ts * p.l_st + h * p.l_sh + dg * R;  // token ts, head h, head_dim dg*R
+    const int col0 = c * G;
+    const int lo = max(col0, o_s), hi = min(col0 + G, o_s + len);  // covered columns [lo, hi)
+    if (lo == col0 && hi == col0 + G) {
+      if (!SCATTER) {
+        uint4 rows[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) rows[r] = __ldg(reinterpret_cast<const uint4*>(cache_r + row0 + r * p.c_sd + col0));
+        if (!decode_chunk_ftz<CT, LT, CODEC, G, R>(rows, sc, lrow + (col0 - o_s) * p.l_st, p.l_st)) {
+#pragma unroll
+          for (int i = 0; i < G; ++i) {
+            uint4 outv;
+            LT* o = reinterpret_cast<LT*>(&outv);
+#pragma unroll
+            for (int r = 0; r < R; ++r) o[r] = C::load(reinterpret_cast<const CT*>(&rows[r])[i], sc);
+            *reinterpret_cast<uint4*>(lrow + (col0 + i - o_s) * p.l_st) = outv;
+          }
+        }
+      } else {
+        uint4 toks[G];
+#pragma unroll
+        for (int i = 0; i < G; ++i) toks[i] = __ldg(reinterpret_cast<const uint4*>(lrow + (col0 + i - o_s) * p.l_st));
+        if (!encode_chunk_bounded<CT, LT, CODEC, G, R>(toks, sc, cache_w + row0 + col0, p.c_sd)) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            uint4 v;
+            CT* e = reinterpret_cast<CT*>(&v);
+#pragma unroll
+            for (int i = 0; i < G; ++i) e[i] = C::store(reinterpret_cast<const LT*>(&toks[i])[r], sc);
+            *reinterpret_cast<uint4*>(cache_w + row0 + r * p.c_sd + col0) = v;
+          }
+        }
+      }
+    } else if (!SCATTER) {
+      uint4 rows[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) rows[r] = __ldg(reinterpret_cast<const uint4*>(cache_r + row0 + r * p.c_sd + col0));
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        if (col0 + i < lo || col0 + i >= hi) continue;
+        uint4 outv;
+        LT* o = reinterpret_cast<LT*>(&outv);
+#pragma unroll
+        for (int r = 0; r < R; ++r) o[r] = C::load(reinterpret_cast<const CT*>(&rows[r])[i], sc);
+        *reinterpret_cast<uint4*>(lrow + (col0 + i - o_s) * p.l_st) = outv;
+      }
+    } else {
+#pragma unroll 1
+      for (int c0 = lo; c0 < hi; c0 += KTOK) {
+        uint4 tv[KTOK];
+#pragma unroll
+        for (int i = 0; i < KTOK; ++i)
+          if (c0 + i < hi) tv[i] = __ldg(reinterpret_cast<const uint4*>(lrow + (c0 + i - o_s) * p.l_st));
+#pragma unroll
+        for (int i = 0; i < KTOK; ++i) {
+          if (c0 + i >= hi) continue;
+          const LT* x = reinterpret_cast<const LT*>(&tv[i]);
+#pragma unroll
+          for (int r = 0; r < R; ++r) cache_w[row0 + r * p.c_sd + c0 + i] = C::store(x[r], sc);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Segment tile kernel: the single tokens and the scatter run ends.
 //
 // A warp owns a window of 32 tokens of one (kv, layer) plane.  It loads the
 // window's slots (plus the next 32, since runs may cross the window end), and
 // finds "segments": runs of tokens whose slots are consecutive inside one
 // cache block, capped at 32 tokens and cut at offsets that are multiples of
 // min(block_size, 32) so every segment stays chunk-aligned in slot space.  The
-// warp handles every segment that STARTS in its window, whole.  Per segment the
-// lanes split the (head, head_dim-group) units; a unit moves R head_dim rows
-// (R = 16 / sizeof(linear element)) through the 16-byte cache chunks (G =
-// 16 / sizeof(cache element) offsets each) that the segment touches:
-//   gather : R chunk loads, then one 16-byte token row per covered column;
-//   scatter: for a fully covered chunk, G token-row loads then R chunk stores;
-//            for a partially covered chunk, element stores (no read-modify-
-//            write, so concurrent segments of one block never race).
-// No shared memory, no block barriers; FP8 codecs run in registers.
+// warp handles every segment that STARTS in its window, whole.
+// MODE 2 moves the single tokens (element items), MODE 3 (scatters only) the
+// runs of 2..kRunMin-1 tokens (move_run with batched token loads); the runs of
+// kRunMin tokens or more go through tile_run_kernel, launched first, which also
+// writes the segment map these launches use to skip windows.  Each launch keeps
+// the register budget its path needs.  No shared memory, no block barriers;
+// FP8 codecs run in registers.
 // ---------------------------------------------------------------------------
-// MODE 1 handles segments of at least kRunMin tokens (plus zero rows), MODE 2 the single tokens,
-// MODE 3 (scatters only) the runs of 2..kRunMin-1 tokens;
-// the two are launched back to back so each keeps the register budget its path needs.
 template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE, bool GROUPED>
 __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg_kernel(const __grid_constant__ TileLaunch p) {
   constexpr int G = 16 / sizeof(CT);
-  constexpr int R = 16 / sizeof(LT);
-  // Runs of this many tokens or more take the 16-byte chunk path (MODE 1).  A gather reads
-  // whole chunks, so even a ragged end of 2..G-1 tokens costs one round trip per item, where
-  // the element path would walk its tokens one after another; a scatter must not write the
-  // chunk's other slots, so its runs shorter than a chunk stay on the element path.
-  constexpr int kRunMin = SCATTER ? G : 2;
-  // launch that owns a segment of len tokens
-  auto seg_mode = [](int len) { return len >= kRunMin ? 1 : (len >= 2 ? 3 : 2); };
+  static_assert(MODE == 2 || (MODE == 3 && SCATTER), "tile_seg_kernel: single tokens and scatter run ends only");
+  // launch that owns a segment of len tokens (1 = tile_run_kernel)
+  auto seg_mode = [](int len) { return len >= run_min_tokens<CT, SCATTER>() ? 1 : (len >= 2 ? 3 : 2); };
   using C = Codec<CT, LT, CODEC>;
   const int lane = threadIdx.x & 31;
-  const int upr = static_cast<int>(p.head_dim) / R;
   const int NH = static_cast<int>(p.num_heads);
-  const int units = NH * upr;
   const int64_t cap = p.block_size < 32 ? p.block_size : 32;
   const int planes = static_cast<int>(p.num_layers) * p.n_kv;
   const int plane_lo = GROUPED ? static_cast<int>(blockIdx.y) * p.plane_group : static_cast<int>(blockIdx.y);
@@ -448,9 +545,9 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
     const int h_lo = static_cast<int>(wi & ((1 << hs_shift) - 1)) * NHp;
     const int h_hi = h_lo + NHp;
     const int64_t t0 = w * W;
-    if (MODE != 1 && p.seg_map != nullptr) {
-      // Skip the window when the run launch of this call found no single-token run starting in
-      // any of its map windows that cover [t0, t0 + W) (at most 32 / 8 = 4 of them).
+    if (p.seg_map != nullptr) {
+      // Skip the window when the run launch of this call found no segment of this launch's
+      // kind starting in any of its map windows that cover [t0, t0 + W) (at most 32 / 8 = 4).
       const int64_t m0 = t0 >> p.map_shift;
       const int64_t m1 = (min(t0 + W, p.n_tokens) - 1) >> p.map_shift;
       const uint32_t tag = p.seg_epoch << 2, bit = MODE == 2 ? 1u : 2u;
@@ -459,14 +556,14 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
       if (__all_sync(0xffffffffu, (v & ~3u) == tag && (v & bit) == 0u)) continue;
     }
     // Slots of tokens t0 + lane (A) and t0 + 32 + lane (B), as (block element offset, in-block offset).
-    int64_t offA = -1, offB = -1, sA = -1, sB = -1, oA = 0, oB = 0;
+    int64_t offA = -1, sA = -1, sB = -1, oA = 0, oB = 0;
     {
       const int64_t ta = t0 + lane, tb = t0 + 32 + lane;
       if (ta < p.n_tokens) sA = token_slot<SCATTER>(p, ta);
       if (tb < p.n_tokens) sB = token_slot<SCATTER>(p, tb);
       int64_t b;
       if (sA >= 0) { split_slot(sA, p.block_size, &b, &oA); offA = b * p.c_sb + oA; }
-      if (sB >= 0) { split_slot(sB, p.block_size, &b, &oB); offB = b * p.c_sb + oB; }
+      if (sB >= 0) split_slot(sB, p.block_size, &b, &oB);
     }
     int64_t sPrev = -1;  // slot of token t0 - 1 (for lane 0)
     if (lane == 0 && t0 > 0) {
@@ -484,24 +581,10 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
                            (static_cast<uint64_t>(__ballot_sync(0xffffffffu, startB)) << 32) |
                            ~(static_cast<uint64_t>(__ballot_sync(0xffffffffu, sA >= 0)) |
                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, sB >= 0)) << 32));
-    if (MODE == 1 && p.seg_map != nullptr && blockIdx.y == 0) {
-      // Does a single-token run start in this window?  A run's length is bounded by the
-      // next boundary in the 64 loaded slots; 64 - lane > 32, so a run that reaches past
-      // them is long whatever follows, and the single-token launch classifies alike.
-      int mode = 1;
-      if (lane < W && ((mStartA >> lane) & 1u)) {
-        const uint64_t rest = bound >> (lane + 1);
-        const int len = rest ? __ffsll(static_cast<long long>(rest)) : (64 - lane);
-        mode = seg_mode(len);
-      }
-      const uint32_t bits = (__ballot_sync(0xffffffffu, mode == 2) != 0u ? 1u : 0u) |
-                            (__ballot_sync(0xffffffffu, mode == 3) != 0u ? 2u : 0u);
-      if (lane == 0) p.seg_map[w] = (p.seg_epoch << 2) | bits;
-    }
     // The window's segments are the same for every plane: skip the planes when
-    // none is this launch's kind (and, in MODE 1, no zero rows are due).
+    // none is this launch's kind.
     if (GROUPED) {
-      bool work = MODE == 1 && !SCATTER && p.fill_zero && (~__ballot_sync(0xffffffffu, sA >= 0) & wmask) != 0;
+      bool work = false;
       for (uint32_t m = mStartA & wmask; m && !work; m &= m - 1) {
         const int q = __ffs(m) - 1;
         const uint64_t rest = bound >> (q + 1);
@@ -518,20 +601,6 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
       cache_w = reinterpret_cast<CT*>(p.cache[kv]) + l * p.c_sl;
       lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl;
       scl = CODEC ? p.scale[kv] : nullptr;
-    }
-    // zero rows for skipped tokens of this window (gather, fill mode)
-    if (MODE == 1 && !SCATTER && p.fill_zero) {
-      uint32_t mZero = ~__ballot_sync(0xffffffffu, sA >= 0) & wmask;
-      const int64_t left = p.n_tokens - t0;
-      if (left < 32) mZero &= (1u << left) - 1u;
-      while (mZero) {
-        const int q = __ffs(mZero) - 1;
-        mZero &= mZero - 1;
-        for (int u = lane; u < units; u += 32) {
-          const int h = u / upr, dg = u - h * upr;
-          *reinterpret_cast<uint4*>(lin_l + (t0 + q) * p.l_st + h * p.l_sh + dg * R) = make_uint4(0u, 0u, 0u, 0u);
-        }
-      }
     }
     uint32_t mSeg = mStartA & wmask;  // the warp owns the segments that start inside its window
     while (mSeg) {
@@ -679,88 +748,137 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
         }
         continue;
       }
-      const int c_first = o_s / G, nch = (o_s + len - 1) / G - c_first + 1;
-      // (unit, chunk) items: neighbouring lanes take neighbouring chunks of one unit, so one
-      // warp instruction covers whole 32-byte sectors of a cache row.
-      for (int it = lane; it < units * nch; it += 32) {
-        const int u = it / nch;
-        const int c = c_first + (it - u * nch);
-        const int h = u / upr, dg = u - h * upr;
-        float sc = 1.f;
-        if (CODEC) sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? h : l * NH + h)];
-        const int64_t row0 = cbase + h * p.c_sh + static_cast<int64_t>(dg) * R * p.c_sd;
-        LT* lrow = lin_l + ts * p.l_st + h * p.l_sh + dg * R;  // token ts, head h, head_dim dg*R
-        const int col0 = c * G;
-        const int lo = max(col0, o_s), hi = min(col0 + G, o_s + len);  // covered columns [lo, hi)
-        if (lo == col0 && hi == col0 + G) {
-          if (!SCATTER) {
-            uint4 rows[R];
-#pragma unroll
-            for (int r = 0; r < R; ++r) rows[r] = __ldg(reinterpret_cast<const uint4*>(cache_r + row0 + r * p.c_sd + col0));
-            if (!decode_chunk_ftz<CT, LT, CODEC, G, R>(rows, sc, lrow + (col0 - o_s) * p.l_st, p.l_st)) {
-#pragma unroll
-              for (int i = 0; i < G; ++i) {
-                uint4 outv;
-                LT* o = reinterpret_cast<LT*>(&outv);
-#pragma unroll
-                for (int r = 0; r < R; ++r) o[r] = C::load(reinterpret_cast<const CT*>(&rows[r])[i], sc);
-                *reinterpret_cast<uint4*>(lrow + (col0 + i - o_s) * p.l_st) = outv;
-              }
-            }
-          } else {
-            uint4 toks[G];
-#pragma unroll
-            for (int i = 0; i < G; ++i) toks[i] = __ldg(reinterpret_cast<const uint4*>(lrow + (col0 + i - o_s) * p.l_st));
-            if (!encode_chunk_bounded<CT, LT, CODEC, G, R>(toks, sc, cache_w + row0 + col0, p.c_sd)) {
-#pragma unroll
-              for (int r = 0; r < R; ++r) {
-                uint4 v;
-                CT* e = reinterpret_cast<CT*>(&v);
-#pragma unroll
-                for (int i = 0; i < G; ++i) e[i] = C::store(reinterpret_cast<const LT*>(&toks[i])[r], sc);
-                *reinterpret_cast<uint4*>(cache_w + row0 + r * p.c_sd + col0) = v;
-              }
-            }
-          }
-        } else if (!SCATTER) {
-          // partially covered chunk, gather: the whole 16-byte chunk of each cache row is read
-          // (its other slots lie in the same block row), only the covered tokens are written
-          uint4 rows[R];
-#pragma unroll
-          for (int r = 0; r < R; ++r) rows[r] = __ldg(reinterpret_cast<const uint4*>(cache_r + row0 + r * p.c_sd + col0));
-#pragma unroll
-          for (int i = 0; i < G; ++i) {
-            if (col0 + i < lo || col0 + i >= hi) continue;
-            uint4 outv;
-            LT* o = reinterpret_cast<LT*>(&outv);
-#pragma unroll
-            for (int r = 0; r < R; ++r) o[r] = C::load(reinterpret_cast<const CT*>(&rows[r])[i], sc);
-            *reinterpret_cast<uint4*>(lrow + (col0 + i - o_s) * p.l_st) = outv;
-          }
-        } else {
-          // partially covered chunk, scatter: element stores on the cache side (the chunk's
-          // other slots belong to other tokens), 16-byte token rows; the run-end launch loads
-          // up to eight covered rows at a time, the run launch one (its registers go to the
-          // full-chunk transposes)
-          constexpr int kTok = MODE == 3 ? (G < 8 ? G : 8) : 1;
-#pragma unroll 1
-          for (int c0 = lo; c0 < hi; c0 += kTok) {
-            uint4 tv[kTok];
-#pragma unroll
-            for (int i = 0; i < kTok; ++i)
-              if (c0 + i < hi) tv[i] = __ldg(reinterpret_cast<const uint4*>(lrow + (c0 + i - o_s) * p.l_st));
-#pragma unroll
-            for (int i = 0; i < kTok; ++i) {
-              if (c0 + i >= hi) continue;
-              const LT* x = reinterpret_cast<const LT*>(&tv[i]);
-#pragma unroll
-              for (int r = 0; r < R; ++r) cache_w[row0 + r * p.c_sd + c0 + i] = C::store(x[r], sc);
-            }
-          }
-        }
-      }
+      // MODE 3: a scatter run end of 2..G-1 tokens, up to eight token rows loaded at once
+      move_run<CT, LT, CODEC, SCATTER, (G < 8 ? G : 8)>(p, cache_r, cache_w, lin_l, scl, l, cbase, o_s, len, ts, lane);
     }
     }  // planes of the group
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Run launch (the main path): segments of run_min_tokens or more tokens, i.e.
+// the block-table traffic, in two phases per block.
+//   1. Each of the block's 8 warps scans a window of W tokens of the slot
+//      mapping (the same segment rule as the segment kernel), appends the runs
+//      that start in it to a shared-memory list (first token, slot offset,
+//      length), marks the zero rows (gather, fill mode) and, in the blocks of
+//      the first plane, writes the segment map entry of its window for the
+//      single-token and run-end launches that follow.
+//   2. The warps take the list's runs in turn and move each through move_run.
+// One plane per block (grid = token ranges of 8W tokens x planes): nothing of
+// the scan stays live in the walk, blocks are small enough that the last wave
+// stays balanced, and the run path keeps 80 registers for its transposes
+// (3 blocks per SM; 2 with an FP8 codec).
+// ---------------------------------------------------------------------------
+constexpr int kRunWarps = 8;
+constexpr int kRunMaxSeg = kRunWarps * 32 / 2;  // runs have at least 2 tokens
+
+template <typename CT, typename LT, int CODEC, bool SCATTER>
+__global__ void __launch_bounds__(256, CODEC ? 2 : 3) tile_run_kernel(const __grid_constant__ TileLaunch p) {
+  constexpr int R = 16 / sizeof(LT);
+  constexpr int kRunMin = run_min_tokens<CT, SCATTER>();
+  __shared__ int64_t s_soff[kRunMaxSeg];  // element offset of the run's first slot in the plane
+  __shared__ int s_ts[kRunMaxSeg];        // first token, relative to the block's first token
+  __shared__ int s_os[kRunMaxSeg];        // in-block offset of the first slot
+  __shared__ int s_len[kRunMaxSeg];
+  __shared__ uint32_t s_zero[kRunWarps];
+  __shared__ int s_cnt;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int W = p.window;  // 8, 16 or 32
+  const uint32_t wmask = W >= 32 ? 0xffffffffu : ((1u << W) - 1u);
+  const int64_t tb = static_cast<int64_t>(blockIdx.x) * (kRunWarps * W);
+  const int64_t t0 = tb + warp * W;
+  const int64_t cap = p.block_size < 32 ? p.block_size : 32;
+  if (threadIdx.x == 0) s_cnt = 0;
+  pdl_wait();
+  pdl_trigger();
+  __syncthreads();
+  uint32_t zmask = 0;
+  if (t0 < p.n_tokens) {
+    // slots of tokens t0 + lane (A) and t0 + 32 + lane (B): a run that starts in the window may
+    // end past it
+    int64_t offA = -1, sA = -1, sB = -1, oA = 0, oB = 0;
+    {
+      const int64_t ta = t0 + lane, tbb = t0 + 32 + lane;
+      if (ta < p.n_tokens) sA = token_slot<SCATTER>(p, ta);
+      if (tbb < p.n_tokens) sB = token_slot<SCATTER>(p, tbb);
+      int64_t b;
+      if (sA >= 0) { split_slot(sA, p.block_size, &b, &oA); offA = b * p.c_sb + oA; }
+      if (sB >= 0) split_slot(sB, p.block_size, &b, &oB);
+    }
+    int64_t sPrev = -1;  // slot of token t0 - 1 (for lane 0)
+    if (lane == 0 && t0 > 0) sPrev = token_slot<SCATTER>(p, t0 - 1);
+    const int64_t upA = __shfl_up_sync(0xffffffffu, sA, 1);
+    const int64_t lastA = __shfl_sync(0xffffffffu, sA, 31);
+    const int64_t upB = __shfl_up_sync(0xffffffffu, sB, 1);
+    const int64_t prevA = lane == 0 ? sPrev : upA;
+    const int64_t prevB = lane == 0 ? lastA : upB;
+    const bool startA = sA >= 0 && (prevA < 0 || sA != prevA + 1 || (oA % cap) == 0);
+    const bool startB = sB >= 0 && (prevB < 0 || sB != prevB + 1 || (oB % cap) == 0);
+    const uint32_t validA = __ballot_sync(0xffffffffu, sA >= 0);
+    const uint32_t mStartA = __ballot_sync(0xffffffffu, startA);
+    const uint64_t bound = static_cast<uint64_t>(mStartA) |
+                           (static_cast<uint64_t>(__ballot_sync(0xffffffffu, startB)) << 32) |
+                           ~(static_cast<uint64_t>(validA) |
+                             (static_cast<uint64_t>(__ballot_sync(0xffffffffu, sB >= 0)) << 32));
+    // launch that owns the segment starting at this lane's token (0 = none): a run's length is
+    // bounded by the next boundary in the 64 loaded slots; 64 - lane > 32, so a run that reaches
+    // past them is long whatever follows, and the other launches classify alike
+    int mode = 0, len = 0;
+    if (lane < W && ((mStartA >> lane) & 1u)) {
+      const uint64_t rest = bound >> (lane + 1);
+      len = rest ? __ffsll(static_cast<long long>(rest)) : (64 - lane);
+      mode = len >= kRunMin ? 1 : (len >= 2 ? 3 : 2);
+    }
+    if (p.seg_map != nullptr && blockIdx.y == 0) {
+      const uint32_t bits = (__ballot_sync(0xffffffffu, mode == 2) != 0u ? 1u : 0u) |
+                            (__ballot_sync(0xffffffffu, mode == 3) != 0u ? 2u : 0u);
+      if (lane == 0) p.seg_map[t0 / W] = (p.seg_epoch << 2) | bits;
+    }
+    if (!SCATTER && p.fill_zero) {
+      zmask = ~validA & wmask;
+      const int64_t left = p.n_tokens - t0;
+      if (left < 32) zmask &= (1u << left) - 1u;
+    }
+    // at most W / 2 runs start in a window, so the list holds the block's runs
+    const uint32_t m = __ballot_sync(0xffffffffu, mode == 1);
+    int base = 0;
+    if (lane == 0 && m) base = atomicAdd(&s_cnt, __popc(m));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    if (mode == 1) {
+      const int k = base + __popc(m & ((1u << lane) - 1u));
+      s_soff[k] = offA;
+      s_ts[k] = static_cast<int>(t0 - tb) + lane;
+      s_os[k] = static_cast<int>(oA);
+      s_len[k] = len;
+    }
+  }
+  if (lane == 0) s_zero[warp] = zmask;
+  __syncthreads();
+  const int nl = static_cast<int>(p.num_layers);  // planes <= 65535: 32-bit division
+  const int64_t l = static_cast<int>(blockIdx.y) % nl;
+  const int kv = static_cast<int>(blockIdx.y) / nl;
+  const CT* cache_r = reinterpret_cast<const CT*>(p.cache[kv]) + l * p.c_sl;
+  CT* cache_w = reinterpret_cast<CT*>(p.cache[kv]) + l * p.c_sl;
+  LT* lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl;
+  const float* scl = CODEC ? p.scale[kv] : nullptr;
+  const int cnt = s_cnt;
+  for (int e = warp; e < cnt; e += kRunWarps) {
+    const int o_s = s_os[e];
+    move_run<CT, LT, CODEC, SCATTER, 1>(p, cache_r, cache_w, lin_l, scl, l, s_soff[e] - o_s, o_s, s_len[e], tb + s_ts[e],
+                                        lane);
+  }
+  // zero rows for the skipped tokens of this warp's window (gather, fill mode)
+  if (!SCATTER) {
+    const int upr = static_cast<int>(p.head_dim) / R;
+    const int units = static_cast<int>(p.num_heads) * upr;
+    for (uint32_t mz = s_zero[warp]; mz; mz &= mz - 1) {
+      const int q = __ffs(mz) - 1;
+      for (int u = lane; u < units; u += 32) {
+        const int h = u / upr, dg = u - h * upr;
+        *reinterpret_cast<uint4*>(lin_l + (t0 + q) * p.l_st + h * p.l_sh + dg * R) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
   }
 }
 
@@ -934,13 +1052,6 @@ static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
   while (p.window > 8 && (p.n_tokens + p.window - 1) / p.window * planes < 4 * resident_warps) p.window /= 2;
   const int64_t windows = (p.n_tokens + p.window - 1) / p.window;
   p.windows = windows;
-  if (MODE == 1 && p.seg_map != nullptr) {
-    if (windows > p.seg_map_entries) p.seg_map = nullptr;  // too small: the single-token launch scans every window
-    else {
-      p.map_window = p.window;
-      p.map_shift = p.window == 32 ? 5 : (p.window == 16 ? 4 : 3);
-    }
-  }
   // Planes per block: a window's slot scan serves all planes of its group, so
   // group as many planes (up to 8) as still leave every resident warp a few
   // (window, group) items.
@@ -987,9 +1098,36 @@ static int launch_tile_single_fp8(TileLaunch& p, cudaStream_t st) {
   return launch_pdl("tile_single_fp8_kernel", kern, grid, dim3(threads), 0, st, p, tpc, hpc);
 }
 
+// The run launch: windows of 32 tokens (16 or 8 when that leaves resident warps without a few
+// windows), blocks of 8 windows of one plane.  It sets the segment map fields the launches after
+// it read.
+template <typename CT, typename LT, int CODEC, bool SCATTER>
+static int launch_tile_run(TileLaunch& p, cudaStream_t st) {
+  const int threads = kRunWarps * 32;
+  const int64_t planes = p.num_layers * p.n_kv;
+  auto kern = tile_run_kernel<CT, LT, CODEC, SCATTER>;
+  const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kern), threads, 0);
+  const int64_t resident_warps = static_cast<int64_t>(per_sm) * sm_count() * kRunWarps;
+  p.window = 32;
+  while (p.window > 8 && (p.n_tokens + p.window - 1) / p.window * planes < 4 * resident_warps) p.window /= 2;
+  const int64_t windows = (p.n_tokens + p.window - 1) / p.window;
+  p.windows = windows;
+  if (p.seg_map != nullptr) {
+    if (windows > p.seg_map_entries) p.seg_map = nullptr;  // too small: the later launches scan every window
+    else {
+      p.map_window = p.window;
+      p.map_shift = p.window == 32 ? 5 : (p.window == 16 ? 4 : 3);
+    }
+  }
+  const int64_t tblocks = (p.n_tokens + kRunWarps * p.window - 1) / (kRunWarps * p.window);
+  if (tblocks > 0x7fffffff) return fail(MAK_E_UNSUPPORTED, "tile run launch: %lld token blocks", (long long)tblocks);
+  const dim3 grid(static_cast<unsigned>(tblocks), static_cast<unsigned>(planes));
+  return launch_pdl("tile_run_kernel", kern, grid, dim3(threads), 0, st, p);
+}
+
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 static int launch_tile_segments(TileLaunch& p, cudaStream_t st) {
-  int rc = launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 1>(p, st);
+  int rc = launch_tile_run<CT, LT, CODEC, SCATTER>(p, st);
   if (rc) return rc;
   if constexpr (SCATTER) {
     rc = launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 3>(p, st);

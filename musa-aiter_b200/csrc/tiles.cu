@@ -2,16 +2,16 @@
 // innermost ([L][NB][NH][HD][BS], the musa-aiter paged layout of
 // musa_aiter/ops/kv_transfer.py:2987-3000) and token-major rows ([L][T][NH][HD]).
 //
-// Main path (tile_seg_kernel): a warp takes a window of tokens of one (kv,
-// layer) plane, splits the window's slot mapping into segments (runs of
-// consecutive slots inside one block) with ballots, and moves each segment
-// through 16-byte chunks of the cache rows ([d][o0 .. o0 + G)), transposing
-// in registers.  Runs of two or more tokens (block-table traffic and its
-// ragged ends) and single tokens (random slots) are handled by separate
-// instantiations launched back to back, so the single-token, latency-bound
-// path runs at high occupancy while the run path keeps the registers its
-// transposes need; scatters give the run ends shorter than a 16-byte chunk a
-// third instantiation, whose batched token loads would spill the run path.
+// Main path: warps take windows of tokens of one (kv, layer) plane, split the
+// window's slot mapping into segments (runs of consecutive slots inside one
+// block) with ballots, and move each segment through 16-byte chunks of the
+// cache rows ([d][o0 .. o0 + G)), transposing in registers.  Runs of two or
+// more tokens (block-table traffic and its ragged ends) go through
+// tile_run_kernel, single tokens (random slots) through a second launch
+// (tile_single_kernel, or tile_single_fp8_kernel for FP8 caches with
+// head_dim a multiple of 128), so the single-token, latency-bound path runs
+// at high occupancy while the run path keeps the registers its transposes
+// need.
 //
 // Fallback (tile_kernel): any head_dim / block_size / alignment, through a
 // shared-memory transpose of 32-token chunks.
@@ -43,15 +43,14 @@ struct TileLaunch {
   int32_t slots64, n_kv, fill_zero, cache_vec, lin_vec, scale_mode, heads_per_step;
   int32_t window;       // tokens per warp window of the segment kernel (8, 16 or 32)
   int32_t plane_group;  // (kv, layer) planes a segment-kernel block walks per window
-  // Single-token launch (MODE 2): a window's heads are split into 2^head_split_shift groups,
+  // Single-token launch (tile_single_kernel): a window's heads are split into 2^head_split_shift groups,
   // each a separate warp item, when the call has too few windows to fill the device (decode
   // batches); 0 elsewhere.
   int32_t head_split_shift;
-  // Segment map (optional): the run launch (MODE 1) stores, per window of map_window tokens,
-  // (epoch << 2) | (a single-token run starts in it) | (a scatter run end of 2..G-1 tokens
-  // starts in it) << 1; the single-token launch (MODE 2) and the run-end launch (MODE 3) skip
-  // the windows whose entry has this epoch and their bit clear.  Entries of another epoch are
-  // never trusted.
+  // Segment map (optional): the run launch (tile_run_kernel) stores, per window of map_window
+  // tokens, (epoch << 2) | (single tokens of the window are left to the single-token launch);
+  // that launch skips the tokens whose window entry has this epoch and the bit clear.  Entries of
+  // another epoch are never trusted.
   uint32_t* seg_map;
   uint32_t seg_epoch;
   int32_t map_window;       // tokens per map entry (the run launch's window: 8, 16 or 32)
@@ -382,14 +381,13 @@ __global__ void __launch_bounds__(256) tile_kernel(const __grid_constant__ TileL
   }
 }
 
-// Runs of this many tokens or more take the 16-byte chunk path of tile_run_kernel.  A gather
-// reads whole chunks, so even a ragged end of 2..G-1 tokens costs one round trip per item, where
-// the element path would walk its tokens one after another; a scatter must not write a chunk's
-// other slots, so its runs shorter than a chunk go to the run-end launch (MODE 3).
-template <typename CT, bool SCATTER>
-__host__ __device__ constexpr int run_min_tokens() {
-  return SCATTER ? static_cast<int>(16 / sizeof(CT)) : 2;
-}
+// Runs of two or more tokens take the 16-byte chunk path of tile_run_kernel: a gather reads
+// whole chunks, so even a ragged end of 2..G-1 tokens costs one round trip per item where the
+// element path would walk its tokens one after another; a scatter stores the covered part of a
+// partly covered chunk element by element.  Single tokens (random slots) take the element path
+// of the single-token launch, unless their window holds at most kRunSingles of them (the ragged
+// ends of block-table calls) and a segment map tells that launch to skip them.
+constexpr int kRunSingles = 4;
 
 // ---------------------------------------------------------------------------
 // One segment (a run of consecutive slots inside one cache block, at most 32
@@ -500,19 +498,14 @@ __device__ __forceinline__ void move_run(const TileLaunch& p, const CT* cache_r,
 // cache block, capped at 32 tokens and cut at offsets that are multiples of
 // min(block_size, 32) so every segment stays chunk-aligned in slot space.  The
 // warp handles every segment that STARTS in its window, whole.
-// MODE 2 moves the single tokens (element items), MODE 3 (scatters only) the
-// runs of 2..kRunMin-1 tokens (move_run with batched token loads); the runs of
-// kRunMin tokens or more go through tile_run_kernel, launched first, which also
-// writes the segment map these launches use to skip windows.  Each launch keeps
-// the register budget its path needs.  No shared memory, no block barriers;
-// FP8 codecs run in registers.
+// It moves the single tokens (element items); the runs of two or more tokens
+// go through tile_run_kernel, launched first, which also writes the segment
+// map this launch uses to skip windows.  Each launch keeps the register budget
+// its path needs.  No shared memory, no block barriers; FP8 codecs run in
+// registers.
 // ---------------------------------------------------------------------------
-template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE, bool GROUPED>
-__global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg_kernel(const __grid_constant__ TileLaunch p) {
-  constexpr int G = 16 / sizeof(CT);
-  static_assert(MODE == 2 || (MODE == 3 && SCATTER), "tile_seg_kernel: single tokens and scatter run ends only");
-  // launch that owns a segment of len tokens (1 = tile_run_kernel)
-  auto seg_mode = [](int len) { return len >= run_min_tokens<CT, SCATTER>() ? 1 : (len >= 2 ? 3 : 2); };
+template <typename CT, typename LT, int CODEC, bool SCATTER, bool GROUPED>
+__global__ void __launch_bounds__(256, 4) tile_single_kernel(const __grid_constant__ TileLaunch p) {
   using C = Codec<CT, LT, CODEC>;
   const int lane = threadIdx.x & 31;
   const int NH = static_cast<int>(p.num_heads);
@@ -533,8 +526,8 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
   const uint32_t wmask = W >= 32 ? 0xffffffffu : ((1u << W) - 1u);
   const int64_t windows = p.windows;
   const int64_t wstride = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  // head groups of a MODE 2 item: heads [h_lo, h_lo + NHp)
-  const int hs_shift = MODE == 2 ? p.head_split_shift : 0;
+  // head groups of an item: heads [h_lo, h_lo + NHp)
+  const int hs_shift = p.head_split_shift;
   const int NHp = NH >> hs_shift;
   pdl_wait();
   pdl_trigger();
@@ -545,15 +538,17 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
     const int h_lo = static_cast<int>(wi & ((1 << hs_shift) - 1)) * NHp;
     const int h_hi = h_lo + NHp;
     const int64_t t0 = w * W;
+    // Segment map entries of the map windows that cover [t0, t0 + W) (at most 32 / 8 = 4), one
+    // per lane: the window is skipped when the run launch of this call left no single token in
+    // any of them, and a single token is moved only if its own map window left it here.
+    const uint32_t tag = p.seg_epoch << 2;
+    const int64_t m0 = p.seg_map != nullptr ? t0 >> p.map_shift : 0;
+    uint32_t v = 1u;  // no map: every single token is this launch's
     if (p.seg_map != nullptr) {
-      // Skip the window when the run launch of this call found no segment of this launch's
-      // kind starting in any of its map windows that cover [t0, t0 + W) (at most 32 / 8 = 4).
-      const int64_t m0 = t0 >> p.map_shift;
       const int64_t m1 = (min(t0 + W, p.n_tokens) - 1) >> p.map_shift;
-      const uint32_t tag = p.seg_epoch << 2, bit = MODE == 2 ? 1u : 2u;
-      uint32_t v = tag;
+      v = tag;
       if (lane <= m1 - m0) v = p.seg_map[m0 + lane];
-      if (__all_sync(0xffffffffu, (v & ~3u) == tag && (v & bit) == 0u)) continue;
+      if (__all_sync(0xffffffffu, (v & ~3u) == tag && (v & 1u) == 0u)) continue;
     }
     // Slots of tokens t0 + lane (A) and t0 + 32 + lane (B), as (block element offset, in-block offset).
     int64_t offA = -1, sA = -1, sB = -1, oA = 0, oB = 0;
@@ -588,8 +583,7 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
       for (uint32_t m = mStartA & wmask; m && !work; m &= m - 1) {
         const int q = __ffs(m) - 1;
         const uint64_t rest = bound >> (q + 1);
-        const int len = rest ? (__ffsll(static_cast<long long>(rest))) : (64 - q);
-        work = seg_mode(len) == MODE;
+        work = (rest & 1u) != 0u;  // a single token: the next token is a boundary
       }
       if (!work) continue;
     }
@@ -612,8 +606,13 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
       const int o_s = static_cast<int>(__shfl_sync(0xffffffffu, oA, q));
       const int64_t ts = t0 + q;
       const int64_t cbase = soff - o_s;  // block start (element offset)
-      if (seg_mode(len) != MODE) continue;
-      if (MODE == 2) {
+      if (len != 1) continue;
+      {
+        // left to this launch by the run launch? (the map entry of the token's own window)
+        const uint32_t vq = __shfl_sync(0xffffffffu, v, p.seg_map != nullptr ? static_cast<int>((ts >> p.map_shift) - m0) : 0);
+        if ((vq & ~3u) == tag && (vq & 1u) == 0u) continue;
+      }
+      {
         // Single-token segment (random slots): one element per item, head_dim fastest
         // across lanes, so a warp instruction touches consecutive cache rows (whole
         // sectors per instruction) and a contiguous piece of the token row; four items
@@ -746,37 +745,37 @@ __global__ void __launch_bounds__(256, MODE == 2 ? 4 : (CODEC ? 2 : 3)) tile_seg
             else cache_w[ck[k]] = C::store(lv[k], sck[k]);
           }
         }
-        continue;
       }
-      // MODE 3: a scatter run end of 2..G-1 tokens, up to eight token rows loaded at once
-      move_run<CT, LT, CODEC, SCATTER, (G < 8 ? G : 8)>(p, cache_r, cache_w, lin_l, scl, l, cbase, o_s, len, ts, lane);
     }
     }  // planes of the group
   }
 }
 
 // ---------------------------------------------------------------------------
-// Run launch (the main path): segments of run_min_tokens or more tokens, i.e.
-// the block-table traffic, in two phases per block.
+// Run launch (the main path): segments of two or more tokens, i.e. the
+// block-table traffic and its ragged ends, in two phases per block.
 //   1. Each of the block's 8 warps scans a window of W tokens of the slot
-//      mapping (the same segment rule as the segment kernel), appends the runs
-//      that start in it to a shared-memory list (first token, slot offset,
-//      length), marks the zero rows (gather, fill mode) and, in the blocks of
-//      the first plane, writes the segment map entry of its window for the
-//      single-token and run-end launches that follow.
-//   2. The warps take the list's runs in turn and move each through move_run.
+//      mapping (the same segment rule as the single-token kernel), appends the
+//      runs that start in it to a shared-memory list (first token, slot offset,
+//      length) -- and its single tokens too when there are at most kRunSingles
+//      of them and a segment map records that -- marks the zero rows (gather,
+//      fill mode) and, in the blocks of the first plane, writes the segment map
+//      entry of its window for the single-token launch that follows.
+//   2. The warps take the list's segments in turn and move each through
+//      move_run.
 // One plane per block (grid = token ranges of 8W tokens x planes): nothing of
 // the scan stays live in the walk, blocks are small enough that the last wave
 // stays balanced, and the run path keeps 80 registers for its transposes
 // (3 blocks per SM; 2 with an FP8 codec).
 // ---------------------------------------------------------------------------
 constexpr int kRunWarps = 8;
-constexpr int kRunMaxSeg = kRunWarps * 32 / 2;  // runs have at least 2 tokens
+// segments listed per window: s single tokens and r runs (two or more tokens, the last one may
+// end past the window) fit W >= s + 2(r - 1) + 1 tokens, so r + s <= (W + 1 + s) / 2
+constexpr int kRunMaxSeg = kRunWarps * ((32 + 1 + kRunSingles) / 2);
 
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 __global__ void __launch_bounds__(256, CODEC ? 2 : 3) tile_run_kernel(const __grid_constant__ TileLaunch p) {
   constexpr int R = 16 / sizeof(LT);
-  constexpr int kRunMin = run_min_tokens<CT, SCATTER>();
   __shared__ int64_t s_soff[kRunMaxSeg];  // element offset of the run's first slot in the plane
   __shared__ int s_ts[kRunMaxSeg];        // first token, relative to the block's first token
   __shared__ int s_os[kRunMaxSeg];        // in-block offset of the first slot
@@ -821,26 +820,26 @@ __global__ void __launch_bounds__(256, CODEC ? 2 : 3) tile_run_kernel(const __gr
                            (static_cast<uint64_t>(__ballot_sync(0xffffffffu, startB)) << 32) |
                            ~(static_cast<uint64_t>(validA) |
                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, sB >= 0)) << 32));
-    // launch that owns the segment starting at this lane's token (0 = none): a run's length is
-    // bounded by the next boundary in the 64 loaded slots; 64 - lane > 32, so a run that reaches
-    // past them is long whatever follows, and the other launches classify alike
-    int mode = 0, len = 0;
+    // the segment starting at this lane's token (len 0 = none): its length is bounded by the
+    // next boundary in the 64 loaded slots; 64 - lane > 32, so a run that reaches past them is
+    // long whatever follows, and the single-token launch classifies alike
+    int len = 0;
     if (lane < W && ((mStartA >> lane) & 1u)) {
       const uint64_t rest = bound >> (lane + 1);
       len = rest ? __ffsll(static_cast<long long>(rest)) : (64 - lane);
-      mode = len >= kRunMin ? 1 : (len >= 2 ? 3 : 2);
     }
-    if (p.seg_map != nullptr && blockIdx.y == 0) {
-      const uint32_t bits = (__ballot_sync(0xffffffffu, mode == 2) != 0u ? 1u : 0u) |
-                            (__ballot_sync(0xffffffffu, mode == 3) != 0u ? 2u : 0u);
-      if (lane == 0) p.seg_map[t0 / W] = (p.seg_epoch << 2) | bits;
-    }
+    // a window with few single tokens moves them here, when the map can tell the single-token
+    // launch to leave them (the choice depends on the slots only: every plane makes it alike)
+    const uint32_t singles = __ballot_sync(0xffffffffu, len == 1);
+    const bool take_singles = p.seg_map != nullptr && __popc(singles) <= kRunSingles;
+    if (p.seg_map != nullptr && blockIdx.y == 0 && lane == 0)
+      p.seg_map[t0 / W] = (p.seg_epoch << 2) | (singles != 0u && !take_singles ? 1u : 0u);
+    const int mode = len >= 2 || (len == 1 && take_singles) ? 1 : 0;
     if (!SCATTER && p.fill_zero) {
       zmask = ~validA & wmask;
       const int64_t left = p.n_tokens - t0;
       if (left < 32) zmask &= (1u << left) - 1u;
     }
-    // at most W / 2 runs start in a window, so the list holds the block's runs
     const uint32_t m = __ballot_sync(0xffffffffu, mode == 1);
     int base = 0;
     if (lane == 0 && m) base = atomicAdd(&s_cnt, __popc(m));
@@ -865,7 +864,8 @@ __global__ void __launch_bounds__(256, CODEC ? 2 : 3) tile_run_kernel(const __gr
   const int cnt = s_cnt;
   for (int e = warp; e < cnt; e += kRunWarps) {
     const int o_s = s_os[e];
-    move_run<CT, LT, CODEC, SCATTER, 1>(p, cache_r, cache_w, lin_l, scl, l, s_soff[e] - o_s, o_s, s_len[e], tb + s_ts[e],
+    // (two token rows loaded at a time in a partly covered scatter chunk: more spill the run path)
+    move_run<CT, LT, CODEC, SCATTER, 2>(p, cache_r, cache_w, lin_l, scl, l, s_soff[e] - o_s, o_s, s_len[e], tb + s_ts[e],
                                         lane);
   }
   // zero rows for the skipped tokens of this warp's window (gather, fill mode)
@@ -917,14 +917,16 @@ __global__ void __launch_bounds__(256, 4) tile_single_fp8_kernel(const __grid_co
   const int64_t cap = p.block_size < 32 ? p.block_size : 32;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * tpc + warp * 32;
   if (warp * 32 < tpc && t0 < n) {
-    bool scan = true;
+    // the run launch of this call marked, per map window, whether it left single tokens there
+    bool scan = true, mine = true;
     if (p.seg_map != nullptr) {
-      // the run launch of this call marked, per map window, whether a single-token run starts there
       const int64_t m0 = t0 >> p.map_shift, m1 = (min(t0 + 32, n) - 1) >> p.map_shift;
       const uint32_t tag = p.seg_epoch << 2;
       uint32_t v = tag;
       if (lane <= m1 - m0) v = p.seg_map[m0 + lane];
       scan = !__all_sync(0xffffffffu, (v & ~3u) == tag && (v & 1u) == 0u);
+      const uint32_t vt = __shfl_sync(0xffffffffu, v, static_cast<int>(((t0 + lane) >> p.map_shift) - m0));
+      mine = !((vt & ~3u) == tag && (vt & 1u) == 0u);
     }
     if (scan) {
       const int64_t t = t0 + lane;
@@ -937,7 +939,7 @@ __global__ void __launch_bounds__(256, 4) tile_single_fp8_kernel(const __grid_co
       if (s >= 0) split_slot(s, p.block_size, &b, &o);
       const bool start = s >= 0 && (sp < 0 || s != sp + 1 || (o % cap) == 0);
       const bool cont = sn >= 0 && sn == s + 1 && ((o + 1) % cap) != 0;
-      const bool single = start && !cont;
+      const bool single = start && !cont && mine;
       const uint32_t m = __ballot_sync(0xffffffffu, single);
       int base = 0;
       if (lane == 0 && m) base = atomicAdd(&s_cnt, __popc(m));
@@ -1039,11 +1041,12 @@ __global__ void __launch_bounds__(256, 4) tile_single_fp8_kernel(const __grid_co
 // ---------------------------------------------------------------------------
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-template <typename CT, typename LT, int CODEC, bool SCATTER, int MODE>
-static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
+// The single-token launch (tile_single_kernel).
+template <typename CT, typename LT, int CODEC, bool SCATTER>
+static int launch_tile_single(TileLaunch& p, cudaStream_t st) {
   const int threads = 256;
   const int64_t planes = p.num_layers * p.n_kv;
-  auto kern = tile_seg_kernel<CT, LT, CODEC, SCATTER, MODE, false>;
+  auto kern = tile_single_kernel<CT, LT, CODEC, SCATTER, false>;
   const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kern), threads, 0);
   // Narrower windows when 32-token windows would not give every resident warp a few windows
   // (short batches; runs of random slots are one token each, so parallelism comes from windows).
@@ -1062,22 +1065,21 @@ static int launch_tile_segments_mode(TileLaunch& p, cudaStream_t st) {
   // Single tokens with few windows (decode batches): split each window's heads over up to
   // num_heads warp items (head_dim a multiple of 32, power-of-two splits dividing num_heads).
   p.head_split_shift = 0;
-  if (MODE == 2 && p.head_dim % 32 == 0) {
+  if (p.head_dim % 32 == 0) {
     while ((windows << p.head_split_shift) * groups < 4 * resident_warps &&
            p.num_heads % (int64_t{2} << p.head_split_shift) == 0)
       ++p.head_split_shift;
   }
   const int64_t items = windows << p.head_split_shift;
   // About 4 device-fulls of CTAs, spread over the groups; each CTA walks windows grid-stride.
-  // The run-end launch has work in few windows (sequence ends): one device-full.
-  const int64_t target = static_cast<int64_t>(per_sm) * sm_count() * (MODE == 3 ? 1 : 4);
+  const int64_t target = static_cast<int64_t>(per_sm) * sm_count() * 4;
   int64_t gx = std::max<int64_t>(1, target / groups);
   gx = std::min<int64_t>(gx, (items + (threads / 32) - 1) / (threads / 32));
   const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(groups));
   if (p.plane_group > 1)
-    return launch_pdl("tile_seg_kernel", tile_seg_kernel<CT, LT, CODEC, SCATTER, MODE, true>, grid, dim3(threads), 0, st,
+    return launch_pdl("tile_single_kernel", tile_single_kernel<CT, LT, CODEC, SCATTER, true>, grid, dim3(threads), 0, st,
                       p);
-  return launch_pdl("tile_seg_kernel", kern, grid, dim3(threads), 0, st, p);
+  return launch_pdl("tile_single_kernel", kern, grid, dim3(threads), 0, st, p);
 }
 
 // The single-token launch of FP8 calls with head_dim a multiple of 128 (cfg3's random slots,
@@ -1127,17 +1129,13 @@ static int launch_tile_run(TileLaunch& p, cudaStream_t st) {
 
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 static int launch_tile_segments(TileLaunch& p, cudaStream_t st) {
-  int rc = launch_tile_run<CT, LT, CODEC, SCATTER>(p, st);
+  const int rc = launch_tile_run<CT, LT, CODEC, SCATTER>(p, st);
   if (rc) return rc;
-  if constexpr (SCATTER) {
-    rc = launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 3>(p, st);
-    if (rc) return rc;
-  }
   if constexpr (CODEC != 0 && sizeof(CT) == 1) {
     if (p.head_dim % 128 == 0 && p.n_tokens < (int64_t{1} << 31) && p.num_heads <= 65535)
       return launch_tile_single_fp8<LT, CODEC, SCATTER>(p, st);
   }
-  return launch_tile_segments_mode<CT, LT, CODEC, SCATTER, 2>(p, st);
+  return launch_tile_single<CT, LT, CODEC, SCATTER>(p, st);
 }
 
 template <typename CT, typename LT, int CODEC, bool SCATTER>

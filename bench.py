@@ -743,7 +743,7 @@ def setup_workload(args, w: str, dev, rank: int, world: int):
             def step():
                 ma.kv_paged_to_linear(k, v, slots, out_k=ok, out_v=ov)
                 ma.kv_linear_to_paged(ok, ov, k, v, slots)
-            label = "tile_kernel (kv_paged_to_linear / kv_linear_to_paged)"
+            label = "tile_run_kernel + tile_single_kernel (kv_paged_to_linear / kv_linear_to_paged)"
         cfg = {"workload": f"{w}: fp16 [256,16,8,128] K/V, sequences 100/513/1024/2047 (T={t}), gather + scatter back",
                "tokens": t, "scaling": "replicas (one per rank)"}
         return cfg, 4 * 2 * t * nh * hs * 2, step, label
@@ -763,7 +763,7 @@ def setup_workload(args, w: str, dev, rank: int, world: int):
         cfg = {"workload": "cfg2-tile: [L,NB,NH,HD,BS] bf16 caches <-> [2,L,T,NH,HD] buffer, multi-layer gather + scatter",
                "layers_total": args.layers, "layers_per_rank": nl, "num_blocks": nb, "tokens": t,
                "scaling": "strong (layer-sharded)"}
-        return cfg, 4 * payload_bytes(nl, t), step, "tile_seg_kernel (multi-layer, all layers one launch)"
+        return cfg, 4 * payload_bytes(nl, t), step, "tile_run_kernel (multi-layer, all layers one launch)"
     if w.startswith("cfg3"):
         fmt = w.split("-")[1]
         lay = rank_layers(args.layers, world, rank)
@@ -792,7 +792,7 @@ def setup_workload(args, w: str, dev, rank: int, world: int):
                "scale": "per-layer-head amax/448" if fmt == "e4m3" else "scalar amax/57344",
                "scaling": "strong (layer-sharded)",
                "_ceiling": fp8_sector_ceiling(slots, nl, t, load_peak()[0])}
-        return cfg, 2 * nl * t * nh * hd * 6, step, "tile_seg_kernel FP8 (fused quantize-scatter / gather-dequant)"
+        return cfg, 2 * nl * t * nh * hd * 6, step, "tile_single_fp8_kernel + tile_run_kernel (fused quantize-scatter / gather-dequant)"
     if w == "cfg4":
         nl, nb, bs, nh, hs = 10, args.blocks or 8192, 64, 8, 128
         g2 = torch.Generator().manual_seed(2)
@@ -1104,10 +1104,11 @@ def run_ops_sweep(args) -> None:
           lambda: ma.kv_copy_paged_blocks(kc, vc, dk, dv, pairs), note=f"1024 block pairs of {tile.split(' tile')[0]}")
     del dk, dv
 
-    # a14 Flash dense load / cache-back, one layer, 64 sequences of up to 2048 tokens
-    B, S = 64, 2048
+    # a14 Flash dense load / cache-back, one layer, 32 sequences of up to 2048 tokens whose block
+    # tables split one permutation of the 4096 blocks (no block shared: every byte counted moves)
+    B, S = 32, 2048
     lens = torch.randint(S // 2, S + 1, (B,), generator=torch.Generator().manual_seed(4))
-    bt = torch.stack([torch.randperm(NB, generator=torch.Generator().manual_seed(10 + i))[: S // BS] for i in range(B)]).to(torch.int32)
+    bt = torch.randperm(NB, generator=torch.Generator().manual_seed(10))[: B * (S // BS)].view(B, S // BS).to(torch.int32)
     tok = int(lens.sum())
     lens_d, bt_d = lens.to(dev), bt.to(dev)
     ok = torch.empty((B, S, NH, HD), dtype=torch.bfloat16, device=dev)

@@ -42,6 +42,7 @@ struct TileLaunch {
   int64_t num_layers, num_heads, head_dim, block_size, num_slots, n_tokens, n_chunks;
   int32_t slots64, n_kv, fill_zero, cache_vec, lin_vec, scale_mode, heads_per_step;
   int32_t window;       // tokens per warp window of the segment kernel (8, 16 or 32)
+  int32_t run_heads;    // heads per item of the run kernel's walk (fills a warp's 32 lanes)
   int32_t plane_group;  // (kv, layer) planes a segment-kernel block walks per window
   // Single-token launch (tile_single_kernel): a window's heads are split into 2^head_split_shift groups,
   // each a separate warp item, when the call has too few windows to fill the device (decode
@@ -391,9 +392,9 @@ constexpr int kRunSingles = 4;
 
 // ---------------------------------------------------------------------------
 // One segment (a run of consecutive slots inside one cache block, at most 32
-// tokens, chunk-aligned in slot space) of one (kv, layer) plane through the
-// 16-byte cache chunks it touches.  The lanes split the (head, head_dim-group)
-// units x chunks; neighbouring lanes take neighbouring chunks of one unit, so
+// tokens, chunk-aligned in slot space) of one (kv, layer) plane, heads
+// [h_lo, h_hi), through the 16-byte cache chunks it touches.  The lanes split
+// the (head, head_dim-group) units x chunks; neighbouring lanes take neighbouring chunks of one unit, so
 // one warp instruction covers whole 32-byte sectors of a cache row.  A unit
 // moves R head_dim rows (R = 16 / sizeof(linear element)) of G token columns
 // (G = 16 / sizeof(cache element)):
@@ -409,18 +410,20 @@ constexpr int kRunSingles = 4;
 // ---------------------------------------------------------------------------
 template <typename CT, typename LT, int CODEC, bool SCATTER, int KTOK>
 __device__ __forceinline__ void move_run(const TileLaunch& p, const CT* cache_r, CT* cache_w, LT* lin_l, const float* scl,
-                                         int64_t l, int64_t cbase, int o_s, int len, int64_t ts, int lane) {
+                                         int64_t l, int64_t cbase, int o_s, int len, int64_t ts, int h_lo, int h_hi,
+                                         int lane) {
   constexpr int G = 16 / sizeof(CT);
   constexpr int R = 16 / sizeof(LT);
   using C = Codec<CT, LT, CODEC>;
   const int upr = static_cast<int>(p.head_dim) / R;
   const int NH = static_cast<int>(p.num_heads);
-  const int units = NH * upr;
+  const int units = (h_hi - h_lo) * upr;
   const int c_first = o_s / G, nch = (o_s + len - 1) / G - c_first + 1;
   for (int it = lane; it < units * nch; it += 32) {
     const int u = it / nch;
     const int c = c_first + (it - u * nch);
-    const int h = u / upr, dg = u - h * upr;
+    const int hr = u / upr, dg = u - hr * upr;
+    const int h = h_lo + hr;
     float sc = 1.f;
     if (CODEC) sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? h : l * NH + h)];
     const int64_t row0 = cbase + h * p.c_sh + static_cast<int64_t>(dg) * R * p.c_sd;
@@ -761,8 +764,10 @@ __global__ void __launch_bounds__(256, 4) tile_single_kernel(const __grid_consta
 //      of them and a segment map records that -- marks the zero rows (gather,
 //      fill mode) and, in the blocks of the first plane, writes the segment map
 //      entry of its window for the single-token launch that follows.
-//   2. The warps take the list's segments in turn and move each through
-//      move_run.
+//   2. The warps take (segment, head group) items of the list in turn and move
+//      each through move_run; a group holds as many heads as fill the 32 lanes
+//      with the (unit, chunk) pairs of a run as long as a block's chunk span
+//      (bf16, head_dim 128, block_size 16: one head; FP8: two).
 // One plane per block (grid = token ranges of 8W tokens x planes): nothing of
 // the scan stays live in the walk, blocks are small enough that the last wave
 // stays balanced, and the run path keeps 80 registers for its transposes
@@ -861,12 +866,16 @@ __global__ void __launch_bounds__(256, CODEC ? 2 : 3) tile_run_kernel(const __gr
   CT* cache_w = reinterpret_cast<CT*>(p.cache[kv]) + l * p.c_sl;
   LT* lin_l = reinterpret_cast<LT*>(p.lin[kv]) + l * p.l_sl;
   const float* scl = CODEC ? p.scale[kv] : nullptr;
-  const int cnt = s_cnt;
-  for (int e = warp; e < cnt; e += kRunWarps) {
+  const int NH = static_cast<int>(p.num_heads);
+  const int hpi = p.run_heads;
+  const int groups = (NH + hpi - 1) / hpi;
+  const int items = s_cnt * groups;
+  for (int it = warp; it < items; it += kRunWarps) {
+    const int e = it / groups, h = (it - e * groups) * hpi;
     const int o_s = s_os[e];
     // (two token rows loaded at a time in a partly covered scatter chunk: more spill the run path)
-    move_run<CT, LT, CODEC, SCATTER, 2>(p, cache_r, cache_w, lin_l, scl, l, s_soff[e] - o_s, o_s, s_len[e], tb + s_ts[e],
-                                        lane);
+    move_run<CT, LT, CODEC, SCATTER, 2>(p, cache_r, cache_w, lin_l, scl, l, s_soff[e] - o_s, o_s, s_len[e], tb + s_ts[e], h,
+                                        min(h + hpi, NH), lane);
   }
   // zero rows for the skipped tokens of this warp's window (gather, fill mode)
   if (!SCATTER) {
@@ -1100,9 +1109,10 @@ static int launch_tile_single_fp8(TileLaunch& p, cudaStream_t st) {
   return launch_pdl("tile_single_fp8_kernel", kern, grid, dim3(threads), 0, st, p, tpc, hpc);
 }
 
-// The run launch: windows of 32 tokens (16 or 8 when that leaves resident warps without a few
-// windows), blocks of 8 windows of one plane.  It sets the segment map fields the launches after
-// it read.
+// The run launch: blocks of 8 windows of one plane; windows of 32 tokens (gathers: 16 or 8 when
+// that leaves resident warps without a few windows; a scatter's scan also reads the owner table,
+// which the smaller blocks pay for more often than they gain).  It sets the segment map fields
+// the launches after it read.
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 static int launch_tile_run(TileLaunch& p, cudaStream_t st) {
   const int threads = kRunWarps * 32;
@@ -1111,9 +1121,18 @@ static int launch_tile_run(TileLaunch& p, cudaStream_t st) {
   const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kern), threads, 0);
   const int64_t resident_warps = static_cast<int64_t>(per_sm) * sm_count() * kRunWarps;
   p.window = 32;
-  while (p.window > 8 && (p.n_tokens + p.window - 1) / p.window * planes < 4 * resident_warps) p.window /= 2;
+  while (!SCATTER && p.window > 8 && (p.n_tokens + p.window - 1) / p.window * planes < 4 * resident_warps) p.window /= 2;
   const int64_t windows = (p.n_tokens + p.window - 1) / p.window;
   p.windows = windows;
+  // heads per walk item: (unit, chunk) pairs of one head for a run spanning a block's chunks
+  const int64_t cap = std::min<int64_t>(p.block_size, 32);
+  const int64_t g = 16 / static_cast<int64_t>(sizeof(CT));
+  const int64_t per_head = (p.head_dim / (16 / static_cast<int64_t>(sizeof(LT)))) * ((cap + g - 1) / g);
+  p.run_heads = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(p.num_heads, 32 / std::max<int64_t>(per_head, 1))));
+  // A scatter with enough whole runs to give every resident warp several moves them whole: on
+  // large calls that measured faster than head groups (FP8 merged store 4683 -> 4896 GB/s), on
+  // small ones slower (Flash cache-back 4509 -> 3812).
+  if (SCATTER && (p.n_tokens + cap - 1) / cap * planes >= 8 * resident_warps) p.run_heads = static_cast<int32_t>(p.num_heads);
   if (p.seg_map != nullptr) {
     if (windows > p.seg_map_entries) p.seg_map = nullptr;  // too small: the later launches scan every window
     else {

@@ -489,23 +489,28 @@ def test_fp8_block_table_load_scales_inside_and_outside_fast_range(cuda_device, 
     eq(ov, rv, "fp8 block-table load v")
 
 
-def _mixed_run_slots(n_target, nb, bs, gen) -> torch.Tensor:
-    """Unique slots in runs of every kind the two tile launches split between them: whole
-    blocks, runs of 1-15 slots from a random in-block offset, lone random slots and negatives."""
+def _mixed_run_slots(n_target, nb, bs, gen, stretch=1) -> torch.Tensor:
+    """Unique slots in runs of every kind the tile launches split between them: whole blocks,
+    runs of 1-15 slots from a random in-block offset, lone random slots (stretches of up to
+    ``stretch`` of them in a row, each in a block of its own) and negatives."""
     perm = torch.randperm(nb, generator=gen).tolist()
     kinds = torch.randint(0, 4, (n_target,), generator=gen).tolist()
     lens = torch.randint(1, bs, (n_target,), generator=gen).tolist()
     offs = torch.randint(0, bs, (n_target,), generator=gen).tolist()
-    out, n, i = [], 0, 0
+    reps = torch.randint(1, stretch + 1, (n_target,), generator=gen).tolist()
+    out, n, i, nxt = [], 0, 0, 0
     while n < n_target:
-        k, b = kinds[i], perm[i]
+        k = kinds[i]
         if k == 0:
-            piece = [b * bs + o for o in range(bs)]
+            piece = [perm[nxt] * bs + o for o in range(bs)]
+            nxt += 1
         elif k == 1:
             o0 = min(offs[i], bs - lens[i])
-            piece = [b * bs + o0 + o for o in range(lens[i])]
+            piece = [perm[nxt] * bs + o0 + o for o in range(lens[i])]
+            nxt += 1
         elif k == 2:
-            piece = [b * bs + offs[i]]
+            piece = [perm[nxt + j] * bs + (offs[i] + 5 * j) % bs for j in range(reps[i])]
+            nxt += reps[i]
         else:
             piece = [-1] * (1 + offs[i] % 3)
         out.extend(piece)
@@ -514,23 +519,26 @@ def _mixed_run_slots(n_target, nb, bs, gen) -> torch.Tensor:
     return torch.tensor(out[:n_target], dtype=torch.int64)
 
 
+@pytest.mark.parametrize("stretch", (1, 24))
 @pytest.mark.parametrize("stale_bits", (0, 1))
 @pytest.mark.parametrize("fp8", (False, True))
-def test_tile_segment_map_skips_only_clean_windows(cuda_device, monkeypatch, fp8, stale_bits):
-    """The single-token and run-end launches skip the windows that the run launch of the same
-    call marked free of their kind: results equal the unmapped launches' and the oracle's for
-    calls whose window sizes differ between the launches (8 to 32 tokens), also when the map
-    already holds this call's epoch (entry = epoch << 2 | bits) marked clean everywhere
-    (stale_bits 0), or marked with only the single-token bit (stale_bits 1: a run-end launch
-    that trusted it would drop the scatter runs of 2..G-1 tokens) -- the run launch rewrites
-    every entry before the other launches read it."""
+def test_tile_segment_map_skips_only_clean_windows(cuda_device, monkeypatch, fp8, stale_bits, stretch):
+    """The run launch moves the single tokens of the windows that hold at most four of them and
+    records, per window, whether it left single tokens to the single-token launch, which skips the
+    other windows and tokens: results equal the unmapped launches' (where the run launch leaves
+    every single token) and the oracle's for calls whose window sizes differ between the two
+    launches (8 to 32 tokens), with lone slots scattered (stretch 1) or in stretches of up to 24
+    (windows with many single tokens next to windows with few), also when the map already holds
+    this call's epoch (entry = epoch << 2 | bit) marked clean everywhere (stale_bits 0) or marked
+    everywhere (stale_bits 1) -- the run launch rewrites every entry before the single-token
+    launch reads it."""
     from musa_aiter import _native
 
-    g = torch.Generator().manual_seed(11)
-    nb, nh, hd, bs = 32768, 1, 16, 16
+    g = torch.Generator().manual_seed(11 + stretch)
+    nb, nh, hd, bs = 32768 if stretch == 1 else 131072, 1, 16, 16
     ks, vs = torch.tensor(0.013), torch.tensor(0.021)
     for t in (600, 40000, 170000):
-        slots = _mixed_run_slots(t, nb, bs, g)
+        slots = _mixed_run_slots(t, nb, bs, g, stretch)
         if fp8:
             kc = torch.randint(0, 256, (nb, nh, hd, bs), generator=g, dtype=torch.uint8)
             vc = torch.randint(0, 256, (nb, nh, hd, bs), generator=g, dtype=torch.uint8)

@@ -232,15 +232,16 @@ MAK_API int mak_kv_linear_to_paged_fp8(const mak_linear_desc* in, const mak_page
 
 /*
  * The four calls above with a segment map: a device vector of uint32 that the
- * pass over runs of consecutive slots fills with (epoch << 2) | (a single-slot
- * run starts here) | (a scatter run of 2 to 15 slots, shorter than a 16-byte
- * chunk, starts here) << 1, one entry per window of 8-32 tokens (ceil(T / 8)
- * entries always suffice; a smaller map is ignored), so that the passes for
- * those runs skip the windows without them instead of scanning them.  epoch
- * in [1, 2^30) must differ from the one
- * of any call still in flight on the same map; entries of other epochs are
- * never trusted, so a map may start with any contents.  Results are identical
- * to the unmapped calls.  Host-side additions, no reference counterpart.
+ * pass over runs of consecutive slots fills with (epoch << 2) | (this window's
+ * single-slot runs are left to the single-slot pass), one entry per window of
+ * 8-32 tokens (ceil(T / 8) entries always suffice; a smaller map is ignored).
+ * With a map, the run pass also moves the single slots of windows holding at
+ * most four of them, and the single-slot pass skips the windows and slots the
+ * map says it has nothing to do for, instead of scanning them.  epoch in
+ * [1, 2^30) must differ from the one of any call still in flight on the same
+ * map; entries of other epochs are never trusted, so a map may start with any
+ * contents.  Results are identical to the unmapped calls.  Host-side
+ * additions, no reference counterpart.
  */
 MAK_API int mak_kv_paged_to_linear_mapped(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,
                                           int32_t slot_dtype, int32_t fill_zero, uint32_t* seg_map,

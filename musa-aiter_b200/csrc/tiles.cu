@@ -771,7 +771,7 @@ __global__ void __launch_bounds__(256, 4) tile_single_kernel(const __grid_consta
 // One plane per block (grid = token ranges of 8W tokens x planes): nothing of
 // the scan stays live in the walk, blocks are small enough that the last wave
 // stays balanced, and the run path keeps 80 registers for its transposes
-// (3 blocks per SM; 2 with an FP8 codec).
+// (3 blocks per SM; 2 for FP8 stores, whose chunk encoder holds 16 token rows).
 // ---------------------------------------------------------------------------
 constexpr int kRunWarps = 8;
 // segments listed per window: s single tokens and r runs (two or more tokens, the last one may
@@ -779,7 +779,7 @@ constexpr int kRunWarps = 8;
 constexpr int kRunMaxSeg = kRunWarps * ((32 + 1 + kRunSingles) / 2);
 
 template <typename CT, typename LT, int CODEC, bool SCATTER>
-__global__ void __launch_bounds__(256, CODEC ? 2 : 3) tile_run_kernel(const __grid_constant__ TileLaunch p) {
+__global__ void __launch_bounds__(256, (CODEC && SCATTER) ? 2 : 3) tile_run_kernel(const __grid_constant__ TileLaunch p) {
   constexpr int R = 16 / sizeof(LT);
   __shared__ int64_t s_soff[kRunMaxSeg];  // element offset of the run's first slot in the plane
   __shared__ int s_ts[kRunMaxSeg];        // first token, relative to the block's first token

@@ -18,6 +18,8 @@ from __future__ import annotations
 
 import ctypes
 import math
+import struct
+import threading
 from typing import Literal
 
 import torch
@@ -543,17 +545,48 @@ def _validate_fp8_cache_tensor(tensor: torch.Tensor, *, name: str) -> None:
     raise ValueError(f"{name}: FP8 cache storage must be torch.uint8 or a supported torch.float8 dtype")
 
 
+# Python-number FP8 scales placed on a device once: (device index, float32 bits) -> 0-d tensor that
+# is never written again, so every stream may read it.
+_SCALAR_SCALES: dict[tuple[int, int], torch.Tensor] = {}
+_SCALAR_SCALES_LOCK = threading.Lock()
+_SCALAR_SCALES_MAX = 1024
+
+
+def _device_scalar_scale(value: float, device: torch.device) -> torch.Tensor:
+    """A float32 0-d device tensor holding ``value``.  The first use of a value on a device fills it
+    and waits for the fill, then the tensor is reused; under stream capture the fill is captured
+    with the call instead (no wait is allowed there)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (index, struct.unpack("<I", struct.pack("<f", value))[0])
+    cached = _SCALAR_SCALES.get(key)
+    if cached is not None:
+        return cached
+    dev = torch.device("cuda", index)
+    if torch.cuda.is_current_stream_capturing():
+        return torch.full((), value, dtype=torch.float32, device=dev)
+    tensor = torch.full((), value, dtype=torch.float32, device=dev)
+    torch.cuda.current_stream(dev).synchronize()
+    with _SCALAR_SCALES_LOCK:
+        if len(_SCALAR_SCALES) >= _SCALAR_SCALES_MAX:
+            _SCALAR_SCALES.clear()
+        _SCALAR_SCALES[key] = tensor
+    return tensor
+
+
 def _ensure_fp8_scale(scale, *, device: torch.device, name: str, num_heads: int, num_layers: int | None = None) -> torch.Tensor:
     """musa_aiter/ops/kv_transfer.py:2110-2121: positive finite scalar, [NH] or [L, NH].
 
-    A Python number is checked on the host and placed with a fill launch: copying it from host
-    memory would synchronise the stream on every call.
+    A Python number is checked on the host and placed on the device once per value (copying it from
+    host memory on every call would synchronise the stream each time, a fill launch per call costs
+    a launch).
     """
     if isinstance(scale, (int, float)) and not isinstance(scale, bool):
         value = float(scale)
         if not math.isfinite(value) or value <= 0.0:
             raise ValueError(f"{name}: FP8 scale must be positive and finite")
-        return torch.full((), value, dtype=torch.float32, device=device)
+        if device.type != "cuda":
+            return torch.full((), value, dtype=torch.float32, device=device)
+        return _device_scalar_scale(value, device)
     scale_tensor = torch.as_tensor(scale, dtype=torch.float32, device=device)
     if scale_tensor.device.type != "cuda" or validation_enabled():
         if not bool(torch.isfinite(scale_tensor).all()) or float(scale_tensor.min().item()) <= 0.0:

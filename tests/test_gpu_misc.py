@@ -287,3 +287,31 @@ def test_memcpy_batch_h2d_d2h(cuda_device):
         ma.lmcache_musa_memcpy_batch_async([dev], [torch.zeros(16, dtype=torch.uint8)], [16])
     assert ma.lmcache_musa_memcpy_batch_async([dev], [dev], [16]) is False
     assert ma.native_lmcache_musa_batch_copy_runtime_versions()[0] >= 12000
+
+
+def test_python_number_fp8_scales_are_placed_once(cuda_device):
+    """FP8 scales given as Python numbers go to the device once per value and device: the same
+    read-only tensor serves later calls on any stream, and results equal tensor scales'."""
+    from musa_aiter.ops import kv_transfer as kt
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    a = kt._device_scalar_scale(0.0173, dev)
+    assert a is kt._device_scalar_scale(0.0173, dev) and a.dtype == torch.float32 and a.dim() == 0
+    assert float(a) == float(torch.tensor(0.0173, dtype=torch.float32))
+    g = torch.Generator().manual_seed(5)
+    nb, nh, hd, bs = 64, 2, 128, 16
+    kl = torch.randn((300, nh, hd), generator=g).to(torch.bfloat16).cuda()
+    vl = torch.randn((300, nh, hd), generator=g).to(torch.bfloat16).cuda()
+    slots = torch.randperm(nb * bs, generator=g)[:300].cuda()
+    outs = []
+    for scales, stream in (((0.0173, 0.031), None), ((0.0173, 0.031), torch.cuda.Stream()),
+                           ((torch.tensor(0.0173).cuda(), torch.tensor(0.031).cuda()), None)):
+        k8 = torch.zeros((nb, nh, hd, bs), dtype=torch.uint8, device="cuda")
+        v8 = torch.zeros_like(k8)
+        with torch.cuda.stream(stream or torch.cuda.current_stream()):
+            ma.kv_linear_to_paged_fp8(kl, vl, k8, v8, slots, *scales)
+            ok, ov = ma.kv_paged_fp8_to_linear(k8, v8, slots, *scales)
+        torch.cuda.synchronize()
+        outs.append((k8, v8, ok, ov))
+    for other in outs[1:]:
+        assert all(torch.equal(x, y) for x, y in zip(outs[0], other))

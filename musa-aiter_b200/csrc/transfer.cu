@@ -9,9 +9,9 @@
 //   mode 1: each staging row is [value_bytes | scale_bytes]; the paged page keeps
 //           all values first (block*stride + t*value_bytes) then all scales
 //           (block*stride + BS*value_bytes + t*scale_bytes).
-// direction 0 writes the paged pages, 1 reads them into staging.  One warp moves
-// one (layer, block) with the widest vector every address allows, four vectors
-// per lane in flight; all layers go in one launch.  Negative block ids are skipped.
+// direction 0 writes the paged pages, 1 reads them into staging.  Warps move
+// pieces of 32 x 8 vectors of one (layer, block) with the widest vector every
+// address allows; all layers go in one launch.  Negative block ids are skipped.
 #include <algorithm>
 
 #include "common.cuh"
@@ -38,62 +38,66 @@ struct VecOf<8> { using T = uint2; };
 template <>
 struct VecOf<4> { using T = uint32_t; };
 
-// Copy `n` vectors of a 2-D span: vector i lies at row i / per_row, column
-// i % per_row, rows `src_pitch` / `dst_pitch` bytes apart (a contiguous span is
-// one row).  Each lane keeps four vectors in flight.
-template <int VEC>
-__device__ __forceinline__ void copy_rows(uint8_t* dst, int64_t dst_pitch, const uint8_t* src, int64_t src_pitch,
-                                          uint32_t per_row, uint32_t n, int lane) {
-  using V = typename VecOf<VEC>::T;
-  for (uint32_t i0 = lane; i0 < n; i0 += 32 * 4) {
-    V r[4];
-    int64_t so[4], dof[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint32_t i = i0 + 32 * u;
-      const uint32_t row = i / per_row, col = i - row * per_row;
-      so[u] = row * src_pitch + static_cast<int64_t>(col) * VEC;
-      dof[u] = row * dst_pitch + static_cast<int64_t>(col) * VEC;
-      if (i < n) r[u] = *reinterpret_cast<const V*>(src + so[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (i0 + 32 * u < n) *reinterpret_cast<V*>(dst + dof[u]) = r[u];
-  }
-}
+// One warp item = up to 32 x kStridedU vectors of one (layer, block): the block's staging
+// rows are contiguous (BS rows at pitch row_bytes), so vector i sits at staging byte i * VEC;
+// on the page it sits at the same offset in mode 0, and in mode 1 at row * value_bytes + col *
+// VEC (value part) or BS * value_bytes + row * scale_bytes + (col - vv) * VEC (scale part), where
+// row / col are i's row and column in vectors of row_bytes.  Lanes carry (row, col) as they step
+// by 32 vectors, so one division per item resolves them; every lane keeps kStridedU vectors in
+// flight, and the items of a block go to different warps.
+constexpr int kStridedU = 8;
 
-// One warp per (layer, block) of the batch: mode 0 moves the block's BS rows as
-// one contiguous span; mode 1 moves the values (BS rows of value_bytes, staging
-// pitch row_bytes, page pitch value_bytes) and then the scales as two 2-D spans.
 template <int VEC>
 __global__ void __launch_bounds__(256) strided_block_kernel(const __grid_constant__ StridedLaunch p) {
+  using V = typename VecOf<VEC>::T;
   const int lane = threadIdx.x & 31;
-  const int64_t units = static_cast<int64_t>(p.num_layers) * p.n_valid;
+  const uint32_t rv = static_cast<uint32_t>(p.row_bytes / VEC);  // vectors per staging row
+  const uint32_t vv = static_cast<uint32_t>(p.value_bytes / VEC);
+  const uint32_t n = static_cast<uint32_t>(p.block_size) * rv;   // vectors per (layer, block)
+  constexpr uint32_t kPer = 32u * kStridedU;
+  const uint32_t per_unit = (n + kPer - 1) / kPer;
+  const int64_t total = static_cast<int64_t>(p.num_layers) * p.n_valid * per_unit;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < units; w += nwarps) {
-    const int layer = static_cast<int>(w / p.n_valid);
-    const int64_t blk_i = w - static_cast<int64_t>(layer) * p.n_valid;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < total; w += nwarps) {
+    const int64_t unit = w / per_unit;
+    const uint32_t part = static_cast<uint32_t>(w - unit * per_unit);
+    const int layer = static_cast<int>(unit / p.n_valid);
+    const int64_t blk_i = unit - static_cast<int64_t>(layer) * p.n_valid;
     const int64_t blk = p.block_ids[p.idx_start + blk_i];
     if (blk < 0) continue;
     uint8_t* staged = p.staging + ((static_cast<int64_t>(p.layer_base + layer) * p.staging_tokens) + p.offset_in_object +
                                    blk_i * p.block_size) * p.row_bytes;
     uint8_t* page = reinterpret_cast<uint8_t*>(p.layers[layer]) + blk * p.block_stride;
-    const uint32_t bs = static_cast<uint32_t>(p.block_size);
-    if (p.mode == 0) {
-      const uint32_t n = static_cast<uint32_t>(p.block_size * p.row_bytes / VEC);
-      if (p.direction == 0) copy_rows<VEC>(page, 0, staged, 0, n, n, lane);
-      else copy_rows<VEC>(staged, 0, page, 0, n, n, lane);
-    } else {
-      const uint32_t vv = static_cast<uint32_t>(p.value_bytes / VEC), sv = static_cast<uint32_t>(p.scale_bytes / VEC);
-      uint8_t* pv = page;
-      uint8_t* ps = page + p.block_size * p.value_bytes;
-      if (p.direction == 0) {
-        if (vv) copy_rows<VEC>(pv, p.value_bytes, staged, p.row_bytes, vv, vv * bs, lane);
-        if (sv) copy_rows<VEC>(ps, p.scale_bytes, staged + p.value_bytes, p.row_bytes, sv, sv * bs, lane);
+    const uint32_t i0 = part * kPer + lane;
+    uint32_t row = i0 / rv, col = i0 - row * rv;
+    int64_t po[kStridedU];
+    V r[kStridedU];
+#pragma unroll
+    for (int u = 0; u < kStridedU; ++u) {
+      const uint32_t i = i0 + 32u * u;
+      if (p.mode == 0 || col < vv) {
+        po[u] = p.mode == 0 ? static_cast<int64_t>(i) * VEC
+                            : static_cast<int64_t>(row) * p.value_bytes + static_cast<int64_t>(col) * VEC;
       } else {
-        if (vv) copy_rows<VEC>(staged, p.row_bytes, pv, p.value_bytes, vv, vv * bs, lane);
-        if (sv) copy_rows<VEC>(staged + p.value_bytes, p.row_bytes, ps, p.scale_bytes, sv, sv * bs, lane);
+        po[u] = p.block_size * p.value_bytes + static_cast<int64_t>(row) * p.scale_bytes +
+                static_cast<int64_t>(col - vv) * VEC;
       }
+      if (i < n) {
+        if (p.direction == 0) r[u] = *reinterpret_cast<const V*>(staged + static_cast<int64_t>(i) * VEC);
+        else r[u] = *reinterpret_cast<const V*>(page + po[u]);
+      }
+      col += 32u;
+      while (col >= rv) {
+        col -= rv;
+        ++row;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kStridedU; ++u) {
+      const uint32_t i = i0 + 32u * u;
+      if (i >= n) continue;
+      if (p.direction == 0) *reinterpret_cast<V*>(page + po[u]) = r[u];
+      else *reinterpret_cast<V*>(staged + static_cast<int64_t>(i) * VEC) = r[u];
     }
   }
 }
@@ -101,8 +105,9 @@ __global__ void __launch_bounds__(256) strided_block_kernel(const __grid_constan
 template <int VEC>
 static int launch_strided(const StridedLaunch& p, cudaStream_t st) {
   const int threads = 256;
-  const int64_t units = static_cast<int64_t>(p.num_layers) * p.n_valid;  // one warp each
-  const int grid = grid_for(reinterpret_cast<const void*>(strided_block_kernel<VEC>), threads, 0, (units + 7) / 8);
+  const int64_t n = p.block_size * (p.row_bytes / VEC);
+  const int64_t items = static_cast<int64_t>(p.num_layers) * p.n_valid * ((n + 32 * kStridedU - 1) / (32 * kStridedU));
+  const int grid = grid_for(reinterpret_cast<const void*>(strided_block_kernel<VEC>), threads, 0, (items + 7) / 8);
   if (grid <= 0) return MAK_OK;
   strided_block_kernel<VEC><<<grid, threads, 0, st>>>(p);
   return launch_status("strided_block_kernel");

@@ -17,7 +17,7 @@ import torch
 
 from .. import _build, _native
 from ..dispatch import emit_native
-from ._common import kernel_slots
+from ._common import kernel_slots, validation_enabled
 
 LayoutName = Literal["layer_first", "page_first"]
 _ABI_VERSION = 1
@@ -99,7 +99,13 @@ def _validate_inputs(src_k, dst_k, src_v, dst_v, src_indices, dst_indices, src_l
 
 
 def _validate_page_indices(src_indices, dst_indices, src_pages: int, dst_pages: int) -> None:
-    """Reference :171-184: entries must be -1 or in range (read back to the host)."""
+    """Reference :171-184: entries must be -1 or in range (read back to the host).
+
+    With device index tables and ``MUSA_AITER_SKIP_VALIDATION=1`` the read-back, which waits for
+    the stream on every call, is skipped: the row kernel skips rows whose page index is negative
+    or out of range on either side."""
+    if src_indices.device.type == "cuda" and dst_indices.device.type == "cuda" and not validation_enabled():
+        return
     s = src_indices.to(device="cpu", dtype=torch.long)
     d = dst_indices.to(device="cpu", dtype=torch.long)
     if s.numel() == 0:

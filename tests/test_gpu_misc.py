@@ -199,22 +199,26 @@ def test_cachegen_constant_and_two_valued_slabs_vs_oracle(cuda_device, dt, bins)
         eq(cb, rcb, "codebook")
 
 
+@pytest.mark.parametrize("vec", (16, 8, 4))
 @pytest.mark.parametrize("mode", (0, 1))
-def test_strided_block_transfer_vs_oracle(cuda_device, mode):
-    """DSV4 staging <-> padded pages, both directions, vs the restated kernel semantics."""
-    g = torch.Generator().manual_seed(12 + mode)
-    nl, nb, bs = 3, 20, 8
-    value_bytes, scale_bytes = (0, 0) if mode == 0 else (576, 16)
-    row = 592 if mode == 0 else value_bytes + scale_bytes
+def test_strided_block_transfer_vs_oracle(cuda_device, mode, vec):
+    """DSV4 staging <-> padded pages, both directions, vs the restated kernel semantics; row,
+    value and scale sizes that allow 16-, 8- and 4-byte vectors, and blocks split over several
+    warp items."""
+    g = torch.Generator().manual_seed(12 + mode + vec)
+    nl, nb, bs = 3, 20, 8 if vec == 16 else 37
+    value_bytes, scale_bytes = (0, 0) if mode == 0 else {16: (576, 16), 8: (584, 8), 4: (652, 4)}[vec]
+    row = {16: 592, 8: 600, 4: 604}[vec] if mode == 0 else value_bytes + scale_bytes
     stride = bs * row + 64  # padded pages
+    stt = max(50, 9 + 4 * bs + 3)  # staging tokens: the batch's blocks start at token 9
     pages = [torch.randint(0, 256, (nb * stride,), generator=g, dtype=torch.int32).to(torch.uint8) for _ in range(nl)]
-    staging = torch.randint(0, 256, (nl, 50, row), generator=g, dtype=torch.int32).to(torch.uint8)
+    staging = torch.randint(0, 256, (nl, stt, row), generator=g, dtype=torch.int32).to(torch.uint8)
     block_ids = torch.tensor([7, 3, -1, 12, 0, 19], dtype=torch.int64)
     idx_start, n_valid, offset = 1, 4, 9
     dpages = [p.cuda() for p in pages]
     dstaging = staging.cuda()
     ok = ma.lmcache_kv_strided_block_transfer(dstaging, [p.data_ptr() for p in dpages], block_ids.cuda(), 0, nl, idx_start,
-                                              n_valid, offset, 50, bs, row, stride, mode, value_bytes, scale_bytes)
+                                              n_valid, offset, stt, bs, row, stride, mode, value_bytes, scale_bytes)
     assert ok is True
     rpages = [p.numpy().copy() for p in pages]
     O.strided_block_transfer(staging.numpy(), rpages, block_ids.numpy(), 0, idx_start, n_valid, offset, bs, row, stride,
@@ -223,13 +227,13 @@ def test_strided_block_transfer_vs_oracle(cuda_device, mode):
         eq(a, b, "staging->paged")
     out = torch.zeros_like(dstaging)
     ok = ma.lmcache_kv_strided_block_transfer(out, [p.data_ptr() for p in dpages], block_ids.cuda(), 1, nl, idx_start,
-                                              n_valid, offset, 50, bs, row, stride, mode, value_bytes, scale_bytes)
+                                              n_valid, offset, stt, bs, row, stride, mode, value_bytes, scale_bytes)
     assert ok is True
     rout = np.zeros(out.shape, np.uint8)
     O.strided_block_transfer(rout, rpages, block_ids.numpy(), 1, idx_start, n_valid, offset, bs, row, stride, mode,
                              value_bytes, scale_bytes)
     eq(out, rout, "paged->staging")
-    assert ma.lmcache_kv_strided_block_transfer(out, [0] * 2, block_ids.cuda(), 1, nl, 0, 1, 0, 50, bs, row, stride, mode) is False
+    assert ma.lmcache_kv_strided_block_transfer(out, [0] * 2, block_ids.cuda(), 1, nl, 0, 1, 0, stt, bs, row, stride, mode) is False
 
 
 def test_flash_random_vs_oracle(cuda_device):
@@ -315,3 +319,29 @@ def test_python_number_fp8_scales_are_placed_once(cuda_device):
         outs.append((k8, v8, ok, ov))
     for other in outs[1:]:
         assert all(torch.equal(x, y) for x, y in zip(outs[0], other))
+
+
+def test_hicache_device_indices_without_validation(cuda_device, monkeypatch):
+    """With device page indices and validation off, a HiCache transfer reads nothing back to the
+    host: pages whose index is -1 or out of range on either side are skipped by the kernel (the
+    rest move exactly as torch indexing moves them), where validation on raises like the
+    reference."""
+    g = torch.Generator().manual_seed(13)
+    L, P, W = 3, 40, 64
+    src_k = torch.randn((L, P, W), generator=g).to(torch.bfloat16).cuda()
+    src_v = torch.randn((L, P, W), generator=g).to(torch.bfloat16).cuda()
+    si = torch.tensor([3, 7, -1, 39, 41, 12, 5, 0], dtype=torch.int64)
+    di = torch.tensor([0, 9, 4, 100, 2, -1, 39, 20], dtype=torch.int64)
+    with pytest.raises(ValueError):
+        ma.hicache_transfer_kv_all_layer(src_k, torch.zeros_like(src_k), src_v, torch.zeros_like(src_v), si.cuda(),
+                                         di.cuda())
+    monkeypatch.setenv("MUSA_AITER_SKIP_VALIDATION", "1")
+    dst_k, dst_v = torch.zeros_like(src_k), torch.zeros_like(src_v)
+    ma.hicache_transfer_kv_all_layer(src_k, dst_k, src_v, dst_v, si.cuda(), di.cuda())
+    want_k, want_v = torch.zeros_like(src_k), torch.zeros_like(src_v)
+    for s, d in zip(si.tolist(), di.tolist()):
+        if 0 <= s < P and 0 <= d < P:
+            want_k[:, d] = src_k[:, s]
+            want_v[:, d] = src_v[:, s]
+    assert torch.equal(dst_k.view(torch.int16), want_k.view(torch.int16))
+    assert torch.equal(dst_v.view(torch.int16), want_v.view(torch.int16))

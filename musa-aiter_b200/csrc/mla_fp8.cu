@@ -781,6 +781,14 @@ static bool mla_pair_ok(const MlaLaunch& L, bool store) {
          L.num_tokens < (int64_t{1} << 30);
 }
 
+// Resident waves of blocks for a launch of nl layers: about one block per 64 KiB of the launch's
+// bf16 side, clamped to 4..16 (the row engine's rule: a large call's last wave then drains fast,
+// a small one keeps four waves).
+static int64_t mla_waves(const MlaLaunch& L, int64_t nl, int64_t resident) {
+  const int64_t bytes = nl * L.num_tokens * (static_cast<int64_t>(L.kv_dim) * 2 + L.pe_bytes);
+  return std::min<int64_t>(16, std::max<int64_t>(4, bytes / (std::max<int64_t>(resident, 1) * (int64_t{64} << 10))));
+}
+
 template <bool STORE, typename T, int F, bool OWN, bool I64>
 static int launch_mla_pairs(MlaLaunch& L, int64_t layers, unsigned char* kv_out, unsigned char* pe_out, cudaStream_t st,
                             const mak_rows_desc* cache) {
@@ -793,7 +801,7 @@ static int launch_mla_pairs(MlaLaunch& L, int64_t layers, unsigned char* kv_out,
     const int64_t nl = std::min<int64_t>(kMlaPlanes, layers - l0);
     for (int64_t q = 0; q < nl; ++q) L.cache[q] = cache->plane_ptrs[l0 + q];
     const int64_t want = (pairs + (kMlaThreads / 32) - 1) / (kMlaThreads / 32);
-    const int64_t cap = std::max<int64_t>(1, (4 * resident + nl - 1) / nl);
+    const int64_t cap = std::max<int64_t>(1, (mla_waves(L, nl, resident) * resident + nl - 1) / nl);
     const dim3 grid(static_cast<unsigned>(std::min(want, cap)), static_cast<unsigned>(nl));
     MlaLaunch P = L;
     P.kv = L.kv + l0 * L.kv_sl;
@@ -830,7 +838,7 @@ static int launch_mla(MlaLaunch& L, int64_t layers, unsigned char* kv_out, unsig
     const int64_t nl = std::min<int64_t>(kMlaPlanes, layers - l0);
     for (int64_t q = 0; q < nl; ++q) L.cache[q] = cache->plane_ptrs[l0 + q];
     const int64_t want = (L.num_tokens + (kMlaThreads / 32) - 1) / (kMlaThreads / 32);
-    const int64_t cap = std::max<int64_t>(1, (4 * resident + nl - 1) / nl);
+    const int64_t cap = std::max<int64_t>(1, (mla_waves(L, nl, resident) * resident + nl - 1) / nl);
     const dim3 grid(static_cast<unsigned>(std::min(want, cap)), static_cast<unsigned>(nl));
     MlaLaunch P = L;
     P.kv = L.kv + l0 * L.kv_sl;

@@ -111,28 +111,28 @@ struct Codec<uint8_t, LT, MAK_FP8_E5M2> {
   }
 };
 
-// FP8 store of one full (R dims x G tokens) chunk from 16-bit token vectors when
+// FP8 store of one full (R dims x G tokens) chunk from 16-bit token vectors (TV:
+// R = 8 dims in a uint4 or R = 4 in a uint2 per token) when
 // every value is finite and |x| / scale stays below the FP8 maximum (the usual
 // case: scales from an amax): one reciprocal per chunk and, per value pair, the
 // packed division-free quotient + flush-to-zero encoder of the MLA FP8 rows
 // (fp8_encode2_quot_finite), which mak_fp8_quotient_selfcheck checks against the
 // IEEE division for every 16-bit input in that range.  Returns false (nothing
 // written) when the chunk needs the per-element reference encoder.
-template <typename CT, typename LT, int CODEC, int G, int R>
-__device__ __forceinline__ bool encode_chunk_bounded(const uint4 (&toks)[G], float sc, CT* dst, int64_t row_pitch) {
-  if constexpr (CODEC == 0 || sizeof(LT) != 2 || sizeof(CT) != 1 || G != 16 || R != 8) {
+template <typename CT, typename LT, int CODEC, int G, int R, typename TV>
+__device__ __forceinline__ bool encode_chunk_bounded(const TV (&toks)[G], float sc, CT* dst, int64_t row_pitch) {
+  if constexpr (CODEC == 0 || sizeof(LT) != 2 || sizeof(CT) != 1 || G != 16 || R * 2 != sizeof(TV)) {
     return false;
   } else {
+    constexpr int W = sizeof(TV) / 4;  // 32-bit words per token vector
     constexpr uint32_t kInf = std::is_same<LT, __half>::value ? 0x7C00u : 0x7F80u;
     constexpr float kBound = CODEC == MAK_FP8_E4M3 ? 447.99f : 57343.f;
     if (!fast_quot_ok(sc)) return false;
     uint32_t m2 = 0;
 #pragma unroll
     for (int i = 0; i < G; ++i) {
-      m2 = __vmaxu2(m2, toks[i].x & 0x7FFF7FFFu);
-      m2 = __vmaxu2(m2, toks[i].y & 0x7FFF7FFFu);
-      m2 = __vmaxu2(m2, toks[i].z & 0x7FFF7FFFu);
-      m2 = __vmaxu2(m2, toks[i].w & 0x7FFF7FFFu);
+#pragma unroll
+      for (int k = 0; k < W; ++k) m2 = __vmaxu2(m2, reinterpret_cast<const uint32_t*>(&toks[i])[k] & 0x7FFF7FFFu);
     }
     const uint32_t mraw = max(m2 & 0xFFFFu, m2 >> 16);
     if (mraw >= kInf) return false;
@@ -404,7 +404,10 @@ constexpr int kRunSingles = 4;
 //            stores; a partly covered one element stores on the cache side (the
 //            chunk's other slots belong to other tokens: no read-modify-write,
 //            so concurrent segments of one block never race), its token rows
-//            loaded KTOK at a time.
+//            loaded KTOK at a time.  FP8 stores from 16-bit rows take R = 4
+//            (8-byte token loads): the 16 token rows of a chunk then fit half
+//            the registers, and every cache store still writes a whole 16-byte
+//            row.
 // cbase = element offset of the block in the plane, o_s = first in-block
 // offset, ts = first token.
 // ---------------------------------------------------------------------------
@@ -413,7 +416,9 @@ __device__ __forceinline__ void move_run(const TileLaunch& p, const CT* cache_r,
                                          int64_t l, int64_t cbase, int o_s, int len, int64_t ts, int h_lo, int h_hi,
                                          int lane) {
   constexpr int G = 16 / sizeof(CT);
-  constexpr int R = 16 / sizeof(LT);
+  constexpr bool kHalfRows = SCATTER && CODEC != 0 && sizeof(CT) == 1 && sizeof(LT) == 2;
+  constexpr int R = kHalfRows ? 4 : 16 / sizeof(LT);
+  using TV = typename std::conditional<kHalfRows, uint2, uint4>::type;  // R dims of one token
   using C = Codec<CT, LT, CODEC>;
   const int upr = static_cast<int>(p.head_dim) / R;
   const int NH = static_cast<int>(p.num_heads);
@@ -446,9 +451,9 @@ __device__ __forceinline__ void move_run(const TileLaunch& p, const CT* cache_r,
           }
         }
       } else {
-        uint4 toks[G];
+        TV toks[G];
 #pragma unroll
-        for (int i = 0; i < G; ++i) toks[i] = __ldg(reinterpret_cast<const uint4*>(lrow + (col0 + i - o_s) * p.l_st));
+        for (int i = 0; i < G; ++i) toks[i] = __ldg(reinterpret_cast<const TV*>(lrow + (col0 + i - o_s) * p.l_st));
         if (!encode_chunk_bounded<CT, LT, CODEC, G, R>(toks, sc, cache_w + row0 + col0, p.c_sd)) {
 #pragma unroll
           for (int r = 0; r < R; ++r) {
@@ -476,10 +481,10 @@ __device__ __forceinline__ void move_run(const TileLaunch& p, const CT* cache_r,
     } else {
 #pragma unroll 1
       for (int c0 = lo; c0 < hi; c0 += KTOK) {
-        uint4 tv[KTOK];
+        TV tv[KTOK];
 #pragma unroll
         for (int i = 0; i < KTOK; ++i)
-          if (c0 + i < hi) tv[i] = __ldg(reinterpret_cast<const uint4*>(lrow + (c0 + i - o_s) * p.l_st));
+          if (c0 + i < hi) tv[i] = __ldg(reinterpret_cast<const TV*>(lrow + (c0 + i - o_s) * p.l_st));
 #pragma unroll
         for (int i = 0; i < KTOK; ++i) {
           if (c0 + i >= hi) continue;
@@ -771,7 +776,8 @@ __global__ void __launch_bounds__(256, 4) tile_single_kernel(const __grid_consta
 // One plane per block (grid = token ranges of 8W tokens x planes): nothing of
 // the scan stays live in the walk, blocks are small enough that the last wave
 // stays balanced, and the run path keeps 80 registers for its transposes
-// (3 blocks per SM; 2 for FP8 stores, whose chunk encoder holds 16 token rows).
+// (3 blocks per SM; 2 for FP8 stores from fp32 rows, whose 16 token rows of a chunk
+// take 64 registers).
 // ---------------------------------------------------------------------------
 constexpr int kRunWarps = 8;
 // segments listed per window: s single tokens and r runs (two or more tokens, the last one may
@@ -779,7 +785,7 @@ constexpr int kRunWarps = 8;
 constexpr int kRunMaxSeg = kRunWarps * ((32 + 1 + kRunSingles) / 2);
 
 template <typename CT, typename LT, int CODEC, bool SCATTER>
-__global__ void __launch_bounds__(256, (CODEC && SCATTER) ? 2 : 3) tile_run_kernel(const __grid_constant__ TileLaunch p) {
+__global__ void __launch_bounds__(256, (CODEC != 0 && SCATTER && sizeof(LT) == 4) ? 2 : 3) tile_run_kernel(const __grid_constant__ TileLaunch p) {
   constexpr int R = 16 / sizeof(LT);
   __shared__ int64_t s_soff[kRunMaxSeg];  // element offset of the run's first slot in the plane
   __shared__ int s_ts[kRunMaxSeg];        // first token, relative to the block's first token
@@ -1127,7 +1133,8 @@ static int launch_tile_run(TileLaunch& p, cudaStream_t st) {
   // heads per walk item: (unit, chunk) pairs of one head for a run spanning a block's chunks
   const int64_t cap = std::min<int64_t>(p.block_size, 32);
   const int64_t g = 16 / static_cast<int64_t>(sizeof(CT));
-  const int64_t per_head = (p.head_dim / (16 / static_cast<int64_t>(sizeof(LT)))) * ((cap + g - 1) / g);
+  const int64_t r = (SCATTER && CODEC != 0 && sizeof(CT) == 1 && sizeof(LT) == 2) ? 4 : 16 / static_cast<int64_t>(sizeof(LT));
+  const int64_t per_head = (p.head_dim / r) * ((cap + g - 1) / g);  // move_run's units x chunks of one head
   p.run_heads = static_cast<int32_t>(std::max<int64_t>(1, std::min<int64_t>(p.num_heads, 32 / std::max<int64_t>(per_head, 1))));
   // A scatter with enough whole runs to give every resident warp several moves them whole: on
   // large calls that measured faster than head groups (FP8 merged store 4683 -> 4896 GB/s), on

@@ -447,6 +447,16 @@ MAK_API int mak_minmax(const void* x, int32_t dtype, int64_t n, float* out_minma
 MAK_API int mak_cachegen_encode(const void* x, int32_t dtype, int64_t n, const float* minmax, int32_t num_bins,
                                 uint8_t* codes, uint64_t* counts, float* cdf, void* stream);
 
+/*
+ * The encode's codebook on the device from mak_minmax's output: the reference builds it with
+ * torch.linspace(min, max, num_bins) in float32 on the tensor's device, or fills it with min when
+ * max == min (musa_aiter/ops/kv_transfer.py:1130-1132, 1147, 1167).  For a CUDA device that is
+ * step = (max - min) / (num_bins - 1), then min + step * i (fused) for i < num_bins / 2 and
+ * max - step * (num_bins - 1 - i) (fused) for the rest: bit-identical to torch.linspace on the GPU,
+ * and no read-back of min / max to the host.  codebook: device float[num_bins].
+ */
+MAK_API int mak_cachegen_codebook(const float* minmax, int32_t num_bins, float* codebook, void* stream);
+
 /* out[i] = codebook[codes[i]] converted to out_dtype (RNE).  Replaces
  * musa_aiter_kv_cachegen_decode_float (csrc/kvcache/kv_transfer_float.mu:868-905). */
 MAK_API int mak_cachegen_decode(const uint8_t* codes, int64_t n, const void* codebook, int32_t codebook_dtype,

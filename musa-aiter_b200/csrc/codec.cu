@@ -76,13 +76,21 @@ __global__ void minmax_kernel(const void* x, int64_t n, int vec_ok, uint32_t* ke
   const int64_t nv = vec_ok ? n / VE : 0;
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
-  for (int64_t i = tid; i < nv; i += nt) {
-    const uint4 v = __ldg(xv + i);
+  // four independent 16-byte loads per thread in flight
+  for (int64_t i0 = tid; i0 < nv; i0 += 4 * nt) {
+    uint4 v[4];
 #pragma unroll
-    for (int e = 0; e < VE; ++e) {
-      const float f = Elem<DT>::at(v, e);
-      lo = fminf(lo, f);
-      hi = fmaxf(hi, f);
+    for (int u = 0; u < 4; ++u)
+      if (i0 + u * nt < nv) v[u] = __ldg(xv + i0 + u * nt);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (i0 + u * nt >= nv) continue;
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        const float f = Elem<DT>::at(v[u], e);
+        lo = fminf(lo, f);
+        hi = fmaxf(hi, f);
+      }
     }
   }
   for (int64_t i = nv * VE + tid; i < n; i += nt) {
@@ -94,9 +102,26 @@ __global__ void minmax_kernel(const void* x, int64_t n, int vec_ok, uint32_t* ke
     lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
     hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
   }
-  if ((threadIdx.x & 31) == 0) {
-    atomicMin(keys + 0, f2key(lo));
-    atomicMax(keys + 1, f2key(hi));
+  // one pair of atomics per block, not per warp: thousands of warps updating the same two
+  // words serialise in L2 (the pass took 30 us for 128 MiB with per-warp atomics)
+  __shared__ float s_lo[32], s_hi[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    s_lo[wid] = lo;
+    s_hi[wid] = hi;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    lo = lane < nw ? s_lo[lane] : 3.402823466e38f;
+    hi = lane < nw ? s_hi[lane] : -3.402823466e38f;
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if (lane == 0) {
+      atomicMin(keys + 0, f2key(lo));
+      atomicMax(keys + 1, f2key(hi));
+    }
   }
 }
 
@@ -135,21 +160,30 @@ __global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
   unsigned int* h = hist[wib * kHistCopies + (threadIdx.x & (kHistCopies - 1))];
-  for (int64_t i = tid; i < nv; i += nt) {
-    const uint4 v = __ldg(xv + i);
-    uint32_t packed[VE / 4];
+  // two independent 16-byte loads per thread in flight
+  for (int64_t i0 = tid; i0 < nv; i0 += 2 * nt) {
+    uint4 vv[2];
 #pragma unroll
-    for (int w = 0; w < VE / 4; ++w) packed[w] = 0;
+    for (int u = 0; u < 2; ++u)
+      if (i0 + u * nt < nv) vv[u] = __ldg(xv + i0 + u * nt);
 #pragma unroll
-    for (int e = 0; e < VE; ++e) {
-      const uint32_t c = cachegen_code(Elem<DT>::at(v, e), lo, scale, top);
-      packed[e >> 2] |= c << (8 * (e & 3));
-      atomicAdd(h + c, 1u);
-    }
-    if (VE == 8) {
-      reinterpret_cast<uint2*>(codes)[i] = make_uint2(packed[0], packed[VE / 4 - 1]);
-    } else {
-      reinterpret_cast<uint32_t*>(codes)[i] = packed[0];
+    for (int u = 0; u < 2; ++u) {
+      const int64_t i = i0 + u * nt;
+      if (i >= nv) continue;
+      uint32_t packed[VE / 4];
+#pragma unroll
+      for (int w = 0; w < VE / 4; ++w) packed[w] = 0;
+#pragma unroll
+      for (int e = 0; e < VE; ++e) {
+        const uint32_t c = cachegen_code(Elem<DT>::at(vv[u], e), lo, scale, top);
+        packed[e >> 2] |= c << (8 * (e & 3));
+        atomicAdd(h + c, 1u);
+      }
+      if (VE == 8) {
+        reinterpret_cast<uint2*>(codes)[i] = make_uint2(packed[0], packed[VE / 4 - 1]);
+      } else {
+        reinterpret_cast<uint32_t*>(codes)[i] = packed[0];
+      }
     }
   }
   for (int64_t i = nv * VE + tid; i < n; i += nt) {
@@ -166,25 +200,54 @@ __global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int
   }
 }
 
-// CDF = [0, cumsum(counts) / n], summed in order in fp32.  The warp stages the counts in
-// shared memory first: the single-thread sum over counts read from global memory waited on
-// one load per bin (27 us for 256 bins).
+// CDF = [0, cumsum(counts) / n], summed strictly in bin order in fp32 (sums past 2^24 round,
+// so the order is part of the result).  Lane l holds bins 8l .. 8l + 7 in registers; the running
+// sum passes from lane to lane by shuffles, each lane adding its eight counts in order, and every
+// lane then divides its own bins.  (A single thread summing counts from shared memory took
+// 12-13 us.)
 __global__ void cachegen_cdf_kernel(const unsigned long long* counts, int bins, int64_t n, float* cdf) {
-  __shared__ float c[257];
   const int lane = threadIdx.x;
-  for (int b = lane; b < bins; b += 32) c[b + 1] = static_cast<float>(counts[b]);
-  __syncwarp();
-  if (lane == 0) {
-    float run = 0.f;
-    const float denom = static_cast<float>(n);
-    c[0] = 0.f;
-    for (int b = 1; b <= bins; ++b) {
-      run = __fadd_rn(run, c[b]);
-      c[b] = __fdiv_rn(run, denom);
-    }
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int b = lane * 8 + j;
+    v[j] = b < bins ? static_cast<float>(counts[b]) : 0.f;
   }
-  __syncwarp();
-  for (int b = lane; b <= bins; b += 32) cdf[b] = c[b];
+  float run = 0.f;
+  for (int k = 0; k < 32; ++k) {
+    if (lane == k) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        run = __fadd_rn(run, v[j]);
+        v[j] = run;
+      }
+    }
+    run = __shfl_sync(0xffffffffu, run, k);
+  }
+  const float denom = static_cast<float>(n);
+  if (lane == 0) cdf[0] = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int b = lane * 8 + j;
+    if (b < bins) cdf[b + 1] = __fdiv_rn(v[j], denom);
+  }
+}
+
+// torch.linspace(min, max, bins) in float32 as PyTorch's CUDA kernel evaluates it: a step
+// divided once, the first half counted up from min and the second half down from max, each a
+// fused multiply-add; a slab with max == min gets min in every bin (the reference's torch.full).
+__global__ void cachegen_codebook_kernel(const float* minmax, int bins, float* codebook) {
+  const float lo = minmax[0], hi = minmax[1];
+  const float step = __fdiv_rn(__fsub_rn(hi, lo), static_cast<float>(bins - 1));
+  const int halfway = bins / 2;
+  for (int i = threadIdx.x; i < bins; i += blockDim.x) {
+    float v = lo;
+    if (!(lo == hi)) {
+      v = i < halfway ? __fmaf_rn(step, static_cast<float>(i), lo)
+                      : __fmaf_rn(-step, static_cast<float>(bins - 1 - i), hi);
+    }
+    codebook[i] = v;
+  }
 }
 
 // 16 codes per 16-byte load, the codebook (as the output type's bits) in shared
@@ -289,6 +352,13 @@ int mak_cachegen_encode(const void* x, int32_t dtype, int64_t n, const float* mi
   if (rc) return rc;
   cachegen_cdf_kernel<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned long long*>(counts), num_bins, n, cdf);
   return launch_status("cachegen_cdf_kernel");
+}
+
+int mak_cachegen_codebook(const float* minmax, int32_t num_bins, float* codebook, void* stream) {
+  if (num_bins < 2 || num_bins > 256) return fail(MAK_E_INVALID, "mak_cachegen_codebook: num_bins must be in [2, 256]");
+  if (!minmax || !codebook) return fail(MAK_E_INVALID, "mak_cachegen_codebook: NULL pointer");
+  cachegen_codebook_kernel<<<1, 256, 0, as_stream(stream)>>>(minmax, num_bins, codebook);
+  return launch_status("cachegen_codebook_kernel");
 }
 
 int mak_cachegen_decode(const uint8_t* codes, int64_t n, const void* codebook, int32_t codebook_dtype, int32_t num_bins,

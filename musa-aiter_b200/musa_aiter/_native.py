@@ -231,6 +231,7 @@ _PROTOTYPES = {
     "mak_runtime_versions": (c_int32, [POINTER(c_int32), POINTER(c_int32)]),
     "mak_minmax": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_void_p]),
     "mak_cachegen_encode": (c_int32, [c_void_p, c_int32, c_int64, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "mak_cachegen_codebook": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p]),
     "mak_cachegen_decode": (c_int32, [c_void_p, c_int64, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p]),
     "mak_mla_fp8_row_bytes": (c_int64, [c_int64, c_int64]),
     "mak_rope_dense": (c_int32, [c_void_p, c_void_p]),

@@ -1949,9 +1949,9 @@ def _staged_rows_copy(src: torch.Tensor, dst: torch.Tensor, indices: torch.Tenso
 
 
 def kv_cachegen_encode(tensor: torch.Tensor, *, num_bins: int = 256) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Uniform-bin uint8 encode with codebook and empirical CDF; the codes and
-    the histogram/CDF are computed on the device (one min/max read-back for the
-    codebook, as in the reference).  Reference: kv_transfer.py:1111-1172."""
+    """Uniform-bin uint8 encode with codebook and empirical CDF, all computed on the device with
+    no read-back (the reference reads min/max back for ``torch.linspace``; the device codebook is
+    bit-identical to it).  Reference: kv_transfer.py:1111-1172."""
     name = "kv_cachegen_encode"
     if num_bins < 2 or num_bins > 256:
         raise ValueError(f"{name}: num_bins must be in [2, 256]")
@@ -1970,25 +1970,18 @@ def kv_cachegen_encode(tensor: torch.Tensor, *, num_bins: int = 256) -> tuple[to
     code = _native.dtype_code(x.dtype)
     mm = torch.empty(2, dtype=torch.float32, device=dev)
     _native.check(lib.mak_minmax(_native.ptr(x), code, x.numel(), _native.ptr(mm), stream), name)
-    # min/max go to the host behind an event while the encode launches are queued: the device
-    # runs min/max, encode and CDF back to back, and the host waits only for the codebook bounds.
-    # A slab with max == min takes the same launches: every code is 0 (the NaN of 0 * inf is
-    # clamped to 0), so counts = [n, 0, ...] and the CDF is [0, 1, ..., 1].
-    mm_host = torch.empty(2, dtype=torch.float32, pin_memory=True)
-    mm_host.copy_(mm, non_blocking=True)
-    ready = torch.cuda.Event()
-    ready.record(torch.cuda.current_stream(dev))
+    # Everything stays on the device: min/max, the codes with their histogram and CDF, and the
+    # codebook (torch.linspace's float32 arithmetic, or min in every bin when max == min), so the
+    # call queues its launches and returns without waiting for the stream.  A slab with
+    # max == min takes the same launches: every code is 0 (the NaN of 0 * inf is clamped to 0),
+    # so counts = [n, 0, ...] and the CDF is [0, 1, ..., 1].
     codes = torch.empty(x.shape, dtype=torch.uint8, device=dev)
     counts = torch.empty(num_bins, dtype=torch.int64, device=dev)
     cdf = torch.empty(num_bins + 1, dtype=torch.float32, device=dev)
+    codebook = torch.empty(num_bins, dtype=torch.float32, device=dev)
     _native.check(lib.mak_cachegen_encode(_native.ptr(x), code, x.numel(), _native.ptr(mm), num_bins, _native.ptr(codes),
                                           _native.ptr(counts), _native.ptr(cdf), stream), name)
-    ready.synchronize()
-    lo, hi = mm_host.tolist()
-    if lo == hi:
-        codebook = torch.full((num_bins,), lo, dtype=torch.float32, device=dev)
-    else:
-        codebook = torch.linspace(lo, hi, num_bins, dtype=torch.float32, device=dev)
+    _native.check(lib.mak_cachegen_codebook(_native.ptr(mm), num_bins, _native.ptr(codebook), stream), name)
     emit_native(name, tensor, "sm100a min/max + encode/histogram + CDF kernels")
     return codes, codebook, cdf
 

@@ -345,3 +345,27 @@ def test_hicache_device_indices_without_validation(cuda_device, monkeypatch):
             want_v[:, d] = src_v[:, s]
     assert torch.equal(dst_k.view(torch.int16), want_k.view(torch.int16))
     assert torch.equal(dst_v.view(torch.int16), want_v.view(torch.int16))
+
+
+def test_cachegen_codebook_matches_torch_linspace(cuda_device):
+    """The device codebook (mak_cachegen_codebook) equals torch.linspace(min, max, bins) in float32
+    on the GPU, bit for bit, for bounds spread over many magnitudes and every bin count the encode
+    takes at its ends and in between; max == min fills min, signed zero included, as the
+    reference's torch.full does."""
+    from musa_aiter import _native
+
+    lib = _native.load()
+    g = torch.Generator().manual_seed(17)
+    lo = torch.randn(600, generator=g) * torch.exp(torch.randn(600, generator=g) * 4)
+    hi = lo + torch.rand(600, generator=g) * torch.exp(torch.randn(600, generator=g) * 4)
+    pairs = [(float(a), float(b)) for a, b in zip(lo.float(), hi.float())] + [(-0.0, -0.0), (3.5, 3.5), (-1.0, 1.0), (0.0, 1e-30)]
+    stream = _native.stream_ptr(torch.device("cuda", torch.cuda.current_device()))
+    for bins in (2, 3, 17, 128, 255, 256):
+        for a, b in pairs:
+            mm = torch.tensor([a, b], dtype=torch.float32, device="cuda")
+            out = torch.empty(bins, dtype=torch.float32, device="cuda")
+            _native.check(lib.mak_cachegen_codebook(_native.ptr(mm), bins, _native.ptr(out), stream), "codebook")
+            a32, b32 = float(mm[0]), float(mm[1])
+            want = torch.full((bins,), a32, dtype=torch.float32, device="cuda") if a32 == b32 else \
+                torch.linspace(a32, b32, bins, dtype=torch.float32, device="cuda")
+            assert torch.equal(out.view(torch.int32), want.view(torch.int32)), (a, b, bins)

@@ -43,6 +43,7 @@ struct TileLaunch {
   int32_t slots64, n_kv, fill_zero, cache_vec, lin_vec, scale_mode, heads_per_step;
   int32_t window;       // tokens per warp window of the segment kernel (8, 16 or 32)
   int32_t run_heads;    // heads per item of the run kernel's walk (fills a warp's 32 lanes)
+  int32_t single_all;   // tile_single_fp8_kernel takes every token (runs, zero rows) with no run launch
   int32_t plane_group;  // (kv, layer) planes a segment-kernel block walks per window
   // Single-token launch (tile_single_kernel): a window's heads are split into 2^head_split_shift groups,
   // each a separate warp item, when the call has too few windows to fill the device (decode
@@ -912,10 +913,16 @@ __global__ void __launch_bounds__(256, (CODEC != 0 && SCATTER && sizeof(LT) == 4
 // registers and a full SM of warps: the single tokens are bound by DRAM sector
 // traffic (a token touches every sector of its head tile), and the number of
 // sector requests in flight decides the rate.
+// For calls of at most kSingleAllTokens tokens (single_all) it is the only tile
+// launch: phase 1 lists every token with a slot, and in a filling gather every
+// token without one as a zero row, and the runs are moved element by element.
 // grid = (token ranges of tpc tokens, planes, head groups of hpc heads).
 // ---------------------------------------------------------------------------
 constexpr int kSingleMaxTok = 256;  // tokens per block, at most (8 scanning warps)
 constexpr int kSingleInFlight = 4;  // items per warp in flight
+// FP8 calls of at most this many tokens skip the run launch: the single-token kernel takes every
+// token (a decode batch's random slots are single tokens; the run launch would only scan them).
+constexpr int64_t kSingleAllTokens = 512;
 
 template <typename LT, int CODEC, bool SCATTER>
 __global__ void __launch_bounds__(256, 4) tile_single_fp8_kernel(const __grid_constant__ TileLaunch p, int tpc, int hpc) {
@@ -954,7 +961,10 @@ __global__ void __launch_bounds__(256, 4) tile_single_fp8_kernel(const __grid_co
       if (s >= 0) split_slot(s, p.block_size, &b, &o);
       const bool start = s >= 0 && (sp < 0 || s != sp + 1 || (o % cap) == 0);
       const bool cont = sn >= 0 && sn == s + 1 && ((o + 1) % cap) != 0;
-      const bool single = start && !cont && mine;
+      // small calls (single_all): every token is listed, element by element for the tokens of
+      // runs too, and in a filling gather the tokens without a slot as zero rows (offset -1)
+      const bool zero_row = !SCATTER && p.single_all && p.fill_zero && t < n && s < 0;
+      const bool single = p.single_all ? (s >= 0 || zero_row) : (start && !cont && mine);
       const uint32_t m = __ballot_sync(0xffffffffu, single);
       int base = 0;
       if (lane == 0 && m) base = atomicAdd(&s_cnt, __popc(m));
@@ -962,7 +972,7 @@ __global__ void __launch_bounds__(256, 4) tile_single_fp8_kernel(const __grid_co
       if (single) {
         const int k = base + __popc(m & ((1u << lane) - 1u));
         s_tok[k] = static_cast<int>(t);
-        s_off[k] = b * p.c_sb + o;
+        s_off[k] = s >= 0 ? b * p.c_sb + o : -1;
       }
     }
   }
@@ -1004,9 +1014,14 @@ __global__ void __launch_bounds__(256, 4) tile_single_fp8_kernel(const __grid_co
         it_h[k] = h_lo + hh;
         it_d[k] = (g << 7) + lane;
         if (!SCATTER) {
-          const uint8_t* c = cache_r + s_off[e] + it_h[k] * p.c_sh + static_cast<int64_t>(it_d[k]) * sd;
+          const int64_t off = s_off[e];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) code[k][i] = c[32 * i * sd];
+          for (int i = 0; i < 4; ++i) code[k][i] = 0;
+          if (off >= 0) {
+            const uint8_t* c = cache_r + off + it_h[k] * p.c_sh + static_cast<int64_t>(it_d[k]) * sd;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) code[k][i] = c[32 * i * sd];
+          }
         } else {
           const LT* x = lin_l + static_cast<int64_t>(s_tok[e]) * p.l_st + it_h[k] * p.l_sh + it_d[k];
 #pragma unroll
@@ -1028,7 +1043,10 @@ __global__ void __launch_bounds__(256, 4) tile_single_fp8_kernel(const __grid_co
       const float sc = scl[p.scale_mode == MAK_SCALE_SCALAR ? 0 : (p.scale_mode == MAK_SCALE_PER_HEAD ? h : l * NH + h)];
       if (!SCATTER) {
         LT* o = lin_l + static_cast<int64_t>(s_tok[it_e[k]]) * p.l_st + h * p.l_sh + it_d[k];
-        if (fp8_ftz_scale_ok<CODEC>(sc)) {
+        if (s_off[it_e[k]] < 0) {  // zero row of a filling gather (single_all)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) o[32 * i] = zero_of<LT>();
+        } else if (fp8_ftz_scale_ok<CODEC>(sc)) {
           const float sf = __fmul_rn(sc, fp8_ftz_bias<CODEC>());  // exact: a power of two
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -1155,12 +1173,22 @@ static int launch_tile_run(TileLaunch& p, cudaStream_t st) {
 
 template <typename CT, typename LT, int CODEC, bool SCATTER>
 static int launch_tile_segments(TileLaunch& p, cudaStream_t st) {
+  if constexpr (CODEC != 0 && sizeof(CT) == 1) {
+    if (p.head_dim % 128 == 0 && p.n_tokens < (int64_t{1} << 31) && p.num_heads <= 65535) {
+      if (p.n_tokens <= kSingleAllTokens) {
+        // small calls (decode batches): the single-token kernel takes every token, runs
+        // element by element and zero rows included, and the run launch is skipped
+        p.seg_map = nullptr;
+        p.single_all = 1;
+        return launch_tile_single_fp8<LT, CODEC, SCATTER>(p, st);
+      }
+      const int rc = launch_tile_run<CT, LT, CODEC, SCATTER>(p, st);
+      if (rc) return rc;
+      return launch_tile_single_fp8<LT, CODEC, SCATTER>(p, st);
+    }
+  }
   const int rc = launch_tile_run<CT, LT, CODEC, SCATTER>(p, st);
   if (rc) return rc;
-  if constexpr (CODEC != 0 && sizeof(CT) == 1) {
-    if (p.head_dim % 128 == 0 && p.n_tokens < (int64_t{1} << 31) && p.num_heads <= 65535)
-      return launch_tile_single_fp8<LT, CODEC, SCATTER>(p, st);
-  }
   return launch_tile_single<CT, LT, CODEC, SCATTER>(p, st);
 }
 

@@ -635,3 +635,35 @@ def test_tile_owned_scatter_duplicates_vs_workspace_and_oracle(cuda_device, monk
         O.kv_linear_to_paged_multi_layer(to_np(kl), to_np(vl), rk, rv, slots.numpy())
     eq(ok_k, rk, "owned scatter k")
     eq(ok_v, rv, "owned scatter v")
+
+
+@pytest.mark.parametrize("fmt", ("e4m3", "e5m2"))
+def test_fp8_small_calls_take_every_token_vs_oracle(cuda_device, fmt):
+    """FP8 calls of at most 512 tokens skip the run launch: one kernel moves every token, the
+    tokens of block-table runs element by element, last writer winning on duplicate slots, and a
+    gather writes zero rows for the tokens without a slot.  Stores and loads at 40, 300 and 512
+    tokens (and 513, the first size that takes the run launch again) equal the oracle's bytes,
+    with multi-layer per-head scales."""
+    g = torch.Generator().manual_seed(31 if fmt == "e4m3" else 32)
+    nl, nb, nh, hd, bs = 2, 256, 2, 128, 16
+    for t in (40, 300, 512, 513):
+        slots = _mixed_run_slots(t, nb, bs, g, stretch=3)
+        slots[t // 3] = slots[t // 2] if slots[t // 2] >= 0 else slots[t // 3]  # a duplicate slot
+        kl = (torch.randn((nl, t, nh, hd), generator=g) * 3.0).to(torch.bfloat16)
+        vl = (torch.randn((nl, t, nh, hd), generator=g) * 3.0).to(torch.bfloat16)
+        ks = torch.rand((nl, nh), generator=g) * 0.02 + 0.005
+        vs = torch.rand((nl, nh), generator=g) * 0.02 + 0.005
+        k8 = torch.randint(0, 120, (nl, nb, nh, hd, bs), generator=g, dtype=torch.uint8)
+        v8 = torch.randint(0, 120, (nl, nb, nh, hd, bs), generator=g, dtype=torch.uint8)
+        dk, dv = k8.cuda(), v8.cuda()
+        ma.kv_linear_to_paged_fp8_multi_layer(kl.cuda(), vl.cuda(), dk, dv, slots.cuda(), ks.cuda(), vs.cuda(), fp8_format=fmt)
+        rk, rv = k8.numpy().copy(), v8.numpy().copy()
+        O.kv_linear_to_paged_fp8_multi_layer(to_np(kl), to_np(vl), rk, rv, slots.numpy(), ks.numpy(), vs.numpy(), fp8_format=fmt)
+        eq(dk, rk, f"store k t={t}")
+        eq(dv, rv, f"store v t={t}")
+        ok, ov = ma.kv_paged_fp8_to_linear_multi_layer(dk, dv, slots.cuda(), ks.cuda(), vs.cuda(), out_dtype=torch.bfloat16,
+                                                       fp8_format=fmt)
+        qk, qv = O.kv_paged_fp8_to_linear_multi_layer(rk, rv, slots.numpy(), ks.numpy(), vs.numpy(), out_dtype="bfloat16",
+                                                       fp8_format=fmt)
+        eq(ok, qk, f"load k t={t}")
+        eq(ov, qv, f"load v t={t}")

@@ -509,7 +509,9 @@ __device__ __forceinline__ void move_run(const TileLaunch& p, const CT* cache_r,
 // warp handles every segment that STARTS in its window, whole.
 // It moves the single tokens (element items); the runs of two or more tokens
 // go through tile_run_kernel, launched first, which also writes the segment
-// map this launch uses to skip windows.  Each launch keeps the register budget
+// map this launch uses to skip windows.  In calls of at most kSingleAllTokens
+// tokens (single_all) it is the only tile launch: every token with a slot is
+// moved element by element, and a filling gather writes the zero rows.  Each launch keeps the register budget
 // its path needs.  No shared memory, no block barriers; FP8 codecs run in
 // registers.
 // ---------------------------------------------------------------------------
@@ -580,15 +582,26 @@ __global__ void __launch_bounds__(256, 4) tile_single_kernel(const __grid_consta
     const int64_t prevB = lane == 0 ? lastA : upB;
     const bool startA = sA >= 0 && (prevA < 0 || sA != prevA + 1 || (oA % cap) == 0);
     const bool startB = sB >= 0 && (prevB < 0 || sB != prevB + 1 || (oB % cap) == 0);
-    const uint32_t mStartA = __ballot_sync(0xffffffffu, startA);  // segments starting at t0 + lane
-    const uint64_t bound = static_cast<uint64_t>(mStartA) |
-                           (static_cast<uint64_t>(__ballot_sync(0xffffffffu, startB)) << 32) |
-                           ~(static_cast<uint64_t>(__ballot_sync(0xffffffffu, sA >= 0)) |
-                             (static_cast<uint64_t>(__ballot_sync(0xffffffffu, sB >= 0)) << 32));
+    const uint32_t validA = __ballot_sync(0xffffffffu, sA >= 0);
+    uint32_t mStartA = __ballot_sync(0xffffffffu, startA);  // segments starting at t0 + lane
+    uint64_t bound = static_cast<uint64_t>(mStartA) |
+                     (static_cast<uint64_t>(__ballot_sync(0xffffffffu, startB)) << 32) |
+                     ~(static_cast<uint64_t>(validA) | (static_cast<uint64_t>(__ballot_sync(0xffffffffu, sB >= 0)) << 32));
+    // Small calls (single_all, no run launch): every token with a slot is moved as a single
+    // token, and a filling gather writes the zero rows of the tokens without one.
+    uint32_t zmask = 0;
+    if (p.single_all) {
+      mStartA = validA;
+      bound = ~0ull;
+      if (!SCATTER && p.fill_zero) {
+        const int64_t left = p.n_tokens - t0;
+        zmask = ~validA & wmask & (left < 32 ? (1u << left) - 1u : 0xffffffffu);
+      }
+    }
     // The window's segments are the same for every plane: skip the planes when
     // none is this launch's kind.
     if (GROUPED) {
-      bool work = false;
+      bool work = zmask != 0u;
       for (uint32_t m = mStartA & wmask; m && !work; m &= m - 1) {
         const int q = __ffs(m) - 1;
         const uint64_t rest = bound >> (q + 1);
@@ -756,6 +769,18 @@ __global__ void __launch_bounds__(256, 4) tile_single_kernel(const __grid_consta
         }
       }
     }
+    if (zmask) {
+      // zero rows of this item's heads [h_lo, h_hi), 16-byte stores
+      constexpr int R = 16 / sizeof(LT);
+      const int upr = static_cast<int>(p.head_dim) / R;
+      for (uint32_t mz = zmask; mz; mz &= mz - 1) {
+        const int q = __ffs(mz) - 1;
+        for (int u = lane; u < NHp * upr; u += 32) {
+          const int h = h_lo + u / upr, dg = u - (u / upr) * upr;
+          *reinterpret_cast<uint4*>(lin_l + (t0 + q) * p.l_st + h * p.l_sh + dg * R) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+    }
     }  // planes of the group
   }
 }
@@ -920,8 +945,9 @@ __global__ void __launch_bounds__(256, (CODEC != 0 && SCATTER && sizeof(LT) == 4
 // ---------------------------------------------------------------------------
 constexpr int kSingleMaxTok = 256;  // tokens per block, at most (8 scanning warps)
 constexpr int kSingleInFlight = 4;  // items per warp in flight
-// FP8 calls of at most this many tokens skip the run launch: the single-token kernel takes every
-// token (a decode batch's random slots are single tokens; the run launch would only scan them).
+// Calls of at most this many tokens skip the run launch: the single-token kernel (or, for FP8
+// caches with head_dim a multiple of 128, tile_single_fp8_kernel) takes every token (a decode
+// batch's random slots are single tokens; the run launch would only scan them).
 constexpr int64_t kSingleAllTokens = 512;
 
 template <typename LT, int CODEC, bool SCATTER>
@@ -1186,6 +1212,12 @@ static int launch_tile_segments(TileLaunch& p, cudaStream_t st) {
       if (rc) return rc;
       return launch_tile_single_fp8<LT, CODEC, SCATTER>(p, st);
     }
+  }
+  if (p.n_tokens <= kSingleAllTokens) {
+    // small calls: the single-token kernel takes every token, with no run launch
+    p.seg_map = nullptr;
+    p.single_all = 1;
+    return launch_tile_single<CT, LT, CODEC, SCATTER>(p, st);
   }
   const int rc = launch_tile_run<CT, LT, CODEC, SCATTER>(p, st);
   if (rc) return rc;

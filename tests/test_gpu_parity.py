@@ -667,3 +667,30 @@ def test_fp8_small_calls_take_every_token_vs_oracle(cuda_device, fmt):
                                                        fp8_format=fmt)
         eq(ok, qk, f"load k t={t}")
         eq(ov, qv, f"load v t={t}")
+
+
+@pytest.mark.parametrize("dt", ("bfloat16", "float16"))
+def test_small_tile_calls_take_every_token_vs_oracle(cuda_device, dt):
+    """16-bit tile calls of at most 512 tokens skip the run launch as well: one kernel moves every
+    token, the tokens of block-table runs element by element, the last writer winning on a
+    duplicate slot, and a gather zero-fills the tokens without a slot.  Scatters and gathers at
+    40, 300, 512 and 513 tokens equal the oracle's bytes."""
+    g = torch.Generator().manual_seed(41 if dt == "bfloat16" else 42)
+    nl, nb, nh, hd, bs = 2, 256, 2, 64, 16
+    for t in (40, 300, 512, 513):
+        slots = _mixed_run_slots(t, nb, bs, g, stretch=3)
+        slots[t // 3] = slots[t // 2] if slots[t // 2] >= 0 else slots[t // 3]  # a duplicate slot
+        kl = torch.randn((nl, t, nh, hd), generator=g).to(TORCH_OF[dt])
+        vl = torch.randn((nl, t, nh, hd), generator=g).to(TORCH_OF[dt])
+        kc = torch.randn((nl, nb, nh, hd, bs), generator=g).to(TORCH_OF[dt])
+        vc = torch.randn((nl, nb, nh, hd, bs), generator=g).to(TORCH_OF[dt])
+        dk, dv = kc.cuda(), vc.cuda()
+        ma.kv_linear_to_paged_multi_layer(kl.cuda(), vl.cuda(), dk, dv, slots.cuda())
+        rk, rv = to_np(kc).copy(), to_np(vc).copy()
+        O.kv_linear_to_paged_multi_layer(to_np(kl), to_np(vl), rk, rv, slots.numpy())
+        eq(dk, rk, f"scatter k t={t}")
+        eq(dv, rv, f"scatter v t={t}")
+        ok, ov = ma.kv_paged_to_linear_multi_layer(dk, dv, slots.cuda())
+        qk, qv = O.kv_paged_to_linear_multi_layer(rk, rv, slots.numpy())
+        eq(ok, qk, f"gather k t={t}")
+        eq(ov, qv, f"gather v t={t}")

@@ -240,7 +240,8 @@ MAK_API int mak_kv_linear_to_paged_fp8(const mak_linear_desc* in, const mak_page
  * map says it has nothing to do for, instead of scanning them.  epoch in
  * [1, 2^30) must differ from the one of any call still in flight on the same
  * map; entries of other epochs are never trusted, so a map may start with any
- * contents.  Results are identical to the unmapped calls.  Host-side
+ * contents.  Calls of at most 512 tokens have no run pass and leave the map
+ * untouched.  Results are identical to the unmapped calls.  Host-side
  * additions, no reference counterpart.
  */
 MAK_API int mak_kv_paged_to_linear_mapped(const mak_paged_desc* cache, const mak_linear_desc* out, const void* slots,

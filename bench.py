@@ -1203,6 +1203,26 @@ def run_ops_sweep(args) -> None:
           note=f"{hp} pages x {Lh} layers x {IB} B, K and V, zero-copy kernel stores over PCIe")
     del lf_k, lf_v, host_k, host_v
 
+    # f3 write-side producers on one layer's [NB, NH, HD, BS] caches: K/V rows written into the
+    # block-table slots (copy_to_kv_cache) and RoPE applied in place at those slots
+    k1 = torch.empty((NB, NH, HD, BS), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    v1 = torch.empty_like(k1).normal_(generator=g)
+    one = f"[{NB},{NH},{HD},{BS}] caches, one layer"
+    for nt in (256, T):
+        sl = slots[:nt]
+        kt = torch.empty((nt, NH, HD), dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        vt = torch.empty_like(kt).normal_(generator=g)
+        timed(f"copy_to_kv_cache ({nt} tokens)", 2 * 2 * nt * NH * HD * 2,
+              lambda: ma.copy_to_kv_cache(kt, vt, k1, v1, sl), note=f"{one}, {nt} block-table tokens")
+        pos = torch.randint(0, 8192, (nt,), generator=torch.Generator().manual_seed(5)).to(dev)
+        ang = torch.arange(8192, dtype=torch.float32, device=dev)[:, None] * torch.rand(
+            HD // 2, generator=torch.Generator().manual_seed(6)).to(dev)[None, :]
+        cos, sin = ang.cos(), ang.sin()
+        timed(f"apply_rope_to_key_cache ({nt} tokens)", 2 * nt * NH * HD * 2,
+              lambda: ma.apply_rope_to_key_cache(k1, sl, pos, cos, sin),
+              note=f"{one}, {nt} block-table tokens, fp32 [8192,{HD // 2}] cos/sin (table reads excluded)")
+    del k1, v1, kt, vt
+
     # a15 CacheGen codec on a [T, 4096] bf16 slab
     x = (torch.empty((16384, 4096), dtype=torch.bfloat16, device=dev).normal_(generator=g) * 5.0)
     timed("kv_cachegen_encode", x.numel() * (2 + 2 + 1), lambda: ma.kv_cachegen_encode(x, num_bins=256),

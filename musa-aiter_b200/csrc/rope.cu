@@ -10,9 +10,13 @@
 // rope_dense_kernel: any x (up to 6 leading dims, strided) with cos / sin
 // broadcast to x[..., :half]; writes a new contiguous output.
 // rope_cache_kernel: in place on selected slots of a [NB][NH][HD][BS] key cache
-// (musa_aiter/ops/cache.py:45-102), one thread per (token, head, pair).
+// (musa_aiter/ops/cache.py:45-102), one warp per (32 tokens, 8 pairs, head group)
+// with lane = token.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -113,37 +117,138 @@ struct RopeCache {
   int64_t c_row, c_last;      // cos strides (elements); c_row = 0 for a 1-D table
   int64_t s_row, s_last;
   int32_t slots64, pos64;
+  int32_t heads_per_item;     // heads rotated by one warp item
+  int32_t vec_tab;            // fp32 tables, unit last stride, rows and bases 16-byte aligned
   RopeTypes t;
 };
 
-__global__ void __launch_bounds__(256) rope_cache_kernel(const __grid_constant__ RopeCache p) {
+constexpr int kRopeJ = 8;  // rotation pairs per warp item
+
+// In the [NB][NH][HD][BS] cache one (block, head, dim) row holds the block's BS tokens
+// side by side, so lanes = tokens makes the 16 tokens of a block-table block read and write
+// one 32-byte sector per (head, dim) together (lanes = pairs touched a sector per element).
+// A lane's cos / sin values for its item's pairs are loaded once and serve every head of the
+// group; a head's 2 x 8 elements are loaded before any is stored.
+template <typename X>
+__device__ __forceinline__ float ld_x(const void* p, int64_t i) {
+  if constexpr (sizeof(X) == 4) return static_cast<const float*>(p)[i];
+  else if constexpr (std::is_same_v<X, __half>) return __half2float(static_cast<const __half*>(p)[i]);
+  else return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+template <typename X>
+__device__ __forceinline__ void st_x(void* p, int64_t i, float v) {
+  if constexpr (sizeof(X) == 4) static_cast<float*>(p)[i] = v;
+  else if constexpr (std::is_same_v<X, __half>) static_cast<__half*>(p)[i] = __float2half_rn(v);
+  else static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+// X = the cache dtype (also the output dtype); table dtypes stay runtime codes.  F32 = every
+// product and sum is promoted to fp32 (a 16-bit cache with an fp32 table, or an fp32 cache), so
+// the rotation is four single fp32 products and a sum / difference; otherwise the promotions are
+// runtime codes.
+template <typename X, bool F32>
+__global__ void __launch_bounds__(256, F32 ? 3 : 2) rope_cache_kernel(const __grid_constant__ RopeCache p) {
   const int half = static_cast<int>(p.head_dim / 2);
-  const int64_t per_token = p.num_heads * half;
-  const int64_t total = p.n_tokens * per_token;
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t tok = idx / per_token;
-    const int64_t r = idx - tok * per_token;
-    const int64_t h = r / half;
-    const int j = static_cast<int>(r - h * half);
+  const int lane = threadIdx.x & 31;
+  const int64_t groups = (p.n_tokens + 31) / 32;
+  const int64_t chunks = (half + kRopeJ - 1) / kRopeJ;
+  const int64_t hgroups = (p.num_heads + p.heads_per_item - 1) / p.heads_per_item;
+  const int64_t items = groups * chunks * hgroups;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t it = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; it < items; it += nwarps) {
+    // head groups fastest: the warps sharing a (token group, pair chunk) share its cos / sin rows
+    const int64_t hg = it % hgroups;
+    const int64_t rest = it / hgroups;
+    const int j0 = static_cast<int>(rest % chunks) * kRopeJ;
+    const int64_t tok = (rest / chunks) * 32 + lane;
+    if (tok >= p.n_tokens) continue;
     const int64_t slot = load_index(p.slots, p.slots64, tok);
     if (slot < 0) continue;
     int64_t b, o;
     split_slot(slot, p.block_size, &b, &o);
     if (b >= p.num_blocks) continue;  // rejected by the host check unless validation is off
     const int64_t pos = load_index(p.positions, p.pos64, tok);
-    const int64_t base = b * p.sb + h * p.sh + o;
-    const int64_t e1 = p.t.interleaved ? 2 * j : j;
-    const int64_t e2 = p.t.interleaved ? 2 * j + 1 : j + half;
-    const float x1 = ld_as_f32(p.cache, base + e1 * p.sd, p.t.x_dt);
-    const float x2 = ld_as_f32(p.cache, base + e2 * p.sd, p.t.x_dt);
-    const float c = ld_as_f32(p.cos, pos * p.c_row + j * p.c_last, p.t.c_dt);
-    const float s = ld_as_f32(p.sin, pos * p.s_row + j * p.s_last, p.t.s_dt);
-    float o1, o2;
-    rotate(x1, x2, c, s, p.t, &o1, &o2);
-    st_from_f32(p.cache, base + e1 * p.sd, p.t.out_dt, o1);
-    st_from_f32(p.cache, base + e2 * p.sd, p.t.out_dt, o2);
+    const int nj = min(kRopeJ, half - j0);
+    float cs[kRopeJ], sn[kRopeJ];
+    // element offsets of pair j0 + q: first at (e0 + q * es) * sd, second one stride further
+    const int64_t es = p.t.interleaved ? 2 : 1;
+    const int64_t e0 = p.t.interleaved ? 2 * j0 : j0;
+    const int64_t gap = (p.t.interleaved ? 1 : half) * p.sd;
+    if (p.vec_tab && nj == kRopeJ) {
+      // the lane's 8 pairs are 32 contiguous bytes of its token's row: two 16-byte loads a table
+      const float4* cr = reinterpret_cast<const float4*>(static_cast<const float*>(p.cos) + pos * p.c_row + j0);
+      const float4* sr = reinterpret_cast<const float4*>(static_cast<const float*>(p.sin) + pos * p.s_row + j0);
+#pragma unroll
+      for (int v = 0; v < kRopeJ / 4; ++v) {
+        const float4 c4 = __ldg(cr + v), s4 = __ldg(sr + v);
+        cs[4 * v] = c4.x, cs[4 * v + 1] = c4.y, cs[4 * v + 2] = c4.z, cs[4 * v + 3] = c4.w;
+        sn[4 * v] = s4.x, sn[4 * v + 1] = s4.y, sn[4 * v + 2] = s4.z, sn[4 * v + 3] = s4.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < kRopeJ; ++q) {
+        const int j = j0 + q;
+        cs[q] = sn[q] = 0.f;
+        if (q < nj) {
+          cs[q] = ld_as_f32(p.cos, pos * p.c_row + j * p.c_last, p.t.c_dt);
+          sn[q] = ld_as_f32(p.sin, pos * p.s_row + j * p.s_last, p.t.s_dt);
+        }
+      }
+    }
+    const int64_t h0 = hg * p.heads_per_item;
+    const int64_t h1 = min(h0 + p.heads_per_item, p.num_heads);
+    for (int64_t h = h0; h < h1; ++h) {
+      const int64_t ba = b * p.sb + h * p.sh + o + e0 * p.sd;
+      const int64_t step = es * p.sd;
+      float x1[kRopeJ], x2[kRopeJ];
+#pragma unroll
+      for (int q = 0; q < kRopeJ; ++q) {
+        x1[q] = x2[q] = 0.f;
+        if (q < nj) {
+          x1[q] = ld_x<X>(p.cache, ba + q * step);
+          x2[q] = ld_x<X>(p.cache, ba + q * step + gap);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kRopeJ; ++q) {
+        if (q < nj) {
+          float o1, o2;
+          if constexpr (F32) {
+            o1 = __fsub_rn(__fmul_rn(x1[q], cs[q]), __fmul_rn(x2[q], sn[q]));
+            o2 = __fadd_rn(__fmul_rn(x1[q], sn[q]), __fmul_rn(x2[q], cs[q]));
+          } else {
+            rotate(x1[q], x2[q], cs[q], sn[q], p.t, &o1, &o2);
+          }
+          st_x<X>(p.cache, ba + q * step, o1);
+          st_x<X>(p.cache, ba + q * step + gap, o2);
+        }
+      }
+    }
   }
+}
+
+template <typename X, bool F32>
+static int launch_rope_cache(RopeCache& p, cudaStream_t st) {
+  const int threads = 256;
+  auto kern = rope_cache_kernel<X, F32>;
+  // Heads per warp item: all of them (cos / sin loaded once per token and pair: lanes read 32
+  // different table rows, so the table loads cost as much L1 time as 8 heads of cache loads),
+  // halved only while the items would not fill the resident warps once.
+  const int64_t groups = (p.n_tokens + 31) / 32;
+  const int64_t chunks = (p.head_dim / 2 + kRopeJ - 1) / kRopeJ;
+  const int64_t resident_warps =
+      static_cast<int64_t>(blocks_per_sm(reinterpret_cast<const void*>(kern), threads, 0)) * sm_count() * (threads / 32);
+  int64_t hpi = p.num_heads;
+  while (hpi > 1 && groups * chunks * ((p.num_heads + hpi - 1) / hpi) < resident_warps) hpi = (hpi + 1) / 2;
+  p.heads_per_item = static_cast<int32_t>(std::min<int64_t>(hpi, 0x7fffffff));
+  const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  p.vec_tab = p.t.c_dt == MAK_DT_F32 && p.t.s_dt == MAK_DT_F32 && p.c_last == 1 && p.s_last == 1 &&
+              p.c_row % 4 == 0 && p.s_row % 4 == 0 && al16(p.cos) && al16(p.sin);
+  const int64_t items = groups * chunks * ((p.num_heads + hpi - 1) / hpi);
+  const int grid = grid_for(reinterpret_cast<const void*>(kern), threads, 0, (items + 7) / 8);
+  kern<<<grid, threads, 0, st>>>(p);
+  return launch_status("rope_cache_kernel");
 }
 
 static bool float_dt(int32_t dt) { return dt == MAK_DT_F16 || dt == MAK_DT_BF16 || dt == MAK_DT_F32; }
@@ -232,11 +337,13 @@ int mak_rope_key_cache(const mak_rope_cache_desc* d, void* stream) {
   p.slots64 = d->slot_dtype == MAK_DT_I64;
   p.pos64 = d->pos_dtype == MAK_DT_I64;
   if (p.n_tokens == 0) return MAK_OK;
-  const int threads = 256;
-  const int64_t work = p.n_tokens * p.num_heads * (p.head_dim / 2);
-  const int grid = grid_for(reinterpret_cast<const void*>(rope_cache_kernel), threads, 0, (work + threads - 1) / threads);
-  rope_cache_kernel<<<grid, threads, 0, as_stream(stream)>>>(p);
-  return launch_status("rope_cache_kernel");
+  const bool f32 = p.t.r1 == MAK_DT_F32 && p.t.r2 == MAK_DT_F32 && p.t.r3 == MAK_DT_F32;
+  cudaStream_t st = as_stream(stream);
+  if (p.t.x_dt == MAK_DT_F32)
+    return f32 ? launch_rope_cache<float, true>(p, st) : launch_rope_cache<float, false>(p, st);
+  if (p.t.x_dt == MAK_DT_F16)
+    return f32 ? launch_rope_cache<__half, true>(p, st) : launch_rope_cache<__half, false>(p, st);
+  return f32 ? launch_rope_cache<__nv_bfloat16, true>(p, st) : launch_rope_cache<__nv_bfloat16, false>(p, st);
 }
 
 }  // extern "C"

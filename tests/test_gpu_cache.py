@@ -101,6 +101,70 @@ def test_random_key_cache_vs_oracle(cuda_device):
     eq(dk, want, "key cache rope")
 
 
+def _block_table_slots(gen, nb, bs, whole, ragged):
+    """`whole` block-table blocks of `bs` tokens, a ragged run of `ragged` tokens, single tokens
+    and negative slots between them (all slots distinct)."""
+    blocks = torch.randperm(nb, generator=gen)[: whole + 2]
+    runs = (blocks[:whole, None] * bs + torch.arange(bs)).flatten()
+    tail = blocks[whole] * bs + torch.arange(ragged)
+    singles = blocks[whole + 1] * bs + torch.tensor([0, 5, 3])
+    return torch.cat([runs[: len(runs) // 2], torch.tensor([-1]), tail, singles, torch.tensor([-1, -7]),
+                      runs[len(runs) // 2:]])
+
+
+@pytest.mark.parametrize("skip_validation", (False, True))
+@pytest.mark.parametrize("inter", (False, True))
+@pytest.mark.parametrize("hd", (128, 20))
+@pytest.mark.parametrize("cn", DT)
+def test_key_cache_block_tables_fp32_tables_vs_oracle(cuda_device, monkeypatch, cn, hd, inter, skip_validation):
+    """fp32 cos / sin tables (every product in fp32) on block-table slots: lanes walk the tokens
+    of a block together; head_dim 20 leaves a partial group of rotation pairs."""
+    if skip_validation:
+        monkeypatch.setenv("MUSA_AITER_SKIP_VALIDATION", "1")
+    gen = torch.Generator().manual_seed(11 + hd)
+    nb, nh, bs = 96, 8, 16
+    kc = (torch.randn((nb, nh, hd, bs), generator=gen) * 3).to(TORCH_OF[cn])
+    slots = _block_table_slots(gen, nb, bs, 40, 7)
+    pos = torch.randint(0, 2048, (slots.numel(),), generator=gen)
+    ang = torch.rand((2048, hd // 2), generator=gen) * 80
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    dk = kc.cuda()
+    ma.apply_rope_to_key_cache(dk, slots.cuda(), pos.cuda(), cos.cuda(), sin.cuda(), interleaved=inter)
+    want = to_np(kc).copy()
+    O.apply_rope_to_key_cache(want, slots.numpy(), pos.numpy(), cos.numpy(), sin.numpy(), cache_dtype=cn,
+                              cos_dtype="float32", sin_dtype="float32", interleaved=inter)
+    eq(dk, want, f"{cn} cache, head_dim {hd}, interleaved={inter}")
+
+
+@pytest.mark.parametrize("table", ("contiguous", "column view"))
+@pytest.mark.parametrize("whole", (300, 1200))
+def test_key_cache_large_block_tables_vs_oracle(cuda_device, whole, table):
+    """Enough tokens for warp items of several heads (300 blocks) and of every head (1200), in a
+    head-strided view of a wider cache, int32 slots and positions; fp32 tables read 16 bytes at a
+    time when contiguous, element by element as a column view of a wider table."""
+    gen = torch.Generator().manual_seed(whole)
+    nb, nh, hd, bs = 1300, 8, 128, 16
+    wide = (torch.randn((nb, nh + 2, hd, bs), generator=gen) * 3).to(torch.bfloat16)
+    slots = _block_table_slots(gen, nb, bs, whole, 11).to(torch.int32)
+    pos = torch.randint(0, 8192, (slots.numel(),), generator=gen).to(torch.int32)
+    ang = torch.rand((8192, hd // 2), generator=gen) * 80
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    if table == "contiguous":
+        dcos, dsin = cos.cuda(), sin.cuda()
+    else:
+        dcos = torch.zeros((8192, hd // 2 + 3), device="cuda")[:, 1:hd // 2 + 1]
+        dsin = torch.zeros((8192, hd // 2 + 3), device="cuda")[:, 2:hd // 2 + 2]
+        dcos.copy_(cos)
+        dsin.copy_(sin)
+    dw = wide.cuda()
+    ma.apply_rope_to_key_cache(dw[:, 1:nh + 1], slots.cuda(), pos.cuda(), dcos, dsin)
+    want = to_np(wide).copy()
+    view = want[:, 1:nh + 1]
+    O.apply_rope_to_key_cache(view, slots.numpy(), pos.numpy(), cos.numpy(), sin.numpy(), cache_dtype="bfloat16",
+                              cos_dtype="float32", sin_dtype="float32")
+    eq(dw, want, f"{whole} whole blocks, heads 1..{nh} of {nh + 2}")
+
+
 def test_reference_errors(cuda_device):
     kc = torch.zeros(1, 1, 4, 2, device="cuda")
     with pytest.raises(ValueError, match="position exceeds cos/sin table"):

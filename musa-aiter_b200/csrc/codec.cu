@@ -69,21 +69,24 @@ struct Elem<MAK_DT_F32> {
 };
 
 // Grid-stride over 16-byte vectors (when x is 16-byte aligned) with a scalar tail.
+constexpr int kMinmaxU = 8;
 template <int DT>
-__global__ void minmax_kernel(const void* x, int64_t n, int vec_ok, uint32_t* keys) {
+__global__ void __launch_bounds__(256, 4) minmax_kernel(const void* x, int64_t n, int vec_ok, uint32_t* keys) {
   constexpr int VE = Elem<DT>::VE;
   float lo = 3.402823466e38f, hi = -3.402823466e38f;
   const int64_t nv = vec_ok ? n / VE : 0;
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
-  // four independent 16-byte loads per thread in flight
-  for (int64_t i0 = tid; i0 < nv; i0 += 4 * nt) {
-    uint4 v[4];
+  pdl_wait();
+  // eight independent 16-byte loads per thread in flight (four left the pass at 0.66 of DRAM
+  // peak, stalled on each iteration's round trip)
+  for (int64_t i0 = tid; i0 < nv; i0 += kMinmaxU * nt) {
+    uint4 v[kMinmaxU];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < kMinmaxU; ++u)
       if (i0 + u * nt < nv) v[u] = __ldg(xv + i0 + u * nt);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kMinmaxU; ++u) {
       if (i0 + u * nt >= nv) continue;
 #pragma unroll
       for (int e = 0; e < VE; ++e) {
@@ -98,6 +101,7 @@ __global__ void minmax_kernel(const void* x, int64_t n, int vec_ok, uint32_t* ke
     lo = fminf(lo, f);
     hi = fmaxf(hi, f);
   }
+  pdl_trigger();
   for (int o = 16; o > 0; o >>= 1) {
     lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
     hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
@@ -125,17 +129,40 @@ __global__ void minmax_kernel(const void* x, int64_t n, int vec_ok, uint32_t* ke
   }
 }
 
+// The CacheGen chain (key init, min/max, finish, count clear, encode, CDF, codebook) is launched
+// with programmatic dependent launch: each small kernel's launch overlaps the previous one's drain.
+__global__ void minmax_init_kernel(uint32_t* keys) {
+  pdl_wait();
+  keys[0] = 0xFFFFFFFFu;  // the min key starts at the largest key, the max key at the smallest
+  keys[1] = 0u;
+  pdl_trigger();
+}
+
+__global__ void clear_counts_kernel(unsigned long long* counts, int bins) {
+  pdl_wait();
+  for (int b = threadIdx.x; b < bins; b += blockDim.x) counts[b] = 0;
+  pdl_trigger();
+}
+
 __global__ void minmax_finish_kernel(uint32_t* keys) {
+  pdl_wait();
+  pdl_trigger();
   float* out = reinterpret_cast<float*>(keys);
   const float lo = key2f(keys[0]), hi = key2f(keys[1]);
   out[0] = lo;
   out[1] = hi;
 }
 
-__device__ __forceinline__ uint32_t cachegen_code(float v, float lo, float scale, float top) {
-  float q = rintf(__fmul_rn(__fsub_rn(v, lo), scale));
-  q = fminf(fmaxf(q, 0.f), top);  // fmaxf drops a NaN (max == min case) to 0
-  return static_cast<uint32_t>(q);
+// The code of v as the bits of an fp32 number 1.5 * 2^23 + code: q is clamped to [0, top] first
+// (fmaxf drops a NaN, the max == min case, to 0), then adding 1.5 * 2^23 rounds it to the nearest
+// integer, ties to even (the sum's unit in the last place is 1), which lands in the low mantissa
+// bits.  Clamping before rounding equals rounding before clamping for integer bounds.  This is
+// the classic magic-number rounding: no conversion-pipe instruction (rint, float-to-int), which
+// run at a quarter of the fp32 rate and bounded the encode pass at two per element.
+constexpr uint32_t kCodeBias = 0x4B400000u;  // bits of 1.5 * 2^23
+__device__ __forceinline__ uint32_t cachegen_code_bits(float v, float lo, float scale, float top) {
+  const float q = fminf(fmaxf(__fmul_rn(__fsub_rn(v, lo), scale), 0.f), top);
+  return __float_as_uint(__fadd_rn(q, 12582912.0f));
 }
 
 // Codes of VE elements per 16-byte vector (one VE-byte store), counted in
@@ -153,6 +180,7 @@ __global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int
   const int wib = threadIdx.x >> 5;
   for (int b = threadIdx.x; b < 8 * kHistCopies * kHistPitch; b += blockDim.x) (&hist[0][0])[b] = 0;
   __syncthreads();
+  pdl_wait();
   const float lo = minmax[0], hi = minmax[1];
   const float scale = __fmul_rn(__frcp_rn(__fsub_rn(hi, lo)), static_cast<float>(bins - 1));
   const float top = static_cast<float>(bins - 1);
@@ -160,25 +188,28 @@ __global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
   unsigned int* h = hist[wib * kHistCopies + (threadIdx.x & (kHistCopies - 1))];
-  // two independent 16-byte loads per thread in flight
+  // two independent 16-byte loads per thread in flight; the slab is walked from its end, so the
+  // first vectors read are the ones the min/max pass read last and are likely still in L2
   for (int64_t i0 = tid; i0 < nv; i0 += 2 * nt) {
     uint4 vv[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u)
-      if (i0 + u * nt < nv) vv[u] = __ldg(xv + i0 + u * nt);
+      if (i0 + u * nt < nv) vv[u] = __ldg(xv + (nv - 1 - (i0 + u * nt)));
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int64_t i = i0 + u * nt;
-      if (i >= nv) continue;
-      uint32_t packed[VE / 4];
-#pragma unroll
-      for (int w = 0; w < VE / 4; ++w) packed[w] = 0;
+      if (i0 + u * nt >= nv) continue;
+      const int64_t i = nv - 1 - (i0 + u * nt);
+      uint32_t cb[VE], packed[VE / 4];
 #pragma unroll
       for (int e = 0; e < VE; ++e) {
-        const uint32_t c = cachegen_code(Elem<DT>::at(vv[u], e), lo, scale, top);
-        packed[e >> 2] |= c << (8 * (e & 3));
-        atomicAdd(h + c, 1u);
+        cb[e] = cachegen_code_bits(Elem<DT>::at(vv[u], e), lo, scale, top);
+        atomicAdd(h + (cb[e] - kCodeBias), 1u);
       }
+      // the low byte of each code's bits is the code: three byte permutes pack four
+#pragma unroll
+      for (int w = 0; w < VE / 4; ++w)
+        packed[w] = __byte_perm(__byte_perm(cb[4 * w], cb[4 * w + 1], 0x0040),
+                                __byte_perm(cb[4 * w + 2], cb[4 * w + 3], 0x0040), 0x5410);
       if (VE == 8) {
         reinterpret_cast<uint2*>(codes)[i] = make_uint2(packed[0], packed[VE / 4 - 1]);
       } else {
@@ -187,10 +218,11 @@ __global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int
     }
   }
   for (int64_t i = nv * VE + tid; i < n; i += nt) {
-    const uint32_t c = cachegen_code(load_f32(x, DT, i), lo, scale, top);
+    const uint32_t c = cachegen_code_bits(load_f32(x, DT, i), lo, scale, top) - kCodeBias;
     codes[i] = static_cast<uint8_t>(c);
     atomicAdd(h + c, 1u);
   }
+  pdl_trigger();
   __syncthreads();
   for (int b = threadIdx.x; b < bins; b += blockDim.x) {
     unsigned int t = 0;
@@ -206,6 +238,8 @@ __global__ void __launch_bounds__(256) cachegen_encode_kernel(const void* x, int
 // lane then divides its own bins.  (A single thread summing counts from shared memory took
 // 12-13 us.)
 __global__ void cachegen_cdf_kernel(const unsigned long long* counts, int bins, int64_t n, float* cdf) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x;
   float v[8];
 #pragma unroll
@@ -237,6 +271,8 @@ __global__ void cachegen_cdf_kernel(const unsigned long long* counts, int bins, 
 // divided once, the first half counted up from min and the second half down from max, each a
 // fused multiply-add; a slab with max == min gets min in every bin (the reference's torch.full).
 __global__ void cachegen_codebook_kernel(const float* minmax, int bins, float* codebook) {
+  pdl_wait();
+  pdl_trigger();
   const float lo = minmax[0], hi = minmax[1];
   const float step = __fdiv_rn(__fsub_rn(hi, lo), static_cast<float>(bins - 1));
   const int halfway = bins / 2;
@@ -309,22 +345,19 @@ int mak_minmax(const void* x, int32_t dtype, int64_t n, float* out_minmax, void*
   if (n <= 0 || !x || !out_minmax) return fail(MAK_E_INVALID, "mak_minmax: empty input or NULL pointer");
   cudaStream_t st = as_stream(stream);
   uint32_t* keys = reinterpret_cast<uint32_t*>(out_minmax);
-  cudaError_t e = cudaMemsetAsync(keys, 0xFF, sizeof(uint32_t), st);  // min key starts at the largest key
-  if (e == cudaSuccess) e = cudaMemsetAsync(keys + 1, 0x00, sizeof(uint32_t), st);
-  if (e != cudaSuccess) return cuda_fail(e, "mak_minmax: init");
+  int rc = launch_pdl("minmax_init_kernel", minmax_init_kernel, dim3(1), dim3(32), 0, st, keys);
+  if (rc) return rc;
   const int threads = 256;
   const int vec_ok = aligned16p(x);
   const void* kern = dtype == MAK_DT_F16 ? reinterpret_cast<const void*>(minmax_kernel<MAK_DT_F16>)
                      : dtype == MAK_DT_BF16 ? reinterpret_cast<const void*>(minmax_kernel<MAK_DT_BF16>)
                                             : reinterpret_cast<const void*>(minmax_kernel<MAK_DT_F32>);
   const int grid = grid_for(kern, threads, 0, (n / 4 + threads - 1) / threads + 1);
-  if (dtype == MAK_DT_F16) minmax_kernel<MAK_DT_F16><<<grid, threads, 0, st>>>(x, n, vec_ok, keys);
-  else if (dtype == MAK_DT_BF16) minmax_kernel<MAK_DT_BF16><<<grid, threads, 0, st>>>(x, n, vec_ok, keys);
-  else minmax_kernel<MAK_DT_F32><<<grid, threads, 0, st>>>(x, n, vec_ok, keys);
-  int rc = launch_status("minmax_kernel");
+  auto mm = dtype == MAK_DT_F16 ? minmax_kernel<MAK_DT_F16> : dtype == MAK_DT_BF16 ? minmax_kernel<MAK_DT_BF16>
+                                                                                     : minmax_kernel<MAK_DT_F32>;
+  rc = launch_pdl("minmax_kernel", mm, dim3(grid), dim3(threads), 0, st, x, n, vec_ok, keys);
   if (rc) return rc;
-  minmax_finish_kernel<<<1, 1, 0, st>>>(keys);
-  return launch_status("minmax_finish_kernel");
+  return launch_pdl("minmax_finish_kernel", minmax_finish_kernel, dim3(1), dim3(1), 0, st, keys);
 }
 
 int mak_cachegen_encode(const void* x, int32_t dtype, int64_t n, const float* minmax, int32_t num_bins, uint8_t* codes,
@@ -334,8 +367,9 @@ int mak_cachegen_encode(const void* x, int32_t dtype, int64_t n, const float* mi
   if (n <= 0) return MAK_OK;
   if (!x || !minmax || !codes || !counts || !cdf) return fail(MAK_E_INVALID, "mak_cachegen_encode: NULL pointer");
   cudaStream_t st = as_stream(stream);
-  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(uint64_t) * num_bins, st);
-  if (e != cudaSuccess) return cuda_fail(e, "mak_cachegen_encode: clear counts");
+  auto* cnt0 = reinterpret_cast<unsigned long long*>(counts);
+  int rc = launch_pdl("clear_counts_kernel", clear_counts_kernel, dim3(1), dim3(256), 0, st, cnt0, num_bins);
+  if (rc) return rc;
   const int threads = 256;
   // vector path: 16-byte input vectors and VE-byte code stores (codes aligned to VE bytes)
   const int ve = dtype == MAK_DT_F32 ? 4 : 8;
@@ -345,20 +379,21 @@ int mak_cachegen_encode(const void* x, int32_t dtype, int64_t n, const float* mi
                      : dtype == MAK_DT_BF16 ? reinterpret_cast<const void*>(cachegen_encode_kernel<MAK_DT_BF16>)
                                             : reinterpret_cast<const void*>(cachegen_encode_kernel<MAK_DT_F32>);
   const int grid = grid_for(kern, threads, 0, (n / ve + threads - 1) / threads + 1);
-  if (dtype == MAK_DT_F16) cachegen_encode_kernel<MAK_DT_F16><<<grid, threads, 0, st>>>(x, n, vec_ok, minmax, num_bins, codes, cnt);
-  else if (dtype == MAK_DT_BF16) cachegen_encode_kernel<MAK_DT_BF16><<<grid, threads, 0, st>>>(x, n, vec_ok, minmax, num_bins, codes, cnt);
-  else cachegen_encode_kernel<MAK_DT_F32><<<grid, threads, 0, st>>>(x, n, vec_ok, minmax, num_bins, codes, cnt);
-  int rc = launch_status("cachegen_encode_kernel");
+  auto enc = dtype == MAK_DT_F16    ? cachegen_encode_kernel<MAK_DT_F16>
+             : dtype == MAK_DT_BF16 ? cachegen_encode_kernel<MAK_DT_BF16>
+                                    : cachegen_encode_kernel<MAK_DT_F32>;
+  rc = launch_pdl("cachegen_encode_kernel", enc, dim3(grid), dim3(threads), 0, st, x, n, vec_ok, minmax, num_bins, codes,
+                  cnt);
   if (rc) return rc;
-  cachegen_cdf_kernel<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned long long*>(counts), num_bins, n, cdf);
-  return launch_status("cachegen_cdf_kernel");
+  return launch_pdl("cachegen_cdf_kernel", cachegen_cdf_kernel, dim3(1), dim3(32), 0, st,
+                    reinterpret_cast<const unsigned long long*>(counts), num_bins, n, cdf);
 }
 
 int mak_cachegen_codebook(const float* minmax, int32_t num_bins, float* codebook, void* stream) {
   if (num_bins < 2 || num_bins > 256) return fail(MAK_E_INVALID, "mak_cachegen_codebook: num_bins must be in [2, 256]");
   if (!minmax || !codebook) return fail(MAK_E_INVALID, "mak_cachegen_codebook: NULL pointer");
-  cachegen_codebook_kernel<<<1, 256, 0, as_stream(stream)>>>(minmax, num_bins, codebook);
-  return launch_status("cachegen_codebook_kernel");
+  return launch_pdl("cachegen_codebook_kernel", cachegen_codebook_kernel, dim3(1), dim3(256), 0, as_stream(stream),
+                    minmax, num_bins, codebook);
 }
 
 int mak_cachegen_decode(const uint8_t* codes, int64_t n, const void* codebook, int32_t codebook_dtype, int32_t num_bins,

@@ -235,6 +235,8 @@ int resolve_last_writer(const void* slots, int32_t slot_dtype, int64_t n, const 
 __global__ void build_slot_mapping_kernel(const void* bt, int bt64, int64_t bt_stride, const void* lens, int len64,
                                           int64_t batch, int64_t max_seq, int64_t bs, int64_t* slots) {
   const int64_t total = batch * max_seq;
+  pdl_wait();
+  pdl_trigger();  // the tile launch that follows waits for this grid's completion all the same
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = i / max_seq, s = i - b * max_seq;
     const int64_t len = load_index(lens, len64, b);
@@ -306,10 +308,10 @@ int mak_build_slot_mapping(const void* block_tables, int32_t bt_dtype, int64_t b
   if (!block_tables || !seq_lens || !slots) return fail(MAK_E_INVALID, "mak_build_slot_mapping: NULL pointer");
   const int threads = 256;
   int grid = grid_for(reinterpret_cast<const void*>(build_slot_mapping_kernel), threads, 0, (total + threads - 1) / threads);
-  build_slot_mapping_kernel<<<grid, threads, 0, as_stream(stream)>>>(block_tables, bt_dtype == MAK_DT_I64, bt_stride,
-                                                                     seq_lens, len_dtype == MAK_DT_I64, batch, max_seq,
-                                                                     block_size, slots);
-  return launch_status("build_slot_mapping_kernel");
+  // programmatic dependent launch: the launch overlaps the previous kernel's drain
+  return launch_pdl("build_slot_mapping_kernel", build_slot_mapping_kernel, dim3(grid), dim3(threads), 0,
+                    as_stream(stream), block_tables, static_cast<int>(bt_dtype == MAK_DT_I64), bt_stride, seq_lens,
+                    static_cast<int>(len_dtype == MAK_DT_I64), batch, max_seq, block_size, slots);
 }
 
 }  // extern "C"

@@ -292,6 +292,8 @@ template <int OUT>
 __global__ void __launch_bounds__(256) cachegen_decode_kernel(const uint8_t* codes, int64_t n, int vec_ok,
                                                               const void* codebook, int cb_dt, int bins, void* out) {
   __shared__ uint32_t book[256];  // output-type bit pattern of each code (0 beyond the codebook)
+  pdl_wait();
+  pdl_trigger();
   for (int c = threadIdx.x; c < 256; c += blockDim.x) {
     const float v = c < bins ? load_f32(codebook, cb_dt, c) : 0.f;
     uint32_t b;
@@ -410,13 +412,11 @@ int mak_cachegen_decode(const uint8_t* codes, int64_t n, const void* codebook, i
                      : out_dtype == MAK_DT_BF16 ? reinterpret_cast<const void*>(cachegen_decode_kernel<MAK_DT_BF16>)
                                                 : reinterpret_cast<const void*>(cachegen_decode_kernel<MAK_DT_F32>);
   const int grid = grid_for(kern, threads, 0, (n / 16 + threads - 1) / threads + 1);
-  if (out_dtype == MAK_DT_F16)
-    cachegen_decode_kernel<MAK_DT_F16><<<grid, threads, 0, st>>>(codes, n, vec_ok, codebook, codebook_dtype, num_bins, out);
-  else if (out_dtype == MAK_DT_BF16)
-    cachegen_decode_kernel<MAK_DT_BF16><<<grid, threads, 0, st>>>(codes, n, vec_ok, codebook, codebook_dtype, num_bins, out);
-  else
-    cachegen_decode_kernel<MAK_DT_F32><<<grid, threads, 0, st>>>(codes, n, vec_ok, codebook, codebook_dtype, num_bins, out);
-  return launch_status("cachegen_decode_kernel");
+  auto dec = out_dtype == MAK_DT_F16    ? cachegen_decode_kernel<MAK_DT_F16>
+             : out_dtype == MAK_DT_BF16 ? cachegen_decode_kernel<MAK_DT_BF16>
+                                        : cachegen_decode_kernel<MAK_DT_F32>;
+  return launch_pdl("cachegen_decode_kernel", dec, dim3(grid), dim3(threads), 0, st, codes, n, vec_ok, codebook,
+                    codebook_dtype, num_bins, out);
 }
 
 }  // extern "C"

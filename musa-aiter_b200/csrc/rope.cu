@@ -156,6 +156,8 @@ __global__ void __launch_bounds__(256, F32 ? 3 : 2) rope_cache_kernel(const __gr
   const int64_t hgroups = (p.num_heads + p.heads_per_item - 1) / p.heads_per_item;
   const int64_t items = groups * chunks * hgroups;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  pdl_wait();
+  pdl_trigger();
   for (int64_t it = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; it < items; it += nwarps) {
     // head groups fastest: the warps sharing a (token group, pair chunk) share its cos / sin rows
     const int64_t hg = it % hgroups;
@@ -247,8 +249,7 @@ static int launch_rope_cache(RopeCache& p, cudaStream_t st) {
               p.c_row % 4 == 0 && p.s_row % 4 == 0 && al16(p.cos) && al16(p.sin);
   const int64_t items = groups * chunks * ((p.num_heads + hpi - 1) / hpi);
   const int grid = grid_for(reinterpret_cast<const void*>(kern), threads, 0, (items + 7) / 8);
-  kern<<<grid, threads, 0, st>>>(p);
-  return launch_status("rope_cache_kernel");
+  return launch_pdl("rope_cache_kernel", kern, dim3(grid), dim3(threads), 0, st, p);
 }
 
 static bool float_dt(int32_t dt) { return dt == MAK_DT_F16 || dt == MAK_DT_BF16 || dt == MAK_DT_F32; }

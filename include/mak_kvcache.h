@@ -581,7 +581,9 @@ typedef struct mak_rope_cache_desc {
  * Rotate key_cache[block, :, :, offset] of every token in place with the cos /
  * sin row of its position.  Slots must be distinct within one call (the caller
  * splits repeated slots into successive calls, which keeps the reference's
- * token order).  Replaces apply_rope_to_key_cache (musa_aiter/ops/cache.py:45-102).
+ * token order).  Tokens with a negative slot or position, or a block past
+ * num_blocks, are skipped; positions must lie inside the cos / sin table.
+ * Replaces apply_rope_to_key_cache (musa_aiter/ops/cache.py:45-102).
  */
 MAK_API int mak_rope_key_cache(const mak_rope_cache_desc* desc, void* stream);
 

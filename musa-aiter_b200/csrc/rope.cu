@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(256, F32 ? 3 : 2) rope_cache_kernel(const __gr
     split_slot(slot, p.block_size, &b, &o);
     if (b >= p.num_blocks) continue;  // rejected by the host check unless validation is off
     const int64_t pos = load_index(p.positions, p.pos64, tok);
+    if (pos < 0) continue;  // rejected by the host check unless validation is off
     const int nj = min(kRopeJ, half - j0);
     float cs[kRopeJ], sn[kRopeJ];
     // element offsets of pair j0 + q: first at (e0 + q * es) * sd, second one stride further

@@ -165,6 +165,27 @@ def test_key_cache_large_block_tables_vs_oracle(cuda_device, whole, table):
     eq(dw, want, f"{whole} whole blocks, heads 1..{nh} of {nh + 2}")
 
 
+def test_key_cache_negative_positions_skipped_without_validation(cuda_device, monkeypatch):
+    """With validation off nothing is read back, and a token whose position is negative (which
+    the host check rejects) is skipped by the kernel instead of reading before the table."""
+    monkeypatch.setenv("MUSA_AITER_SKIP_VALIDATION", "1")
+    gen = torch.Generator().manual_seed(21)
+    nb, nh, hd, bs = 32, 4, 64, 16
+    kc = (torch.randn((nb, nh, hd, bs), generator=gen) * 3).to(torch.bfloat16)
+    slots = _block_table_slots(gen, nb, bs, 6, 5)
+    pos = torch.randint(0, 512, (slots.numel(),), generator=gen)
+    pos[::7] = -3
+    ang = torch.rand((512, hd // 2), generator=gen) * 80
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    dk = kc.cuda()
+    ma.apply_rope_to_key_cache(dk, slots.cuda(), pos.cuda(), cos.cuda(), sin.cuda())
+    keep = pos >= 0
+    want = to_np(kc).copy()
+    O.apply_rope_to_key_cache(want, slots[keep].numpy(), pos[keep].numpy(), cos.numpy(), sin.numpy(),
+                              cache_dtype="bfloat16", cos_dtype="float32", sin_dtype="float32")
+    eq(dk, want, "negative positions skipped")
+
+
 def test_reference_errors(cuda_device):
     kc = torch.zeros(1, 1, 4, 2, device="cuda")
     with pytest.raises(ValueError, match="position exceeds cos/sin table"):

@@ -112,19 +112,22 @@ def _block_table_slots(gen, nb, bs, whole, ragged):
                       runs[len(runs) // 2:]])
 
 
+@pytest.mark.parametrize("whole", (40, 70))
 @pytest.mark.parametrize("skip_validation", (False, True))
 @pytest.mark.parametrize("inter", (False, True))
 @pytest.mark.parametrize("hd", (128, 20))
 @pytest.mark.parametrize("cn", DT)
-def test_key_cache_block_tables_fp32_tables_vs_oracle(cuda_device, monkeypatch, cn, hd, inter, skip_validation):
+def test_key_cache_block_tables_fp32_tables_vs_oracle(cuda_device, monkeypatch, cn, hd, inter, skip_validation,
+                                                      whole):
     """fp32 cos / sin tables (every product in fp32) on block-table slots: lanes walk the tokens
-    of a block together; head_dim 20 leaves a partial group of rotation pairs."""
+    of a block together; head_dim 20 leaves a partial group of rotation pairs; 40 and 70 whole
+    blocks give calls below and above 1024 tokens."""
     if skip_validation:
         monkeypatch.setenv("MUSA_AITER_SKIP_VALIDATION", "1")
-    gen = torch.Generator().manual_seed(11 + hd)
+    gen = torch.Generator().manual_seed(11 + hd + whole)
     nb, nh, bs = 96, 8, 16
     kc = (torch.randn((nb, nh, hd, bs), generator=gen) * 3).to(TORCH_OF[cn])
-    slots = _block_table_slots(gen, nb, bs, 40, 7)
+    slots = _block_table_slots(gen, nb, bs, whole, 7)
     pos = torch.randint(0, 2048, (slots.numel(),), generator=gen)
     ang = torch.rand((2048, hd // 2), generator=gen) * 80
     cos, sin = torch.cos(ang), torch.sin(ang)
@@ -165,14 +168,16 @@ def test_key_cache_large_block_tables_vs_oracle(cuda_device, whole, table):
     eq(dw, want, f"{whole} whole blocks, heads 1..{nh} of {nh + 2}")
 
 
-def test_key_cache_negative_positions_skipped_without_validation(cuda_device, monkeypatch):
+@pytest.mark.parametrize("whole", (6, 80))
+def test_key_cache_negative_positions_skipped_without_validation(cuda_device, monkeypatch, whole):
     """With validation off nothing is read back, and a token whose position is negative (which
-    the host check rejects) is skipped by the kernel instead of reading before the table."""
+    the host check rejects) is skipped by the kernel instead of reading before the table (calls
+    of 6 and 80 whole blocks)."""
     monkeypatch.setenv("MUSA_AITER_SKIP_VALIDATION", "1")
-    gen = torch.Generator().manual_seed(21)
-    nb, nh, hd, bs = 32, 4, 64, 16
+    gen = torch.Generator().manual_seed(21 + whole)
+    nb, nh, hd, bs = 96, 4, 64, 16
     kc = (torch.randn((nb, nh, hd, bs), generator=gen) * 3).to(torch.bfloat16)
-    slots = _block_table_slots(gen, nb, bs, 6, 5)
+    slots = _block_table_slots(gen, nb, bs, whole, 5)
     pos = torch.randint(0, 512, (slots.numel(),), generator=gen)
     pos[::7] = -3
     ang = torch.rand((512, hd // 2), generator=gen) * 80

@@ -290,6 +290,30 @@ def test_cachegen(misc):
             assert same_bits(O.from_f32(O.kv_cachegen_decode(enc, cb), dt), misc[f"{p}/dec"]), name
 
 
+@pytest.mark.parametrize("bins", (2, 17, 256))
+def test_cachegen_magic_number_rounding_matches_rint_clamp(bins):
+    """The encode kernel forms a code as clamp(q, 0, bins - 1) + 1.5 * 2^23 in fp32 and keeps the
+    low mantissa bits (no rint / float-to-int conversion); the oracle rounds half to even and
+    clamps.  Same codes for every quotient the kernel can meet: uniform values over and beyond the
+    range, every half-integer and its fp32 neighbours, signed zero, infinities and NaN (which
+    fmaxf, like numpy's fmax, drops to 0)."""
+    rng = np.random.default_rng(bins)
+    top = np.float32(bins - 1)
+    halves = np.arange(-4, bins + 4, dtype=np.float32)[:, None] + np.float32(0.5)
+    q = np.concatenate([
+        rng.uniform(-3, bins + 3, 200_000).astype(np.float32),
+        halves.ravel(),
+        np.nextafter(halves, np.float32(-np.inf)).ravel(),
+        np.nextafter(halves, np.float32(np.inf)).ravel(),
+        np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 3e38, -3e38, 1e-45], dtype=np.float32),
+    ])
+    with np.errstate(invalid="ignore"):
+        want = np.fmin(np.fmax(np.rint(q), np.float32(0)), top).astype(np.uint32)
+        clamped = np.fmin(np.fmax(q, np.float32(0)), top).astype(np.float32)
+        got = (clamped + np.float32(12582912.0)).astype(np.float32).view(np.uint32) - np.uint32(0x4B400000)
+    assert np.array_equal(got, want)
+
+
 # ---- MLA FP8 rows: the reference's element codec under per-128 group scales ----
 
 
